@@ -1,0 +1,134 @@
+/* moteopt: the B200-native optimizer step of the Mote trainer (Muon + AdamW + global grad-norm clip), as a C ABI.
+ *
+ * Every entry point takes plain device pointers, element counts, host-side hyperparameters and the CUDA stream to
+ * enqueue on; none allocates device memory, none synchronises the host. Scratch memory is the caller's
+ * `workspace` (query its size with the matching *_workspace_size function; it must stay allocated until the work
+ * enqueued on `stream` has finished; 256-byte aligned). The first bytes of the workspace hold a status word and the last grad norm,
+ * which moteopt_read_status() reads back.
+ *
+ * Every function returns MOTEOPT_OK (0) or a negative error code; moteopt_last_error() describes the last failure
+ * of the calling thread. References below are to the reference project noahsabaj/mote, path:line.
+ */
+#ifndef MOTEOPT_H_
+#define MOTEOPT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOTEOPT_API __attribute__((visibility("default")))
+#else
+#define MOTEOPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* moteopt_stream_t; /* a cudaStream_t; NULL = the legacy default stream */
+
+#define MOTEOPT_OK 0
+#define MOTEOPT_ERR_INVALID (-1)   /* bad argument: shape, dtype, null pointer, workspace too small */
+#define MOTEOPT_ERR_CUDA (-2)      /* a CUDA runtime call or kernel launch failed */
+#define MOTEOPT_ERR_LIMIT (-3)     /* more tensors than one call supports */
+#define MOTEOPT_ERR_DEVICE (-4)    /* the current device is not an sm_100 (B200-class) GPU */
+
+#define MOTEOPT_DTYPE_F32 0
+#define MOTEOPT_DTYPE_BF16 1
+
+/* status word bits (moteopt_read_status) */
+#define MOTEOPT_STATUS_WAIT_TIMEOUT 1   /* a pipeline wait in the Newton-Schulz kernel gave up (a library bug) */
+#define MOTEOPT_STATUS_ABORTED 2        /* a kernel unwound early after such a timeout */
+#define MOTEOPT_STATUS_NONFINITE 4      /* the global grad norm was NaN or Inf (the step proceeds, as torch's does) */
+
+/* One Muon parameter: a 2-D matrix [rows, cols] or a 3-D stack [batch, rows, cols] of matrices that are
+ * orthogonalised one by one (mote/train/muon.py:46-100, the `_muon_stack` case of muon.py:121). */
+typedef struct moteopt_muon_param {
+  float* param;                 /* fp32, contiguous */
+  const void* grad;             /* same shape, fp32 or bf16 (grad_dtype), contiguous */
+  float* momentum_buffer;       /* fp32, same shape; zeros before the first step (muon.py:66-67) */
+  int64_t batch;                /* 1 for a matrix */
+  int64_t rows, cols;
+  double lr;                    /* the effective lr: the group's, or its `param_lr` override (muon.py:77) */
+  double decay;                 /* the decoupled decay d of muon.py:78 (lr*wd, or lr^2/lr_max*wd for Muon-SW); 0 = none */
+  double momentum;              /* muon.py:55 */
+  int nesterov;                 /* muon.py:70 */
+  int grad_dtype;               /* MOTEOPT_DTYPE_* */
+} moteopt_muon_param;
+
+typedef struct moteopt_muon_config {
+  int ns_steps;                 /* Newton-Schulz iterations (muon.py:47, default 5) */
+  double rms_scale;             /* update scale = rms_scale * sqrt(max(rows, cols)) (muon.py:82, default 0.2) */
+  double ns_eps;                /* normalisation epsilon (muon.py:27, 1e-7) */
+} moteopt_muon_config;
+
+/* One AdamW tensor (torch.optim.AdamW as constructed at mote/train/train.py:98). */
+typedef struct moteopt_adamw_tensor {
+  float* param;
+  const void* grad;
+  float* exp_avg;               /* zeros before the first step */
+  float* exp_avg_sq;            /* zeros before the first step */
+  int64_t numel;
+  double lr;
+  double weight_decay;
+  int64_t step;                 /* the step count including this update (1 on the first step) */
+  int grad_dtype;
+} moteopt_adamw_tensor;
+
+typedef struct moteopt_adamw_hparams {
+  double beta1, beta2, eps;     /* train.py:98: betas=(0.9, beta2), eps=1e-8 */
+} moteopt_adamw_hparams;
+
+/* Gradient pre-processing of mote/train/train.py:944-946. */
+typedef struct moteopt_grad_config {
+  int clip;                     /* 1: clip_grad_norm_(all params, max_norm) before the updates */
+  double max_norm;
+  double grad_divisor;          /* train.py:945: grads /= total_n first; 0 or 1 = no division */
+} moteopt_grad_config;
+
+MOTEOPT_API int moteopt_version(void);
+MOTEOPT_API const char* moteopt_last_error(void);
+
+/* Read (and optionally clear) the workspace's status word and the last [total norm, clip coefficient].
+ * Synchronises `stream`. Either output may be NULL. */
+MOTEOPT_API int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream);
+
+/* ---- the whole optimizer step of mote/train/train.py:944-947: grads /= total_n; clip_grad_norm_(params, clip);
+ *      MultiOpt.step() = AdamW.step() then Muon.step() (train.py:64-66). The clip is folded into the update
+ *      kernels: the grads are read, never rewritten. `out_norm` (device, may be NULL) receives the total grad norm
+ *      before clipping, which clip_grad_norm_ returns and the trainer logs as grad_norm (train.py:954). */
+MOTEOPT_API size_t moteopt_optimizer_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps,
+                                             const moteopt_adamw_tensor* adamw, int n_adamw);
+MOTEOPT_API int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,
+                           const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* adamw_hp,
+                           const moteopt_grad_config* grad_cfg, float* out_norm, void* workspace,
+                           size_t workspace_bytes, moteopt_stream_t stream);
+
+/* ---- Muon.step() of one or more param groups (mote/train/muon.py:52-100). Parameters whose grad is NULL are
+ *      skipped by the caller (muon.py:61-62). `grad_scale` (device, may be NULL) multiplies every grad first. */
+MOTEOPT_API size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps);
+MOTEOPT_API int moteopt_muon_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* cfg,
+                      const float* grad_scale, void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
+
+/* ---- torch.optim.AdamW.step() (train.py:98; torch's single-tensor update with amsgrad=False). */
+MOTEOPT_API int moteopt_adamw_step(const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* hp,
+                       const float* grad_scale, moteopt_stream_t stream);
+
+/* ---- torch.nn.utils.clip_grad_norm_(params, max_norm) (train.py:946): the 2-norm of the per-tensor norms, then
+ *      grads *= min(1, max_norm / (norm + 1e-6)) in place. `out_norm` (device, may be NULL) receives the norm. */
+MOTEOPT_API size_t moteopt_clip_grad_norm_workspace_size(const int64_t* numels, int n);
+MOTEOPT_API int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int* dtypes, int n, double max_norm,
+                           float* out_norm, void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
+
+/* ---- newton_schulz(G, steps, eps) (mote/train/muon.py:26-43): G [batch, rows, cols] fp32 or bf16 -> out bf16 of
+ *      the same shape. Every matrix is normalised by its own Frobenius norm; the iteration runs on the transpose
+ *      of a matrix with more rows than columns. */
+MOTEOPT_API size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols);
+MOTEOPT_API int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, int64_t rows, int64_t cols,
+                          int steps, double eps, void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOTEOPT_H_ */

@@ -1,0 +1,907 @@
+// C-ABI entry points of the optimizer step (include/moteopt.h): argument checking, workspace layout, tensor-map
+// encoding (cached per workspace and shape group) and the launch sequence. No device memory is allocated here.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "moteopt.h"
+#include "mt_kernels.cuh"
+#include "ns_gemm.cuh"
+
+using namespace moteopt;
+
+namespace {
+
+thread_local std::string t_err;
+
+int fail(int code, const std::string& msg) {
+  t_err = msg;
+  return code;
+}
+
+#define MO_CUDA(expr)                                                                          \
+  do {                                                                                         \
+    cudaError_t e_ = (expr);                                                                   \
+    if (e_ != cudaSuccess) return fail(MOTEOPT_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define MO_LAUNCHED(what)                                                                      \
+  do {                                                                                         \
+    cudaError_t e_ = cudaGetLastError();                                                       \
+    if (e_ != cudaSuccess) return fail(MOTEOPT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+#define MO_TRY(expr)            \
+  do {                          \
+    int r_ = (expr);            \
+    if (r_ != MOTEOPT_OK) return r_; \
+  } while (0)
+
+constexpr size_t kHeaderBytes = 256;
+struct Header {
+  int status;
+  float norm;
+  float coef;
+  int pad;
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// per-device setup
+struct DeviceState {
+  bool ready = false;
+  int sms = 0;
+};
+std::mutex g_mu;
+DeviceState g_dev[64];
+
+int device_setup(int* sms) {
+  int dev = 0;
+  MO_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MOTEOPT_ERR_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0, count = 0;
+    MO_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    MO_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+    MO_CUDA(cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev));
+    if (major != 10 || minor != 0)
+      return fail(MOTEOPT_ERR_DEVICE, "libmoteopt is built for sm_100a (B200); device " + std::to_string(dev) +
+                                          " is sm_" + std::to_string(major) + std::to_string(minor));
+    MO_CUDA(cudaFuncSetAttribute(ns::ns_phase_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
+    d.sms = count;
+    d.ready = true;
+  }
+  *sms = d.sms;
+  return MOTEOPT_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tensor maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor [depth][outer][inner], row-major, 128-byte swizzled box {box_inner, box_outer, 1}
+int make_map(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uint64_t depth, uint32_t box_inner,
+             uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(MOTEOPT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {inner, outer, depth};
+  cuuint64_t strides[2] = {inner * 2, inner * outer * 2};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MOTEOPT_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return MOTEOPT_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Newton-Schulz batch layout
+struct MatRef {
+  int src;     // Muon param index (step mode) or 0 (direct mode)
+  int slice;   // matrix index inside a 3-D stack / the batch
+};
+
+struct GroupPlan {
+  int rows, cols;          // source matrix dims (R x C)
+  int transposed;          // R > C
+  int mv, nv, m, n;        // X dims: valid and padded to multiples of 8
+  std::vector<MatRef> mats;
+  size_t off_x0 = 0, off_x1 = 0, off_a = 0, off_b = 0;
+};
+
+struct Layout {
+  std::vector<GroupPlan> groups;          // Newton-Schulz shape groups, in launch order
+  std::vector<int> mat_chunk_start;       // per matrix (group-major order): sum-of-squares chunk prefix
+  std::vector<int> norm_tensor_chunk_start;
+  size_t off_norm = 0, off_mom = 0, bytes = 0;
+};
+
+constexpr int kMaxMatsPerGroup = ns::kMaxApply;
+
+struct ShapeKey {
+  int64_t rows, cols;
+  bool operator<(const ShapeKey& o) const { return std::tie(rows, cols) < std::tie(o.rows, o.cols); }
+};
+
+// shapes: per source (batch, rows, cols); norm_numels: the tensors of the global grad norm (may be empty)
+int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shapes, const std::vector<int64_t>& norm_numels,
+                 int ns_steps, Layout* L) {
+  L->groups.clear();
+  std::map<ShapeKey, std::vector<MatRef>> by_shape;
+  std::vector<ShapeKey> order;
+  for (size_t s = 0; s < shapes.size(); ++s) {
+    const int64_t b = std::get<0>(shapes[s]), r = std::get<1>(shapes[s]), c = std::get<2>(shapes[s]);
+    if (b < 1 || r < 1 || c < 1) return fail(MOTEOPT_ERR_INVALID, "Muon matrices must have batch, rows, cols >= 1");
+    if (r > (1 << 20) || c > (1 << 20)) return fail(MOTEOPT_ERR_INVALID, "matrix dimension above 2^20");
+    const ShapeKey k{r, c};
+    if (!by_shape.count(k)) order.push_back(k);
+    auto& v = by_shape[k];
+    for (int64_t e = 0; e < b; ++e) v.push_back(MatRef{static_cast<int>(s), static_cast<int>(e)});
+  }
+  for (const ShapeKey& k : order) {
+    const auto& all = by_shape[k];
+    for (size_t start = 0; start < all.size(); start += kMaxMatsPerGroup) {
+      GroupPlan g;
+      g.rows = static_cast<int>(k.rows);
+      g.cols = static_cast<int>(k.cols);
+      g.transposed = k.rows > k.cols;
+      g.mv = g.transposed ? g.cols : g.rows;
+      g.nv = g.transposed ? g.rows : g.cols;
+      g.m = static_cast<int>(align_up(g.mv, 8));
+      g.n = static_cast<int>(align_up(g.nv, 8));
+      g.mats.assign(all.begin() + start, all.begin() + std::min(all.size(), start + kMaxMatsPerGroup));
+      L->groups.push_back(std::move(g));
+    }
+  }
+  // largest Gram contraction first: a longest-processing-time order for the static tile schedule
+  std::stable_sort(L->groups.begin(), L->groups.end(), [](const GroupPlan& a, const GroupPlan& b) {
+    return static_cast<int64_t>(a.m) * a.n > static_cast<int64_t>(b.m) * b.n;
+  });
+  // chunk prefixes
+  L->mat_chunk_start.assign(1, 0);
+  for (const GroupPlan& g : L->groups)
+    for (size_t i = 0; i < g.mats.size(); ++i)
+      L->mat_chunk_start.push_back(L->mat_chunk_start.back() +
+                                   static_cast<int>(cdiv(static_cast<int64_t>(g.rows) * g.cols, kChunk)));
+  L->norm_tensor_chunk_start.assign(1, 0);
+  for (int64_t n : norm_numels) {
+    if (n < 0) return fail(MOTEOPT_ERR_INVALID, "negative numel");
+    L->norm_tensor_chunk_start.push_back(L->norm_tensor_chunk_start.back() + static_cast<int>(cdiv(n, kChunk)));
+  }
+  size_t off = kHeaderBytes;
+  L->off_norm = off;
+  off = align_up(off + 4 * static_cast<size_t>(L->norm_tensor_chunk_start.back()), 256);
+  L->off_mom = off;
+  off = align_up(off + 4 * static_cast<size_t>(L->mat_chunk_start.back()), 1024);
+  for (GroupPlan& g : L->groups) {
+    const size_t cnt = g.mats.size();
+    const size_t xb = cnt * g.m * g.n * 2, ab = cnt * g.m * g.m * 2;
+    g.off_x0 = off;
+    off = align_up(off + xb, 1024);
+    if (ns_steps > 0) {
+      g.off_x1 = off;
+      off = align_up(off + xb, 1024);
+      g.off_a = off;
+      off = align_up(off + ab, 1024);
+      g.off_b = off;
+      off = align_up(off + ab, 1024);
+    }
+  }
+  L->bytes = off;
+  return MOTEOPT_OK;
+}
+
+// cache of encoded tensor maps, keyed by the group's buffers and geometry
+struct MapKey {
+  uintptr_t x0, x1, a, b;
+  int m, n, count, dev;
+  bool operator<(const MapKey& o) const {
+    return std::tie(x0, x1, a, b, m, n, count, dev) < std::tie(o.x0, o.x1, o.a, o.b, o.m, o.n, o.count, o.dev);
+  }
+};
+struct MapSet {
+  CUtensorMap xk[2], xmn[2], ak, bk;
+};
+std::mutex g_map_mu;
+std::map<MapKey, MapSet> g_maps;
+
+int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
+  int dev = 0;
+  MO_CUDA(cudaGetDevice(&dev));
+  const int cnt = static_cast<int>(g.mats.size());
+  MapKey key{reinterpret_cast<uintptr_t>(ws + g.off_x0), reinterpret_cast<uintptr_t>(ws + g.off_x1),
+             reinterpret_cast<uintptr_t>(ws + g.off_a), reinterpret_cast<uintptr_t>(ws + g.off_b), g.m, g.n, cnt, dev};
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return MOTEOPT_OK;
+  }
+  MapSet s;
+  std::memset(&s, 0, sizeof(s));
+  void* x[2] = {ws + g.off_x0, ws + g.off_x1};
+  for (int k = 0; k < 2; ++k) {
+    MO_TRY(make_map(&s.xk[k], x[k], g.n, g.m, cnt, ns::BK, ns::BM));
+    MO_TRY(make_map(&s.xmn[k], x[k], g.n, g.m, cnt, 64, ns::BK));
+  }
+  MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::BM));
+  MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::BM));
+  if (g_maps.size() > 4096) g_maps.clear();
+  g_maps[key] = s;
+  *out = s;
+  return MOTEOPT_OK;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// launch helpers
+int grid_for(int chunks, int sms) { return std::max(1, std::min(chunks, sms * 8)); }
+
+struct GradSource {          // one tensor of the global grad norm
+  const void* g;
+  int64_t numel;
+  int dtype;
+};
+
+int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chunk_start, float* partials, bool has_div,
+                 float div, int sms, cudaStream_t st) {
+  SumsqArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.partials = partials;
+  A.has_div = has_div;
+  A.div = div;
+  for (size_t s0 = 0; s0 < src.size(); s0 += kMaxNormSeg) {
+    const size_t n = std::min(src.size() - s0, static_cast<size_t>(kMaxNormSeg));
+    A.n = static_cast<int>(n);
+    A.chunk_base = chunk_start[s0];
+    for (size_t i = 0; i < n; ++i) {
+      A.seg[i] = SumsqSeg{src[s0 + i].g, src[s0 + i].numel, src[s0 + i].dtype, 0};
+      A.chunk_start[i] = chunk_start[s0 + i] - A.chunk_base;
+    }
+    A.chunk_start[n] = chunk_start[s0 + n] - A.chunk_base;
+    if (A.chunk_start[n] == 0) continue;
+    sumsq_kernel<<<grid_for(A.chunk_start[n], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("sumsq_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+int launch_finalize(const std::vector<int>& tensor_chunk_start, const float* partials, bool clip, double max_norm,
+                    float* out, int* status, cudaStream_t st) {
+  const int n = static_cast<int>(tensor_chunk_start.size()) - 1;
+  if (n > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "more than 4096 tensors in one grad-norm call");
+  FinalizeArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.n_tensors = n;
+  A.has_clip = clip;
+  A.max_norm = static_cast<float>(max_norm);
+  A.partials = partials;
+  A.out = out;
+  A.status = status;
+  for (int i = 0; i <= n; ++i) A.tensor_chunk_start[i] = tensor_chunk_start[i];
+  norm_finalize_kernel<<<1, 1024, 0, st>>>(A);
+  MO_LAUNCHED("norm_finalize_kernel");
+  return MOTEOPT_OK;
+}
+
+int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp, bool has_div, float div,
+                 const float* coef, int sms, cudaStream_t st) {
+  AdamArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.has_div = has_div;
+  A.div = div;
+  A.coef = coef;
+  const double w = 1.0 - hp->beta1;
+  A.lerp_w = static_cast<float>(w);
+  A.lerp_small = std::fabs(static_cast<float>(w)) < 0.5f;
+  A.one_minus_w = 1.0f - static_cast<float>(w);
+  A.beta2 = static_cast<float>(hp->beta2);
+  A.one_minus_beta2 = static_cast<float>(1.0 - hp->beta2);
+  A.eps = static_cast<float>(hp->eps);
+  for (int s0 = 0; s0 < n; s0 += kMaxAdamSeg) {
+    const int cnt = std::min(n - s0, kMaxAdamSeg);
+    A.n = cnt;
+    A.chunk_start[0] = 0;
+    for (int i = 0; i < cnt; ++i) {
+      const moteopt_adamw_tensor& x = t[s0 + i];
+      AdamSeg& S = A.seg[i];
+      S.p = x.param;
+      S.g = x.grad;
+      S.m = x.exp_avg;
+      S.v = x.exp_avg_sq;
+      S.numel = x.numel;
+      S.dtype = x.grad_dtype;
+      const double step = static_cast<double>(x.step);
+      const double bc1 = 1.0 - std::pow(hp->beta1, step);
+      const double bc2 = 1.0 - std::pow(hp->beta2, step);
+      S.neg_step_size = static_cast<float>(-(x.lr / bc1));
+      S.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
+      S.has_decay = x.weight_decay != 0.0;
+      S.decay_mul = static_cast<float>(1.0 - x.lr * x.weight_decay);
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kChunk));
+    }
+    if (A.chunk_start[cnt] == 0) continue;
+    adamw_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("adamw_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+int check_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp) {
+  if (n < 0 || (n > 0 && (t == nullptr || hp == nullptr))) return fail(MOTEOPT_ERR_INVALID, "bad AdamW tensor list");
+  for (int i = 0; i < n; ++i) {
+    const moteopt_adamw_tensor& x = t[i];
+    if (x.numel < 0) return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": negative numel");
+    if (x.numel > 0 && (!x.param || !x.grad || !x.exp_avg || !x.exp_avg_sq))
+      return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": null pointer");
+    if (x.grad_dtype != kF32 && x.grad_dtype != kBF16)
+      return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": grad dtype must be fp32 or bf16");
+    if (x.step < 1) return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": step must be >= 1");
+    if (cdiv(x.numel, kChunk) > (1 << 30)) return fail(MOTEOPT_ERR_LIMIT, "AdamW tensor too large");
+  }
+  return MOTEOPT_OK;
+}
+
+int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cfg) {
+  if (n < 0 || (n > 0 && (p == nullptr || cfg == nullptr))) return fail(MOTEOPT_ERR_INVALID, "bad Muon param list");
+  if (cfg != nullptr && (cfg->ns_steps < 0 || cfg->ns_steps > 100)) return fail(MOTEOPT_ERR_INVALID, "ns_steps out of range");
+  for (int i = 0; i < n; ++i) {
+    const moteopt_muon_param& x = p[i];
+    if (!x.param || !x.grad || !x.momentum_buffer)
+      return fail(MOTEOPT_ERR_INVALID, "Muon param " + std::to_string(i) + ": null pointer");
+    if (x.batch < 1 || x.rows < 1 || x.cols < 1)
+      return fail(MOTEOPT_ERR_INVALID, "Muon param " + std::to_string(i) + ": batch, rows and cols must be >= 1");
+    if (x.grad_dtype != kF32 && x.grad_dtype != kBF16)
+      return fail(MOTEOPT_ERR_INVALID, "Muon param " + std::to_string(i) + ": grad dtype must be fp32 or bf16");
+  }
+  return MOTEOPT_OK;
+}
+
+// The Muon update of `n` params: momentum, normalisation, Newton-Schulz with the apply fused into the last phase.
+int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg, const Layout& L, char* ws,
+             bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st) {
+  if (n == 0) return MOTEOPT_OK;
+  float* mom_partials = reinterpret_cast<float*>(ws + L.off_mom);
+  // flatten the matrices in group-major order
+  struct Mat {
+    const moteopt_muon_param* p;
+    int slice;
+    const GroupPlan* g;
+    int pos;   // index inside its group
+  };
+  std::vector<Mat> mats;
+  for (const GroupPlan& g : L.groups)
+    for (size_t k = 0; k < g.mats.size(); ++k)
+      mats.push_back(Mat{&P[g.mats[k].src], g.mats[k].slice, &g, static_cast<int>(k)});
+  const int nm = static_cast<int>(mats.size());
+  auto elem_off = [](const Mat& m) { return static_cast<int64_t>(m.slice) * m.p->rows * m.p->cols; };
+  auto gptr = [&](const Mat& m) -> const void* {
+    const int64_t off = elem_off(m);
+    return m.p->grad_dtype == kBF16 ? static_cast<const void*>(static_cast<const __nv_bfloat16*>(m.p->grad) + off)
+                                    : static_cast<const void*>(static_cast<const float*>(m.p->grad) + off);
+  };
+
+  // 1. momentum + per-chunk sum of u^2
+  {
+    MomArgs A;
+    std::memset(&A, 0, sizeof(A));
+    A.has_div = has_div;
+    A.div = div;
+    A.coef = coef;
+    A.partials = mom_partials;
+    for (int s0 = 0; s0 < nm; s0 += kMaxMomSeg) {
+      const int cnt = std::min(nm - s0, kMaxMomSeg);
+      A.n = cnt;
+      A.chunk_base = L.mat_chunk_start[s0];
+      for (int i = 0; i < cnt; ++i) {
+        const Mat& m = mats[s0 + i];
+        MomSeg& S = A.seg[i];
+        S.g = gptr(m);
+        S.buf = m.p->momentum_buffer + elem_off(m);
+        S.numel = m.p->rows * m.p->cols;
+        S.mom = static_cast<float>(m.p->momentum);
+        S.nesterov = m.p->nesterov != 0;
+        S.dtype = m.p->grad_dtype;
+        A.chunk_start[i] = L.mat_chunk_start[s0 + i] - A.chunk_base;
+      }
+      A.chunk_start[cnt] = L.mat_chunk_start[s0 + cnt] - A.chunk_base;
+      muon_momentum_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+      MO_LAUNCHED("muon_momentum_kernel");
+    }
+  }
+  // 2. X0 = bf16(u / (||u|| + eps)) into each group's X0 buffer
+  {
+    NormArgs A;
+    std::memset(&A, 0, sizeof(A));
+    A.has_div = has_div;
+    A.div = div;
+    A.coef = coef;
+    A.partials = mom_partials;
+    A.eps = static_cast<float>(cfg->ns_eps);
+    A.status = status;
+    for (int s0 = 0; s0 < nm; s0 += kMaxNormMat) {
+      const int cnt = std::min(nm - s0, kMaxNormMat);
+      A.n = cnt;
+      int max_tiles = 0;
+      for (int i = 0; i < cnt; ++i) {
+        const Mat& m = mats[s0 + i];
+        const GroupPlan& g = *m.g;
+        NormMat& M = A.mat[i];
+        M.g = gptr(m);
+        M.buf = m.p->momentum_buffer + elem_off(m);
+        M.x = ws + g.off_x0 + static_cast<size_t>(m.pos) * g.m * g.n * 2;
+        M.rows = g.rows;
+        M.cols = g.cols;
+        M.m_pad = g.m;
+        M.n_pad = g.n;
+        M.transposed = g.transposed;
+        M.dtype = m.p->grad_dtype;
+        M.mom = static_cast<float>(m.p->momentum);
+        M.nesterov = m.p->nesterov != 0;
+        M.chunk0 = L.mat_chunk_start[s0 + i];
+        M.chunk1 = L.mat_chunk_start[s0 + i + 1];
+        M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
+        M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
+        max_tiles = std::max(max_tiles, M.tiles);
+      }
+      ns_normalize_kernel<<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+      MO_LAUNCHED("ns_normalize_kernel");
+    }
+  }
+  return MOTEOPT_OK;
+}
+
+// Newton-Schulz iterations over every group; if `apply_src` is non-null the last phase applies the Muon update.
+int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>* apply, int* status, int sms,
+           cudaStream_t st, int* final_src) {
+  *final_src = 0;
+  if (steps == 0) return MOTEOPT_OK;
+  // launch sets: <= kMaxGroups groups and <= kMaxApply matrices each
+  std::vector<std::pair<size_t, size_t>> sets;   // [begin, end) group ranges
+  {
+    size_t b = 0, mats = 0;
+    for (size_t i = 0; i < L.groups.size(); ++i) {
+      const size_t c = L.groups[i].mats.size();
+      if (i > b && (i - b >= static_cast<size_t>(ns::kMaxGroups) || mats + c > static_cast<size_t>(ns::kMaxApply))) {
+        sets.emplace_back(b, i);
+        b = i;
+        mats = 0;
+      }
+      mats += c;
+    }
+    if (b < L.groups.size()) sets.emplace_back(b, L.groups.size());
+  }
+  static thread_local ns::Launch Lh;   // ~20 KB: kept off the stack
+  size_t mat_base = 0;
+  for (const auto& set : sets) {
+    std::memset(&Lh, 0, sizeof(Lh));
+    Lh.n_groups = static_cast<int>(set.second - set.first);
+    Lh.status = status;
+    int first = 0;
+    for (size_t gi = set.first; gi < set.second; ++gi) {
+      const GroupPlan& g = L.groups[gi];
+      ns::Group& G = Lh.g[gi - set.first];
+      MapSet ms;
+      MO_TRY(group_maps(ws, g, &ms));
+      G.xk[0] = ms.xk[0];
+      G.xk[1] = ms.xk[1];
+      G.xmn[0] = ms.xmn[0];
+      G.xmn[1] = ms.xmn[1];
+      G.ak = ms.ak;
+      G.bk = ms.bk;
+      G.x[0] = reinterpret_cast<__nv_bfloat16*>(ws + g.off_x0);
+      G.x[1] = reinterpret_cast<__nv_bfloat16*>(ws + g.off_x1);
+      G.a = reinterpret_cast<__nv_bfloat16*>(ws + g.off_a);
+      G.b = reinterpret_cast<__nv_bfloat16*>(ws + g.off_b);
+      G.m = g.m;
+      G.n = g.n;
+      G.mv = g.mv;
+      G.nv = g.nv;
+      G.count = static_cast<int>(g.mats.size());
+      G.first = first;
+      G.transposed = g.transposed;
+      if (apply != nullptr)
+        for (size_t k = 0; k < g.mats.size(); ++k) Lh.mats[first + k] = (*apply)[mat_base + first + k];
+      first += G.count;
+    }
+    int src = 0;
+    for (int it = 0; it < steps; ++it) {
+      for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
+        Lh.phase = ph;
+        Lh.src = src;
+        Lh.apply = (apply != nullptr && ph == ns::kUpdate && it == steps - 1);
+        Lh.tile_start[0] = 0;
+        for (int gi = 0; gi < Lh.n_groups; ++gi) {
+          const ns::Group& G = Lh.g[gi];
+          const int out_cols = ph == ns::kUpdate ? G.n : G.m;
+          Lh.tiles_m[gi] = static_cast<int>(cdiv(G.m, ns::BM));
+          Lh.tiles_n[gi] = static_cast<int>(cdiv(out_cols, ns::BN));
+          Lh.tile_start[gi + 1] = Lh.tile_start[gi] + G.count * Lh.tiles_m[gi] * Lh.tiles_n[gi];
+        }
+        const int tiles = Lh.tile_start[Lh.n_groups];
+        ns::ns_phase_kernel<<<std::min(tiles, sms), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
+        MO_LAUNCHED("ns_phase_kernel");
+        if (ph == ns::kUpdate && !Lh.apply) src ^= 1;
+      }
+    }
+    *final_src = src;
+    mat_base += first;
+  }
+  return MOTEOPT_OK;
+}
+
+std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L) {
+  std::vector<ns::MatApply> out;
+  for (const GroupPlan& g : L.groups)
+    for (const MatRef& r : g.mats) {
+      const moteopt_muon_param& p = P[r.src];
+      ns::MatApply a;
+      a.p = p.param + static_cast<int64_t>(r.slice) * p.rows * p.cols;
+      a.neg_lr = static_cast<float>(-p.lr);
+      a.has_decay = p.decay != 0.0;
+      a.decay_mul = static_cast<float>(1.0 - p.decay);
+      a.scale = static_cast<float>(cfg->rms_scale * std::pow(static_cast<double>(std::max(p.rows, p.cols)), 0.5));
+      out.push_back(a);
+    }
+  return out;
+}
+
+// ns_steps == 0: O = X0 (the normalised update) applied directly
+int run_apply_x0(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, cudaStream_t st) {
+  const std::vector<ns::MatApply> tab = muon_apply_table(P, cfg, L);
+  OutArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.apply = 1;
+  std::vector<OutMat> all;
+  size_t k = 0;
+  for (const GroupPlan& g : L.groups)
+    for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
+      OutMat M;
+      std::memset(&M, 0, sizeof(M));
+      M.x = ws + g.off_x0 + pos * g.m * g.n * 2;
+      M.out = tab[k].p;
+      M.rows = g.rows;
+      M.cols = g.cols;
+      M.m_pad = g.m;
+      M.n_pad = g.n;
+      M.transposed = g.transposed;
+      M.tiles_x = static_cast<int>(cdiv(g.cols, kNormTile));
+      M.tiles = M.tiles_x * static_cast<int>(cdiv(g.rows, kNormTile));
+      M.neg_lr = tab[k].neg_lr;
+      M.decay_mul = tab[k].decay_mul;
+      M.has_decay = tab[k].has_decay;
+      M.scale = tab[k].scale;
+      all.push_back(M);
+    }
+  (void)P;
+  for (size_t s0 = 0; s0 < all.size(); s0 += kMaxOutMat) {
+    const size_t cnt = std::min(all.size() - s0, static_cast<size_t>(kMaxOutMat));
+    A.n = static_cast<int>(cnt);
+    int max_tiles = 0;
+    for (size_t i = 0; i < cnt; ++i) {
+      A.mat[i] = all[s0 + i];
+      max_tiles = std::max(max_tiles, A.mat[i].tiles);
+    }
+    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ns_out_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+int check_ws(void* ws, size_t have, size_t need) {
+  if (ws == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(MOTEOPT_ERR_INVALID, "workspace must be 256-byte aligned");
+  if (have < need)
+    return fail(MOTEOPT_ERR_INVALID, "workspace too small: " + std::to_string(have) + " < " + std::to_string(need) + " bytes");
+  return MOTEOPT_OK;
+}
+
+std::vector<std::tuple<int64_t, int64_t, int64_t>> muon_shapes(const moteopt_muon_param* p, int n) {
+  std::vector<std::tuple<int64_t, int64_t, int64_t>> s;
+  for (int i = 0; i < n; ++i) s.emplace_back(p[i].batch, p[i].rows, p[i].cols);
+  return s;
+}
+
+// The whole step: (optional) grad norm + clip coefficient, AdamW, Muon.
+int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* mcfg, const moteopt_adamw_tensor* adam,
+             int n_adam, const moteopt_adamw_hparams* ahp, const moteopt_grad_config* gcfg, const float* ext_scale,
+             float* out_norm, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  MO_TRY(check_muon(muon, n_muon, mcfg));
+  MO_TRY(check_adamw(adam, n_adam, ahp));
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  const bool clip = gcfg != nullptr && gcfg->clip;
+  std::vector<int64_t> norm_numels;
+  if (clip) {
+    for (int i = 0; i < n_adam; ++i) norm_numels.push_back(adam[i].numel);
+    for (int i = 0; i < n_muon; ++i) norm_numels.push_back(muon[i].batch * muon[i].rows * muon[i].cols);
+  }
+  Layout L;
+  MO_TRY(build_layout(muon_shapes(muon, n_muon), norm_numels, n_muon > 0 ? mcfg->ns_steps : 0, &L));
+  MO_TRY(check_ws(workspace, ws_bytes, L.bytes));
+  char* ws = static_cast<char*>(workspace);
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  int* status = &hdr->status;
+  MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
+  const bool has_div = gcfg != nullptr && gcfg->grad_divisor != 0.0 && gcfg->grad_divisor != 1.0;
+  const float div = has_div ? static_cast<float>(gcfg->grad_divisor) : 1.0f;
+  const float* coef = ext_scale;
+  if (clip) {
+    std::vector<GradSource> src;
+    for (int i = 0; i < n_adam; ++i) src.push_back(GradSource{adam[i].grad, adam[i].numel, adam[i].grad_dtype});
+    for (int i = 0; i < n_muon; ++i)
+      src.push_back(GradSource{muon[i].grad, muon[i].batch * muon[i].rows * muon[i].cols, muon[i].grad_dtype});
+    float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+    MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, div, sms, st));
+    MO_TRY(launch_finalize(L.norm_tensor_chunk_start, partials, true, gcfg->max_norm, &hdr->norm, status, st));
+    coef = &hdr->coef;
+    if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
+  }
+  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st));
+  if (n_muon > 0) {
+    MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st));
+    if (mcfg->ns_steps == 0) {
+      MO_TRY(run_apply_x0(muon, mcfg, L, ws, st));
+    } else {
+      const std::vector<ns::MatApply> tab = muon_apply_table(muon, mcfg, L);
+      int final_src = 0;
+      MO_TRY(run_ns(L, ws, mcfg->ns_steps, &tab, status, sms, st, &final_src));
+    }
+  }
+  return MOTEOPT_OK;
+}
+
+}  // namespace
+
+// =================================================================================================================
+extern "C" {
+
+int moteopt_version(void) { return 1; }
+
+const char* moteopt_last_error(void) { return t_err.c_str(); }
+
+int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream) {
+  if (workspace == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  Header h;
+  MO_CUDA(cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, st));
+  MO_CUDA(cudaStreamSynchronize(st));
+  if (status) *status = h.status;
+  if (norm_and_coef) {
+    norm_and_coef[0] = h.norm;
+    norm_and_coef[1] = h.coef;
+  }
+  if (clear) MO_CUDA(cudaMemsetAsync(workspace, 0, sizeof(int), st));
+  return MOTEOPT_OK;
+}
+
+size_t moteopt_optimizer_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps,
+                                             const moteopt_adamw_tensor* adamw, int n_adamw) {
+  if (n_muon < 0 || n_adamw < 0 || (n_muon > 0 && !muon) || (n_adamw > 0 && !adamw)) return 0;
+  std::vector<int64_t> numels;
+  for (int i = 0; i < n_adamw; ++i) numels.push_back(adamw[i].numel);
+  for (int i = 0; i < n_muon; ++i) numels.push_back(muon[i].batch * muon[i].rows * muon[i].cols);
+  Layout L;
+  if (build_layout(muon_shapes(muon, n_muon), numels, ns_steps, &L) != MOTEOPT_OK) return 0;
+  return L.bytes;
+}
+
+int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,
+                           const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* adamw_hp,
+                           const moteopt_grad_config* grad_cfg, float* out_norm, void* workspace,
+                           size_t workspace_bytes, moteopt_stream_t stream) {
+  return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, grad_cfg, nullptr, out_norm, workspace,
+                  workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps) {
+  if (n_muon < 0 || (n_muon > 0 && !muon)) return 0;
+  Layout L;
+  if (build_layout(muon_shapes(muon, n_muon), {}, ns_steps, &L) != MOTEOPT_OK) return 0;
+  return L.bytes;
+}
+
+int moteopt_muon_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* cfg,
+                      const float* grad_scale, void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  return run_step(muon, n_muon, cfg, nullptr, 0, nullptr, nullptr, grad_scale, nullptr, workspace, workspace_bytes,
+                  reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moteopt_adamw_step(const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* hp,
+                       const float* grad_scale, moteopt_stream_t stream) {
+  int r = check_adamw(adamw, n_adamw, hp);
+  if (r != MOTEOPT_OK) return r;
+  int sms = 0;
+  r = device_setup(&sms);
+  if (r != MOTEOPT_OK) return r;
+  return launch_adamw(adamw, n_adamw, hp, false, 1.0f, grad_scale, sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t moteopt_clip_grad_norm_workspace_size(const int64_t* numels, int n) {
+  if (n < 0 || (n > 0 && !numels)) return 0;
+  Layout L;
+  if (build_layout({}, std::vector<int64_t>(numels, numels + n), 0, &L) != MOTEOPT_OK) return 0;
+  return L.bytes;
+}
+
+int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int* dtypes, int n, double max_norm,
+                           float* out_norm, void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!grads || !numels || !dtypes))) return fail(MOTEOPT_ERR_INVALID, "bad grad list");
+  if (n > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "more than 4096 tensors in one clip_grad_norm call");
+  for (int i = 0; i < n; ++i) {
+    if (dtypes[i] != kF32 && dtypes[i] != kBF16) return fail(MOTEOPT_ERR_INVALID, "grad dtype must be fp32 or bf16");
+    if (numels[i] < 0 || (numels[i] > 0 && grads[i] == nullptr)) return fail(MOTEOPT_ERR_INVALID, "bad grad tensor");
+  }
+  int sms = 0;
+  int r = device_setup(&sms);
+  if (r != MOTEOPT_OK) return r;
+  Layout L;
+  r = build_layout({}, std::vector<int64_t>(numels, numels + n), 0, &L);
+  if (r != MOTEOPT_OK) return r;
+  r = check_ws(workspace, workspace_bytes, L.bytes);
+  if (r != MOTEOPT_OK) return r;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
+  std::vector<GradSource> src;
+  for (int i = 0; i < n; ++i) src.push_back(GradSource{grads[i], numels[i], dtypes[i]});
+  float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+  r = launch_sumsq(src, L.norm_tensor_chunk_start, partials, false, 1.0f, sms, st);
+  if (r != MOTEOPT_OK) return r;
+  r = launch_finalize(L.norm_tensor_chunk_start, partials, true, max_norm, &hdr->norm, &hdr->status, st);
+  if (r != MOTEOPT_OK) return r;
+  ScaleArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.coef = &hdr->coef;
+  for (int s0 = 0; s0 < n; s0 += kMaxNormSeg) {
+    const int cnt = std::min(n - s0, kMaxNormSeg);
+    A.n = cnt;
+    A.chunk_start[0] = 0;
+    for (int i = 0; i < cnt; ++i) {
+      A.seg[i] = SumsqSeg{grads[s0 + i], numels[s0 + i], dtypes[s0 + i], 0};
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(numels[s0 + i], kChunk));
+    }
+    if (A.chunk_start[cnt] == 0) continue;
+    clip_scale_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("clip_scale_kernel");
+  }
+  if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
+  return MOTEOPT_OK;
+}
+
+size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
+  Layout L;
+  if (build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L) != MOTEOPT_OK) return 0;
+  return L.bytes;
+}
+
+int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, int64_t rows, int64_t cols, int steps,
+                          double eps, void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  if (!G || !out) return fail(MOTEOPT_ERR_INVALID, "null input or output");
+  if (g_dtype != kF32 && g_dtype != kBF16) return fail(MOTEOPT_ERR_INVALID, "G must be fp32 or bf16");
+  if (steps < 0 || steps > 100) return fail(MOTEOPT_ERR_INVALID, "steps out of range");
+  int sms = 0;
+  int r = device_setup(&sms);
+  if (r != MOTEOPT_OK) return r;
+  Layout L;
+  r = build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L);
+  if (r != MOTEOPT_OK) return r;
+  r = check_ws(workspace, workspace_bytes, L.bytes);
+  if (r != MOTEOPT_OK) return r;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
+  const size_t esz = g_dtype == kBF16 ? 2 : 4;
+  const int64_t per = rows * cols;
+  // per-matrix sum of squares, in the layout's matrix order
+  std::vector<GradSource> src;
+  std::vector<const GroupPlan*> gofm;
+  std::vector<int> posm;
+  for (const GroupPlan& g : L.groups)
+    for (size_t k = 0; k < g.mats.size(); ++k) {
+      src.push_back(GradSource{static_cast<const char*>(G) + static_cast<size_t>(g.mats[k].slice) * per * esz, per, g_dtype});
+      gofm.push_back(&g);
+      posm.push_back(static_cast<int>(k));
+    }
+  float* partials = reinterpret_cast<float*>(ws + L.off_mom);
+  r = launch_sumsq(src, L.mat_chunk_start, partials, false, 1.0f, sms, st);
+  if (r != MOTEOPT_OK) return r;
+  NormArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.partials = partials;
+  A.eps = static_cast<float>(eps);
+  A.status = &hdr->status;
+  const int nm = static_cast<int>(src.size());
+  for (int s0 = 0; s0 < nm; s0 += kMaxNormMat) {
+    const int cnt = std::min(nm - s0, kMaxNormMat);
+    A.n = cnt;
+    int max_tiles = 0;
+    for (int i = 0; i < cnt; ++i) {
+      const GroupPlan& g = *gofm[s0 + i];
+      NormMat& M = A.mat[i];
+      M.g = src[s0 + i].g;
+      M.buf = nullptr;
+      M.x = ws + g.off_x0 + static_cast<size_t>(posm[s0 + i]) * g.m * g.n * 2;
+      M.rows = g.rows;
+      M.cols = g.cols;
+      M.m_pad = g.m;
+      M.n_pad = g.n;
+      M.transposed = g.transposed;
+      M.dtype = g_dtype;
+      M.chunk0 = L.mat_chunk_start[s0 + i];
+      M.chunk1 = L.mat_chunk_start[s0 + i + 1];
+      M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
+      M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
+      max_tiles = std::max(max_tiles, M.tiles);
+    }
+    ns_normalize_kernel<<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ns_normalize_kernel");
+  }
+  int final_src = 0;
+  r = run_ns(L, ws, steps, nullptr, &hdr->status, sms, st, &final_src);
+  if (r != MOTEOPT_OK) return r;
+  // copy out (transpose back)
+  OutArgs O;
+  std::memset(&O, 0, sizeof(O));
+  O.apply = 0;
+  int k = 0;
+  std::vector<OutMat> all;
+  for (const GroupPlan& g : L.groups)
+    for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
+      OutMat M;
+      std::memset(&M, 0, sizeof(M));
+      M.x = ws + (final_src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+      M.out = static_cast<char*>(out) + static_cast<size_t>(g.mats[pos].slice) * per * 2;
+      M.rows = g.rows;
+      M.cols = g.cols;
+      M.m_pad = g.m;
+      M.n_pad = g.n;
+      M.transposed = g.transposed;
+      M.tiles_x = static_cast<int>(cdiv(g.cols, kNormTile));
+      M.tiles = M.tiles_x * static_cast<int>(cdiv(g.rows, kNormTile));
+      all.push_back(M);
+    }
+  for (size_t s0 = 0; s0 < all.size(); s0 += kMaxOutMat) {
+    const size_t cnt = std::min(all.size() - s0, static_cast<size_t>(kMaxOutMat));
+    O.n = static_cast<int>(cnt);
+    int max_tiles = 0;
+    for (size_t i = 0; i < cnt; ++i) {
+      O.mat[i] = all[s0 + i];
+      max_tiles = std::max(max_tiles, O.mat[i].tiles);
+    }
+    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(O);
+    MO_LAUNCHED("ns_out_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,341 @@
+// Memory-bound kernels of the optimizer step (sm_100a). Each is a grid-stride loop over fixed 16K-element chunks
+// of a segment list, with 128-bit loads where the pointers allow. Reductions are deterministic: a fixed per-thread
+// order, a fixed warp-shuffle tree and a fixed cross-warp order per chunk, one partial per chunk, and a fixed-order
+// second pass, so results are bitwise identical from run to run.
+//
+// Rounding follows the reference's torch ops one by one (see the per-kernel comments); __fmul_rn / __fadd_rn /
+// __fdiv_rn keep the compiler from contracting what torch rounds separately, fmaf is used where torch fuses.
+#pragma once
+
+#include "mt_types.h"
+#include "ptx.cuh"
+
+namespace moteopt {
+
+__device__ __forceinline__ int find_seg(const int* chunk_start, int n, int chunk) {
+  int lo = 0, hi = n - 1;
+  while (lo < hi) {   // last segment whose start <= chunk
+    const int mid = (lo + hi + 1) >> 1;
+    if (chunk_start[mid] <= chunk) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float load_g1(const void* g, int64_t i, int dt) {
+  return dt == kBF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(g)[i])
+                     : reinterpret_cast<const float*>(g)[i];
+}
+
+__device__ __forceinline__ float4 load_g4(const void* g, int64_t i, int dt) {
+  if (dt == kBF16) {
+    const uint2 w = *reinterpret_cast<const uint2*>(reinterpret_cast<const __nv_bfloat16*>(g) + i);
+    return make_float4(bf16_lo(w.x), bf16_hi(w.x), bf16_lo(w.y), bf16_hi(w.y));
+  }
+  return *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(g) + i);
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__device__ __forceinline__ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
+__device__ __forceinline__ bool g_vec_ok(const void* g, int dt) { return dt == kBF16 ? aligned8(g) : aligned16(g); }
+
+// train.py:945-946: g / total_n (fp32 division), then * clip coefficient (fp32 multiply)
+struct GradXform {
+  int has_div;
+  float div;
+  int has_coef;
+  float coef;
+  __device__ __forceinline__ float operator()(float g) const {
+    if (has_div) g = __fdiv_rn(g, div);
+    if (has_coef) g = __fmul_rn(g, coef);
+    return g;
+  }
+};
+
+// Sum of a per-thread fp32 value over the block, in a fixed order. Result valid in thread 0.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  if (threadIdx.x == 0) {
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += red[k];
+  }
+  __syncthreads();
+  return s;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// sum of squares of (g / div) per chunk
+__global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
+  __shared__ float red[kMtThreads / 32];
+  const int total = A.chunk_start[A.n];
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const SumsqSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    const GradXform X{A.has_div, A.div, 0, 1.f};
+    float acc = 0.f;
+    if (g_vec_ok(S.g, S.dtype)) {
+      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
+        const float4 g = load_g4(S.g, i, S.dtype);
+        const float a = X(g.x), b = X(g.y), d = X(g.z), e = X(g.w);
+        acc = fmaf(a, a, acc); acc = fmaf(b, b, acc); acc = fmaf(d, d, acc); acc = fmaf(e, e, acc);
+      }
+      for (int64_t i = vend + threadIdx.x; i < end; i += kMtThreads) {
+        const float a = X(load_g1(S.g, i, S.dtype));
+        acc = fmaf(a, a, acc);
+      }
+    } else {
+      for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) {
+        const float a = X(load_g1(S.g, i, S.dtype));
+        acc = fmaf(a, a, acc);
+      }
+    }
+    const float tot = block_sum(acc, red);
+    if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// per-tensor norms -> total norm (the norm of the per-tensor norms, as torch's get_total_norm) -> clip coefficient
+__global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_constant__ FinalizeArgs A) {
+  __shared__ double red[32];
+  double acc = 0.0;
+  for (int t = threadIdx.x; t < A.n_tensors; t += blockDim.x) {
+    double s = 0.0;
+    for (int c = A.tensor_chunk_start[t]; c < A.tensor_chunk_start[t + 1]; ++c) s += static_cast<double>(A.partials[c]);
+    const float nt = static_cast<float>(sqrt(s));
+    acc += static_cast<double>(nt) * static_cast<double>(nt);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += red[k];
+    const float total = static_cast<float>(sqrt(s));
+    float coef = 1.0f;
+    if (A.has_clip) {
+      // clamp(max_norm / (total + 1e-6), max=1) in fp32; a NaN norm gives a NaN coefficient, as in torch
+      const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
+      coef = (c > 1.0f) ? 1.0f : c;
+    }
+    A.out[0] = total;
+    A.out[1] = coef;
+    if (!isfinite(total)) atomicOr(A.status, kStatusNonFinite);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// AdamW, torch's single-tensor update in torch's rounding order:
+//   p *= (1 - lr*wd)                      param.mul_(1 - lr*wd)
+//   m  = lerp(m, g, 1-beta1)              exp_avg.lerp_(grad, 1-beta1)            (fused: m + w*(g-m))
+//   v  = v*beta2; v = fma((1-b2)*g, g, v) exp_avg_sq.mul_(beta2).addcmul_(g, g, value=1-beta2)
+//   d  = sqrt(v)/sqrt(bc2) + eps          (exp_avg_sq.sqrt() / bias_correction2_sqrt).add_(eps)
+//   p += ((-step_size)*m) / d             param.addcdiv_(exp_avg, denom, value=-step_size)
+struct AdamConsts {
+  float lerp_w, one_minus_w, beta2, omb2, eps;
+  int lerp_small;
+};
+
+__device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamSeg& S, const AdamConsts& K) {
+  if (S.has_decay) p = __fmul_rn(p, S.decay_mul);
+  const float d = __fsub_rn(g, m);
+  m = K.lerp_small ? fmaf(K.lerp_w, d, m) : fmaf(-K.one_minus_w, d, g);
+  v = __fmul_rn(v, K.beta2);
+  v = fmaf(__fmul_rn(K.omb2, g), g, v);
+  const float den = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), S.bc2_sqrt), K.eps);
+  p = __fadd_rn(p, __fdiv_rn(__fmul_rn(S.neg_step_size, m), den));
+}
+
+__global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant__ AdamArgs A) {
+  const int total = A.chunk_start[A.n];
+  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const AdamSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype);
+    int64_t i0 = begin;
+    if (vec) {
+      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
+        float4 p = *reinterpret_cast<float4*>(S.p + i);
+        float4 m = *reinterpret_cast<float4*>(S.m + i);
+        float4 v = *reinterpret_cast<float4*>(S.v + i);
+        const float4 g = load_g4(S.g, i, S.dtype);
+        adam_elem(p.x, X(g.x), m.x, v.x, S, K);
+        adam_elem(p.y, X(g.y), m.y, v.y, S, K);
+        adam_elem(p.z, X(g.z), m.z, v.z, S, K);
+        adam_elem(p.w, X(g.w), m.w, v.w, S, K);
+        *reinterpret_cast<float4*>(S.p + i) = p;
+        *reinterpret_cast<float4*>(S.m + i) = m;
+        *reinterpret_cast<float4*>(S.v + i) = v;
+      }
+      i0 = vend;
+    }
+    for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
+      float p = S.p[i], m = S.m[i], v = S.v[i];
+      adam_elem(p, X(load_g1(S.g, i, S.dtype)), m, v, S, K);
+      S.p[i] = p; S.m[i] = m; S.v[i] = v;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Muon momentum (muon.py:69-70): buf = buf*mom + g (two roundings); u = g + mom*buf (fused, torch's add(alpha=)).
+// Writes buf and, per chunk, the sum of u^2 for the per-matrix Frobenius norm.
+__device__ __forceinline__ float mom_elem(float g, float& buf, float mom, int nesterov) {
+  buf = __fadd_rn(__fmul_rn(buf, mom), g);
+  return nesterov ? fmaf(mom, buf, g) : buf;
+}
+
+__global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
+  __shared__ float red[kMtThreads / 32];
+  const int total = A.chunk_start[A.n];
+  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const MomSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    float acc = 0.f;
+    int64_t i0 = begin;
+    if (aligned16(S.buf) && g_vec_ok(S.g, S.dtype)) {
+      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
+        float4 b = *reinterpret_cast<float4*>(S.buf + i);
+        const float4 g = load_g4(S.g, i, S.dtype);
+        const float u0 = mom_elem(X(g.x), b.x, S.mom, S.nesterov);
+        const float u1 = mom_elem(X(g.y), b.y, S.mom, S.nesterov);
+        const float u2 = mom_elem(X(g.z), b.z, S.mom, S.nesterov);
+        const float u3 = mom_elem(X(g.w), b.w, S.mom, S.nesterov);
+        *reinterpret_cast<float4*>(S.buf + i) = b;
+        acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+      }
+      i0 = vend;
+    }
+    for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
+      float b = S.buf[i];
+      const float u = mom_elem(X(load_g1(S.g, i, S.dtype)), b, S.mom, S.nesterov);
+      S.buf[i] = b;
+      acc = fmaf(u, u, acc);
+    }
+    const float tot = block_sum(acc, red);
+    if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// X0 = bf16(u / (||u||_F + eps)), transposed when the matrix has more rows than columns, zero padded.
+// grid: (tiles of the largest matrix, matrices). u is recomputed from the grad and the updated momentum buffer
+// exactly as the momentum kernel computed it (momentum mode), or read from G (direct mode, buf == null).
+__global__ void __launch_bounds__(kMtThreads) ns_normalize_kernel(const __grid_constant__ NormArgs A) {
+  __shared__ float tile[kNormTile][kNormTile + 1];
+  __shared__ float s_den;
+  const NormMat& M = A.mat[blockIdx.y];
+  if (static_cast<int>(blockIdx.x) >= M.tiles) return;
+  const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
+  const int i0 = ti * kNormTile, j0 = tj * kNormTile;   // destination tile origin (X rows i, cols j)
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int c = M.chunk0; c < M.chunk1; ++c) s += static_cast<double>(A.partials[c]);
+    const float nrm = static_cast<float>(sqrt(s));
+    s_den = __fadd_rn(nrm, A.eps);
+  }
+  __syncthreads();
+  const float den = s_den;
+  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4 threads
+  const int mv = M.transposed ? M.cols : M.rows;            // valid X rows
+  const int nv = M.transposed ? M.rows : M.cols;            // valid X cols
+  // Load the tile in source order (coalesced along the source's columns) into tile[src_r][src_c].
+  // Source tile origin: (i0, j0) if not transposed, (j0, i0) if transposed.
+  const int sr0 = M.transposed ? j0 : i0, sc0 = M.transposed ? i0 : j0;
+  for (int r = ty; r < kNormTile; r += 4) {
+    const int sr = sr0 + r, sc = sc0 + tx;
+    float val = 0.f;
+    if (sr < M.rows && sc < M.cols) {
+      const int64_t idx = static_cast<int64_t>(sr) * M.cols + sc;
+      float u = X(load_g1(M.g, idx, M.dtype));
+      if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, M.buf[idx], u) : M.buf[idx];
+      val = bf16_round_f(__fdiv_rn(u, den));
+    }
+    tile[r][tx] = val;
+  }
+  __syncthreads();
+  __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(M.x);
+  for (int r = ty; r < kNormTile; r += 4) {
+    const int i = i0 + r, j = j0 + tx;
+    if (i < M.m_pad && j < M.n_pad) {
+      const float val = (i < mv && j < nv) ? (M.transposed ? tile[tx][r] : tile[r][tx]) : 0.f;
+      x[static_cast<int64_t>(i) * M.n_pad + j] = __float2bfloat16_rn(val);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The final iterate back to the caller's orientation: out[r][c] = X[c][r] (transposed) or X[r][c]; or, in apply mode,
+// the Muon apply of muon.py:97-99 into the fp32 parameter.
+__global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constant__ OutArgs A) {
+  __shared__ float tile[kNormTile][kNormTile + 1];
+  const OutMat& M = A.mat[blockIdx.y];
+  if (static_cast<int>(blockIdx.x) >= M.tiles) return;
+  const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
+  const int r0 = ti * kNormTile, c0 = tj * kNormTile;      // output tile origin (rows r, cols c of R x C)
+  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(M.x);
+  // X tile origin: (r0, c0) or (c0, r0) if transposed; load coalesced along X's columns
+  const int xr0 = M.transposed ? c0 : r0, xc0 = M.transposed ? r0 : c0;
+  for (int r = ty; r < kNormTile; r += 4) {
+    const int xr = xr0 + r, xc = xc0 + tx;
+    tile[r][tx] = (xr < M.m_pad && xc < M.n_pad) ? __bfloat162float(x[static_cast<int64_t>(xr) * M.n_pad + xc]) : 0.f;
+  }
+  __syncthreads();
+  for (int r = ty; r < kNormTile; r += 4) {
+    const int orow = r0 + r, ocol = c0 + tx;
+    if (orow < M.rows && ocol < M.cols) {
+      const float o = M.transposed ? tile[tx][r] : tile[r][tx];
+      const int64_t idx = static_cast<int64_t>(orow) * M.cols + ocol;
+      if (A.apply) {
+        float* p = reinterpret_cast<float*>(M.out);
+        float v = p[idx];
+        if (M.has_decay) v = __fmul_rn(v, M.decay_mul);
+        p[idx] = fmaf(M.neg_lr, __fmul_rn(o, M.scale), v);
+      } else {
+        reinterpret_cast<__nv_bfloat16*>(M.out)[idx] = __float2bfloat16_rn(o);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// g *= coef in place (the scaling half of clip_grad_norm_)
+__global__ void __launch_bounds__(kMtThreads) clip_scale_kernel(const __grid_constant__ ScaleArgs A) {
+  const int total = A.chunk_start[A.n];
+  const float coef = *A.coef;
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const SumsqSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) {
+      if (S.dtype == kBF16) {
+        __nv_bfloat16* g = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(S.g));
+        g[i] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(g[i]), coef));
+      } else {
+        float* g = reinterpret_cast<float*>(const_cast<void*>(S.g));
+        g[i] = __fmul_rn(g[i], coef);
+      }
+    }
+  }
+}
+
+}  // namespace moteopt

@@ -1,0 +1,150 @@
+// Argument blocks of the memory-bound multi-tensor kernels, shared by host and device code. Every block is passed
+// by value as a kernel parameter (CUDA 12.1+ allows up to 32 KB), so a step needs no descriptor upload and no
+// allocation. Lists longer than one block holds are split into several launches by the host.
+#pragma once
+
+#include <cstdint>
+
+namespace moteopt {
+
+constexpr int kChunk = 16384;          // elements per work unit of the multi-tensor kernels
+constexpr int kMtThreads = 256;
+
+enum DType : int { kF32 = 0, kBF16 = 1 };
+
+// ---- global grad norm (torch.nn.utils.clip_grad_norm_, called at mote/train/train.py:946)
+constexpr int kMaxNormSeg = 512;
+struct SumsqSeg {
+  const void* g;
+  int64_t numel;
+  int dtype;
+  int pad_;
+};
+struct SumsqArgs {
+  int n;
+  int chunk_base;            // index of this launch's first chunk in the partials array
+  int has_div;               // divide by `div` first (train.py:945, grads /= total_n)
+  float div;
+  float* partials;           // one fp32 sum of squares per chunk
+  int chunk_start[kMaxNormSeg + 1];
+  SumsqSeg seg[kMaxNormSeg];
+};
+
+constexpr int kMaxFinalTensors = 4096;
+struct FinalizeArgs {
+  int n_tensors;
+  int has_clip;
+  float max_norm;
+  const float* partials;
+  float* out;                // out[0] = total norm, out[1] = clip coefficient (1 when no clip)
+  int* status;
+  int tensor_chunk_start[kMaxFinalTensors + 1];
+};
+
+// ---- AdamW (torch.optim.AdamW single-tensor update, constructed at mote/train/train.py:98)
+constexpr int kMaxAdamSeg = 320;
+struct AdamSeg {
+  float* p;
+  const void* g;
+  float* m;
+  float* v;
+  int64_t numel;
+  float decay_mul;           // 1 - lr*wd (fp64 on the host, rounded once)
+  float neg_step_size;       // -lr / (1 - beta1^t)
+  float bc2_sqrt;            // sqrt(1 - beta2^t)
+  int dtype;                 // grad dtype
+  int has_decay;
+  int pad_;
+};
+struct AdamArgs {
+  int n;
+  int has_div;
+  float div;
+  const float* coef;         // device clip coefficient, or null
+  float lerp_w;              // 1 - beta1 (lerp weight)
+  int lerp_small;            // weight < 0.5: m + w*(g-m); else g - (g-m)*(1-w)
+  float one_minus_w;
+  float beta2;
+  float one_minus_beta2;
+  float eps;
+  int chunk_start[kMaxAdamSeg + 1];
+  AdamSeg seg[kMaxAdamSeg];
+};
+
+// ---- Muon momentum (mote/train/muon.py:66-70), one segment per matrix (a 3-D stack contributes one per slice)
+constexpr int kMaxMomSeg = 512;
+struct MomSeg {
+  const void* g;
+  float* buf;
+  int64_t numel;
+  float mom;
+  int nesterov;
+  int dtype;
+  int pad_;
+};
+struct MomArgs {
+  int n;
+  int chunk_base;
+  int has_div;
+  float div;
+  const float* coef;
+  float* partials;           // per chunk: sum of u^2 (feeds the Newton-Schulz normalisation)
+  int chunk_start[kMaxMomSeg + 1];
+  MomSeg seg[kMaxMomSeg];
+};
+
+// ---- Newton-Schulz normalisation X0 = bf16(u / (||u||_F + eps)) with the transpose rule (muon.py:32-36)
+constexpr int kMaxNormMat = 320;
+constexpr int kNormTile = 64;
+struct NormMat {
+  const void* g;             // source: the grad (momentum mode) or G itself (direct mode)
+  const float* buf;          // momentum buffer after this step's update (momentum mode), else null
+  void* x;                   // destination [m_pad][n_pad] bf16 (zero padded)
+  int rows, cols;            // the source matrix (R x C)
+  int m_pad, n_pad;          // destination dims: (C, R) padded if transposed, else (R, C) padded
+  int transposed;
+  int dtype;
+  float mom;
+  int nesterov;
+  int chunk0, chunk1;        // this matrix's sum-of-squares partials [chunk0, chunk1)
+  int tiles_x;               // destination tiles along n_pad
+  int tiles;                 // total destination tiles
+};
+struct NormArgs {
+  int n;
+  int has_div;
+  float div;
+  const float* coef;
+  const float* partials;
+  float eps;
+  int* status;
+  NormMat mat[kMaxNormMat];
+};
+
+// ---- copy the final iterate out of the workspace (standalone newton_schulz), or apply it (ns_steps == 0)
+constexpr int kMaxOutMat = 320;
+struct OutMat {
+  const void* x;             // [m_pad][n_pad] bf16 iterate
+  void* out;                 // bf16 [R][C] output, or the fp32 parameter in apply mode
+  int rows, cols;            // R x C
+  int m_pad, n_pad;
+  int transposed;
+  int tiles_x, tiles;
+  float neg_lr, decay_mul, scale;
+  int has_decay;
+};
+struct OutArgs {
+  int n;
+  int apply;
+  OutMat mat[kMaxOutMat];
+};
+
+// ---- in-place clip of the grads (standalone clip_grad_norm_)
+struct ScaleArgs {
+  int n;
+  const float* coef;
+  int chunk_start[kMaxNormSeg + 1];
+  SumsqSeg seg[kMaxNormSeg];
+};
+
+}  // namespace moteopt

@@ -1,0 +1,73 @@
+// Launch descriptors of the Newton-Schulz phase kernel, shared by host and device code.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+namespace moteopt {
+namespace ns {
+
+constexpr int BM = 128;        // output rows per tile (TMEM lanes)
+constexpr int BN = 256;        // output columns per tile (TMEM columns per accumulator)
+constexpr int BK = 64;         // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int kThreads = 192;  // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, warps 2-5: epilogue
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+constexpr uint32_t kTmemCols = 512;   // two 128 x 256 fp32 accumulators
+
+constexpr int kMaxGroups = 8;     // shape groups per launch
+constexpr int kMaxApply = 512;    // matrices whose parameter update is fused into the last launch
+
+enum Phase : int {
+  kGram = 0,     // A = X X^T                         (m x m, K = n)
+  kPoly = 1,     // B = b*A + c*(A A)                 (m x m, K = m)
+  kUpdate = 2,   // X' = a*X + B X   (or the Muon apply on the last iteration)   (m x n, K = m)
+};
+
+// One shape group: `count` matrices that share (m, n) after the transpose rule (m <= n). Buffers are
+// [count][m][n] (X) and [count][m][m] (A, B), bf16, row-major, with m and n padded up to multiples of 8 and the
+// padding kept at zero (the iteration maps zero rows/columns to zero).
+struct alignas(64) Group {
+  CUtensorMap xk[2];    // X ping/pong as a K-major operand: dims {n, m, count}, box {64, 128, 1}
+  CUtensorMap xmn[2];   // X ping/pong as an MN-major operand: dims {n, m, count}, box {64, 64, 1}
+  CUtensorMap ak;       // A: dims {m, m, count}, box {64, 128, 1}
+  CUtensorMap bk;       // B: dims {m, m, count}, box {64, 128, 1}
+  __nv_bfloat16* x[2];
+  __nv_bfloat16* a;
+  __nv_bfloat16* b;
+  int m, n;             // padded dims of X (m <= n)
+  int mv, nv;           // valid dims of X
+  int count;            // matrices in the group
+  int first;            // index of the group's first matrix in the launch's matrix numbering
+  int transposed;       // X = u^T (the parameter has more rows than columns)
+  int pad_;
+};
+
+// The fused Muon apply of one matrix (mote/train/muon.py:93-99): p = p*(1-decay) (if decay), p += -lr*(O*scale).
+struct MatApply {
+  float* p;             // first element of this matrix inside its (2-D or 3-D) parameter
+  float neg_lr;
+  float decay_mul;
+  float scale;
+  int has_decay;
+};
+
+struct Launch {
+  Group g[kMaxGroups];
+  int n_groups;
+  int phase;
+  int src;              // which X buffer holds the current iterate
+  int apply;            // kUpdate only: write the parameter update instead of X'
+  int tile_start[kMaxGroups + 1];
+  int tiles_m[kMaxGroups];
+  int tiles_n[kMaxGroups];
+  int* status;
+  MatApply mats[kMaxApply];
+};
+
+}  // namespace ns
+}  // namespace moteopt

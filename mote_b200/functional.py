@@ -1,0 +1,160 @@
+"""Functional form of the optimizer step over plain tensors: the one place that packs tensors into the C ABI's
+descriptor arrays. The optimizer classes (optim.py), the tests and bench.py all go through here.
+
+    optimizer_step(muon=[MuonItem...], adamw=[AdamWItem...], ...)   # mote/train/train.py:944-947
+    muon_step(...)                                                  # mote/train/muon.py:52-100
+    adamw_step(...)                                                 # torch.optim.AdamW.step (train.py:98)
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib as L
+from .ops import grad_dtype_code, stream_handle, workspace
+
+
+@dataclass
+class MuonItem:
+    """One Muon parameter for one step (mote/train/muon.py:60-79): `lr` is already the effective rate (param_lr
+    override resolved) and `decay` the decoupled decay of muon.py:78 (0 for none)."""
+    param: torch.Tensor
+    grad: torch.Tensor
+    momentum_buffer: torch.Tensor
+    lr: float
+    decay: float = 0.0
+    momentum: float = 0.95
+    nesterov: bool = True
+
+
+@dataclass
+class AdamWItem:
+    """One AdamW tensor for one step; `step` counts this update (1 on the first)."""
+    param: torch.Tensor
+    grad: torch.Tensor
+    exp_avg: torch.Tensor
+    exp_avg_sq: torch.Tensor
+    lr: float
+    weight_decay: float
+    step: int
+
+
+def _check_param(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be on a CUDA device: the optimizer runs only on the GPU")
+    if t.dtype != torch.float32:
+        raise TypeError(f"{what} must be fp32 (the master-parameter dtype), got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{what} must be contiguous")
+
+
+def muon_array(items: Sequence[MuonItem]):
+    arr = (L.MuonParam * max(1, len(items)))()
+    for i, it in enumerate(items):
+        p, g, b = it.param, it.grad, it.momentum_buffer
+        _check_param(p, "Muon param")
+        _check_param(b, "Muon momentum buffer")
+        if g.shape != p.shape or b.shape != p.shape:
+            raise ValueError(f"Muon param {i}: grad/momentum shape {tuple(g.shape)}/{tuple(b.shape)} != {tuple(p.shape)}")
+        if not g.is_contiguous():
+            raise ValueError(f"Muon param {i}: grad must be contiguous")
+        if p.ndim not in (2, 3):
+            raise AssertionError("Muon is for 2-D matrices (or 3-D stacks of them)")
+        batch = p.shape[0] if p.ndim == 3 else 1
+        e = arr[i]
+        e.param, e.grad, e.momentum_buffer = p.data_ptr(), g.data_ptr(), b.data_ptr()
+        e.batch, e.rows, e.cols = batch, p.shape[-2], p.shape[-1]
+        e.lr, e.decay, e.momentum = float(it.lr), float(it.decay), float(it.momentum)
+        e.nesterov, e.grad_dtype = int(bool(it.nesterov)), grad_dtype_code(g)
+    return arr
+
+
+def adamw_array(items: Sequence[AdamWItem]):
+    arr = (L.AdamWTensor * max(1, len(items)))()
+    for i, it in enumerate(items):
+        for t, w in ((it.param, "param"), (it.exp_avg, "exp_avg"), (it.exp_avg_sq, "exp_avg_sq")):
+            _check_param(t, f"AdamW {w}")
+            if t.shape != it.param.shape:
+                raise ValueError(f"AdamW tensor {i}: {w} shape mismatch")
+        if it.grad.shape != it.param.shape or not it.grad.is_contiguous():
+            raise ValueError(f"AdamW tensor {i}: grad must be contiguous with the param's shape")
+        e = arr[i]
+        e.param, e.grad, e.exp_avg, e.exp_avg_sq = (it.param.data_ptr(), it.grad.data_ptr(), it.exp_avg.data_ptr(),
+                                                    it.exp_avg_sq.data_ptr())
+        e.numel, e.lr, e.weight_decay, e.step = it.param.numel(), float(it.lr), float(it.weight_decay), int(it.step)
+        e.grad_dtype = grad_dtype_code(it.grad)
+    return arr
+
+
+def _device(muon: Sequence[MuonItem], adamw: Sequence[AdamWItem]) -> torch.device:
+    for it in list(muon) + list(adamw):
+        return it.param.device
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+@torch.no_grad()
+def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (), *, ns_steps: int = 5,
+                   rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
+                   max_norm: Optional[float] = None, grad_divisor: Optional[float] = None,
+                   out_norm: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+    """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
+    AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
+    max_norm is given."""
+    dev = _device(muon, adamw)
+    m_arr, a_arr = muon_array(muon), adamw_array(adamw)
+    nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adamw))
+    if nbytes == 0:
+        raise L.MoteoptError("optimizer_step: invalid shapes")
+    ws = workspace(dev, nbytes)
+    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
+    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+    gc = L.GradConfig(int(max_norm is not None), float(max_norm or 0.0), float(grad_divisor or 0.0))
+    if max_norm is not None and out_norm is None:
+        out_norm = torch.empty((), dtype=torch.float32, device=dev)
+    L.check(L.lib.moteopt_optimizer_step(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp), C.byref(gc),
+                                         C.c_void_p(out_norm.data_ptr() if out_norm is not None else 0),
+                                         C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
+            "moteopt_optimizer_step")
+    return out_norm
+
+
+@torch.no_grad()
+def muon_step(muon: Sequence[MuonItem], *, ns_steps: int = 5, rms_scale: float = 0.2, ns_eps: float = 1e-7,
+              grad_scale: Optional[torch.Tensor] = None) -> None:
+    """mote/train/muon.py:52-100 for a list of parameters (any mix of groups and shapes)."""
+    if not muon:
+        return
+    dev = _device(muon, ())
+    arr = muon_array(muon)
+    nbytes = L.lib.moteopt_muon_step_workspace_size(arr, len(muon), ns_steps)
+    if nbytes == 0:
+        raise L.MoteoptError("muon_step: invalid shapes")
+    ws = workspace(dev, nbytes)
+    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
+    L.check(L.lib.moteopt_muon_step(arr, len(muon), C.byref(cfg),
+                                    C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
+                                    C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
+            "moteopt_muon_step")
+
+
+@torch.no_grad()
+def adamw_step(adamw: Sequence[AdamWItem], *, betas=(0.9, 0.999), eps: float = 1e-8,
+               grad_scale: Optional[torch.Tensor] = None) -> None:
+    """torch.optim.AdamW.step (single-tensor arithmetic, amsgrad=False) for a list of tensors."""
+    if not adamw:
+        return
+    dev = _device((), adamw)
+    arr = adamw_array(adamw)
+    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+    L.check(L.lib.moteopt_adamw_step(arr, len(adamw), C.byref(hp),
+                                     C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
+                                     C.c_void_p(stream_handle(dev))), "moteopt_adamw_step")
+
+
+def items_from_lists(params: List[torch.Tensor], grads: List[torch.Tensor], bufs: List[torch.Tensor], lr: float,
+                     decay: float, momentum: float = 0.95, nesterov: bool = True) -> List[MuonItem]:
+    return [MuonItem(p, g, b, lr, decay, momentum, nesterov) for p, g, b in zip(params, grads, bufs)]

@@ -1,0 +1,222 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle and the reference's golden outputs.
+
+Tolerances (why each is what it is is in tests/test_oracle_golden.py's docstring):
+  * Newton-Schulz, 1 iteration: <= 1e-3 relative Frobenius (same rounding points; only fp32 summation order differs)
+  * Newton-Schulz, 2 iterations: <= 5e-3
+  * Newton-Schulz, 5 iterations: <= 4e-2, and no farther from the exact fp64 iteration than the oracle + 3e-3
+  * AdamW exp_avg / exp_avg_sq and Muon momentum: 1e-6 relative per element (RMS-floored)
+  * params after 10 steps: AdamW 1e-6 (RMS-floored, 1e-9 absolute); Muon 1e-2 relative Frobenius
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moteopt_oracle as O
+from tests.conftest import golden
+from tests.golden.cases import ADAM_SHAPES, ADAM_WDS, NS_CASES, ns_input
+from mote_b200 import configs
+
+pytestmark = pytest.mark.gpu
+
+P_ATOL = 1e-9
+
+
+def _close(a, b, rel, atol=0.0):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
+    return int((np.abs(a - b) > rel * np.maximum(np.abs(b), rms) + atol).sum())
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mote_b200 import ops  # noqa: F401  (loads libmoteopt.so: fails loudly if it is missing)
+    return torch.device("cuda", 0)
+
+
+def _ns_gpu(u: np.ndarray, steps: int, dev) -> np.ndarray:
+    from mote_b200 import ops
+    out = ops.newton_schulz(torch.from_numpy(u).to(dev), steps=steps)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+def _status_ok(dev):
+    from mote_b200 import ops
+    st, _ = ops.read_status(dev)
+    assert st & 3 == 0, f"kernel status {st}"
+
+
+@pytest.mark.parametrize("name,shape,seed", NS_CASES)
+def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
+    ref = golden("ns_reference")
+    u = ns_input(shape, seed)
+    exact = O.newton_schulz_f64(u, 5)
+    for steps, tol in ((1, 1e-3), (2, 5e-3), (5, 4e-2)):
+        g = _ns_gpu(u, steps, dev)
+        o = O.newton_schulz(u, steps)
+        r = O.bf16_from_bits(ref[f"{name}_s{steps}"]).reshape(shape)
+        assert O.rel_frob(g, o) <= tol, (name, steps, O.rel_frob(g, o))
+        assert O.rel_frob(g, r) <= tol, (name, steps, O.rel_frob(g, r))
+        if steps == 5:
+            assert O.rel_frob(g, exact) <= O.rel_frob(o, exact) + 3e-3
+    _status_ok(dev)
+
+
+@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (2, 3072, 768), (2, 512, 2048), (1, 1000, 264)])
+def test_newton_schulz_benchmark_shapes(dev, shape):
+    u = ns_input(shape, 123)
+    for steps, tol in ((1, 1e-3), (5, 4e-2)):
+        g = _ns_gpu(u, steps, dev)
+        o = O.newton_schulz(u, steps)
+        assert O.rel_frob(g, o) <= tol, (shape, steps, O.rel_frob(g, o))
+    assert O.rel_frob(g, O.newton_schulz_f64(u, 5)) <= O.rel_frob(o, O.newton_schulz_f64(u, 5)) + 3e-3
+    _status_ok(dev)
+
+
+def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
+    from mote_b200 import ops
+    u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
+    a = ops.newton_schulz(u, 5)
+    b = ops.newton_schulz(u.to(torch.bfloat16), 5)
+    assert torch.equal(a, b)
+
+
+def _to(dev, xs):
+    return [torch.from_numpy(np.ascontiguousarray(x)).to(dev) for x in xs]
+
+
+def test_full_step_c0_ten_steps_matches_oracle(dev):
+    """train.py:944-947 on the c0 workload through the C ABI (bf16 grads), 10 steps, against the oracle."""
+    from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
+    w = configs.c0()
+    inp = configs.make_params(w, seed=0)
+    ap = _to(dev, inp.adam_params)
+    mp = _to(dev, inp.muon_params)
+    am = [torch.zeros_like(p) for p in ap]
+    av = [torch.zeros_like(p) for p in ap]
+    mb = [torch.zeros_like(p) for p in mp]
+    nd = len(w.adam_decay_shapes)
+    st = O.StepState()
+    st.muon_bufs = [None] * len(mp)
+    st.exp_avgs = [np.zeros_like(p) for p in inp.adam_params]
+    st.exp_avg_sqs = [np.zeros_like(p) for p in inp.adam_params]
+    st.adam_steps = [0] * len(ap)
+    mg = O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, nesterov=True, weight_decay=w.muon_wd, ns_steps=w.ns_steps)
+    div = 4.0
+    for step in range(10):
+        ag_np, mg_np = configs.make_grads(w, seed=0, step=step)
+        ag = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in ag_np]
+        mgg = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in mg_np]
+        muon = [MuonItem(p, g, b, w.muon_lr, w.muon_lr * w.muon_wd, w.muon_momentum, True) for p, g, b in zip(mp, mgg, mb)]
+        adam = [AdamWItem(p, g, m, v, w.adam_lr, w.adam_wd if i < nd else 0.0, step + 1)
+                for i, (p, g, m, v) in enumerate(zip(ap, ag, am, av))]
+        norm = optimizer_step(muon, adam, ns_steps=w.ns_steps, betas=w.betas, eps=w.eps, max_norm=w.clip,
+                              grad_divisor=div)
+        # oracle
+        allg = [x.copy() for x in ag_np] + [x.copy() for x in mg_np]
+        for x in allg:
+            x[...] = (x / np.float32(div)).astype(np.float32)
+        total = O.clip_grad_norm(allg, w.clip)
+        for i in range(len(ap)):
+            st.adam_steps[i] += 1
+            O.adamw_update(inp.adam_params[i], allg[i], st.exp_avgs[i], st.exp_avg_sqs[i], w.adam_lr, w.betas[0],
+                           w.betas[1], w.eps, w.adam_wd if i < nd else 0.0, st.adam_steps[i])
+        O.muon_step(inp.muon_params, allg[len(ap):], st.muon_bufs, mg)
+        assert _close(norm.item(), total, 1e-6) == 0, (norm.item(), total)
+        if step in (0, 9):
+            for i in range(len(ap)):
+                assert _close(am[i].cpu().numpy(), st.exp_avgs[i], 1e-6) == 0
+                assert _close(av[i].cpu().numpy(), st.exp_avg_sqs[i], 1e-6) == 0
+                assert _close(ap[i].cpu().numpy(), inp.adam_params[i], 1e-6, atol=P_ATOL) == 0
+            for i in range(len(mp)):
+                assert _close(mb[i].cpu().numpy(), st.muon_bufs[i], 1e-6) == 0
+                assert O.rel_frob(mp[i].cpu().numpy(), inp.muon_params[i]) < 1e-2, (step, i)
+    _status_ok(dev)
+
+
+def test_adamw_and_clip_match_reference(dev):
+    """The AdamW/clip fixture of the reference (5 steps, clip active) through the C ABI."""
+    from mote_b200.functional import AdamWItem, optimizer_step
+    g = golden("adamw_reference")
+    n = len(ADAM_SHAPES)
+    ps = _to(dev, [g[f"p0_{i}"] for i in range(n)])
+    ms = [torch.zeros_like(p) for p in ps]
+    vs = [torch.zeros_like(p) for p in ps]
+    for step in range(5):
+        grads = _to(dev, [g[f"g{step}_{i}"] for i in range(n)])
+        items = [AdamWItem(ps[i], grads[i], ms[i], vs[i], 3e-4, ADAM_WDS[i], step + 1) for i in range(n)]
+        norm = optimizer_step((), items, betas=(0.9, 0.95), eps=1e-8, max_norm=0.05)
+        assert _close(norm.item(), g[f"norm{step}"], 1e-5) == 0
+        if step in (0, 4):
+            for i in range(n):
+                # torch's CPU norm sits a few ulp off the exact one; through v ~ coef^2 that is ~1e-6 (test docstring)
+                assert _close(ms[i].cpu().numpy(), g[f"m{step + 1}_{i}"], 1e-5) == 0
+                assert _close(vs[i].cpu().numpy(), g[f"v{step + 1}_{i}"], 1e-5) == 0
+                assert _close(ps[i].cpu().numpy(), g[f"p{step + 1}_{i}"], 1e-5, atol=P_ATOL) == 0
+    _status_ok(dev)
+
+
+def test_clip_grad_norm_matches_oracle(dev):
+    from mote_b200 import ops
+    rng = np.random.default_rng(5)
+    shapes = [(1000, 3), (17,), (4, 4, 4), (70000,)]
+    gs = [O.bf16_round(rng.standard_normal(s).astype(np.float32)) for s in shapes]
+    for dt in (torch.float32, torch.bfloat16):
+        params = [torch.nn.Parameter(torch.zeros(s, device=dev)) for s in shapes]
+        for p, x in zip(params, gs):
+            p.grad = torch.from_numpy(x).to(dev).to(dt)
+        ref = [x.copy() for x in gs]
+        tot = O.clip_grad_norm(ref, 1.0)
+        n = ops.clip_grad_norm_(params, 1.0)
+        assert _close(n.item(), tot, 1e-6) == 0
+        for p, r in zip(params, ref):
+            got = p.grad.float().cpu().numpy()
+            want = r if dt == torch.float32 else O.bf16_round(r)
+            assert _close(got, want, 1e-6 if dt == torch.float32 else 1e-2) == 0
+
+
+def test_muon_batched_reference_case(dev):
+    """tests/test_muon_batched.py:46-67 of the reference through the C ABI, against its stored result."""
+    from mote_b200.functional import MuonItem, muon_step
+    g = golden("muon_reference")
+    for sw in (0, 1):
+        ps = _to(dev, [g[f"batched_p0_{i}"] for i in range(6)])
+        bufs = [torch.zeros_like(p) for p in ps]
+        for it in range(3):
+            grads = _to(dev, [(g[f"batched_g_{i}"] * np.float32(1.0 + 0.1 * it)).astype(np.float32) for i in range(6)])
+            lr, wd, lr_max = 1e-2, 0.1, 2e-2
+            decay = (lr * lr / lr_max if sw else lr) * wd
+            muon_step([MuonItem(p, gr, b, lr, decay, 0.95, True) for p, gr, b in zip(ps, grads, bufs)])
+        for i in range(6):
+            ref_p = g[f"batched_sw{sw}_p3_{i}"]
+            got = ps[i].cpu().numpy()
+            assert np.allclose(got, ref_p, atol=2e-3, rtol=1e-2)
+            assert _close(bufs[i].cpu().numpy(), g[f"batched_sw{sw}_buf_{i}"], 1e-6) == 0
+
+
+def test_step_is_bitwise_deterministic(dev):
+    from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
+    w = configs.c0()
+    outs = []
+    for _ in range(2):
+        inp = configs.make_params(w, seed=1)
+        mp = _to(dev, inp.muon_params)
+        ap = _to(dev, inp.adam_params)
+        mb = [torch.zeros_like(p) for p in mp]
+        am = [torch.zeros_like(p) for p in ap]
+        av = [torch.zeros_like(p) for p in ap]
+        norms = []
+        for step in range(3):
+            ag, mg = configs.make_grads(w, seed=1, step=step)
+            muon = [MuonItem(p, torch.from_numpy(x).to(dev), b, 0.02, 0.002) for p, x, b in zip(mp, mg, mb)]
+            adam = [AdamWItem(p, torch.from_numpy(x).to(dev), m, v, 3e-4, 0.1, step + 1)
+                    for p, x, m, v in zip(ap, ag, am, av)]
+            norms.append(optimizer_step(muon, adam, betas=(0.9, 0.95), max_norm=0.01).item())
+        outs.append(([p.cpu() for p in mp + ap + mb + am + av], norms))
+    for a, b in zip(outs[0][0], outs[1][0]):
+        assert torch.equal(a, b)
+    assert outs[0][1] == outs[1][1]
