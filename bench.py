@@ -1,0 +1,374 @@
+"""Benchmark of the B200 optimizer step (Muon + AdamW + global grad-norm clip) on the Mote-96M-shaped workload.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1]
+
+One step = train.py:944-947 of the reference: grads /= 1 (no divisor), clip_grad_norm_(all grads, 1.0), AdamW on
+the embedding and vectors, Muon (momentum + 5 Newton-Schulz iterations + apply) on every hidden matrix. Inputs
+(fp32 params, bf16 grads, fp32 optimizer state; 1.1 GB) stay resident in HBM and are larger than L2, so nothing is
+flushed between steps. Prints one JSON line (rank 0).
+
+--impl reference times the reference's arithmetic on the host CPU: the numpy restatement in oracle/ (the reference
+is Python and cannot be installed on the GPU host), one bounded sample per step, extrapolated to the full step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "ms/optimizer step (96M set)"
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons every 100 ms while the timed region runs."""
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={','.join(self.FIELDS)}",
+                                          "--format=csv,noheader,nounits", "-i", self.gpu_id, "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def cpu_baseline_sample(w, seconds_cap: float = 30.0):
+    """Time the oracle (numpy restatement of the reference step) on one matrix of every Muon shape plus the full
+    AdamW set and the grad norm, on this host's cores; extrapolate to the whole step by matrix counts."""
+    import numpy as np
+    from oracle import moteopt_oracle as O
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    shapes = {}
+    for s in w.muon_shapes:
+        shapes[tuple(s)] = shapes.get(tuple(s), 0) + 1
+    t_shape = {}
+    grp = O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=w.muon_wd, ns_steps=w.ns_steps)
+    for s in shapes:
+        p = (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
+        g = O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3))
+        bufs = [None]
+        t0 = time.perf_counter()
+        O.muon_step([p], [g], bufs, grp)
+        t_shape[s] = time.perf_counter() - t0
+    ap = [(rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for s in w.adam_shapes]
+    ag = [O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3)) for s in w.adam_shapes]
+    t0 = time.perf_counter()
+    O.adamw_step(ap, ag, [None] * len(ap), [None] * len(ap), [0] * len(ap),
+                 O.AdamWGroup(lr=w.adam_lr, betas=w.betas, eps=w.eps, weight_decay=w.adam_wd))
+    t_adam = time.perf_counter() - t0
+    # grad norm over every grad: time it on the AdamW grads plus one matrix per shape, scale by element count
+    sample = ag + [O.bf16_round(rng.standard_normal(s, dtype=np.float32)) for s in shapes]
+    n_sample = sum(x.size for x in sample)
+    t0 = time.perf_counter()
+    O.grad_total_norm(sample)
+    t_norm = (time.perf_counter() - t0) * (sum(w.numel()) / n_sample)
+    total = sum(shapes[s] * t_shape[s] for s in shapes) + t_adam + t_norm
+    desc = ("oracle/moteopt_oracle.py (numpy, bf16-exact rounding) on one matrix of each Muon shape "
+            f"{sorted(shapes)}, the full AdamW set and a norm sample; scaled by matrix counts to the full step")
+    return {"value": total * 1e3, "unit": "ms/step", "cores": int(cores), "kind": "port", "sample": desc}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    from mote_b200 import _lib as L
+    from mote_b200 import configs
+    from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    w = configs.CONFIGS[args.config]()
+    nd = len(w.adam_decay_shapes)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+
+    def randn(shape, std, dtype=torch.float32):
+        return (torch.randn(shape, generator=gen, device=dev) * std).to(dtype)
+
+    mp = [randn(s, 0.02) for s in w.muon_shapes]
+    ap = [randn(s, 0.02) for s in w.adam_shapes]
+    # grads live in one flat bf16 buffer so the end-to-end run can refresh them with one host->device copy
+    shapes = list(w.adam_shapes) + list(w.muon_shapes)
+    sizes = [int(torch.Size(s).numel()) for s in shapes]
+    flat = randn((sum(sizes),), 1e-3, torch.bfloat16)
+    views = list(torch.split(flat, sizes))
+    grads = [v.view(s) for v, s in zip(views, shapes)]
+    ag, mg = grads[: len(ap)], grads[len(ap):]
+    mb = [torch.zeros_like(p) for p in mp]
+    am = [torch.zeros_like(p) for p in ap]
+    av = [torch.zeros_like(p) for p in ap]
+    norm = torch.empty((), dtype=torch.float32, device=dev)
+    muon_items = [MuonItem(p, g, b, w.muon_lr, w.muon_lr * w.muon_wd, w.muon_momentum, True) for p, g, b in zip(mp, mg, mb)]
+    counter = {"step": 0}
+
+    def step():
+        counter["step"] += 1
+        adam_items = [AdamWItem(p, g, m, v, w.adam_lr, w.adam_wd if i < nd else 0.0, counter["step"])
+                      for i, (p, g, m, v) in enumerate(zip(ap, ag, am, av))]
+        optimizer_step(muon_items, adam_items, ns_steps=w.ns_steps, betas=w.betas, eps=w.eps, max_norm=w.clip,
+                       out_norm=norm)
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # NS span events, one pair per timed step
+    ns_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for a, b in ns_ev:
+        a.record(stream)
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    launches0 = L.lib.moteopt_launch_count()
+    with ClockSampler(gpu_id) as clk:
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for k in range(args.steps):
+            L.check(L.lib.moteopt_profile_ns_events(ns_ev[k][0].cuda_event, ns_ev[k][1].cuda_event), "events")
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
+    launches = L.lib.moteopt_launch_count() - launches0
+    ms = e0.elapsed_time(e1) / args.steps
+    ns_ms = statistics.mean(a.elapsed_time(b) for a, b in ns_ev)
+    st, _ = __import__("mote_b200.ops", fromlist=["read_status"]).read_status(dev)
+    if st & 3:
+        raise RuntimeError(f"kernel status {st}")
+
+    # AdamW bandwidth on a flat 1e8-element tensor (the metric's "AdamW % HBM BW")
+    n_flat = 100_000_000
+    fp = randn((n_flat,), 0.02)
+    fg = randn((n_flat,), 1e-3, torch.bfloat16)
+    fm, fv = torch.zeros_like(fp), torch.zeros_like(fp)
+    for k in range(3):
+        optimizer_step((), [AdamWItem(fp, fg, fm, fv, 3e-4, 0.1, k + 1)], betas=w.betas)
+    torch.cuda.synchronize(dev)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for k in range(10):
+        optimizer_step((), [AdamWItem(fp, fg, fm, fv, 3e-4, 0.1, k + 4)], betas=w.betas)
+    a1.record(stream)
+    torch.cuda.synchronize(dev)
+    adam_ms = a0.elapsed_time(a1) / 10
+    del fp, fg, fm, fv
+
+    # end to end through the public API with host buffers: grads copied in from pinned memory, norm read back
+    host_grads = flat.cpu().pin_memory()
+    host_norm = torch.empty((), dtype=torch.float32).pin_memory()
+    e2e_steps = max(5, min(50, args.steps // 6))
+    for _ in range(3):
+        flat.copy_(host_grads, non_blocking=True)
+        step()
+        host_norm.copy_(norm, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(stream)
+    for _ in range(e2e_steps):
+        flat.copy_(host_grads, non_blocking=True)
+        step()
+        host_norm.copy_(norm, non_blocking=True)
+    h1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = h0.elapsed_time(h1) / e2e_steps
+
+    peaks, src = load_peaks()
+    ns_flops = w.ns_flops()
+    achieved = ns_flops / (ns_ms * 1e-3) / 1e12
+    traffic = None
+    prof = ROOT / "profiles" / "ns_phase_kernel_c1_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+    adam_gbs = 28.0 * n_flat / (adam_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: seeded params N(0,0.02^2) fp32, grads N(0,1e-3^2) bf16 (no dataset: an optimizer step)",
+        "config": {"workload": w.name, "muon_matrices": len(w.muon_shapes), "muon_elems": w.numel()[0],
+                   "adamw_elems": w.numel()[1], "ns_steps": w.ns_steps, "clip": w.clip,
+                   "parallelism": f"dp{world}" if world > 1 else "single",
+                   "l2": "inputs (1.1 GB) larger than L2; no flush"},
+        "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel", "achieved": round(achieved, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "traffic": traffic, "peak_source": f"{src} (burst bf16)",
+                     "ns_ms_per_step": round(ns_ms, 4), "launches_per_step": 15, "ns_tflop_per_step": ns_flops / 1e12},
+        "adamw_hbm": {"achieved": round(adam_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                      "frac": round(adam_gbs / peaks["hbm_gbs"], 4), "elems": n_flat, "ms": round(adam_ms, 4)},
+        "e2e": {"value": round(e2e_ms, 4), "unit": "ms/step", "h2d_bytes_per_step": int(flat.numel() * 2),
+                "d2h_bytes_per_step": 4},
+        "clocks": clk.summary(),
+        "gpu_launches": int(launches),
+    }
+    return line
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def run_reference(args, rank: int, world: int):
+    """The reference's arithmetic (oracle/ numpy restatement) on the host CPU, one bounded sample per step."""
+    import numpy as np
+    from mote_b200 import configs
+    from oracle import moteopt_oracle as O
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    w = configs.CONFIGS[args.config]()
+    rng = np.random.default_rng(0)
+    counts = {}
+    for s in w.muon_shapes:
+        counts[tuple(s)] = counts.get(tuple(s), 0) + 1
+    shapes = sorted(counts)
+    # one Newton-Schulz iteration of one matrix per step, cycling through the shapes; the rest of the step
+    # (momentum, normalisation, apply, AdamW, grad norm) is timed once and added
+    xs = {s: O.ns_normalize(rng.standard_normal(s, dtype=np.float32)) for s in shapes}
+    t_iter = {s: [] for s in shapes}
+    for k in range(args.warmup + args.steps):
+        s = shapes[k % len(shapes)]
+        t0 = time.perf_counter()
+        O.ns_iterate(xs[s], 1)
+        dt = time.perf_counter() - t0
+        if k >= args.warmup:
+            t_iter[s].append(dt)
+    for s in shapes:   # a shape not reached by a short run gets one measurement here
+        if not t_iter[s]:
+            t0 = time.perf_counter()
+            O.ns_iterate(xs[s], 1)
+            t_iter[s].append(time.perf_counter() - t0)
+    # element-wise parts on one matrix per shape: momentum, normalisation, apply
+    t_elem = 0.0
+    grp = O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=w.muon_wd, ns_steps=0)
+    for s in shapes:
+        p = rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
+        g = O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3))
+        t0 = time.perf_counter()
+        O.muon_step([p], [g], [None], grp)
+        t_elem += counts[s] * (time.perf_counter() - t0)
+    ap = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in w.adam_shapes]
+    ag = [O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3)) for s in w.adam_shapes]
+    t0 = time.perf_counter()
+    O.adamw_step(ap, ag, [None] * len(ap), [None] * len(ap), [0] * len(ap),
+                 O.AdamWGroup(lr=w.adam_lr, betas=w.betas, eps=w.eps, weight_decay=w.adam_wd))
+    t_rest = time.perf_counter() - t0
+    sample = ag + [xs[s] for s in shapes]
+    t0 = time.perf_counter()
+    O.grad_total_norm(sample)
+    t_rest += (time.perf_counter() - t0) * (sum(w.numel()) / sum(x.size for x in sample))
+    total = sum(counts[s] * w.ns_steps * statistics.median(t_iter[s]) for s in shapes) + t_elem + t_rest
+    ms = total * 1e3
+    desc = (f"oracle/moteopt_oracle.py (numpy) on the host: per step one Newton-Schulz iteration of one matrix, "
+            f"cycling {shapes}; + momentum/normalise/apply per shape, full AdamW and a norm sample, once; "
+            "extrapolated to the full step by matrix counts")
+    return {"metric": METRIC, "value": round(ms, 3), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "impl": "reference",
+            "data": "synthetic: seeded params N(0,0.02^2) fp32, grads N(0,1e-3^2) bf16",
+            "config": {"workload": w.name, "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(ms, 3), "unit": "ms/step", "cores": int(cores), "kind": "port",
+                             "sample": desc},
+            "e2e": {"value": round(ms, 3), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return 0
+        print(json.dumps(run_reference(args, rank, world)), flush=True)
+        return 0
+    if world > 1:
+        from mote_b200 import dist_bench
+        line = dist_bench.run(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
+    line = run_ours(args, rank, world, local_rank)
+    if not args.no_cpu_baseline:
+        from mote_b200 import configs
+        line["cpu_baseline"] = cpu_baseline_sample(configs.CONFIGS[args.config]())
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -89,6 +89,13 @@ typedef struct moteopt_grad_config {
 MOTEOPT_API int moteopt_version(void);
 MOTEOPT_API const char* moteopt_last_error(void);
 
+/* Measurement hooks (no counterpart in the reference, which has no kernels of its own). The launch count is the
+ * number of kernels this library has enqueued since it was loaded. With events set (two cudaEvent_t, or NULL to
+ * clear), every later moteopt_optimizer_step / moteopt_muon_step on the calling thread records the first before its
+ * first Newton-Schulz launch and the second after its last, on the step's stream. */
+MOTEOPT_API unsigned long long moteopt_launch_count(void);
+MOTEOPT_API int moteopt_profile_ns_events(void* start_event, void* end_event);
+
 /* Read (and optionally clear) the workspace's status word and the last [total norm, clip coefficient].
  * Synchronises `stream`. Either output may be NULL. */
 MOTEOPT_API int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream);

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -33,8 +34,12 @@ int fail(int code, const std::string& msg) {
     if (e_ != cudaSuccess) return fail(MOTEOPT_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
+std::atomic<unsigned long long> g_launches{0};
+thread_local cudaEvent_t t_ns_ev[2] = {nullptr, nullptr};
+
 #define MO_LAUNCHED(what)                                                                      \
   do {                                                                                         \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                                       \
     cudaError_t e_ = cudaGetLastError();                                                       \
     if (e_ != cudaSuccess) return fail(MOTEOPT_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e_)); \
   } while (0)
@@ -141,7 +146,7 @@ struct Layout {
   std::vector<GroupPlan> groups;          // Newton-Schulz shape groups, in launch order
   std::vector<int> mat_chunk_start;       // per matrix (group-major order): sum-of-squares chunk prefix
   std::vector<int> norm_tensor_chunk_start;
-  size_t off_norm = 0, off_mom = 0, bytes = 0;
+  size_t off_norm = 0, off_mom = 0, off_den = 0, bytes = 0;
 };
 
 constexpr int kMaxMatsPerGroup = ns::kMaxApply;
@@ -200,7 +205,9 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
   L->off_norm = off;
   off = align_up(off + 4 * static_cast<size_t>(L->norm_tensor_chunk_start.back()), 256);
   L->off_mom = off;
-  off = align_up(off + 4 * static_cast<size_t>(L->mat_chunk_start.back()), 1024);
+  off = align_up(off + 4 * static_cast<size_t>(L->mat_chunk_start.back()), 256);
+  L->off_den = off;
+  off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 1024);
   for (GroupPlan& g : L->groups) {
     const size_t cnt = g.mats.size();
     const size_t xb = cnt * g.m * g.n * 2, ab = cnt * g.m * g.m * 2;
@@ -289,6 +296,25 @@ int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chu
     if (A.chunk_start[n] == 0) continue;
     sumsq_kernel<<<grid_for(A.chunk_start[n], sms), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("sumsq_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+// per-matrix ||u||_F + eps from the sum-of-squares partials
+int launch_denoms(const Layout& L, const float* partials, float* den, float eps, cudaStream_t st) {
+  const int nm = static_cast<int>(L.mat_chunk_start.size()) - 1;
+  DenomArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.eps = eps;
+  A.partials = partials;
+  A.den = den;
+  for (int s0 = 0; s0 < nm; s0 += kMaxDenom) {
+    const int cnt = std::min(nm - s0, kMaxDenom);
+    A.n = cnt;
+    A.base = s0;
+    for (int i = 0; i <= cnt; ++i) A.chunk_start[i] = L.mat_chunk_start[s0 + i];
+    mat_denom_kernel<<<(cnt + 7) / 8, 256, 0, st>>>(A);
+    MO_LAUNCHED("mat_denom_kernel");
   }
   return MOTEOPT_OK;
 }
@@ -438,14 +464,14 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
   }
   // 2. X0 = bf16(u / (||u|| + eps)) into each group's X0 buffer
   {
+    float* den = reinterpret_cast<float*>(ws + L.off_den);
+    MO_TRY(launch_denoms(L, mom_partials, den, static_cast<float>(cfg->ns_eps), st));
     NormArgs A;
     std::memset(&A, 0, sizeof(A));
     A.has_div = has_div;
     A.div = div;
     A.coef = coef;
-    A.partials = mom_partials;
-    A.eps = static_cast<float>(cfg->ns_eps);
-    A.status = status;
+    A.den = den;
     for (int s0 = 0; s0 < nm; s0 += kMaxNormMat) {
       const int cnt = std::min(nm - s0, kMaxNormMat);
       A.n = cnt;
@@ -465,8 +491,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
         M.dtype = m.p->grad_dtype;
         M.mom = static_cast<float>(m.p->momentum);
         M.nesterov = m.p->nesterov != 0;
-        M.chunk0 = L.mat_chunk_start[s0 + i];
-        M.chunk1 = L.mat_chunk_start[s0 + i + 1];
+        M.den_index = s0 + i;
         M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
         M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
         max_tiles = std::max(max_tiles, M.tiles);
@@ -475,6 +500,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
       MO_LAUNCHED("ns_normalize_kernel");
     }
   }
+  (void)status;
   return MOTEOPT_OK;
 }
 
@@ -672,7 +698,9 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     } else {
       const std::vector<ns::MatApply> tab = muon_apply_table(muon, mcfg, L);
       int final_src = 0;
+      if (t_ns_ev[0] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[0], st));
       MO_TRY(run_ns(L, ws, mcfg->ns_steps, &tab, status, sms, st, &final_src));
+      if (t_ns_ev[1] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[1], st));
     }
   }
   return MOTEOPT_OK;
@@ -684,6 +712,16 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
 extern "C" {
 
 int moteopt_version(void) { return 1; }
+
+unsigned long long moteopt_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int moteopt_profile_ns_events(void* start_event, void* end_event) {
+  if ((start_event == nullptr) != (end_event == nullptr))
+    return fail(MOTEOPT_ERR_INVALID, "give both events or neither");
+  t_ns_ev[0] = static_cast<cudaEvent_t>(start_event);
+  t_ns_ev[1] = static_cast<cudaEvent_t>(end_event);
+  return MOTEOPT_OK;
+}
 
 const char* moteopt_last_error(void) { return t_err.c_str(); }
 
@@ -835,11 +873,12 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
   float* partials = reinterpret_cast<float*>(ws + L.off_mom);
   r = launch_sumsq(src, L.mat_chunk_start, partials, false, 1.0f, sms, st);
   if (r != MOTEOPT_OK) return r;
+  float* den = reinterpret_cast<float*>(ws + L.off_den);
+  r = launch_denoms(L, partials, den, static_cast<float>(eps), st);
+  if (r != MOTEOPT_OK) return r;
   NormArgs A;
   std::memset(&A, 0, sizeof(A));
-  A.partials = partials;
-  A.eps = static_cast<float>(eps);
-  A.status = &hdr->status;
+  A.den = den;
   const int nm = static_cast<int>(src.size());
   for (int s0 = 0; s0 < nm; s0 += kMaxNormMat) {
     const int cnt = std::min(nm - s0, kMaxNormMat);
@@ -857,8 +896,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
       M.n_pad = g.n;
       M.transposed = g.transposed;
       M.dtype = g_dtype;
-      M.chunk0 = L.mat_chunk_start[s0 + i];
-      M.chunk1 = L.mat_chunk_start[s0 + i + 1];
+      M.den_index = s0 + i;
       M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
       M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
       max_tiles = std::max(max_tiles, M.tiles);

@@ -234,24 +234,30 @@ __global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// den[m] = fp32(sqrt(sum of matrix m's partials)) + eps (muon.py:33: X.norm() + eps). One warp per matrix; lane l
+// sums chunks l, l+32, ... in fp64, then a fixed xor tree: deterministic.
+__global__ void __launch_bounds__(256) mat_denom_kernel(const __grid_constant__ DenomArgs A) {
+  const int mat = blockIdx.x * 8 + static_cast<int>(threadIdx.x >> 5);
+  if (mat >= A.n) return;
+  const int lane = threadIdx.x & 31;
+  double s = 0.0;
+  for (int c = A.chunk_start[mat] + lane; c < A.chunk_start[mat + 1]; c += 32) s += static_cast<double>(A.partials[c]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) A.den[A.base + mat] = __fadd_rn(static_cast<float>(sqrt(s)), A.eps);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // X0 = bf16(u / (||u||_F + eps)), transposed when the matrix has more rows than columns, zero padded.
 // grid: (tiles of the largest matrix, matrices). u is recomputed from the grad and the updated momentum buffer
 // exactly as the momentum kernel computed it (momentum mode), or read from G (direct mode, buf == null).
 __global__ void __launch_bounds__(kMtThreads) ns_normalize_kernel(const __grid_constant__ NormArgs A) {
   __shared__ float tile[kNormTile][kNormTile + 1];
-  __shared__ float s_den;
   const NormMat& M = A.mat[blockIdx.y];
   if (static_cast<int>(blockIdx.x) >= M.tiles) return;
   const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
   const int i0 = ti * kNormTile, j0 = tj * kNormTile;   // destination tile origin (X rows i, cols j)
-  if (threadIdx.x == 0) {
-    double s = 0.0;
-    for (int c = M.chunk0; c < M.chunk1; ++c) s += static_cast<double>(A.partials[c]);
-    const float nrm = static_cast<float>(sqrt(s));
-    s_den = __fadd_rn(nrm, A.eps);
-  }
-  __syncthreads();
-  const float den = s_den;
+  const float den = A.den[M.den_index];
   const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4 threads
   const int mv = M.transposed ? M.cols : M.rows;            // valid X rows

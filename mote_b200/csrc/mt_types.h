@@ -106,7 +106,8 @@ struct NormMat {
   int dtype;
   float mom;
   int nesterov;
-  int chunk0, chunk1;        // this matrix's sum-of-squares partials [chunk0, chunk1)
+  int den_index;             // this matrix's ||u||_F + eps in NormArgs::den
+  int pad_;
   int tiles_x;               // destination tiles along n_pad
   int tiles;                 // total destination tiles
 };
@@ -115,10 +116,19 @@ struct NormArgs {
   int has_div;
   float div;
   const float* coef;
-  const float* partials;
-  float eps;
-  int* status;
+  const float* den;          // per matrix: ||u||_F + eps (mat_denom_kernel)
   NormMat mat[kMaxNormMat];
+};
+
+// ---- per-matrix Frobenius norm from the sum-of-squares partials: den = fp32(sqrt(sum)) + eps
+constexpr int kMaxDenom = 4096;
+struct DenomArgs {
+  int n;
+  int base;                  // den index of this launch's first matrix
+  float eps;
+  const float* partials;
+  float* den;
+  int chunk_start[kMaxDenom + 1];
 };
 
 // ---- copy the final iterate out of the workspace (standalone newton_schulz), or apply it (ns_steps == 0)

@@ -135,19 +135,6 @@ __device__ __forceinline__ void store_bf16_row(__nv_bfloat16* dst, const float (
     if (k * 8 < cols_left) d4[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
 }
 
-__device__ __forceinline__ void load_bf16_row(const __nv_bfloat16* src, float (&v)[32], int cols_left) {
-  const uint4* s4 = reinterpret_cast<const uint4*>(src);
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    uint4 w = make_uint4(0, 0, 0, 0);
-    if (k * 8 < cols_left) w = s4[k];
-    v[8 * k + 0] = bf16_lo(w.x); v[8 * k + 1] = bf16_hi(w.x);
-    v[8 * k + 2] = bf16_lo(w.y); v[8 * k + 3] = bf16_hi(w.y);
-    v[8 * k + 4] = bf16_lo(w.z); v[8 * k + 5] = bf16_hi(w.z);
-    v[8 * k + 6] = bf16_lo(w.w); v[8 * k + 7] = bf16_hi(w.w);
-  }
-}
-
 // mote/train/muon.py:93-99 for the 32 columns j..j+31 of row i of the orthogonalised iterate.
 __device__ __forceinline__ void apply_row(const Group& G, const MatApply& ma, int i, int j, const float (&o)[32]) {
   if (i >= G.mv) return;
@@ -197,10 +184,28 @@ __device__ __forceinline__ void apply_row(const Group& G, const MatApply& ma, in
   }
 }
 
+// Unpack 8 bf16 (one uint4) into floats.
+__device__ __forceinline__ void unpack8(const uint4& w, float* v) {
+  v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+  v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z); v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
+}
+
+// Round a pair to bf16 and back (one cvt.rn.bf16x2.f32 for two values).
+__device__ __forceinline__ void round2(float& a, float& b) {
+  const uint32_t p = pack_bf16x2(a, b);
+  a = bf16_lo(p);
+  b = bf16_hi(p);
+}
+
+// Epilogue warps 2..9: warp w reads TMEM lane quarter (w % 4) and owns columns [128*h, 128*h + 128) of the tile,
+// h = (w - 2) / 4. The bf16 operand the phase's polynomial needs (A for kPoly, X for kUpdate) is loaded before the
+// accumulator is waited for, so its latency hides behind the tile's MMAs.
 __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, uint64_t* tempty, uint32_t tmem_base,
                                              const WaitCtx& ctx) {
+  constexpr int kChunks = BN / 32 / 2;   // 32-column chunks per epilogue warp
   const int total = L.tile_start[L.n_groups];
-  const int q = static_cast<int>(warp_id() & 3u);   // the TMEM lane quarter this warp may read
+  const int q = static_cast<int>(warp_id() & 3u);
+  const int half = (static_cast<int>(warp_id()) - 2) >> 2;
   const int row = q * 32 + static_cast<int>(lane_id());
   int local = 0;
   for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
@@ -209,17 +214,34 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
     const Group& G = L.g[gi];
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
-    // warp-uniform outcome: the TMEM loads below are .sync.aligned
-    if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], use, ctx) ? 1 : 0)) break;
-    tc_fence_after();
     const int out_cols = L.phase == kUpdate ? G.n : G.m;
     const int i = i0 + row;
     const bool row_ok = i < G.m;
-    for (int c = 0; c < BN / 32; ++c) {
-      const int j = j0 + c * 32;
+    const int jc0 = j0 + half * (kChunks * 32);   // first column of this warp
+    const size_t row_off = L.phase == kUpdate ? (static_cast<size_t>(b) * G.m + i) * G.n
+                                              : (static_cast<size_t>(b) * G.m + i) * G.m;
+    // prefetch the polynomial's bf16 operand for this warp's columns
+    uint4 aux[kChunks][4];
+    if (L.phase != kGram) {
+      const __nv_bfloat16* src = (L.phase == kPoly ? G.a : G.x[L.src]) + row_off;
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = jc0 + c * 32 + k * 8;
+          aux[c][k] = (row_ok && j < out_cols) ? *reinterpret_cast<const uint4*>(src + j) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    // warp-uniform outcome: the TMEM loads below are .sync.aligned
+    if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], use, ctx) ? 1 : 0)) break;
+    tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int j = jc0 + c * 32;
       if (j >= out_cols) break;   // uniform across the warp
       uint32_t r[32];
-      tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + c * 32), r);
+      tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                    static_cast<uint32_t>(acc * BN + half * (kChunks * 32) + c * 32), r);
       tmem_ld_wait(r);
       if (!row_ok) continue;
       const int cols_left = out_cols - j;
@@ -227,35 +249,41 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
       if (L.phase == kGram) {
 #pragma unroll
         for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-        store_bf16_row(G.a + (static_cast<size_t>(b) * G.m + i) * G.m + j, v, cols_left);
-      } else if (L.phase == kPoly) {
-        float a[32];
-        const size_t off = (static_cast<size_t>(b) * G.m + i) * G.m + j;
-        load_bf16_row(G.a + off, a, cols_left);
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float aa = bf16_round_f(__uint_as_float(r[k]));                // A @ A
-          const float t1 = bf16_round_f(__fmul_rn(kNsB, a[k]));                // b * A
-          const float t2 = bf16_round_f(__fmul_rn(kNsC, aa));                  // c * (A @ A)
-          v[k] = __fadd_rn(t1, t2);                                            // rounded by the store
-        }
-        store_bf16_row(G.b + off, v, cols_left);
+        store_bf16_row(G.a + row_off + j, v, cols_left);
       } else {
-        float x[32];
-        const size_t off = (static_cast<size_t>(b) * G.m + i) * G.n + j;
-        load_bf16_row(G.x[L.src] + off, x, cols_left);
+        float a[32];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float bx = bf16_round_f(__uint_as_float(r[k]));                // B @ X
-          const float ax = bf16_round_f(__fmul_rn(kNsA, x[k]));                // a * X
-          v[k] = __fadd_rn(ax, bx);
-        }
-        if (L.apply) {
+        for (int k = 0; k < 4; ++k) unpack8(aux[c][k], a + 8 * k);
+        if (L.phase == kPoly) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = bf16_round_f(v[k]);             // O (bf16)
-          apply_row(G, L.mats[G.first + b], i, j, v);
+          for (int k = 0; k < 32; k += 2) {
+            float aa0 = __uint_as_float(r[k]), aa1 = __uint_as_float(r[k + 1]);
+            round2(aa0, aa1);                                                   // A @ A
+            float t10 = __fmul_rn(kNsB, a[k]), t11 = __fmul_rn(kNsB, a[k + 1]);
+            round2(t10, t11);                                                   // b * A
+            float t20 = __fmul_rn(kNsC, aa0), t21 = __fmul_rn(kNsC, aa1);
+            round2(t20, t21);                                                   // c * (A @ A)
+            v[k] = __fadd_rn(t10, t20);                                         // rounded by the store
+            v[k + 1] = __fadd_rn(t11, t21);
+          }
+          store_bf16_row(G.b + row_off + j, v, cols_left);
         } else {
-          store_bf16_row(G.x[L.src ^ 1] + off, v, cols_left);
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            float bx0 = __uint_as_float(r[k]), bx1 = __uint_as_float(r[k + 1]);
+            round2(bx0, bx1);                                                   // B @ X
+            float ax0 = __fmul_rn(kNsA, a[k]), ax1 = __fmul_rn(kNsA, a[k + 1]);
+            round2(ax0, ax1);                                                   // a * X
+            v[k] = __fadd_rn(ax0, bx0);
+            v[k + 1] = __fadd_rn(ax1, bx1);
+          }
+          if (L.apply) {
+#pragma unroll
+            for (int k = 0; k < 32; k += 2) round2(v[k], v[k + 1]);            // O (bf16)
+            apply_row(G, L.mats[G.first + b], i, j, v);
+          } else {
+            store_bf16_row(G.x[L.src ^ 1] + row_off + j, v, cols_left);
+          }
         }
       }
     }
@@ -287,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_cons
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4 * 32);
+      mbar_init(&tempty[a], kEpiWarps * 32);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;

@@ -1,0 +1,92 @@
+"""The C ABI without a GPU: the library loads, exports every function include/moteopt.h declares, the ctypes
+mirrors of the header's structs have the C layout, and the workspace-size functions (pure host code) agree with the
+layout rules."""
+
+import re
+import subprocess
+import tempfile
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "moteopt.h"
+
+
+def declared():
+    txt = HEADER.read_text()
+    return sorted(set(re.findall(r"MOTEOPT_API\s+[\w\s\*]+?\b(moteopt_\w+)\s*\(", txt)))
+
+
+def test_header_declares_the_bound_entry_points():
+    from mote_b200 import _lib
+    assert declared() == sorted(_lib.EXPORTS)
+
+
+def test_library_exports_every_declared_symbol():
+    from mote_b200 import _lib
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    syms = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    for name in declared():
+        assert name in syms, name
+        assert hasattr(_lib.lib, name)
+
+
+def test_ctypes_structs_match_the_c_layout():
+    import ctypes as C
+    from mote_b200 import _lib
+    src = r'''
+#include <stdio.h>
+#include <stddef.h>
+#include "moteopt.h"
+#define P(T) printf(#T " %zu\n", sizeof(T));
+#define O(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
+int main(void) {
+  P(moteopt_muon_param) P(moteopt_muon_config) P(moteopt_adamw_tensor) P(moteopt_adamw_hparams) P(moteopt_grad_config)
+  O(moteopt_muon_param, lr) O(moteopt_muon_param, nesterov) O(moteopt_muon_param, grad_dtype)
+  O(moteopt_adamw_tensor, numel) O(moteopt_adamw_tensor, step) O(moteopt_adamw_tensor, grad_dtype)
+  O(moteopt_muon_config, rms_scale) O(moteopt_grad_config, max_norm)
+  return 0;
+}
+'''
+    with tempfile.TemporaryDirectory() as d:
+        c = Path(d) / "p.c"
+        c.write_text(src)
+        exe = Path(d) / "p"
+        subprocess.run(["gcc", "-I", str(ROOT / "include"), str(c), "-o", str(exe)], check=True)
+        got = dict(ln.rsplit(" ", 1) for ln in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                                check=True).stdout.splitlines())
+    m = {"moteopt_muon_param": _lib.MuonParam, "moteopt_muon_config": _lib.MuonConfig,
+         "moteopt_adamw_tensor": _lib.AdamWTensor, "moteopt_adamw_hparams": _lib.AdamWHparams,
+         "moteopt_grad_config": _lib.GradConfig}
+    for k, v in got.items():
+        if "." in k:
+            t, f = k.split(".")
+            assert getattr(m[t], f).offset == int(v), k
+        else:
+            assert C.sizeof(m[k]) == int(v), k
+
+
+def test_workspace_sizes_follow_the_layout():
+    from mote_b200 import _lib
+    lib = _lib.lib
+    # 48 x 768^2: header, partials, denominators, then X0, X1, A, B at 1024-byte alignment
+    n = lib.moteopt_newton_schulz_workspace_size(48, 768, 768)
+    per = 48 * 768 * 768 * 2
+    assert n >= 4 * per and n < 4 * per + 64 * 1024
+    # a transposed shape needs the same buffers as its transpose
+    assert lib.moteopt_newton_schulz_workspace_size(2, 3072, 768) == lib.moteopt_newton_schulz_workspace_size(2, 768, 3072)
+    # invalid shapes report 0
+    assert lib.moteopt_newton_schulz_workspace_size(0, 8, 8) == 0
+    assert lib.moteopt_newton_schulz_workspace_size(1, -1, 8) == 0
+
+
+def test_entry_points_reject_bad_arguments_without_touching_a_device():
+    import ctypes as C
+    from mote_b200 import _lib
+    lib = _lib.lib
+    rc = lib.moteopt_newton_schulz(None, 0, None, 1, 8, 8, 5, 1e-7, None, 0, None)
+    assert rc == -1 and b"null" in lib.moteopt_last_error()
+    rc = lib.moteopt_profile_ns_events(C.c_void_p(1), None)
+    assert rc == -1

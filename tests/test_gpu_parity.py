@@ -166,7 +166,7 @@ def test_clip_grad_norm_matches_oracle(dev):
     shapes = [(1000, 3), (17,), (4, 4, 4), (70000,)]
     gs = [O.bf16_round(rng.standard_normal(s).astype(np.float32)) for s in shapes]
     for dt in (torch.float32, torch.bfloat16):
-        params = [torch.nn.Parameter(torch.zeros(s, device=dev)) for s in shapes]
+        params = [torch.nn.Parameter(torch.zeros(s, device=dev, dtype=dt)) for s in shapes]
         for p, x in zip(params, gs):
             p.grad = torch.from_numpy(x).to(dev).to(dt)
         ref = [x.copy() for x in gs]
