@@ -111,9 +111,9 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// 3-D bf16 tensor [depth][outer][inner], row-major, 128-byte swizzled box {box_inner, box_outer, 1}
+// 3-D bf16 tensor [depth][outer][inner], row-major, swizzled box {box_inner, box_outer, 1}
 int make_map(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uint64_t depth, uint32_t box_inner,
-             uint32_t box_outer) {
+             uint32_t box_outer, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return fail(MOTEOPT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[3] = {inner, outer, depth};
@@ -121,7 +121,7 @@ int make_map(CUtensorMap* m, void* base, uint64_t inner, uint64_t outer, uint64_
   cuuint32_t box[3] = {box_inner, box_outer, 1};
   cuuint32_t es[3] = {1, 1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, es,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(MOTEOPT_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
   return MOTEOPT_OK;
@@ -235,7 +235,7 @@ struct MapKey {
   }
 };
 struct MapSet {
-  CUtensorMap xk[2], xmn[2], ak, bk;
+  CUtensorMap xk[2], xmn[2], ak, bk, xe[2], ae, be;
 };
 std::mutex g_map_mu;
 std::map<MapKey, MapSet> g_maps;
@@ -261,6 +261,10 @@ int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
   }
   MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::BM));
   MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::BM));
+  for (int k = 0; k < 2; ++k)
+    MO_TRY(make_map(&s.xe[k], x[k], g.n, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
+  MO_TRY(make_map(&s.ae, ws + g.off_a, g.m, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
+  MO_TRY(make_map(&s.be, ws + g.off_b, g.m, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
   if (g_maps.size() > 4096) g_maps.clear();
   g_maps[key] = s;
   *out = s;
@@ -410,7 +414,7 @@ int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cf
   return MOTEOPT_OK;
 }
 
-// The Muon update of `n` params: momentum, normalisation, Newton-Schulz with the apply fused into the last phase.
+// The first half of the Muon update of `n` params: momentum and the Newton-Schulz normalisation X0.
 int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg, const Layout& L, char* ws,
              bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st) {
   if (n == 0) return MOTEOPT_OK;
@@ -504,9 +508,8 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
   return MOTEOPT_OK;
 }
 
-// Newton-Schulz iterations over every group; if `apply_src` is non-null the last phase applies the Muon update.
-int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>* apply, int* status, int sms,
-           cudaStream_t st, int* final_src) {
+// Newton-Schulz iterations over every group; `final_src` receives the X buffer holding the result.
+int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStream_t st, int* final_src) {
   *final_src = 0;
   if (steps == 0) return MOTEOPT_OK;
   // launch sets: <= kMaxGroups groups and <= kMaxApply matrices each
@@ -525,7 +528,6 @@ int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>
     if (b < L.groups.size()) sets.emplace_back(b, L.groups.size());
   }
   static thread_local ns::Launch Lh;   // ~20 KB: kept off the stack
-  size_t mat_base = 0;
   for (const auto& set : sets) {
     std::memset(&Lh, 0, sizeof(Lh));
     Lh.n_groups = static_cast<int>(set.second - set.first);
@@ -542,6 +544,10 @@ int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>
       G.xmn[1] = ms.xmn[1];
       G.ak = ms.ak;
       G.bk = ms.bk;
+      G.xe[0] = ms.xe[0];
+      G.xe[1] = ms.xe[1];
+      G.ae = ms.ae;
+      G.be = ms.be;
       G.x[0] = reinterpret_cast<__nv_bfloat16*>(ws + g.off_x0);
       G.x[1] = reinterpret_cast<__nv_bfloat16*>(ws + g.off_x1);
       G.a = reinterpret_cast<__nv_bfloat16*>(ws + g.off_a);
@@ -553,8 +559,6 @@ int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>
       G.count = static_cast<int>(g.mats.size());
       G.first = first;
       G.transposed = g.transposed;
-      if (apply != nullptr)
-        for (size_t k = 0; k < g.mats.size(); ++k) Lh.mats[first + k] = (*apply)[mat_base + first + k];
       first += G.count;
     }
     int src = 0;
@@ -562,7 +566,6 @@ int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>
       for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
         Lh.phase = ph;
         Lh.src = src;
-        Lh.apply = (apply != nullptr && ph == ns::kUpdate && it == steps - 1);
         Lh.tile_start[0] = 0;
         for (int gi = 0; gi < Lh.n_groups; ++gi) {
           const ns::Group& G = Lh.g[gi];
@@ -574,11 +577,10 @@ int run_ns(const Layout& L, char* ws, int steps, const std::vector<ns::MatApply>
         const int tiles = Lh.tile_start[Lh.n_groups];
         ns::ns_phase_kernel<<<std::min(tiles, sms), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
         MO_LAUNCHED("ns_phase_kernel");
-        if (ph == ns::kUpdate && !Lh.apply) src ^= 1;
+        if (ph == ns::kUpdate) src ^= 1;
       }
     }
     *final_src = src;
-    mat_base += first;
   }
   return MOTEOPT_OK;
 }
@@ -599,8 +601,9 @@ std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const mo
   return out;
 }
 
-// ns_steps == 0: O = X0 (the normalised update) applied directly
-int run_apply_x0(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, cudaStream_t st) {
+// The Muon apply (muon.py:97-99) from the final iterate: X0 when ns_steps == 0, else the last phase's output.
+int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int src,
+              cudaStream_t st) {
   const std::vector<ns::MatApply> tab = muon_apply_table(P, cfg, L);
   OutArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -611,7 +614,7 @@ int run_apply_x0(const moteopt_muon_param* P, const moteopt_muon_config* cfg, co
     for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
       OutMat M;
       std::memset(&M, 0, sizeof(M));
-      M.x = ws + g.off_x0 + pos * g.m * g.n * 2;
+      M.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
       M.out = tab[k].p;
       M.rows = g.rows;
       M.cols = g.cols;
@@ -693,15 +696,13 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
   if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st));
   if (n_muon > 0) {
     MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st));
-    if (mcfg->ns_steps == 0) {
-      MO_TRY(run_apply_x0(muon, mcfg, L, ws, st));
-    } else {
-      const std::vector<ns::MatApply> tab = muon_apply_table(muon, mcfg, L);
-      int final_src = 0;
+    int final_src = 0;
+    if (mcfg->ns_steps > 0) {
       if (t_ns_ev[0] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[0], st));
-      MO_TRY(run_ns(L, ws, mcfg->ns_steps, &tab, status, sms, st, &final_src));
+      MO_TRY(run_ns(L, ws, mcfg->ns_steps, status, sms, st, &final_src));
       if (t_ns_ev[1] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[1], st));
     }
+    MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st));
   }
   return MOTEOPT_OK;
 }
@@ -905,7 +906,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
     MO_LAUNCHED("ns_normalize_kernel");
   }
   int final_src = 0;
-  r = run_ns(L, ws, steps, nullptr, &hdr->status, sms, st, &final_src);
+  r = run_ns(L, ws, steps, &hdr->status, sms, st, &final_src);
   if (r != MOTEOPT_OK) return r;
   // copy out (transpose back)
   OutArgs O;

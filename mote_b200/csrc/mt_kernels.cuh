@@ -248,6 +248,11 @@ __global__ void __launch_bounds__(256) mat_denom_kernel(const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Tiled transpose helpers of the Newton-Schulz normalisation and the final apply: a 64 x 64 tile is read with 4
+// consecutive elements per thread along the source's rows and written with 4 consecutive elements along the
+// destination's rows; when the two orientations differ, the tile goes through shared memory.
+constexpr int kTileRowsPerPass = kMtThreads / (kNormTile / 4);   // 16
+
 // X0 = bf16(u / (||u||_F + eps)), transposed when the matrix has more rows than columns, zero padded.
 // grid: (tiles of the largest matrix, matrices). u is recomputed from the grad and the updated momentum buffer
 // exactly as the momentum kernel computed it (momentum mode), or read from G (direct mode, buf == null).
@@ -259,65 +264,133 @@ __global__ void __launch_bounds__(kMtThreads) ns_normalize_kernel(const __grid_c
   const int i0 = ti * kNormTile, j0 = tj * kNormTile;   // destination tile origin (X rows i, cols j)
   const float den = A.den[M.den_index];
   const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
-  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;   // 64 x 4 threads
-  const int mv = M.transposed ? M.cols : M.rows;            // valid X rows
-  const int nv = M.transposed ? M.rows : M.cols;            // valid X cols
-  // Load the tile in source order (coalesced along the source's columns) into tile[src_r][src_c].
-  // Source tile origin: (i0, j0) if not transposed, (j0, i0) if transposed.
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;   // 16 x 16 threads, 4 columns each
+  const int mv = M.transposed ? M.cols : M.rows;
+  const int nv = M.transposed ? M.rows : M.cols;
   const int sr0 = M.transposed ? j0 : i0, sc0 = M.transposed ? i0 : j0;
-  for (int r = ty; r < kNormTile; r += 4) {
-    const int sr = sr0 + r, sc = sc0 + tx;
-    float val = 0.f;
-    if (sr < M.rows && sc < M.cols) {
-      const int64_t idx = static_cast<int64_t>(sr) * M.cols + sc;
-      float u = X(load_g1(M.g, idx, M.dtype));
-      if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, M.buf[idx], u) : M.buf[idx];
-      val = bf16_round_f(__fdiv_rn(u, den));
+  const bool vec = (M.cols % 4 == 0) && aligned16(M.buf == nullptr ? M.g : M.buf) && g_vec_ok(M.g, M.dtype);
+  float v[4][4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {   // source rows sr0 + ty + 16k, columns sc0 + 4tx .. +3
+    const int sr = sr0 + ty + kTileRowsPerPass * k, sc = sc0 + 4 * tx;
+    const int64_t idx = static_cast<int64_t>(sr) * M.cols + sc;
+    float gv[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (sr < M.rows) {
+      if (vec && sc + 3 < M.cols) {
+        const float4 g4 = load_g4(M.g, idx, M.dtype);
+        gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+        if (M.buf != nullptr) {
+          const float4 b4 = *reinterpret_cast<const float4*>(M.buf + idx);
+          bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (sc + e < M.cols) {
+            gv[e] = load_g1(M.g, idx + e, M.dtype);
+            if (M.buf != nullptr) bv[e] = M.buf[idx + e];
+          }
+      }
     }
-    tile[r][tx] = val;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float u = X(gv[e]);
+      if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, bv[e], u) : bv[e];
+      const bool ok = sr < M.rows && sc + e < M.cols;
+      v[k][e] = ok ? bf16_round_f(__fdiv_rn(u, den)) : 0.f;
+    }
   }
-  __syncthreads();
   __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(M.x);
-  for (int r = ty; r < kNormTile; r += 4) {
-    const int i = i0 + r, j = j0 + tx;
+  if (M.transposed) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[ty + kTileRowsPerPass * k][4 * tx + e] = v[k][e];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {   // destination rows i0 + ty + 16k, columns j0 + 4tx .. +3 (m_pad, n_pad: x8)
+    const int i = i0 + ty + kTileRowsPerPass * k, j = j0 + 4 * tx;
     if (i < M.m_pad && j < M.n_pad) {
-      const float val = (i < mv && j < nv) ? (M.transposed ? tile[tx][r] : tile[r][tx]) : 0.f;
-      x[static_cast<int64_t>(i) * M.n_pad + j] = __float2bfloat16_rn(val);
+      float w[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[e] = (i < mv && j + e < nv) ? v[k][e] : 0.f;
+      uint2 pk = make_uint2(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]));
+      *reinterpret_cast<uint2*>(x + static_cast<int64_t>(i) * M.n_pad + j) = pk;
     }
   }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
 // The final iterate back to the caller's orientation: out[r][c] = X[c][r] (transposed) or X[r][c]; or, in apply mode,
-// the Muon apply of muon.py:97-99 into the fp32 parameter.
+// the Muon apply of muon.py:97-99 into the fp32 parameter: p = p*(1-decay) (if decay); p += -lr*(O*scale).
 __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constant__ OutArgs A) {
   __shared__ float tile[kNormTile][kNormTile + 1];
   const OutMat& M = A.mat[blockIdx.y];
   if (static_cast<int>(blockIdx.x) >= M.tiles) return;
   const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
   const int r0 = ti * kNormTile, c0 = tj * kNormTile;      // output tile origin (rows r, cols c of R x C)
-  const int tx = threadIdx.x & 63, ty = threadIdx.x >> 6;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(M.x);
-  // X tile origin: (r0, c0) or (c0, r0) if transposed; load coalesced along X's columns
   const int xr0 = M.transposed ? c0 : r0, xc0 = M.transposed ? r0 : c0;
-  for (int r = ty; r < kNormTile; r += 4) {
-    const int xr = xr0 + r, xc = xc0 + tx;
-    tile[r][tx] = (xr < M.m_pad && xc < M.n_pad) ? __bfloat162float(x[static_cast<int64_t>(xr) * M.n_pad + xc]) : 0.f;
+  float v[4][4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {   // X rows xr0 + ty + 16k, columns xc0 + 4tx .. +3 (n_pad is a multiple of 8)
+    const int xr = xr0 + ty + kTileRowsPerPass * k, xc = xc0 + 4 * tx;
+    if (xr < M.m_pad && xc < M.n_pad) {
+      const uint2 w = *reinterpret_cast<const uint2*>(x + static_cast<int64_t>(xr) * M.n_pad + xc);
+      v[k][0] = bf16_lo(w.x); v[k][1] = bf16_hi(w.x); v[k][2] = bf16_lo(w.y); v[k][3] = bf16_hi(w.y);
+    } else {
+      v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
+    }
   }
-  __syncthreads();
-  for (int r = ty; r < kNormTile; r += 4) {
-    const int orow = r0 + r, ocol = c0 + tx;
-    if (orow < M.rows && ocol < M.cols) {
-      const float o = M.transposed ? tile[tx][r] : tile[r][tx];
-      const int64_t idx = static_cast<int64_t>(orow) * M.cols + ocol;
-      if (A.apply) {
-        float* p = reinterpret_cast<float*>(M.out);
-        float v = p[idx];
-        if (M.has_decay) v = __fmul_rn(v, M.decay_mul);
-        p[idx] = fmaf(M.neg_lr, __fmul_rn(o, M.scale), v);
+  if (M.transposed) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) tile[ty + kTileRowsPerPass * k][4 * tx + e] = v[k][e];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
+  }
+  const bool vec = (M.cols % 4 == 0) && aligned16(M.out);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {   // output rows r0 + ty + 16k, columns c0 + 4tx .. +3
+    const int orow = r0 + ty + kTileRowsPerPass * k, ocol = c0 + 4 * tx;
+    if (orow >= M.rows || ocol >= M.cols) continue;
+    const int64_t idx = static_cast<int64_t>(orow) * M.cols + ocol;
+    if (A.apply) {
+      float* p = reinterpret_cast<float*>(M.out);
+      if (vec) {
+        float4 pv = *reinterpret_cast<float4*>(p + idx);
+        float* pe = reinterpret_cast<float*>(&pv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float q = pe[e];
+          if (M.has_decay) q = __fmul_rn(q, M.decay_mul);
+          pe[e] = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+        }
+        *reinterpret_cast<float4*>(p + idx) = pv;
       } else {
-        reinterpret_cast<__nv_bfloat16*>(M.out)[idx] = __float2bfloat16_rn(o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (ocol + e < M.cols) {
+            float q = p[idx + e];
+            if (M.has_decay) q = __fmul_rn(q, M.decay_mul);
+            p[idx + e] = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+          }
       }
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(M.out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (ocol + e < M.cols) o[idx + e] = __float2bfloat16_rn(v[k][e]);
     }
   }
 }

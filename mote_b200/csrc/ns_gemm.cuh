@@ -4,7 +4,7 @@
 // shape group at once:
 //   kGram:   A  = bf16(X X^T)
 //   kPoly:   B  = bf16( bf16(b*A) + bf16(c * bf16(A A)) )          (A is symmetric, so A A = A A^T)
-//   kUpdate: X' = bf16( bf16(a*X) + bf16(B X) )                    or, on the last iteration, the Muon apply
+//   kUpdate: X' = bf16( bf16(a*X) + bf16(B X) )
 // The rounding points are the reference's: every torch op on a bf16 tensor rounds its fp32 result to bf16.
 //
 // Structure: a persistent grid (one CTA per SM, 197 KB of shared memory) walks a static tile list. Warp 0 streams
@@ -123,73 +123,6 @@ __device__ __forceinline__ void run_mma(const Launch& L, uint8_t* sa, uint8_t* s
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Epilogue of one 32-column chunk of one row: v[] holds the fp32 accumulator (or its transform), `cols_left`
-// (> 0, a multiple of 8) how many of the 32 columns exist.
-__device__ __forceinline__ void store_bf16_row(__nv_bfloat16* dst, const float (&v)[32], int cols_left) {
-  uint32_t pk[16];
-#pragma unroll
-  for (int k = 0; k < 16; ++k) pk[k] = pack_bf16x2(v[2 * k], v[2 * k + 1]);
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int k = 0; k < 4; ++k)
-    if (k * 8 < cols_left) d4[k] = make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
-}
-
-// mote/train/muon.py:93-99 for the 32 columns j..j+31 of row i of the orthogonalised iterate.
-__device__ __forceinline__ void apply_row(const Group& G, const MatApply& ma, int i, int j, const float (&o)[32]) {
-  if (i >= G.mv) return;
-  if (!G.transposed) {
-    // p[i][j + k], row stride nv
-    float* pr = ma.p + static_cast<size_t>(i) * G.nv + j;
-    const int lim = min(32, G.nv - j);
-    const bool vec = ((reinterpret_cast<uintptr_t>(pr) & 15u) == 0) && (G.nv % 4 == 0);
-    if (vec) {
-#pragma unroll
-      for (int k = 0; k < 32; k += 4) {
-        if (k < lim) {
-          float4 pv = *reinterpret_cast<float4*>(pr + k);
-          float* pe = reinterpret_cast<float*>(&pv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float x = pe[e];
-            if (ma.has_decay) x = __fmul_rn(x, ma.decay_mul);
-            pe[e] = fmaf(ma.neg_lr, __fmul_rn(o[k + e], ma.scale), x);
-          }
-          *reinterpret_cast<float4*>(pr + k) = pv;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        if (k < lim) {
-          float x = pr[k];
-          if (ma.has_decay) x = __fmul_rn(x, ma.decay_mul);
-          pr[k] = fmaf(ma.neg_lr, __fmul_rn(o[k], ma.scale), x);
-        }
-      }
-    }
-  } else {
-    // the parameter is the transpose: p[j + k][i], row stride mv (consecutive threads -> consecutive i)
-    float* pc = ma.p + static_cast<size_t>(j) * G.mv + i;
-    const int lim = min(32, G.nv - j);
-#pragma unroll
-    for (int k = 0; k < 32; ++k) {
-      if (k < lim) {
-        float* q = pc + static_cast<size_t>(k) * G.mv;
-        float x = *q;
-        if (ma.has_decay) x = __fmul_rn(x, ma.decay_mul);
-        *q = fmaf(ma.neg_lr, __fmul_rn(o[k], ma.scale), x);
-      }
-    }
-  }
-}
-
-// Unpack 8 bf16 (one uint4) into floats.
-__device__ __forceinline__ void unpack8(const uint4& w, float* v) {
-  v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
-  v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z); v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
-}
-
 // Round a pair to bf16 and back (one cvt.rn.bf16x2.f32 for two values).
 __device__ __forceinline__ void round2(float& a, float& b) {
   const uint32_t p = pack_bf16x2(a, b);
@@ -197,99 +130,134 @@ __device__ __forceinline__ void round2(float& a, float& b) {
   b = bf16_hi(p);
 }
 
-// Epilogue warps 2..9: warp w reads TMEM lane quarter (w % 4) and owns columns [128*h, 128*h + 128) of the tile,
-// h = (w - 2) / 4. The bf16 operand the phase's polynomial needs (A for kPoly, X for kUpdate) is loaded before the
-// accumulator is waited for, so its latency hides behind the tile's MMAs.
-__device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, uint64_t* tempty, uint32_t tmem_base,
-                                             const WaitCtx& ctx) {
-  constexpr int kChunks = BN / 32 / 2;   // 32-column chunks per epilogue warp
+// Byte offset of 16-byte chunk c (0..3) of row r (0..31) in a 32 x 32 bf16 subtile with the 64-byte TMA swizzle
+// (chunk bits [4,5] ^= row bits [7,8] of the address). Row-per-thread accesses are bank-conflict free.
+__device__ __forceinline__ uint32_t sw64(int r, int c) {
+  return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+}
+
+// Epilogue warps 2..9: warp w reads TMEM lane quarter (w % 4), i.e. tile rows [32q, 32q+32), and owns columns
+// [128h, 128h+128) with h = (w - 2) / 4, in four 32-column chunks. Each chunk goes through one of the warp's two
+// 2 KB shared-memory subtiles: the phase's bf16 operand (A for kPoly, X for kUpdate) arrives there by TMA, each
+// thread combines its row with the accumulator and writes the result back in place, and one lane TMA-stores the
+// subtile. No per-thread global access remains, so the epilogue costs no L1 bandwidth.
+__device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, uint64_t* tempty, uint8_t* ebuf,
+                                             uint64_t* ebar, uint32_t tmem_base, const WaitCtx& ctx) {
+  constexpr int kChunks = BN / EPI_TILE / 2;
   const int total = L.tile_start[L.n_groups];
+  const int ew = static_cast<int>(warp_id()) - 2;
   const int q = static_cast<int>(warp_id() & 3u);
-  const int half = (static_cast<int>(warp_id()) - 2) >> 2;
-  const int row = q * 32 + static_cast<int>(lane_id());
+  const int half = ew >> 2;
+  const int lane = static_cast<int>(lane_id());
+  uint8_t* buf[2] = {ebuf + (ew * 2) * EPI_BUF_BYTES, ebuf + (ew * 2 + 1) * EPI_BUF_BYTES};
+  uint64_t* bar[2] = {&ebar[ew * 2], &ebar[ew * 2 + 1]};
+  uint32_t bphase[2] = {0u, 0u};
+  const bool has_aux = L.phase != kGram;
+  bool ok = true;
   int local = 0;
-  for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+  for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
     int gi, b, i0, j0;
     decode_tile(L, t, gi, b, i0, j0);
     const Group& G = L.g[gi];
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
     const int out_cols = L.phase == kUpdate ? G.n : G.m;
-    const int i = i0 + row;
-    const bool row_ok = i < G.m;
-    const int jc0 = j0 + half * (kChunks * 32);   // first column of this warp
-    const size_t row_off = L.phase == kUpdate ? (static_cast<size_t>(b) * G.m + i) * G.n
-                                              : (static_cast<size_t>(b) * G.m + i) * G.m;
-    // prefetch the polynomial's bf16 operand for this warp's columns
-    uint4 aux[kChunks][4];
-    if (L.phase != kGram) {
-      const __nv_bfloat16* src = (L.phase == kPoly ? G.a : G.x[L.src]) + row_off;
-#pragma unroll
-      for (int c = 0; c < kChunks; ++c)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int j = jc0 + c * 32 + k * 8;
-          aux[c][k] = (row_ok && j < out_cols) ? *reinterpret_cast<const uint4*>(src + j) : make_uint4(0, 0, 0, 0);
+    const int row0 = i0 + q * 32;
+    const bool rows_ok = row0 < G.m;   // warp-uniform: whole subtile beyond the matrix -> nothing to store
+    const int jc0 = j0 + half * (kChunks * EPI_TILE);
+    const CUtensorMap* omap = L.phase == kGram ? &G.ae : (L.phase == kPoly ? &G.be : &G.xe[L.src ^ 1]);
+    const CUtensorMap* amap = L.phase == kPoly ? &G.ae : &G.xe[L.src];
+    int nch = 0;
+    while (nch < kChunks && jc0 + nch * EPI_TILE < out_cols) ++nch;
+    const bool work = rows_ok && nch > 0;
+    // prefetch the operand subtiles of the first two chunks (the previous tile's stores must have left them)
+    if (lane == 0 && work) {
+      bulk_wait_read<0>();
+      if (has_aux) {
+        for (int c = 0; c < 2 && c < nch; ++c) {
+          mbar_arrive_expect_tx(bar[c], EPI_BUF_BYTES);
+          tma_load_3d(buf[c], amap, bar[c], jc0 + c * EPI_TILE, row0, b);
         }
+      }
     }
+    __syncwarp();
     // warp-uniform outcome: the TMEM loads below are .sync.aligned
     if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], use, ctx) ? 1 : 0)) break;
     tc_fence_after();
-#pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const int j = jc0 + c * 32;
-      if (j >= out_cols) break;   // uniform across the warp
+    for (int c = 0; c < nch; ++c) {
+      const int bi = c & 1;
       uint32_t r[32];
       tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                    static_cast<uint32_t>(acc * BN + half * (kChunks * 32) + c * 32), r);
+                    static_cast<uint32_t>(acc * BN + half * (kChunks * EPI_TILE) + c * EPI_TILE), r);
       tmem_ld_wait(r);
-      if (!row_ok) continue;
-      const int cols_left = out_cols - j;
-      float v[32];
+      if (!rows_ok) continue;
+      uint8_t* row = buf[bi];
+      if (has_aux) {
+        if (!__all_sync(0xffffffffu, mbar_wait(bar[bi], bphase[bi], ctx) ? 1 : 0)) { ok = false; break; }
+        bphase[bi] ^= 1u;
+      } else if (c >= 2) {
+        if (lane == 0) bulk_wait_read<1>();   // the store of chunk c-2 has left this buffer
+        __syncwarp();
+      }
+      uint32_t out[16];
       if (L.phase == kGram) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-        store_bf16_row(G.a + row_off + j, v, cols_left);
+        for (int k = 0; k < 16; ++k) out[k] = pack_bf16x2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
       } else {
-        float a[32];
+        uint32_t in[16];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) unpack8(aux[c][k], a + 8 * k);
+        for (int cc = 0; cc < 4; ++cc) {
+          const uint4 w = *reinterpret_cast<const uint4*>(row + sw64(lane, cc));
+          in[4 * cc] = w.x; in[4 * cc + 1] = w.y; in[4 * cc + 2] = w.z; in[4 * cc + 3] = w.w;
+        }
         if (L.phase == kPoly) {
 #pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            float aa0 = __uint_as_float(r[k]), aa1 = __uint_as_float(r[k + 1]);
-            round2(aa0, aa1);                                                   // A @ A
-            float t10 = __fmul_rn(kNsB, a[k]), t11 = __fmul_rn(kNsB, a[k + 1]);
-            round2(t10, t11);                                                   // b * A
+          for (int k = 0; k < 16; ++k) {
+            float aa0 = __uint_as_float(r[2 * k]), aa1 = __uint_as_float(r[2 * k + 1]);
+            round2(aa0, aa1);                                                                   // A @ A
+            float t10 = __fmul_rn(kNsB, bf16_lo(in[k])), t11 = __fmul_rn(kNsB, bf16_hi(in[k]));
+            round2(t10, t11);                                                                   // b * A
             float t20 = __fmul_rn(kNsC, aa0), t21 = __fmul_rn(kNsC, aa1);
-            round2(t20, t21);                                                   // c * (A @ A)
-            v[k] = __fadd_rn(t10, t20);                                         // rounded by the store
-            v[k + 1] = __fadd_rn(t11, t21);
+            round2(t20, t21);                                                                   // c * (A @ A)
+            out[k] = pack_bf16x2(__fadd_rn(t10, t20), __fadd_rn(t11, t21));
           }
-          store_bf16_row(G.b + row_off + j, v, cols_left);
         } else {
 #pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            float bx0 = __uint_as_float(r[k]), bx1 = __uint_as_float(r[k + 1]);
-            round2(bx0, bx1);                                                   // B @ X
-            float ax0 = __fmul_rn(kNsA, a[k]), ax1 = __fmul_rn(kNsA, a[k + 1]);
-            round2(ax0, ax1);                                                   // a * X
-            v[k] = __fadd_rn(ax0, bx0);
-            v[k + 1] = __fadd_rn(ax1, bx1);
-          }
-          if (L.apply) {
-#pragma unroll
-            for (int k = 0; k < 32; k += 2) round2(v[k], v[k + 1]);            // O (bf16)
-            apply_row(G, L.mats[G.first + b], i, j, v);
-          } else {
-            store_bf16_row(G.x[L.src ^ 1] + row_off + j, v, cols_left);
+          for (int k = 0; k < 16; ++k) {
+            float bx0 = __uint_as_float(r[2 * k]), bx1 = __uint_as_float(r[2 * k + 1]);
+            round2(bx0, bx1);                                                                   // B @ X
+            float ax0 = __fmul_rn(kNsA, bf16_lo(in[k])), ax1 = __fmul_rn(kNsA, bf16_hi(in[k]));
+            round2(ax0, ax1);                                                                   // a * X
+            out[k] = pack_bf16x2(__fadd_rn(ax0, bx0), __fadd_rn(ax1, bx1));
           }
         }
       }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc)
+        *reinterpret_cast<uint4*>(row + sw64(lane, cc)) = make_uint4(out[4 * cc], out[4 * cc + 1], out[4 * cc + 2], out[4 * cc + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_3d(omap, row, jc0 + c * EPI_TILE, row0, b);
+        bulk_commit();
+        if (has_aux && c + 2 < nch) {   // refill this buffer with the operand of chunk c+2
+          bulk_wait_read<0>();
+          mbar_arrive_expect_tx(bar[bi], EPI_BUF_BYTES);
+          tma_load_3d(row, amap, bar[bi], jc0 + (c + 2) * EPI_TILE, row0, b);
+        }
+      }
+      __syncwarp();
     }
     tc_fence_before();
     mbar_arrive(&tempty[acc]);
   }
+  if (lane == 0) {
+    bulk_wait<0>();   // stores complete before the CTA exits
+    if (!ok) {        // unwinding: operand loads still in flight land before shared memory goes away
+      for (int k = 0; k < 2; ++k) mbar_wait_drain(bar[k], bphase[k]);
+    }
+  }
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -298,13 +266,15 @@ __global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_cons
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* ebuf = smem + STAGES * STAGE_BYTES;                        // 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ebuf + EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* ebar = drain + 1;                                         // 2 per epilogue warp
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
@@ -318,15 +288,19 @@ __global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_cons
       mbar_init(&tempty[a], kEpiWarps * 32);
     }
     mbar_init(drain, 1);
+    for (int e = 0; e < 2 * kEpiWarps; ++e) mbar_init(&ebar[e], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane_id() == 0) {
     for (int g = 0; g < L.n_groups; ++g) {
       const Group& G = L.g[g];
-      if (L.phase == kGram) tma_prefetch_desc(&G.xk[L.src]);
-      if (L.phase == kPoly) tma_prefetch_desc(&G.ak);
-      if (L.phase == kUpdate) { tma_prefetch_desc(&G.bk); tma_prefetch_desc(&G.xmn[L.src]); }
+      if (L.phase == kGram) { tma_prefetch_desc(&G.xk[L.src]); tma_prefetch_desc(&G.ae); }
+      if (L.phase == kPoly) { tma_prefetch_desc(&G.ak); tma_prefetch_desc(&G.be); }
+      if (L.phase == kUpdate) {
+        tma_prefetch_desc(&G.bk); tma_prefetch_desc(&G.xmn[L.src]);
+        tma_prefetch_desc(&G.xe[0]); tma_prefetch_desc(&G.xe[1]);
+      }
     }
   }
   if (warp == 1) {
@@ -347,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_cons
     if (lane_id() == 0) run_mma(L, sa, sb, full, empty, tfull, tempty, drain, tmem_base, ctx);
     __syncwarp();
   } else {
-    run_epilogue(L, tfull, tempty, tmem_base, ctx);
+    run_epilogue(L, tfull, tempty, ebuf, ebar, tmem_base, ctx);
   }
   tc_fence_before();
   __syncthreads();

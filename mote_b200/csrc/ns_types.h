@@ -17,11 +17,14 @@ constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kEpiWarps = 8;   // two epilogue warps per TMEM lane quarter, each owning half of the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;   // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, 2-9: epilogue
-constexpr int kSmemBytes = STAGES * STAGE_BYTES + 1024 /*alignment slack*/ + 256 /*barriers*/;
+constexpr int EPI_TILE = 32;                                 // epilogue subtile: 32 rows x 32 columns, bf16
+constexpr int EPI_BUF_BYTES = EPI_TILE * EPI_TILE * 2;       // 2 KB, 64-byte swizzled
+constexpr int EPI_BYTES = kEpiWarps * 2 * EPI_BUF_BYTES;     // two buffers per epilogue warp
+constexpr int kSmemBytes = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*alignment slack*/ + 512 /*barriers*/;
 constexpr uint32_t kTmemCols = 512;   // two 128 x 256 fp32 accumulators
 
 constexpr int kMaxGroups = 8;     // shape groups per launch
-constexpr int kMaxApply = 512;    // matrices whose parameter update is fused into the last launch
+constexpr int kMaxApply = 512;    // matrices per shape group
 
 enum Phase : int {
   kGram = 0,     // A = X X^T                         (m x m, K = n)
@@ -37,6 +40,9 @@ struct alignas(64) Group {
   CUtensorMap xmn[2];   // X ping/pong as an MN-major operand: dims {n, m, count}, box {64, 64, 1}
   CUtensorMap ak;       // A: dims {m, m, count}, box {64, 128, 1}
   CUtensorMap bk;       // B: dims {m, m, count}, box {64, 128, 1}
+  CUtensorMap xe[2];    // epilogue views (box {32, 32, 1}, 64-byte swizzle): X ping/pong
+  CUtensorMap ae;       //   A
+  CUtensorMap be;       //   B
   __nv_bfloat16* x[2];
   __nv_bfloat16* a;
   __nv_bfloat16* b;
@@ -48,7 +54,7 @@ struct alignas(64) Group {
   int pad_;
 };
 
-// The fused Muon apply of one matrix (mote/train/muon.py:93-99): p = p*(1-decay) (if decay), p += -lr*(O*scale).
+// The Muon apply of one matrix (mote/train/muon.py:93-99): p = p*(1-decay) (if decay), p += -lr*(O*scale).
 struct MatApply {
   float* p;             // first element of this matrix inside its (2-D or 3-D) parameter
   float neg_lr;
@@ -62,12 +68,10 @@ struct Launch {
   int n_groups;
   int phase;
   int src;              // which X buffer holds the current iterate
-  int apply;            // kUpdate only: write the parameter update instead of X'
   int tile_start[kMaxGroups + 1];
   int tiles_m[kMaxGroups];
   int tiles_n[kMaxGroups];
   int* status;
-  MatApply mats[kMaxApply];
 };
 
 }  // namespace ns
