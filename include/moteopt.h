@@ -127,6 +127,20 @@ MOTEOPT_API size_t moteopt_clip_grad_norm_workspace_size(const int64_t* numels, 
 MOTEOPT_API int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int* dtypes, int n, double max_norm,
                            float* out_norm, void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
 
+/* ---- clip_grad_norm_ for callers that cannot allocate device memory. It has no counterpart in the reference: it
+ *      does what moteopt_clip_grad_norm does, but keeps its scratch in a fixed array inside this library instead of
+ *      a caller-provided workspace, for callers that may not call cudaMalloc (or any allocating routine) at the
+ *      point of the call: a host runtime with its own memory pool that forbids outside allocations, a region where
+ *      allocation would break stream ordering, or a C caller without an allocator of its own. Limit: the grads'
+ *      element counts, each rounded up to a multiple of 16384, may sum to at most 65536 x 16384 (2^30) elements,
+ *      and n <= 4096; beyond that it returns MOTEOPT_ERR_LIMIT and does nothing. The array (256 KB + 256 B) lives on
+ *      every device that loads the library until the process exits. The first call on a device looks up the
+ *      array's device address; make that first call before any CUDA graph capture on that device. Calls share the
+ *      array: calls that can overlap on the GPU (different streams without ordering, or several host threads) race
+ *      and must be serialised by the caller. `out_norm` (device, may be NULL) receives the total norm. */
+MOTEOPT_API int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, const int* dtypes, int n,
+                                               double max_norm, float* out_norm, moteopt_stream_t stream);
+
 /* ---- newton_schulz(G, steps, eps) (mote/train/muon.py:26-43): G [batch, rows, cols] fp32 or bf16 -> out bf16 of
  *      the same shape. Every matrix is normalised by its own Frobenius norm; the iteration runs on the transpose
  *      of a matrix with more rows than columns. */

@@ -25,7 +25,7 @@ EXPORTS = (
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
     "moteopt_adamw_step",
-    "moteopt_clip_grad_norm_workspace_size", "moteopt_clip_grad_norm",
+    "moteopt_clip_grad_norm_workspace_size", "moteopt_clip_grad_norm", "moteopt_clip_grad_norm_noalloc",
     "moteopt_newton_schulz_workspace_size", "moteopt_newton_schulz",
 )
 
@@ -79,6 +79,7 @@ def _load() -> C.CDLL:
         "moteopt_adamw_step": (i32, [C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), vp, vp]),
         "moteopt_clip_grad_norm_workspace_size": (sz, [C.POINTER(C.c_int64), i32]),
         "moteopt_clip_grad_norm": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp, sz, vp]),
+        "moteopt_clip_grad_norm_noalloc": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp]),
         "moteopt_newton_schulz_workspace_size": (sz, [i64, i64, i64]),
         "moteopt_newton_schulz": (i32, [vp, i32, vp, i64, i64, i64, i32, dbl, vp, sz, vp]),
     }

@@ -836,6 +836,112 @@ int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int*
   return MOTEOPT_OK;
 }
 
+// ---- clip_grad_norm_ without a caller-provided workspace ------------------------------------------------------
+// Scratch of moteopt_clip_grad_norm_noalloc: one fp32 sum of squares per 16K-element chunk plus a 256-byte header
+// (status, norm, clip coefficient), in a file-scope device array. Every device that loads this library holds it
+// (256 KB + 256 B) until the process exits; all calls on a device share it.
+}  // extern "C"
+
+namespace {
+constexpr int kNoAllocMaxChunks = 65536;   // 65536 x 16384 = 2^30 grad elements per call
+constexpr size_t kNoAllocBytes = kHeaderBytes + sizeof(float) * static_cast<size_t>(kNoAllocMaxChunks);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// The device address of the scratch array for the current device (host code cannot use the symbol itself).
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  MO_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(MOTEOPT_ERR_DEVICE, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    MO_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return MOTEOPT_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, const int* dtypes, int n,
+                                   double max_norm, float* out_norm, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!grads || !numels || !dtypes))) return fail(MOTEOPT_ERR_INVALID, "bad grad list");
+  if (n > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "more than 4096 tensors in one clip_grad_norm call");
+  int64_t chunks = 0;
+  for (int i = 0; i < n; ++i) {
+    if (dtypes[i] != kF32 && dtypes[i] != kBF16) return fail(MOTEOPT_ERR_INVALID, "grad dtype must be fp32 or bf16");
+    if (numels[i] < 0 || (numels[i] > 0 && grads[i] == nullptr)) return fail(MOTEOPT_ERR_INVALID, "bad grad tensor");
+    chunks += cdiv(numels[i], kChunk);
+  }
+  if (chunks > kNoAllocMaxChunks)
+    return fail(MOTEOPT_ERR_LIMIT, "moteopt_clip_grad_norm_noalloc: " + std::to_string(chunks) +
+                                       " chunks of 16384 elements (the per-tensor element counts rounded up) exceed "
+                                       "its fixed scratch of " + std::to_string(kNoAllocMaxChunks) +
+                                       "; use moteopt_clip_grad_norm with a workspace");
+  int sms = 0;
+  int r = device_setup(&sms);
+  if (r != MOTEOPT_OK) return r;
+  void* scratch = nullptr;
+  r = noalloc_scratch(&scratch);
+  if (r != MOTEOPT_OK) return r;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(scratch);
+  Header* hdr = reinterpret_cast<Header*>(ws);
+  float* partials = reinterpret_cast<float*>(ws + kHeaderBytes);
+  // the header carries the previous call's status bits: clear it (every partial is overwritten)
+  MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
+  // fixed-size argument blocks on the stack: no host or device allocation on this path
+  SumsqArgs S;
+  FinalizeArgs F;
+  ScaleArgs A;
+  F.n_tensors = n;
+  F.has_clip = 1;
+  F.max_norm = static_cast<float>(max_norm);
+  F.partials = partials;
+  F.out = &hdr->norm;
+  F.status = &hdr->status;
+  F.tensor_chunk_start[0] = 0;
+  for (int i = 0; i < n; ++i)
+    F.tensor_chunk_start[i + 1] = F.tensor_chunk_start[i] + static_cast<int>(cdiv(numels[i], kChunk));
+  S.partials = partials;
+  S.has_div = 0;
+  S.div = 1.0f;
+  A.coef = &hdr->coef;
+  for (int s0 = 0; s0 < n; s0 += kMaxNormSeg) {
+    const int cnt = std::min(n - s0, kMaxNormSeg);
+    S.n = cnt;
+    S.chunk_base = F.tensor_chunk_start[s0];
+    for (int i = 0; i < cnt; ++i) {
+      S.seg[i] = SumsqSeg{grads[s0 + i], numels[s0 + i], dtypes[s0 + i], 0};
+      S.chunk_start[i] = F.tensor_chunk_start[s0 + i] - S.chunk_base;
+    }
+    S.chunk_start[cnt] = F.tensor_chunk_start[s0 + cnt] - S.chunk_base;
+    if (S.chunk_start[cnt] == 0) continue;
+    sumsq_kernel<<<grid_for(S.chunk_start[cnt], sms), kMtThreads, 0, st>>>(S);
+    MO_LAUNCHED("sumsq_kernel");
+  }
+  norm_finalize_kernel<<<1, 1024, 0, st>>>(F);
+  MO_LAUNCHED("norm_finalize_kernel");
+  for (int s0 = 0; s0 < n; s0 += kMaxNormSeg) {
+    const int cnt = std::min(n - s0, kMaxNormSeg);
+    A.n = cnt;
+    for (int i = 0; i < cnt; ++i) {
+      A.seg[i] = SumsqSeg{grads[s0 + i], numels[s0 + i], dtypes[s0 + i], 0};
+      A.chunk_start[i] = F.tensor_chunk_start[s0 + i] - F.tensor_chunk_start[s0];
+    }
+    A.chunk_start[cnt] = F.tensor_chunk_start[s0 + cnt] - F.tensor_chunk_start[s0];
+    if (A.chunk_start[cnt] == 0) continue;
+    clip_scale_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("clip_scale_kernel");
+  }
+  if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
+  return MOTEOPT_OK;
+}
+
 size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
   Layout L;
   if (build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L) != MOTEOPT_OK) return 0;
