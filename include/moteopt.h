@@ -111,6 +111,25 @@ MOTEOPT_API int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muo
                            const moteopt_grad_config* grad_cfg, float* out_norm, void* workspace,
                            size_t workspace_bytes, moteopt_stream_t stream);
 
+/* ---- the sharded (multi-GPU) step of the same path, which the reference does not have: each rank updates only the
+ *      parameters it owns, so the global clip is assembled from per-rank sums of squares.
+ *      moteopt_grad_sumsq: out_sum (device fp64) = sum over the listed grads of (g / grad_divisor)^2 (fixed order).
+ *      moteopt_clip_coef_from_sums: out_norm_coef (device, 2 floats) = [sqrt(sum of sums[0..n) in order),
+ *      min(1, max_norm / (norm + 1e-6)) or 1 when clip == 0].
+ *      moteopt_optimizer_step_with_coef: moteopt_optimizer_step with the clip coefficient given (device float; NULL
+ *      for none) instead of computed. */
+MOTEOPT_API size_t moteopt_grad_sumsq_workspace_size(const int64_t* numels, int n);
+MOTEOPT_API int moteopt_grad_sumsq(const void* const* grads, const int64_t* numels, const int* dtypes, int n,
+                                   double grad_divisor, double* out_sum, void* workspace, size_t workspace_bytes,
+                                   moteopt_stream_t stream);
+MOTEOPT_API int moteopt_clip_coef_from_sums(const double* sums, int n, int clip, double max_norm, float* out_norm_coef,
+                                            moteopt_stream_t stream);
+MOTEOPT_API int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon,
+                                                 const moteopt_muon_config* muon_cfg, const moteopt_adamw_tensor* adamw,
+                                                 int n_adamw, const moteopt_adamw_hparams* adamw_hp,
+                                                 double grad_divisor, const float* grad_coef, void* workspace,
+                                                 size_t workspace_bytes, moteopt_stream_t stream);
+
 /* ---- Muon.step() of one or more param groups (mote/train/muon.py:52-100). Parameters whose grad is NULL are
  *      skipped by the caller (muon.py:61-62). `grad_scale` (device, may be NULL) multiplies every grad first. */
 MOTEOPT_API size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps);

@@ -22,7 +22,8 @@ STATUS_NONFINITE = 4
 EXPORTS = (
     "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count",
     "moteopt_profile_ns_events",
-    "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step",
+    "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_with_coef",
+    "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
     "moteopt_adamw_step",
     "moteopt_clip_grad_norm_workspace_size", "moteopt_clip_grad_norm", "moteopt_clip_grad_norm_noalloc",
@@ -74,6 +75,12 @@ def _load() -> C.CDLL:
         "moteopt_optimizer_step_workspace_size": (sz, [C.POINTER(MuonParam), i32, i32, C.POINTER(AdamWTensor), i32]),
         "moteopt_optimizer_step": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(AdamWTensor), i32,
                                          C.POINTER(AdamWHparams), C.POINTER(GradConfig), vp, vp, sz, vp]),
+        "moteopt_optimizer_step_with_coef": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
+                                                   C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp, vp, sz,
+                                                   vp]),
+        "moteopt_grad_sumsq_workspace_size": (sz, [C.POINTER(C.c_int64), i32]),
+        "moteopt_grad_sumsq": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp, sz, vp]),
+        "moteopt_clip_coef_from_sums": (i32, [vp, i32, i32, dbl, vp, vp]),
         "moteopt_muon_step_workspace_size": (sz, [C.POINTER(MuonParam), i32, i32]),
         "moteopt_muon_step": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), vp, vp, sz, vp]),
         "moteopt_adamw_step": (i32, [C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), vp, vp]),

@@ -760,6 +760,65 @@ int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muon, const mot
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,
+                                     const moteopt_adamw_tensor* adamw, int n_adamw,
+                                     const moteopt_adamw_hparams* adamw_hp, double grad_divisor, const float* grad_coef,
+                                     void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  moteopt_grad_config gc;
+  gc.clip = 0;
+  gc.max_norm = 0.0;
+  gc.grad_divisor = grad_divisor;
+  return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, &gc, grad_coef, nullptr, workspace,
+                  workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t moteopt_grad_sumsq_workspace_size(const int64_t* numels, int n) {
+  return moteopt_clip_grad_norm_workspace_size(numels, n);
+}
+
+int moteopt_grad_sumsq(const void* const* grads, const int64_t* numels, const int* dtypes, int n, double grad_divisor,
+                       double* out_sum, void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!grads || !numels || !dtypes)) || out_sum == nullptr)
+    return fail(MOTEOPT_ERR_INVALID, "bad grad list or null output");
+  for (int i = 0; i < n; ++i) {
+    if (dtypes[i] != kF32 && dtypes[i] != kBF16) return fail(MOTEOPT_ERR_INVALID, "grad dtype must be fp32 or bf16");
+    if (numels[i] < 0 || (numels[i] > 0 && grads[i] == nullptr)) return fail(MOTEOPT_ERR_INVALID, "bad grad tensor");
+  }
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  Layout L;
+  MO_TRY(build_layout({}, std::vector<int64_t>(numels, numels + n), 0, &L));
+  MO_TRY(check_ws(workspace, workspace_bytes, L.bytes));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  std::vector<GradSource> src;
+  for (int i = 0; i < n; ++i) src.push_back(GradSource{grads[i], numels[i], dtypes[i]});
+  float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+  const bool has_div = grad_divisor != 0.0 && grad_divisor != 1.0;
+  MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, has_div ? static_cast<float>(grad_divisor) : 1.f,
+                      sms, st));
+  partials_total_kernel<<<1, 1024, 0, st>>>(partials, L.norm_tensor_chunk_start.back(), out_sum);
+  MO_LAUNCHED("partials_total_kernel");
+  return MOTEOPT_OK;
+}
+
+int moteopt_clip_coef_from_sums(const double* sums, int n, int clip, double max_norm, float* out_norm_coef,
+                                moteopt_stream_t stream) {
+  if (n < 1 || sums == nullptr || out_norm_coef == nullptr) return fail(MOTEOPT_ERR_INVALID, "bad sums");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  CoefArgs A;
+  A.n = n;
+  A.has_clip = clip != 0;
+  A.max_norm = static_cast<float>(max_norm);
+  A.sums = sums;
+  A.out = out_norm_coef;
+  A.status = nullptr;
+  coef_from_sums_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(A);
+  MO_LAUNCHED("coef_from_sums_kernel");
+  return MOTEOPT_OK;
+}
+
 size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps) {
   if (n_muon < 0 || (n_muon > 0 && !muon)) return 0;
   Layout L;

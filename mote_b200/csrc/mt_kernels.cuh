@@ -132,6 +132,39 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Sum of every chunk partial in fixed order, in fp64 (one rank's share of the global sum of squares).
+__global__ void __launch_bounds__(1024) partials_total_kernel(const float* partials, int n, double* out) {
+  __shared__ double red[32];
+  double acc = 0.0;
+  for (int c = threadIdx.x; c < n; c += blockDim.x) acc += static_cast<double>(partials[c]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double s = 0.0;
+    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += red[k];
+    *out = s;
+  }
+}
+
+// total norm = sqrt(sum of the ranks' sums, in rank order) and the clip coefficient, as norm_finalize_kernel.
+__global__ void coef_from_sums_kernel(const __grid_constant__ CoefArgs A) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  double s = 0.0;
+  for (int r = 0; r < A.n; ++r) s += A.sums[r];
+  const float total = static_cast<float>(sqrt(s));
+  float coef = 1.0f;
+  if (A.has_clip) {
+    const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
+    coef = (c > 1.0f) ? 1.0f : c;
+  }
+  A.out[0] = total;
+  A.out[1] = coef;
+  if (A.status != nullptr && !isfinite(total)) atomicOr(A.status, kStatusNonFinite);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // AdamW, torch's single-tensor update in torch's rounding order:
 //   p *= (1 - lr*wd)                      param.mul_(1 - lr*wd)
 //   m  = lerp(m, g, 1-beta1)              exp_avg.lerp_(grad, 1-beta1)            (fused: m + w*(g-m))

@@ -41,6 +41,16 @@ struct FinalizeArgs {
   int tensor_chunk_start[kMaxFinalTensors + 1];
 };
 
+// ---- the clip coefficient from per-rank sums of squares (sharded step): total = sqrt(sum in rank order)
+struct CoefArgs {
+  int n;
+  int has_clip;
+  float max_norm;
+  const double* sums;
+  float* out;                // out[0] = total norm, out[1] = clip coefficient
+  int* status;
+};
+
 // ---- AdamW (torch.optim.AdamW single-tensor update, constructed at mote/train/train.py:98)
 constexpr int kMaxAdamSeg = 320;
 struct AdamSeg {

@@ -1,0 +1,150 @@
+"""bench.py's N > 1 leg: the sharded optimizer step of mote_b200.distributed on N GPUs of one node, one process per
+GPU (launched by torch.distributed.run), NCCL over NVLink.
+
+Each rank holds the whole c1 model in its flat param regions and its own local bf16 grads; one step is the
+reduce-scatter of the grads, the global clip from per-rank sums, the owned updates and the all-gather of the params.
+Time is measured with CUDA events on each rank and the maximum over ranks is reported.
+"""
+
+from __future__ import annotations
+
+import datetime
+import json
+import os
+import statistics
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+from . import configs
+from .distributed import ShardedStep, cuda_compute, make_plan
+
+ROOT = Path(__file__).resolve().parent.parent
+METRIC = "ms/optimizer step (96M set)"
+
+
+def run(args, rank: int, world: int, local_rank: int):
+    from bench import ClockSampler, load_peaks   # the driver-facing helpers live in bench.py
+    from . import _lib as L
+    from .ops import read_status
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    try:
+        w = configs.CONFIGS[args.config]()
+        plan = make_plan(w.muon_shapes, w.adam_shapes, world, ns_steps=w.ns_steps)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)   # identical params on every rank
+        pm = torch.zeros(plan.muon_len, dtype=torch.float32, device=dev)
+        pa = torch.zeros(plan.adam_len, dtype=torch.float32, device=dev)
+        nd = len(w.adam_decay_shapes)
+        st = ShardedStep(plan, rank, pm, pa, torch.zeros(plan.muon_len, dtype=torch.bfloat16, device=dev),
+                         torch.zeros(plan.adam_len, dtype=torch.bfloat16, device=dev),
+                         cuda_compute(ns_steps=w.ns_steps, betas=w.betas, eps=w.eps), muon_lr=w.muon_lr,
+                         muon_wd=w.muon_wd, momentum=w.muon_momentum, adam_lr=w.adam_lr,
+                         adam_wd=[w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))])
+        for i in range(len(w.muon_shapes)):
+            st.muon_view(pm, i).normal_(0.0, 0.02, generator=gen)
+        for i in range(len(w.adam_shapes)):
+            st.adam_view(pa, i).normal_(0.0, 0.02, generator=gen)
+        gen.manual_seed(1000 + rank)   # local grads differ per rank
+        st.gm.copy_(torch.randn(plan.muon_len, generator=gen, device=dev) * 1e-3)
+        st.ga.copy_(torch.randn(plan.adam_len, generator=gen, device=dev) * 1e-3)
+        stream = torch.cuda.current_stream(dev)
+
+        for _ in range(args.warmup):
+            st.step(max_norm=w.clip)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        ns_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in ns_ev:
+            a.record(stream)
+            b.record(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+        l0 = L.lib.moteopt_launch_count()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        with ClockSampler(gpu_id) as clk:
+            e0.record(stream)
+            for k in range(args.steps):
+                L.check(L.lib.moteopt_profile_ns_events(ns_ev[k][0].cuda_event, ns_ev[k][1].cuda_event), "events")
+                st.step(max_norm=w.clip)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
+        launches = L.lib.moteopt_launch_count() - l0
+        ms_local = e0.elapsed_time(e1) / args.steps
+        ns_local = statistics.mean(a.elapsed_time(b) for a, b in ns_ev) if st.mine else 0.0
+        status, _ = read_status(dev)
+        if status & 3:
+            raise RuntimeError(f"rank {rank}: kernel status {status}")
+
+        # end to end: this rank's local grads copied in from pinned host memory, the grad norm read back
+        host_m = st.gm.cpu().pin_memory()
+        host_a = st.ga.cpu().pin_memory()
+        host_norm = torch.empty((), dtype=torch.float32).pin_memory()
+        e2e_steps = max(5, min(30, args.steps // 6))
+        for _ in range(2):
+            st.gm.copy_(host_m, non_blocking=True)
+            st.ga.copy_(host_a, non_blocking=True)
+            host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        h0.record(stream)
+        for _ in range(e2e_steps):
+            st.gm.copy_(host_m, non_blocking=True)
+            st.ga.copy_(host_a, non_blocking=True)
+            host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+        h1.record(stream)
+        torch.cuda.synchronize(dev)
+        e2e_local = h0.elapsed_time(h1) / e2e_steps
+
+        my_flops = sum(w.ns_steps * _ns_flops(w.muon_shapes[i]) for i in st.mine)
+        vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops], dtype=torch.float64, device=dev)
+        allv = [torch.zeros_like(vals) for _ in range(world)]
+        dist.all_gather(allv, vals)
+        allv = torch.stack(allv).cpu()
+        ms = float(allv[:, 0].max())
+        e2e = float(allv[:, 1].max())
+        slow = int(allv[:, 2].argmax())
+        peaks, src = load_peaks()
+        ns_ms = float(allv[slow, 2])
+        achieved = float(allv[slow, 4]) / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+        line = {
+            "metric": METRIC, "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded params N(0,0.02^2) fp32 (same on every rank), local grads N(0,1e-3^2) bf16 per rank",
+            "config": {"workload": w.name, "parallelism": f"muon-owner+zero1 x{world}", "collectives":
+                       "NCCL reduce-scatter (grads) + all-gather (fp32 params) + all-gather (per-rank sum of squares)",
+                       "l2": "inputs larger than L2; no flush"},
+            "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel", "achieved": round(achieved, 1),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "traffic": None, "peak_source": f"{src} (burst bf16)", "rank": slow,
+                         "ns_ms_per_step": round(ns_ms, 4)},
+            "e2e": {"value": round(e2e, 4), "unit": "ms/step",
+                    "h2d_bytes_per_step": int((st.gm.numel() + st.ga.numel()) * 2), "d2h_bytes_per_step": 4},
+            "clocks": clk.summary(),
+            "gpu_launches": int(allv[:, 3].sum()),
+        }
+        return line
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _ns_flops(shape) -> float:
+    batch = 1
+    for d in shape[:-2]:
+        batch *= int(d)
+    m, n = sorted((int(shape[-2]), int(shape[-1])))
+    return batch * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+if __name__ == "__main__":
+    print(json.dumps({"note": "run through bench.py under torch.distributed.run"}))

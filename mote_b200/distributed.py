@@ -1,0 +1,262 @@
+"""The optimizer step across the GPUs of one node (the reference has no multi-GPU code; this is the build's own).
+
+Layout. Two flat buffers per tensor kind (params, grads): a Muon region and an AdamW region.
+  * Muon region: rank r's segment holds the Muon parameters it owns, whole, in declaration order, padded to the
+    longest segment. Ownership is greedy longest-processing-time over each matrix's estimated cost (Newton-Schulz
+    FLOPs at the tensor rate plus optimizer bytes at HBM rate), so ranks finish together.
+  * AdamW region: every AdamW parameter concatenated in declaration order; rank r owns the r-th of N equal slices
+    (ZeRO-1: exp_avg / exp_avg_sq exist only for the owned slice).
+Every parameter is a contiguous view of its region, so a model's parameters can live there.
+
+Step (grads: each rank's local, unreduced grads in the grad regions):
+  1. reduce-scatter (sum) of both grad regions: rank r receives the reduced grads of its own segments;
+  2. rank r's sum of (g / divisor)^2 over what it owns, all-gathered and summed in rank order -> the global norm and
+     clip coefficient (bitwise identical on every rank);
+  3. rank r runs AdamW on its slice and Muon (momentum, Newton-Schulz, apply) on its matrices;
+  4. all-gather of both param regions: every rank holds the updated model.
+Collectives go through torch.distributed (NCCL on GPUs; gloo works for the host-side tests). The compute steps are
+injected (`Compute`), so the same choreography runs with the CUDA library or with a CPU stand-in.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+ALIGN = 64   # elements: every segment and every parameter starts 256-byte aligned in fp32
+
+
+def _round_up(x: int, a: int) -> int:
+    return (x + a - 1) // a * a
+
+
+def muon_cost(shape: Sequence[int], ns_steps: int = 5, tflops: float = 1000.0, hbm_gbs: float = 6000.0) -> float:
+    """Estimated seconds of one Muon parameter's update on one B200: Newton-Schulz FLOPs + 28 B/element."""
+    batch = 1
+    for d in shape[:-2]:
+        batch *= int(d)
+    m, n = sorted((int(shape[-2]), int(shape[-1])))
+    flops = batch * ns_steps * (4.0 * m * m * n + 2.0 * m ** 3)
+    return flops / (tflops * 1e12) + batch * m * n * 28.0 / (hbm_gbs * 1e9)
+
+
+@dataclass
+class ShardPlan:
+    world: int
+    muon_shapes: List[Tuple[int, ...]]
+    adam_shapes: List[Tuple[int, ...]]
+    owner: List[int] = field(default_factory=list)             # rank owning each Muon param
+    muon_off: List[int] = field(default_factory=list)          # element offset of each Muon param in its region
+    m_seg: int = 0                                              # Muon segment length per rank (elements)
+    m_used: List[int] = field(default_factory=list)            # elements of rank r's segment that hold params
+    adam_off: List[int] = field(default_factory=list)          # element offset of each AdamW param
+    a_total: int = 0
+    a_seg: int = 0
+
+    @property
+    def muon_len(self) -> int:
+        return self.world * self.m_seg
+
+    @property
+    def adam_len(self) -> int:
+        return self.world * self.a_seg
+
+    def owned_muon(self, rank: int) -> List[int]:
+        return [i for i, o in enumerate(self.owner) if o == rank]
+
+    def adam_pieces(self, rank: int) -> List[Tuple[int, int, int]]:
+        """(param index, first element inside the param, length) of the AdamW elements rank owns."""
+        lo, hi = rank * self.a_seg, min((rank + 1) * self.a_seg, self.a_total)
+        out = []
+        for i, s in enumerate(self.adam_shapes):
+            n = _numel(s)
+            a, b = max(lo, self.adam_off[i]), min(hi, self.adam_off[i] + n)
+            if a < b:
+                out.append((i, a - self.adam_off[i], b - a))
+        return out
+
+
+def _numel(shape) -> int:
+    n = 1
+    for d in shape:
+        n *= int(d)
+    return n
+
+
+def make_plan(muon_shapes, adam_shapes, world: int, ns_steps: int = 5) -> ShardPlan:
+    plan = ShardPlan(world, [tuple(s) for s in muon_shapes], [tuple(s) for s in adam_shapes])
+    load = [0.0] * world
+    plan.owner = [-1] * len(muon_shapes)
+    order = sorted(range(len(muon_shapes)), key=lambda i: (-muon_cost(muon_shapes[i], ns_steps), i))
+    for i in order:
+        r = min(range(world), key=lambda k: (load[k], k))
+        plan.owner[i] = r
+        load[r] += muon_cost(muon_shapes[i], ns_steps)
+    used = [0] * world
+    plan.muon_off = [0] * len(muon_shapes)
+    for i, s in enumerate(muon_shapes):        # declaration order inside each segment
+        r = plan.owner[i]
+        plan.muon_off[i] = used[r]             # relative to the segment; made absolute below
+        used[r] += _round_up(_numel(s), ALIGN)
+    plan.m_seg = _round_up(max(used) if used else 0, ALIGN)
+    plan.m_used = used
+    for i in range(len(muon_shapes)):
+        plan.muon_off[i] += plan.owner[i] * plan.m_seg
+    off = 0
+    for s in adam_shapes:
+        plan.adam_off.append(off)
+        off += _numel(s)
+    plan.a_total = off
+    plan.a_seg = _round_up(-(-off // world), ALIGN) if off else 0
+    return plan
+
+
+# -----------------------------------------------------------------------------------------------------------------
+@dataclass
+class Compute:
+    """The step's compute, injected: `sumsq(views, divisor) -> 0-dim fp64 tensor` (sum of (g/divisor)^2 over the
+    views), `coef(sums, max_norm) -> 2-element fp32 tensor [norm, coef]`, `update(muon_items, adam_items, coef,
+    divisor)` with items as in mote_b200.functional."""
+    sumsq: Callable
+    coef: Callable
+    update: Callable
+
+
+def _reduce_scatter(out: torch.Tensor, flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
+    """out (seg elements) = this rank's segment of the sum of every rank's `flat`; `flat` is left as it was."""
+    if seg == 0:
+        return
+    if dist.get_backend(group) == "nccl":
+        dist.reduce_scatter_tensor(out, flat, op=dist.ReduceOp.SUM, group=group)
+    else:   # gloo has no reduce-scatter of a flat tensor: an all-reduce of a copy gives the same sums
+        tmp = flat.clone()
+        dist.all_reduce(tmp, op=dist.ReduceOp.SUM, group=group)
+        out.copy_(tmp[rank * seg:(rank + 1) * seg])
+
+
+def _all_gather_inplace(flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
+    if seg == 0:
+        return
+    dist.all_gather_into_tensor(flat, flat[rank * seg:(rank + 1) * seg].clone() if dist.get_backend(group) != "nccl"
+                                else flat[rank * seg:(rank + 1) * seg], group=group)
+
+
+class ShardedStep:
+    """Rank-local state and the step of the module docstring. `params_m`/`params_a` are the fp32 param regions,
+    `grads_m`/`grads_a` the local grad regions (fp32 or bf16), of length plan.muon_len / plan.adam_len. The grad
+    regions are only read: the reduced grads of the rank's own segments land in rank-local buffers."""
+
+    def __init__(self, plan: ShardPlan, rank: int, params_m: torch.Tensor, params_a: torch.Tensor,
+                 grads_m: torch.Tensor, grads_a: torch.Tensor, compute: Compute, *, muon_lr: float,
+                 muon_wd: float, momentum: float = 0.95, nesterov: bool = True, adam_lr: float, adam_wd: Sequence[float],
+                 group=None):
+        self.plan, self.rank, self.group = plan, rank, group
+        self.pm, self.pa, self.gm, self.ga = params_m, params_a, grads_m, grads_a
+        self.compute = compute
+        self.muon_lr, self.muon_wd, self.momentum, self.nesterov = muon_lr, muon_wd, momentum, nesterov
+        self.adam_lr, self.adam_wd = adam_lr, list(adam_wd)
+        self.mine = plan.owned_muon(rank)
+        self.bufs = {i: torch.zeros(plan.muon_shapes[i], dtype=torch.float32, device=params_m.device) for i in self.mine}
+        self.pieces = plan.adam_pieces(rank)
+        self.gm_seg = torch.zeros(plan.m_seg, dtype=grads_m.dtype, device=grads_m.device)
+        self.ga_seg = torch.zeros(plan.a_seg, dtype=grads_a.dtype, device=grads_a.device)
+        self.m_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
+        self.v_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
+        self.steps = 0
+
+    def muon_view(self, flat: torch.Tensor, i: int) -> torch.Tensor:
+        o, s = self.plan.muon_off[i], self.plan.muon_shapes[i]
+        return flat[o:o + _numel(s)].view(s)
+
+    def adam_view(self, flat: torch.Tensor, i: int) -> torch.Tensor:
+        o, s = self.plan.adam_off[i], self.plan.adam_shapes[i]
+        return flat[o:o + _numel(s)].view(s)
+
+    def reduced_muon_grad(self, i: int) -> torch.Tensor:
+        o = self.plan.muon_off[i] - self.rank * self.plan.m_seg
+        s = self.plan.muon_shapes[i]
+        return self.gm_seg[o:o + _numel(s)].view(s)
+
+    def reduced_adam_grad(self, i: int, start: int, n: int) -> torch.Tensor:
+        o = self.plan.adam_off[i] + start - self.rank * self.plan.a_seg
+        return self.ga_seg[o:o + n]
+
+    def owned_grad_views(self) -> List[torch.Tensor]:
+        views = [self.reduced_muon_grad(i).reshape(-1) for i in self.mine]
+        views += [self.reduced_adam_grad(i, start, n) for i, start, n in self.pieces]
+        return views
+
+    @torch.no_grad()
+    def step(self, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None) -> torch.Tensor:
+        from .functional import AdamWItem, MuonItem
+        plan, r = self.plan, self.rank
+        _reduce_scatter(self.gm_seg, self.gm, plan.m_seg, r, self.group)
+        _reduce_scatter(self.ga_seg, self.ga, plan.a_seg, r, self.group)
+        mine = self.compute.sumsq(self.owned_grad_views(), grad_divisor)
+        sums = torch.empty(plan.world, dtype=torch.float64, device=mine.device)
+        dist.all_gather_into_tensor(sums, mine.reshape(1), group=self.group)
+        norm_coef = self.compute.coef(sums, max_norm)
+        self.steps += 1
+        muon = [MuonItem(self.muon_view(self.pm, i), self.reduced_muon_grad(i), self.bufs[i], self.muon_lr,
+                         self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
+                for i in self.mine]
+        adam = []
+        base = r * plan.a_seg
+        for i, start, n in self.pieces:
+            o = plan.adam_off[i] + start
+            adam.append(AdamWItem(self.pa[o:o + n], self.reduced_adam_grad(i, start, n), self.m_state[o - base:o - base + n],
+                                  self.v_state[o - base:o - base + n], self.adam_lr, self.adam_wd[i], self.steps))
+        self.compute.update(muon, adam, norm_coef[1:2] if max_norm is not None else None, grad_divisor)
+        _all_gather_inplace(self.pm, plan.m_seg, r, self.group)
+        _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
+        return norm_coef[0]
+
+
+def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_scale: float = 0.2) -> Compute:
+    """The step's compute on the CUDA library (libmoteopt.so)."""
+    import ctypes as C
+
+    from . import _lib as L
+    from .functional import adamw_array, muon_array
+    from .ops import grad_dtype_code, stream_handle, workspace
+
+    def sumsq(views, divisor):
+        dev = views[0].device if views else torch.device("cuda", torch.cuda.current_device())
+        out = torch.zeros((), dtype=torch.float64, device=dev)
+        if not views:
+            return out
+        n = len(views)
+        ptrs = L.array(C.c_void_p, [v.data_ptr() for v in views])
+        numels = L.array(C.c_int64, [v.numel() for v in views])
+        dts = L.array(C.c_int, [grad_dtype_code(v) for v in views])
+        ws = workspace(dev, L.lib.moteopt_grad_sumsq_workspace_size(numels, n))
+        L.check(L.lib.moteopt_grad_sumsq(ptrs, numels, dts, n, float(divisor or 0.0), C.c_void_p(out.data_ptr()),
+                                         C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
+                "moteopt_grad_sumsq")
+        return out
+
+    def coef(sums, max_norm):
+        out = torch.empty(2, dtype=torch.float32, device=sums.device)
+        L.check(L.lib.moteopt_clip_coef_from_sums(C.c_void_p(sums.data_ptr()), sums.numel(), int(max_norm is not None),
+                                                  float(max_norm or 0.0), C.c_void_p(out.data_ptr()),
+                                                  C.c_void_p(stream_handle(sums.device))), "moteopt_clip_coef_from_sums")
+        return out
+
+    def update(muon, adam, coef_t, divisor):
+        dev = (muon[0].param if muon else adam[0].param).device if (muon or adam) else None
+        if dev is None:
+            return
+        m_arr, a_arr = muon_array(muon), adamw_array(adam)
+        nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adam))
+        ws = workspace(dev, nbytes)
+        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
+        hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+        L.check(L.lib.moteopt_optimizer_step_with_coef(
+            m_arr, len(muon), C.byref(cfg), a_arr, len(adam), C.byref(hp), float(divisor or 0.0),
+            C.c_void_p(coef_t.data_ptr() if coef_t is not None else 0), C.c_void_p(ws.data_ptr()), ws.numel(),
+            C.c_void_p(stream_handle(dev))), "moteopt_optimizer_step_with_coef")
+
+    return Compute(sumsq, coef, update)

@@ -1,0 +1,171 @@
+"""The sharded (multi-GPU) step's host logic on CPU ranks: 2 gloo processes run mote_b200.distributed.ShardedStep
+with the oracle as the compute, and must end bitwise equal to one process running the oracle step on the summed
+grads; both ranks must hold identical params. Also: the shard plan's ownership and layout rules."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from mote_b200 import configs
+from mote_b200.distributed import Compute, ShardedStep, make_plan, muon_cost
+from oracle import moteopt_oracle as O
+
+DIV = 3.0
+CLIP = 0.02
+STEPS = 3
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _coef(norm2: float, max_norm):
+    norm = np.float32(np.sqrt(norm2))
+    if max_norm is None:
+        return norm, np.float32(1.0)
+    return norm, O.clip_coef(norm, max_norm)
+
+
+def oracle_compute(w):
+    """The step's compute as the oracle (numpy on CPU tensors' memory)."""
+    def sumsq(views, divisor):
+        s = 0.0
+        for v in views:
+            g = v.numpy().astype(np.float32)
+            if divisor:
+                g = (g / np.float32(divisor)).astype(np.float32)
+            s += float((g.astype(np.float64) ** 2).sum())
+        return torch.tensor(s, dtype=torch.float64)
+
+    def coef(sums, max_norm):
+        norm, c = _coef(float(sum(sums.tolist())), max_norm)
+        return torch.tensor([norm, c], dtype=torch.float32)
+
+    def update(muon, adam, coef_t, divisor):
+        c = np.float32(coef_t.item()) if coef_t is not None else None
+
+        def eff(g):
+            x = g.numpy().astype(np.float32).copy()
+            if divisor:
+                x = (x / np.float32(divisor)).astype(np.float32)
+            if c is not None:
+                x = (x * c).astype(np.float32)
+            return x
+        for it in adam:
+            O.adamw_update(it.param.numpy(), eff(it.grad), it.exp_avg.numpy(), it.exp_avg_sq.numpy(), it.lr,
+                           w.betas[0], w.betas[1], w.eps, it.weight_decay, it.step)
+        for it in muon:   # the item carries decay = lr * wd (muon.py:78); hand the oracle the matching wd
+            grp = O.MuonGroup(lr=it.lr, momentum=it.momentum, nesterov=it.nesterov,
+                              weight_decay=it.decay / it.lr if it.decay else 0.0, ns_steps=w.ns_steps)
+            bufs = [it.momentum_buffer.numpy()]
+            O.muon_step([it.param.numpy()], [eff(it.grad)], bufs, grp)
+    return Compute(sumsq, coef, update)
+
+
+def small_workload():
+    return configs.Workload("dist_test", [(48, 64), (64, 48), (2, 32, 40), (40, 40), (16, 80)],
+                            [(30, 16)], [(16,), (7,)], muon_wd=0.1, adam_wd=0.1, ns_steps=3)
+
+
+def _rank_main(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = small_workload()
+        plan = make_plan(w.muon_shapes, w.adam_shapes, world, ns_steps=w.ns_steps)
+        inp = configs.make_params(w, seed=0)
+        pm = torch.zeros(plan.muon_len)
+        pa = torch.zeros(plan.adam_len)
+        gm = torch.zeros(plan.muon_len)
+        ga = torch.zeros(plan.adam_len)
+        nd = len(w.adam_decay_shapes)
+        st = ShardedStep(plan, rank, pm, pa, gm, ga, oracle_compute(w), muon_lr=w.muon_lr, muon_wd=w.muon_wd,
+                         adam_lr=w.adam_lr, adam_wd=[w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))])
+        for i, p in enumerate(inp.muon_params):
+            st.muon_view(pm, i).copy_(torch.from_numpy(p))
+        for i, p in enumerate(inp.adam_params):
+            st.adam_view(pa, i).copy_(torch.from_numpy(p))
+        norms = []
+        for step in range(STEPS):
+            ag, mg = configs.make_grads(w, seed=100 + rank, step=step)   # local grads differ per rank
+            for i, g in enumerate(mg):
+                st.muon_view(gm, i).copy_(torch.from_numpy(g))
+            for i, g in enumerate(ag):
+                st.adam_view(ga, i).copy_(torch.from_numpy(g))
+            norms.append(float(st.step(max_norm=CLIP, grad_divisor=DIV)))
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), pm=pm.numpy(), pa=pa.numpy(), norms=np.array(norms),
+                 muon_off=np.array(plan.muon_off), adam_off=np.array(plan.adam_off))
+    finally:
+        dist.destroy_process_group()
+
+
+def _reference(world):
+    """One process: grads summed over the ranks, then the oracle step with the same norm arithmetic."""
+    w = small_workload()
+    inp = configs.make_params(w, seed=0)
+    nd = len(w.adam_decay_shapes)
+    ms, vs = [np.zeros_like(p) for p in inp.adam_params], [np.zeros_like(p) for p in inp.adam_params]
+    bufs = [None] * len(inp.muon_params)
+    norms = []
+    for step in range(STEPS):
+        tot_a = [np.zeros_like(p) for p in inp.adam_params]
+        tot_m = [np.zeros_like(p) for p in inp.muon_params]
+        for r in range(world):
+            ag, mg = configs.make_grads(w, seed=100 + r, step=step)
+            tot_a = [(x + y).astype(np.float32) for x, y in zip(tot_a, ag)]
+            tot_m = [(x + y).astype(np.float32) for x, y in zip(tot_m, mg)]
+        allg = [(g / np.float32(DIV)).astype(np.float32) for g in tot_a + tot_m]
+        norm, c = _coef(float(sum((g.astype(np.float64) ** 2).sum() for g in allg)), CLIP)
+        norms.append(float(norm))
+        allg = [(g * c).astype(np.float32) for g in allg]
+        for i in range(len(inp.adam_params)):
+            O.adamw_update(inp.adam_params[i], allg[i], ms[i], vs[i], w.adam_lr, w.betas[0], w.betas[1], w.eps,
+                           w.adam_wd if i < nd else 0.0, step + 1)
+        O.muon_step(inp.muon_params, allg[len(inp.adam_params):], bufs,
+                    O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=(w.muon_lr * w.muon_wd) / w.muon_lr,
+                                ns_steps=w.ns_steps))
+    return inp, norms
+
+
+def test_plan_owns_every_matrix_once_and_balances_cost():
+    w = configs.c1()
+    for world in (2, 4, 8):
+        plan = make_plan(w.muon_shapes, w.adam_shapes, world)
+        assert sorted(set(plan.owner)) == list(range(world))
+        loads = [sum(muon_cost(w.muon_shapes[i]) for i in plan.owned_muon(r)) for r in range(world)]
+        assert max(loads) <= 1.25 * (sum(loads) / world)
+        # segments never overlap and every offset is aligned
+        spans = sorted((plan.muon_off[i], plan.muon_off[i] + int(np.prod(s))) for i, s in enumerate(w.muon_shapes))
+        assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+        assert all(o % 64 == 0 for o in plan.muon_off)
+        got = sum(n for r in range(world) for _, _, n in plan.adam_pieces(r))
+        assert got == plan.a_total
+
+
+@pytest.mark.timeout(300)
+def test_two_cpu_ranks_match_one_process(tmp_path):
+    world = 2
+    mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    outs = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
+    assert np.array_equal(outs[0]["pm"], outs[1]["pm"]) and np.array_equal(outs[0]["pa"], outs[1]["pa"])
+    assert np.array_equal(outs[0]["norms"], outs[1]["norms"])
+    inp, norms = _reference(world)
+    assert np.allclose(outs[0]["norms"], norms, rtol=1e-6, atol=0)
+    w = small_workload()
+    for i, (p, s) in enumerate(zip(inp.muon_params, w.muon_shapes)):
+        o = int(outs[0]["muon_off"][i])
+        got = outs[0]["pm"][o:o + p.size].reshape(s)
+        assert np.array_equal(got, p), (i, float(np.abs(got - p).max()))
+    for i, (p, s) in enumerate(zip(inp.adam_params, w.adam_shapes)):
+        o = int(outs[0]["adam_off"][i])
+        assert np.array_equal(outs[0]["pa"][o:o + p.size].reshape(s), p), i
