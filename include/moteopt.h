@@ -77,6 +77,10 @@ typedef struct moteopt_adamw_tensor {
 
 typedef struct moteopt_adamw_hparams {
   double beta1, beta2, eps;     /* train.py:98: betas=(0.9, beta2), eps=1e-8 */
+  float* device_step;           /* NULL: bias corrections from each tensor's host `step`. Else a device fp32 step
+                                   counter shared by every tensor: the call adds 1 to it and computes the bias
+                                   corrections on the device (the form torch's capturable AdamW keeps), so a captured
+                                   CUDA graph of the step stays correct on replay */
 } moteopt_adamw_hparams;
 
 /* Gradient pre-processing of mote/train/train.py:944-946. */

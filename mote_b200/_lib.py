@@ -49,7 +49,7 @@ class AdamWTensor(C.Structure):
 
 
 class AdamWHparams(C.Structure):
-    _fields_ = [("beta1", C.c_double), ("beta2", C.c_double), ("eps", C.c_double)]
+    _fields_ = [("beta1", C.c_double), ("beta2", C.c_double), ("eps", C.c_double), ("device_step", C.c_void_p)]
 
 
 class GradConfig(C.Structure):

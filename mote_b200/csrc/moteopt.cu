@@ -355,6 +355,13 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
   A.beta2 = static_cast<float>(hp->beta2);
   A.one_minus_beta2 = static_cast<float>(1.0 - hp->beta2);
   A.eps = static_cast<float>(hp->eps);
+  A.beta1d = hp->beta1;
+  A.beta2d = hp->beta2;
+  A.dstep = hp->device_step;
+  if (hp->device_step != nullptr && n > 0) {
+    step_increment_kernel<<<1, 32, 0, st>>>(hp->device_step);
+    MO_LAUNCHED("step_increment_kernel");
+  }
   for (int s0 = 0; s0 < n; s0 += kMaxAdamSeg) {
     const int cnt = std::min(n - s0, kMaxAdamSeg);
     A.n = cnt;
@@ -375,6 +382,8 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       S.bc2_sqrt = static_cast<float>(std::pow(bc2, 0.5));
       S.has_decay = x.weight_decay != 0.0;
       S.decay_mul = static_cast<float>(1.0 - x.lr * x.weight_decay);
+      S.lr = x.lr;
+      S.wd = x.weight_decay;
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kChunk));
     }
     if (A.chunk_start[cnt] == 0) continue;
@@ -393,7 +402,8 @@ int check_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparam
       return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": null pointer");
     if (x.grad_dtype != kF32 && x.grad_dtype != kBF16)
       return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": grad dtype must be fp32 or bf16");
-    if (x.step < 1) return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": step must be >= 1");
+    if (x.step < 1 && hp->device_step == nullptr)
+      return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": step must be >= 1");
     if (cdiv(x.numel, kChunk) > (1 << 30)) return fail(MOTEOPT_ERR_LIMIT, "AdamW tensor too large");
   }
   return MOTEOPT_OK;

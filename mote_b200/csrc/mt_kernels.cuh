@@ -190,9 +190,16 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
   const int total = A.chunk_start[A.n];
   const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
+  const double dstep = A.dstep != nullptr ? static_cast<double>(*A.dstep) : 0.0;
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
-    const AdamSeg& S = A.seg[s];
+    AdamSeg S = A.seg[s];
+    if (A.dstep != nullptr) {   // the host computes these in fp64 from its step count; the same formulas here
+      const double bc1 = 1.0 - pow(A.beta1d, dstep);
+      const double bc2 = 1.0 - pow(A.beta2d, dstep);
+      S.neg_step_size = static_cast<float>(-(S.lr / bc1));
+      S.bc2_sqrt = static_cast<float>(pow(bc2, 0.5));
+    }
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype);
@@ -220,6 +227,11 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
       S.p[i] = p; S.m[i] = m; S.v[i] = v;
     }
   }
+}
+
+// torch's `step_t += 1` on a device step counter (fp32, exact for integer counts below 2^24)
+__global__ void step_increment_kernel(float* step) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *step = *step + 1.0f;
 }
 
 // ---------------------------------------------------------------------------------------------------------------

@@ -65,6 +65,7 @@ struct AdamSeg {
   int dtype;                 // grad dtype
   int has_decay;
   int pad_;
+  double lr, wd;             // for the device-step mode, which recomputes the three scalars above per step
 };
 struct AdamArgs {
   int n;
@@ -77,6 +78,8 @@ struct AdamArgs {
   float beta2;
   float one_minus_beta2;
   float eps;
+  const float* dstep;        // device step counter (already incremented for this step), or null: host scalars
+  double beta1d, beta2d;
   int chunk_start[kMaxAdamSeg + 1];
   AdamSeg seg[kMaxAdamSeg];
 };

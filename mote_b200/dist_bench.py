@@ -18,7 +18,7 @@ import torch
 import torch.distributed as dist
 
 from . import configs
-from .distributed import ShardedStep, cuda_compute, make_plan
+from .distributed import ShardedStep, capture, cuda_compute, make_plan
 
 ROOT = Path(__file__).resolve().parent.parent
 METRIC = "ms/optimizer step (96M set)"
@@ -59,26 +59,45 @@ def run(args, rank: int, world: int, local_rank: int):
             st.step(max_norm=w.clip)
         torch.cuda.synchronize(dev)
         dist.barrier()
-        ns_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        # eager steps with the library's Newton-Schulz event hook (the roofline's kernel time)
+        n_eager = max(3, min(20, args.steps))
+        ns_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_eager)]
         for a, b in ns_ev:
             a.record(stream)
             b.record(stream)
+        torch.cuda.synchronize(dev)
+        for k in range(n_eager):
+            L.check(L.lib.moteopt_profile_ns_events(ns_ev[k][0].cuda_event, ns_ev[k][1].cuda_event), "events")
+            st.step(max_norm=w.clip)
+        torch.cuda.synchronize(dev)
+        L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
+        ns_local = statistics.mean(a.elapsed_time(b) for a, b in ns_ev) if st.mine else 0.0
+        # the whole sharded step (NCCL collectives + kernels) captured in a CUDA graph and replayed
+        graph = None
+        capture_error = ""
+        l0 = L.lib.moteopt_launch_count()
+        try:
+            graph, _norm = capture(st, max_norm=w.clip)
+        except Exception as exc:  # noqa: BLE001  (recorded in the JSON line; the eager step is timed instead)
+            graph = None
+            capture_error = f"{type(exc).__name__}: {exc}"[:200]
+        per_step = L.lib.moteopt_launch_count() - l0
+        run_step = graph.replay if graph is not None else (lambda: st.step(max_norm=w.clip))
+        for _ in range(3):
+            run_step()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
-        l0 = L.lib.moteopt_launch_count()
         torch.cuda.synchronize(dev)
         dist.barrier()
+        l1 = L.lib.moteopt_launch_count()
         with ClockSampler(gpu_id) as clk:
             e0.record(stream)
-            for k in range(args.steps):
-                L.check(L.lib.moteopt_profile_ns_events(ns_ev[k][0].cuda_event, ns_ev[k][1].cuda_event), "events")
-                st.step(max_norm=w.clip)
+            for _ in range(args.steps):
+                run_step()
             e1.record(stream)
             torch.cuda.synchronize(dev)
-        L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
-        launches = L.lib.moteopt_launch_count() - l0
+        launches = per_step * args.steps if graph is not None else L.lib.moteopt_launch_count() - l1
         ms_local = e0.elapsed_time(e1) / args.steps
-        ns_local = statistics.mean(a.elapsed_time(b) for a, b in ns_ev) if st.mine else 0.0
         status, _ = read_status(dev)
         if status & 3:
             raise RuntimeError(f"rank {rank}: kernel status {status}")
@@ -88,18 +107,25 @@ def run(args, rank: int, world: int, local_rank: int):
         host_a = st.ga.cpu().pin_memory()
         host_norm = torch.empty((), dtype=torch.float32).pin_memory()
         e2e_steps = max(5, min(30, args.steps // 6))
-        for _ in range(2):
+        norm_t = _norm if graph is not None else None
+
+        def e2e_step():
             st.gm.copy_(host_m, non_blocking=True)
             st.ga.copy_(host_a, non_blocking=True)
-            host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+            if graph is not None:
+                graph.replay()
+                host_norm.copy_(norm_t, non_blocking=True)
+            else:
+                host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
         torch.cuda.synchronize(dev)
         dist.barrier()
         h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         h0.record(stream)
         for _ in range(e2e_steps):
-            st.gm.copy_(host_m, non_blocking=True)
-            st.ga.copy_(host_a, non_blocking=True)
-            host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+            e2e_step()
         h1.record(stream)
         torch.cuda.synchronize(dev)
         e2e_local = h0.elapsed_time(h1) / e2e_steps
@@ -120,7 +146,9 @@ def run(args, rank: int, world: int, local_rank: int):
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded params N(0,0.02^2) fp32 (same on every rank), local grads N(0,1e-3^2) bf16 per rank",
-            "config": {"workload": w.name, "parallelism": f"muon-owner+zero1 x{world}", "collectives":
+            "config": {"workload": w.name, "parallelism": f"muon-owner+zero1 x{world}",
+                       "launch": "CUDA graph of the whole sharded step" if graph is not None
+                       else f"eager (graph capture failed: {capture_error})", "collectives":
                        "NCCL reduce-scatter (grads) + all-gather (fp32 params) + all-gather (per-rank sum of squares)",
                        "l2": "inputs larger than L2; no flush"},
             "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel", "achieved": round(achieved, 1),
@@ -132,8 +160,10 @@ def run(args, rank: int, world: int, local_rank: int):
             "clocks": clk.summary(),
             "gpu_launches": int(allv[:, 3].sum()),
         }
+        del graph, run_step, norm_t
         return line
     finally:
+        torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()
 

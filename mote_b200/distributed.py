@@ -166,6 +166,7 @@ class ShardedStep:
         self.m_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
         self.v_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
         self.steps = 0
+        self.graph = None
 
     def muon_view(self, flat: torch.Tensor, i: int) -> torch.Tensor:
         o, s = self.plan.muon_off[i], self.plan.muon_shapes[i]
@@ -215,8 +216,22 @@ class ShardedStep:
         return norm_coef[0]
 
 
+def capture(step: ShardedStep, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None):
+    """Record one ShardedStep.step (its NCCL collectives and kernels) in a CUDA graph on every rank. The compute must
+    keep AdamW's step count on the device (cuda_compute does). Returns (graph, norm tensor); replaying the graph is
+    one step. Capture on every rank together, after at least one eager step; drop the graph before
+    destroy_process_group."""
+    torch.cuda.synchronize()
+    dist.barrier(group=step.group)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        norm = step.step(max_norm=max_norm, grad_divisor=grad_divisor)
+    return g, norm
+
+
 def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_scale: float = 0.2) -> Compute:
-    """The step's compute on the CUDA library (libmoteopt.so)."""
+    """The step's compute on the CUDA library (libmoteopt.so). AdamW's step count is a device counter (so that a
+    captured step stays correct when replayed)."""
     import ctypes as C
 
     from . import _lib as L
@@ -245,15 +260,19 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
                                                   C.c_void_p(stream_handle(sums.device))), "moteopt_clip_coef_from_sums")
         return out
 
+    counter = {}
+
     def update(muon, adam, coef_t, divisor):
         dev = (muon[0].param if muon else adam[0].param).device if (muon or adam) else None
         if dev is None:
             return
+        if dev not in counter:
+            counter[dev] = torch.zeros((), dtype=torch.float32, device=dev)
         m_arr, a_arr = muon_array(muon), adamw_array(adam)
         nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adam))
         ws = workspace(dev, nbytes)
         cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
-        hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+        hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps), counter[dev].data_ptr())
         L.check(L.lib.moteopt_optimizer_step_with_coef(
             m_arr, len(muon), C.byref(cfg), a_arr, len(adam), C.byref(hp), float(divisor or 0.0),
             C.c_void_p(coef_t.data_ptr() if coef_t is not None else 0), C.c_void_p(ws.data_ptr()), ws.numel(),

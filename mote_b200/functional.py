@@ -100,10 +100,12 @@ def _device(muon: Sequence[MuonItem], adamw: Sequence[AdamWItem]) -> torch.devic
 def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (), *, ns_steps: int = 5,
                    rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
                    max_norm: Optional[float] = None, grad_divisor: Optional[float] = None,
-                   out_norm: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+                   out_norm: Optional[torch.Tensor] = None,
+                   device_step: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
     AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
-    max_norm is given."""
+    max_norm is given. With `device_step` (a 0-dim fp32 CUDA tensor) AdamW's step count is that counter, which the
+    call increments on the device (the AdamItems' `step` is then ignored)."""
     dev = _device(muon, adamw)
     m_arr, a_arr = muon_array(muon), adamw_array(adamw)
     nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adamw))
@@ -111,7 +113,8 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
         raise L.MoteoptError("optimizer_step: invalid shapes")
     ws = workspace(dev, nbytes)
     cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
-    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps),
+                        device_step.data_ptr() if device_step is not None else None)
     gc = L.GradConfig(int(max_norm is not None), float(max_norm or 0.0), float(grad_divisor or 0.0))
     if max_norm is not None and out_norm is None:
         out_norm = torch.empty((), dtype=torch.float32, device=dev)
@@ -149,10 +152,55 @@ def adamw_step(adamw: Sequence[AdamWItem], *, betas=(0.9, 0.999), eps: float = 1
         return
     dev = _device((), adamw)
     arr = adamw_array(adamw)
-    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps))
+    hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps), None)
     L.check(L.lib.moteopt_adamw_step(arr, len(adamw), C.byref(hp),
                                      C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
                                      C.c_void_p(stream_handle(dev))), "moteopt_adamw_step")
+
+
+class CapturedStep:
+    """optimizer_step over a fixed set of tensors, captured once into a CUDA graph and then replayed, so a step
+    costs one graph launch on the host instead of ~20 kernel launches and their argument packing.
+
+    The tensors (params, grads, state) must stay the same objects at the same addresses; the hyperparameters (lr,
+    decay, betas, clip, divisor) are the ones given here, fixed at capture (build a new CapturedStep to change
+    them). AdamW's step count is a device counter starting at `start_step`. The first call runs the step eagerly
+    (it also warms the library up), the second captures it and replays it, every later call replays. Returns the
+    pre-clip grad norm tensor (overwritten by every call)."""
+
+    def __init__(self, muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (), *, ns_steps: int = 5,
+                 rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
+                 max_norm: Optional[float] = None, grad_divisor: Optional[float] = None, start_step: int = 0):
+        self.dev = _device(muon, adamw)
+        self.kw = dict(ns_steps=ns_steps, rms_scale=rms_scale, ns_eps=ns_eps, betas=betas, eps=eps,
+                       max_norm=max_norm, grad_divisor=grad_divisor)
+        self.muon, self.adamw = list(muon), list(adamw)
+        self.device_step = torch.full((), float(start_step), dtype=torch.float32, device=self.dev)
+        self.out_norm = torch.zeros((), dtype=torch.float32, device=self.dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.calls = 0
+        self.launches_per_step = 0
+
+    def _run(self):
+        optimizer_step(self.muon, self.adamw, out_norm=self.out_norm, device_step=self.device_step, **self.kw)
+
+    @torch.no_grad()
+    def __call__(self) -> torch.Tensor:
+        if self.graph is not None:
+            self.graph.replay()
+        elif self.calls == 0:
+            self._run()
+        else:
+            torch.cuda.synchronize(self.dev)
+            g = torch.cuda.CUDAGraph()
+            n0 = L.lib.moteopt_launch_count()
+            with torch.cuda.graph(g):
+                self._run()
+            self.launches_per_step = int(L.lib.moteopt_launch_count() - n0)
+            self.graph = g
+            g.replay()
+        self.calls += 1
+        return self.out_norm
 
 
 def items_from_lists(params: List[torch.Tensor], grads: List[torch.Tensor], bufs: List[torch.Tensor], lr: float,

@@ -46,7 +46,7 @@ int main(void) {
   P(moteopt_muon_param) P(moteopt_muon_config) P(moteopt_adamw_tensor) P(moteopt_adamw_hparams) P(moteopt_grad_config)
   O(moteopt_muon_param, lr) O(moteopt_muon_param, nesterov) O(moteopt_muon_param, grad_dtype)
   O(moteopt_adamw_tensor, numel) O(moteopt_adamw_tensor, step) O(moteopt_adamw_tensor, grad_dtype)
-  O(moteopt_muon_config, rms_scale) O(moteopt_grad_config, max_norm)
+  O(moteopt_muon_config, rms_scale) O(moteopt_grad_config, max_norm) O(moteopt_adamw_hparams, device_step)
   return 0;
 }
 '''

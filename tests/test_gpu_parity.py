@@ -220,3 +220,35 @@ def test_step_is_bitwise_deterministic(dev):
     for a, b in zip(outs[0][0], outs[1][0]):
         assert torch.equal(a, b)
     assert outs[0][1] == outs[1][1]
+
+
+def test_captured_step_replays_equal_eager_steps(dev):
+    """CapturedStep (one CUDA graph of the whole step, AdamW's step count on the device) == eager optimizer_step."""
+    from mote_b200.functional import AdamWItem, CapturedStep, MuonItem, optimizer_step
+    w = configs.c0()
+    sets = []
+    for _ in range(2):
+        inp = configs.make_params(w, seed=3)
+        mp = _to(dev, inp.muon_params)
+        ap = _to(dev, inp.adam_params)
+        ag_np, mg_np = configs.make_grads(w, seed=3, step=0)
+        mg = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in mg_np]
+        ag = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in ag_np]
+        sets.append((mp, ap, mg, ag, [torch.zeros_like(p) for p in mp], [torch.zeros_like(p) for p in ap],
+                     [torch.zeros_like(p) for p in ap]))
+    mp, ap, mg, ag, mb, am, av = sets[0]
+    norms_eager = []
+    for k in range(4):
+        norms_eager.append(optimizer_step([MuonItem(p, g, b, 0.02, 0.002) for p, g, b in zip(mp, mg, mb)],
+                                          [AdamWItem(p, g, m, v, 3e-4, 0.1, k + 1) for p, g, m, v in zip(ap, ag, am, av)],
+                                          betas=(0.9, 0.95), max_norm=0.01).item())
+    mp2, ap2, mg2, ag2, mb2, am2, av2 = sets[1]
+    cs = CapturedStep([MuonItem(p, g, b, 0.02, 0.002) for p, g, b in zip(mp2, mg2, mb2)],
+                      [AdamWItem(p, g, m, v, 3e-4, 0.1, 0) for p, g, m, v in zip(ap2, ag2, am2, av2)],
+                      betas=(0.9, 0.95), max_norm=0.01)
+    norms_graph = [cs().item() for _ in range(4)]
+    assert cs.graph is not None and cs.launches_per_step > 0
+    assert norms_graph == norms_eager
+    for a, b in zip(mp + ap + mb + am + av, mp2 + ap2 + mb2 + am2 + av2):
+        assert torch.equal(a, b)
+    assert cs.device_step.item() == 4.0
