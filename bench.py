@@ -267,7 +267,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     ns_flops = w.ns_flops()
     achieved = ns_flops / (ns_ms * 1e-3) / 1e12
     traffic = None
-    prof = ROOT / "profiles" / "ns_phase_kernel_c1_traffic.json"
+    prof = ROOT / "profiles" / "ns_phase_kernel2_c1_traffic.json"
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
     adam_gbs = 28.0 * n_flat / (adam_ms * 1e-3) / 1e9
@@ -281,7 +281,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "parallelism": f"dp{world}" if world > 1 else "single",
                    "l2": "inputs (1.1 GB) larger than L2; no flush",
                    "launch": "CUDA graph of the whole step (mote_b200.CapturedStep)", "eager_ms_per_step": round(eager_ms, 4)},
-        "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel", "achieved": round(achieved, 1),
+        "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel2", "achieved": round(achieved, 1),
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      "traffic": traffic, "peak_source": f"{src} (burst bf16)",
                      "ns_ms_per_step": round(ns_ms, 4), "ns_launches_per_step": 15, "ns_tflop_per_step": ns_flops / 1e12,

@@ -16,6 +16,7 @@
 #include "moteopt.h"
 #include "mt_kernels.cuh"
 #include "ns_gemm.cuh"
+#include "ns_gemm2.cuh"
 
 using namespace moteopt;
 
@@ -66,6 +67,7 @@ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 struct DeviceState {
   bool ready = false;
   int sms = 0;
+  int pairs = 0;   // co-resident CTA pairs of the 2-CTA Newton-Schulz kernel
 };
 std::mutex g_mu;
 DeviceState g_dev[64];
@@ -85,11 +87,33 @@ int device_setup(int* sms) {
       return fail(MOTEOPT_ERR_DEVICE, "libmoteopt is built for sm_100a (B200); device " + std::to_string(dev) +
                                           " is sm_" + std::to_string(major) + std::to_string(minor));
     MO_CUDA(cudaFuncSetAttribute(ns::ns_phase_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
+    MO_CUDA(cudaFuncSetAttribute(ns2::ns_phase_kernel2, cudaFuncAttributeMaxDynamicSharedMemorySize, ns2::kSmem2Bytes));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (count / 2), 1, 1);
+    cfg.blockDim = dim3(ns::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = ns2::kSmem2Bytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters, ns2::ns_phase_kernel2, &cfg));
+    if (clusters < 1) return fail(MOTEOPT_ERR_DEVICE, "the 2-CTA Newton-Schulz kernel cannot be resident on this device");
     d.sms = count;
+    d.pairs = clusters;
     d.ready = true;
   }
   *sms = d.sms;
   return MOTEOPT_OK;
+}
+
+int device_pairs() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  return std::max(1, g_dev[dev].pairs);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -577,16 +601,16 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
         Lh.phase = ph;
         Lh.src = src;
         Lh.tile_start[0] = 0;
-        for (int gi = 0; gi < Lh.n_groups; ++gi) {
+        for (int gi = 0; gi < Lh.n_groups; ++gi) {   // 256 x 256 tiles, one per CTA pair
           const ns::Group& G = Lh.g[gi];
           const int out_cols = ph == ns::kUpdate ? G.n : G.m;
-          Lh.tiles_m[gi] = static_cast<int>(cdiv(G.m, ns::BM));
-          Lh.tiles_n[gi] = static_cast<int>(cdiv(out_cols, ns::BN));
+          Lh.tiles_m[gi] = static_cast<int>(cdiv(G.m, ns2::TM));
+          Lh.tiles_n[gi] = static_cast<int>(cdiv(out_cols, ns2::TN));
           Lh.tile_start[gi + 1] = Lh.tile_start[gi] + G.count * Lh.tiles_m[gi] * Lh.tiles_n[gi];
         }
         const int tiles = Lh.tile_start[Lh.n_groups];
-        ns::ns_phase_kernel<<<std::min(tiles, sms), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
-        MO_LAUNCHED("ns_phase_kernel");
+        ns2::ns_phase_kernel2<<<2 * std::min(tiles, device_pairs()), ns::kThreads, ns2::kSmem2Bytes, st>>>(Lh);
+        MO_LAUNCHED("ns_phase_kernel2");
         if (ph == ns::kUpdate) src ^= 1;
       }
     }
