@@ -53,6 +53,19 @@ class Workload:
             tot += batch * self.ns_steps * (4.0 * a * a * b + 2.0 * a ** 3)
         return tot
 
+    def ns_flops_issued(self, tile: int = 256) -> float:
+        """Newton-Schulz FLOPs the tensor cores perform per step: the Gram (X X^T) and polynomial (A A) products are
+        symmetric, so only their output blocks on and above the diagonal (tile x tile, clipped at the edge) are
+        computed; the update product B X is computed whole."""
+        tot = 0.0
+        for s in self.muon_shapes:
+            batch = int(np.prod(s[:-2])) if len(s) > 2 else 1
+            a, b = min(s[-2], s[-1]), max(s[-2], s[-1])
+            edges = [min(tile, a - i) for i in range(0, a, tile)]
+            upper = sum(edges[i] * edges[j] for i in range(len(edges)) for j in range(i, len(edges)))
+            tot += batch * self.ns_steps * (2.0 * upper * b + 2.0 * upper * a + 2.0 * a * a * b)
+        return tot
+
     def state_bytes(self) -> float:
         """Algorithmic HBM bytes per step: Muon 20 B/element (bf16 grad read twice, fp32 momentum and param read
         and written), AdamW 28 B/element (bf16 grad twice, fp32 param, exp_avg, exp_avg_sq read and written)."""

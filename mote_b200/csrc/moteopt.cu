@@ -259,7 +259,7 @@ struct MapKey {
   }
 };
 struct MapSet {
-  CUtensorMap xk[2], xmn[2], ak, bk, xe[2], ae, be;
+  CUtensorMap xk[2], xmn[2], ak, bk, amn, bmn, xe[2], ae, be;
 };
 std::mutex g_map_mu;
 std::map<MapKey, MapSet> g_maps;
@@ -285,6 +285,8 @@ int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
   }
   MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::BM));
   MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::BM));
+  MO_TRY(make_map(&s.amn, ws + g.off_a, g.m, g.m, cnt, 64, ns::BK));
+  MO_TRY(make_map(&s.bmn, ws + g.off_b, g.m, g.m, cnt, 64, ns::BK));
   for (int k = 0; k < 2; ++k)
     MO_TRY(make_map(&s.xe[k], x[k], g.n, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
   MO_TRY(make_map(&s.ae, ws + g.off_a, g.m, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
@@ -578,6 +580,8 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
       G.xmn[1] = ms.xmn[1];
       G.ak = ms.ak;
       G.bk = ms.bk;
+      G.amn = ms.amn;
+      G.bmn = ms.bmn;
       G.xe[0] = ms.xe[0];
       G.xe[1] = ms.xe[1];
       G.ae = ms.ae;
@@ -604,9 +608,12 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
         for (int gi = 0; gi < Lh.n_groups; ++gi) {   // 256 x 256 tiles, one per CTA pair
           const ns::Group& G = Lh.g[gi];
           const int out_cols = ph == ns::kUpdate ? G.n : G.m;
-          Lh.tiles_m[gi] = static_cast<int>(cdiv(G.m, ns2::TM));
+          const int T = static_cast<int>(cdiv(G.m, ns2::TM));
+          Lh.tiles_m[gi] = T;
           Lh.tiles_n[gi] = static_cast<int>(cdiv(out_cols, ns2::TN));
-          Lh.tile_start[gi + 1] = Lh.tile_start[gi] + G.count * Lh.tiles_m[gi] * Lh.tiles_n[gi];
+          // A and B are symmetric: their phases compute the upper-triangle blocks only
+          const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
+          Lh.tile_start[gi + 1] = Lh.tile_start[gi] + G.count * per;
         }
         const int tiles = Lh.tile_start[Lh.n_groups];
         ns2::ns_phase_kernel2<<<2 * std::min(tiles, device_pairs()), ns::kThreads, ns2::kSmem2Bytes, st>>>(Lh);

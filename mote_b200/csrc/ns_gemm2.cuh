@@ -31,17 +31,42 @@ constexpr int STAGE2_BYTES = A2_BYTES + B2_BYTES;
 constexpr int EPI2_BYTES = kEpiWarps * 2 * EPI_BUF_BYTES;   // per warp: two subtiles, operand in and result out
 constexpr int kSmem2Bytes = STAGES2 * STAGE2_BYTES + EPI2_BYTES + 1024 + 512;
 
+// Tile t of a launch -> (group, matrix, row block, column block). A = X X^T and B = bA + cA^2 are symmetric, so the
+// Gram and polynomial phases compute only the blocks on and above the diagonal (tiles_m (tiles_m + 1) / 2 per
+// matrix, row-major over the upper triangle); a block below it is read as the transpose of its mirror (see
+// operand_mn).
 __device__ __forceinline__ void decode_tile2(const Launch& L, int t, int& gi, int& b, int& i0, int& j0) {
   gi = 0;
   while (gi + 1 < L.n_groups && t >= L.tile_start[gi + 1]) ++gi;
   const int local = t - L.tile_start[gi];
-  const int per = L.tiles_m[gi] * L.tiles_n[gi];
-  b = local / per;
-  const int r = local - b * per;
-  const int ti = r / L.tiles_n[gi];
-  const int tj = r - ti * L.tiles_n[gi];
+  const int T = L.tiles_m[gi];
+  int ti, tj;
+  if (L.phase == kUpdate) {
+    const int per = T * L.tiles_n[gi];
+    b = local / per;
+    const int r = local - b * per;
+    ti = r / L.tiles_n[gi];
+    tj = r - ti * L.tiles_n[gi];
+  } else {
+    const int per = T * (T + 1) / 2;
+    b = local / per;
+    int r = local - b * per;
+    ti = 0;
+    while (r >= T - ti) { r -= T - ti; ++ti; }
+    tj = ti + r;
+  }
   i0 = ti * TM;
   j0 = tj * TN;
+}
+
+// Whether k-block kb of tile (i0, j0) reads its A operand (rows i) and its B operand (rows j, or X for kUpdate) in
+// MN-major form. In kPoly (A A) and kUpdate (B X) the row block i of the symmetric left factor is stored only at and
+// above the diagonal: columns k in a block left of i are read from the mirror block (k, i) as a transposed box.
+// kPoly's right factor is A again (rows j); kUpdate's is X, always MN-major.
+__device__ __forceinline__ void operand_mn(const Launch& L, int i0, int j0, int kb, bool& a_mn, bool& b_mn) {
+  const int kt = (kb * BK) / TM;
+  a_mn = L.phase != kGram && kt < i0 / TM;
+  b_mn = L.phase == kUpdate || (L.phase == kPoly && kt < j0 / TN);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -59,18 +84,28 @@ __device__ __forceinline__ void producer2(const Launch& L, uint32_t rank, uint8_
     const Group& G = L.g[gi];
     const int nk = (phase_k(L, G) + BK - 1) / BK;
     const CUtensorMap* amap = L.phase == kGram ? &G.xk[L.src] : (L.phase == kPoly ? &G.ak : &G.bk);
+    const CUtensorMap* amap_mn = L.phase == kPoly ? &G.amn : &G.bmn;
     const CUtensorMap* bmap = L.phase == kGram ? &G.xk[L.src] : (L.phase == kPoly ? &G.ak : &G.xmn[L.src]);
+    const CUtensorMap* bmap_mn = L.phase == kPoly ? &G.amn : &G.xmn[L.src];
     const int ia = i0 + HM * static_cast<int>(rank), jb = j0 + (TN / 2) * static_cast<int>(rank);
     for (int kb = 0; kb < nk; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, ctx)) { ok = false; break; }
       const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
       if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE2_BYTES);
       const int k0 = kb * BK;
-      tma_load_3d_pair(sa + stage * A2_BYTES, amap, bar, k0, ia, b);
+      bool a_mn, b_mn;
+      operand_mn(L, i0, j0, kb, a_mn, b_mn);
+      uint8_t* dsta = sa + stage * A2_BYTES;
+      if (a_mn) {   // rows ia..ia+127 of the block left of the diagonal = columns of the stored mirror block
+        tma_load_3d_pair(dsta, amap_mn, bar, ia, k0, b);
+        tma_load_3d_pair(dsta + BK * 64 * 2, amap_mn, bar, ia + 64, k0, b);
+      } else {
+        tma_load_3d_pair(dsta, amap, bar, k0, ia, b);
+      }
       uint8_t* dst = sb + stage * B2_BYTES;
-      if (L.phase == kUpdate) {   // X[k0:k0+64, jb:jb+128] as two 64 x 64 boxes, 128-byte swizzled along j
-        tma_load_3d_pair(dst, bmap, bar, jb, k0, b);
-        tma_load_3d_pair(dst + BK * 64 * 2, bmap, bar, jb + 64, k0, b);
+      if (b_mn) {   // [k0:k0+64, jb:jb+128] as two 64 x 64 boxes, 128-byte swizzled along j
+        tma_load_3d_pair(dst, bmap_mn, bar, jb, k0, b);
+        tma_load_3d_pair(dst + BK * 64 * 2, bmap_mn, bar, jb + 64, k0, b);
       } else {
         tma_load_3d_pair(dst, bmap, bar, k0, jb, b);
       }
@@ -96,8 +131,6 @@ __device__ __forceinline__ void mma2(const Launch& L, uint8_t* sa, uint8_t* sb, 
                                      const WaitCtx& ctx) {
   const int total = L.tile_start[L.n_groups];
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const bool mn_b = L.phase == kUpdate;
-  const uint32_t idesc = idesc_bf16_f32(TM, TN, false, mn_b);
   int stage = 0;
   uint32_t phase = 0;
   int local = 0;
@@ -117,10 +150,13 @@ __device__ __forceinline__ void mma2(const Launch& L, uint8_t* sa, uint8_t* sb, 
       tc_fence_after();
       const uint32_t a0 = smem_u32(sa + stage * A2_BYTES);
       const uint32_t b0 = smem_u32(sb + stage * B2_BYTES);
+      bool a_mn, b_mn;
+      operand_mn(L, i0, j0, kb, a_mn, b_mn);
+      const uint32_t idesc = idesc_bf16_f32(TM, TN, a_mn, b_mn);
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t adesc = sdesc_sw128(a0 + kk * 32, 16, 1024);
-        const uint64_t bdesc = mn_b ? sdesc_sw128(b0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
+        const uint64_t adesc = a_mn ? sdesc_sw128(a0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(a0 + kk * 32, 16, 1024);
+        const uint64_t bdesc = b_mn ? sdesc_sw128(b0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
         umma_bf16_pair(d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
       }
       umma_commit_pair_both(&empty[stage]);   // both CTAs may refill the stage once these MMAs have read it
@@ -296,9 +332,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_phas
     for (int g = 0; g < L.n_groups; ++g) {
       const Group& G = L.g[g];
       if (L.phase == kGram) { tma_prefetch_desc(&G.xk[L.src]); tma_prefetch_desc(&G.ae); }
-      if (L.phase == kPoly) { tma_prefetch_desc(&G.ak); tma_prefetch_desc(&G.be); }
+      if (L.phase == kPoly) { tma_prefetch_desc(&G.ak); tma_prefetch_desc(&G.amn); tma_prefetch_desc(&G.be); }
       if (L.phase == kUpdate) {
-        tma_prefetch_desc(&G.bk); tma_prefetch_desc(&G.xmn[L.src]);
+        tma_prefetch_desc(&G.bk); tma_prefetch_desc(&G.bmn); tma_prefetch_desc(&G.xmn[L.src]);
         tma_prefetch_desc(&G.xe[0]); tma_prefetch_desc(&G.xe[1]);
       }
     }

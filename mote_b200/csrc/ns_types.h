@@ -40,6 +40,8 @@ struct alignas(64) Group {
   CUtensorMap xmn[2];   // X ping/pong as an MN-major operand: dims {n, m, count}, box {64, 64, 1}
   CUtensorMap ak;       // A: dims {m, m, count}, box {64, 128, 1}
   CUtensorMap bk;       // B: dims {m, m, count}, box {64, 128, 1}
+  CUtensorMap amn;      // A as an MN-major operand (a stored upper block read transposed): box {64, 64, 1}
+  CUtensorMap bmn;      // B likewise
   CUtensorMap xe[2];    // epilogue views (box {32, 32, 1}, 64-byte swizzle): X ping/pong
   CUtensorMap ae;       //   A
   CUtensorMap be;       //   B
@@ -73,6 +75,8 @@ struct Launch {
   int tiles_n[kMaxGroups];
   int* status;
 };
+// passed by value as a __grid_constant__ kernel parameter: within the 32764-byte parameter limit of sm_70+ launches
+static_assert(sizeof(Launch) <= 32764, "Launch exceeds the kernel parameter space");
 
 }  // namespace ns
 }  // namespace moteopt

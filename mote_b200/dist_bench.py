@@ -130,7 +130,7 @@ def run(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         e2e_local = h0.elapsed_time(h1) / e2e_steps
 
-        my_flops = sum(w.ns_steps * _ns_flops(w.muon_shapes[i]) for i in st.mine)
+        my_flops = sum(w.ns_steps * _ns_flops_issued(w.muon_shapes[i]) for i in st.mine)
         vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops], dtype=torch.float64, device=dev)
         allv = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(allv, vals)
@@ -168,12 +168,9 @@ def run(args, rank: int, world: int, local_rank: int):
         dist.destroy_process_group()
 
 
-def _ns_flops(shape) -> float:
-    batch = 1
-    for d in shape[:-2]:
-        batch *= int(d)
-    m, n = sorted((int(shape[-2]), int(shape[-1])))
-    return batch * (4.0 * m * m * n + 2.0 * m ** 3)
+def _ns_flops_issued(shape) -> float:
+    """Tensor-core FLOPs of one Newton-Schulz iteration of one parameter (upper-triangle Gram / A A blocks)."""
+    return configs.Workload("one", [tuple(shape)], [], [], ns_steps=1).ns_flops_issued()
 
 
 if __name__ == "__main__":

@@ -66,7 +66,8 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
     _status_ok(dev)
 
 
-@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (2, 3072, 768), (2, 512, 2048), (1, 1000, 264)])
+@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (2, 3072, 768), (2, 512, 2048), (1, 1000, 264),
+                                   (1, 1100, 1300)])
 def test_newton_schulz_benchmark_shapes(dev, shape):
     u = ns_input(shape, 123)
     for steps, tol in ((1, 1e-3), (5, 4e-2)):
