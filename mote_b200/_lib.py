@@ -21,7 +21,7 @@ STATUS_NONFINITE = 4
 # every exported symbol of include/moteopt.h
 EXPORTS = (
     "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count",
-    "moteopt_profile_ns_events",
+    "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_with_coef",
     "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
@@ -71,6 +71,7 @@ def _load() -> C.CDLL:
         "moteopt_last_error": (C.c_char_p, []),
         "moteopt_launch_count": (C.c_ulonglong, []),
         "moteopt_profile_ns_events": (i32, [vp, vp]),
+        "moteopt_ns_set_persistent": (i32, [i32]),
         "moteopt_read_status": (i32, [vp, C.POINTER(C.c_int), f32p, i32, vp]),
         "moteopt_optimizer_step_workspace_size": (sz, [C.POINTER(MuonParam), i32, i32, C.POINTER(AdamWTensor), i32]),
         "moteopt_optimizer_step": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(AdamWTensor), i32,

@@ -16,7 +16,6 @@
 #include "moteopt.h"
 #include "mt_kernels.cuh"
 #include "ns_gemm.cuh"
-#include "ns_gemm2.cuh"
 
 using namespace moteopt;
 
@@ -36,6 +35,7 @@ int fail(int code, const std::string& msg) {
   } while (0)
 
 std::atomic<unsigned long long> g_launches{0};
+std::atomic<int> g_ns_persistent{1};   // Newton-Schulz launch mode (moteopt_ns_set_persistent)
 thread_local cudaEvent_t t_ns_ev[2] = {nullptr, nullptr};
 
 #define MO_LAUNCHED(what)                                                                      \
@@ -86,12 +86,11 @@ int device_setup(int* sms) {
     if (major != 10 || minor != 0)
       return fail(MOTEOPT_ERR_DEVICE, "libmoteopt is built for sm_100a (B200); device " + std::to_string(dev) +
                                           " is sm_" + std::to_string(major) + std::to_string(minor));
-    MO_CUDA(cudaFuncSetAttribute(ns::ns_phase_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
-    MO_CUDA(cudaFuncSetAttribute(ns2::ns_phase_kernel2, cudaFuncAttributeMaxDynamicSharedMemorySize, ns2::kSmem2Bytes));
+    MO_CUDA(cudaFuncSetAttribute(ns::ns_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (count / 2), 1, 1);
     cfg.blockDim = dim3(ns::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = ns2::kSmem2Bytes;
+    cfg.dynamicSmemBytes = ns::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -100,7 +99,7 @@ int device_setup(int* sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters, ns2::ns_phase_kernel2, &cfg));
+    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters, ns::ns_gemm_kernel, &cfg));
     if (clusters < 1) return fail(MOTEOPT_ERR_DEVICE, "the 2-CTA Newton-Schulz kernel cannot be resident on this device");
     d.sms = count;
     d.pairs = clusters;
@@ -170,7 +169,7 @@ struct Layout {
   std::vector<GroupPlan> groups;          // Newton-Schulz shape groups, in launch order
   std::vector<int> mat_chunk_start;       // per matrix (group-major order): sum-of-squares chunk prefix
   std::vector<int> norm_tensor_chunk_start;
-  size_t off_norm = 0, off_mom = 0, off_den = 0, bytes = 0;
+  size_t off_norm = 0, off_mom = 0, off_den = 0, off_done = 0, bytes = 0;
 };
 
 constexpr int kMaxMatsPerGroup = ns::kMaxApply;
@@ -231,7 +230,9 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
   L->off_mom = off;
   off = align_up(off + 4 * static_cast<size_t>(L->mat_chunk_start.back()), 256);
   L->off_den = off;
-  off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 1024);
+  off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 256);
+  L->off_done = off;   // persistent Newton-Schulz: per matrix of a launch set and phase, completion arrivals
+  off = align_up(off + 4 * 3 * static_cast<size_t>(ns::kMaxApply), 1024);
   for (GroupPlan& g : L->groups) {
     const size_t cnt = g.mats.size();
     const size_t xb = cnt * g.m * g.n * 2, ab = cnt * g.m * g.m * 2;
@@ -280,11 +281,11 @@ int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
   std::memset(&s, 0, sizeof(s));
   void* x[2] = {ws + g.off_x0, ws + g.off_x1};
   for (int k = 0; k < 2; ++k) {
-    MO_TRY(make_map(&s.xk[k], x[k], g.n, g.m, cnt, ns::BK, ns::BM));
+    MO_TRY(make_map(&s.xk[k], x[k], g.n, g.m, cnt, ns::BK, ns::HM));
     MO_TRY(make_map(&s.xmn[k], x[k], g.n, g.m, cnt, 64, ns::BK));
   }
-  MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::BM));
-  MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::BM));
+  MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::HM));
+  MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::HM));
   MO_TRY(make_map(&s.amn, ws + g.off_a, g.m, g.m, cnt, 64, ns::BK));
   MO_TRY(make_map(&s.bmn, ws + g.off_b, g.m, g.m, cnt, 64, ns::BK));
   for (int k = 0; k < 2; ++k)
@@ -564,6 +565,7 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
     if (b < L.groups.size()) sets.emplace_back(b, L.groups.size());
   }
   static thread_local ns::Launch Lh;   // ~20 KB: kept off the stack
+  int* done = reinterpret_cast<int*>(ws + L.off_done);
   for (const auto& set : sets) {
     std::memset(&Lh, 0, sizeof(Lh));
     Lh.n_groups = static_cast<int>(set.second - set.first);
@@ -599,29 +601,56 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
       G.transposed = g.transposed;
       first += G.count;
     }
-    int src = 0;
-    for (int it = 0; it < steps; ++it) {
-      for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
-        Lh.phase = ph;
-        Lh.src = src;
-        Lh.tile_start[0] = 0;
-        for (int gi = 0; gi < Lh.n_groups; ++gi) {   // 256 x 256 tiles, one per CTA pair
-          const ns::Group& G = Lh.g[gi];
-          const int out_cols = ph == ns::kUpdate ? G.n : G.m;
-          const int T = static_cast<int>(cdiv(G.m, ns2::TM));
-          Lh.tiles_m[gi] = T;
-          Lh.tiles_n[gi] = static_cast<int>(cdiv(out_cols, ns2::TN));
-          // A and B are symmetric: their phases compute the upper-triangle blocks only
-          const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
-          Lh.tile_start[gi + 1] = Lh.tile_start[gi] + G.count * per;
+    // the tile sequence [iteration][phase][group][matrix][tile]: 256 x 256 tiles, one per CTA pair; A and B are
+    // symmetric, so their phases have the upper-triangle blocks only
+    Lh.src0 = 0;
+    Lh.per_iter = 0;
+    for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
+      Lh.tile_start[ph][0] = 0;
+      for (int gi = 0; gi < Lh.n_groups; ++gi) {
+        const ns::Group& G = Lh.g[gi];
+        const int T = static_cast<int>(cdiv(G.m, ns::TM));
+        Lh.tiles_m[gi] = T;
+        Lh.tiles_n[gi] = static_cast<int>(cdiv(G.n, ns::TN));
+        const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
+        Lh.tile_start[ph][gi + 1] = Lh.tile_start[ph][gi] + G.count * per;
+      }
+      Lh.phase_tiles[ph] = Lh.tile_start[ph][Lh.n_groups];
+      Lh.per_iter += Lh.phase_tiles[ph];
+    }
+    const int pairs = device_pairs();
+    if (g_ns_persistent.load(std::memory_order_relaxed)) {
+      // one cooperative launch for every iteration; the completion counters start at zero
+      MO_CUDA(cudaMemsetAsync(done, 0, sizeof(int) * 3 * static_cast<size_t>(first), st));
+      Lh.done = done;
+      Lh.t_begin = 0;
+      Lh.t_end = steps * Lh.per_iter;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * std::min(Lh.t_end, pairs), 1, 1);
+      cfg.blockDim = dim3(ns::kThreads, 1, 1);
+      cfg.dynamicSmemBytes = ns::kSmemBytes;
+      cfg.stream = st;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      MO_CUDA(cudaLaunchKernelEx(&cfg, ns::ns_gemm_kernel, Lh));
+      MO_LAUNCHED("ns_gemm_kernel (persistent)");
+    } else {
+      Lh.done = nullptr;
+      for (int it = 0; it < steps; ++it) {
+        int t0 = it * Lh.per_iter;
+        for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
+          Lh.t_begin = t0;
+          Lh.t_end = t0 + Lh.phase_tiles[ph];
+          t0 = Lh.t_end;
+          ns::ns_gemm_kernel<<<2 * std::min(Lh.phase_tiles[ph], pairs), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
+          MO_LAUNCHED("ns_gemm_kernel");
         }
-        const int tiles = Lh.tile_start[Lh.n_groups];
-        ns2::ns_phase_kernel2<<<2 * std::min(tiles, device_pairs()), ns::kThreads, ns2::kSmem2Bytes, st>>>(Lh);
-        MO_LAUNCHED("ns_phase_kernel2");
-        if (ph == ns::kUpdate) src ^= 1;
       }
     }
-    *final_src = src;
+    *final_src = steps & 1;
   }
   return MOTEOPT_OK;
 }
@@ -766,6 +795,8 @@ int moteopt_profile_ns_events(void* start_event, void* end_event) {
 }
 
 const char* moteopt_last_error(void) { return t_err.c_str(); }
+
+int moteopt_ns_set_persistent(int enable) { return g_ns_persistent.exchange(enable ? 1 : 0); }
 
 int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream) {
   if (workspace == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");

@@ -1,17 +1,37 @@
-// Newton-Schulz phase kernel for sm_100a (tcgen05 + TMEM + TMA).
+// Newton-Schulz GEMM kernel for sm_100a: tcgen05.mma on CTA pairs, accumulators in TMEM, operands by TMA.
 //
-// One launch runs one phase of one Newton-Schulz iteration (mote/train/muon.py:37-40) for every matrix of every
-// shape group at once:
-//   kGram:   A  = bf16(X X^T)
-//   kPoly:   B  = bf16( bf16(b*A) + bf16(c * bf16(A A)) )          (A is symmetric, so A A = A A^T)
-//   kUpdate: X' = bf16( bf16(a*X) + bf16(B X) )
-// The rounding points are the reference's: every torch op on a bf16 tensor rounds its fp32 result to bf16.
+// The quintic iteration of mote/train/muon.py:37-40 for each matrix X (m x n, m <= n after the transpose rule):
+//   kGram:   A  = bf16(X X^T)                                   (m x m, K = n)
+//   kPoly:   B  = bf16( bf16(b*A) + bf16(c * bf16(A A)) )       (m x m, K = m)
+//   kUpdate: X' = bf16( bf16(a*X) + bf16(B X) )                 (m x n, K = m)
+// The rounding points are the reference's: every torch op on a bf16 tensor rounds its fp32 result to bf16. A and B
+// are symmetric, so kGram and kPoly compute only the 256 x 256 blocks on and above the diagonal; a block below it is
+// read as the transpose of its mirror block (an MN-major operand).
 //
-// Structure: a persistent grid (one CTA per SM, 197 KB of shared memory) walks a static tile list. Warp 0 streams
-// 128x64 A tiles and 256x64 B tiles with TMA into a 4-stage ring; one thread of warp 1 issues tcgen05.mma
-// (M=128, N=256, K=16) into one of two TMEM accumulators; warps 2-5 drain the other accumulator (tcgen05.ld),
-// apply the phase's polynomial in fp32 with bf16 rounding and store. The B operand of kUpdate (X, indexed [k][j])
-// is consumed MN-major straight from the row-major iterate; every other operand is K-major.
+// Work. A launch walks the tile sequence [iteration][phase][group][matrix][tile] over [t_begin, t_end); CTA pair p
+// takes tiles t_begin + p, t_begin + p + P, ... in order (P pairs). Two launch modes share the code:
+//   - one launch per phase (`done` null): the kernel boundary orders the phases;
+//   - one cooperative launch for all iterations (`done` non-null): before a tile reads a matrix's A, B or X, it waits
+//     until every tile that writes it has completed, counted per matrix and phase in `done` (release adds after the
+//     TMA stores complete, acquire loads before the reads). Every dependency points to an earlier tile of the
+//     sequence, each pair walks its tiles in order and all CTAs are co-resident, so the earliest unfinished tile can
+//     always proceed; the phases of different matrices overlap and there is one launch ramp and one tail in all.
+//     Overwrites are safe by the same chain: a tile that rewrites A, B or X[s] waits (through its dependency) for the
+//     tiles that read the previous contents.
+//
+// Per CTA pair (a cluster of two): the pair computes a 256 x 256 output tile with tcgen05.mma.cta_group::2 (M = 256,
+// N = 256, K = 16). CTA r loads rows [128r, 128r+128) of the A operand and rows [128r, 128r+128) of the B operand
+// into its own shared memory; the leader CTA (r = 0) issues the MMAs, which read both CTAs' tiles and accumulate
+// output rows [128r, 128r+128) into CTA r's TMEM. A pipeline stage is 32 KB per CTA, so six stages fit beside the
+// 32 KB epilogue. Roles per CTA: warp 0 lane 0 is the TMA producer, warp 1 lane 0 the MMA issuer (leader only) and
+// TMEM owner, warps 2-9 the epilogue (two accumulators in TMEM: the MMA fills one while the epilogue drains the other).
+//
+// Synchronisation (every wait is bounded, as in ptx.cuh):
+//   full[s]   leader only: the leader's producer arrives with the byte count of both CTAs' loads; both CTAs' TMA
+//             loads (".cta_group::2" form) complete their bytes on it.
+//   empty[s]  both CTAs: the leader's MMA commit arrives on it in both CTAs once the stage has been read.
+//   tfull[a]  both CTAs: the leader's commit after the last k-block of a tile.
+//   tempty[a] leader only: one arrival per epilogue warp of both CTAs (the peer's arrive remotely).
 #pragma once
 
 #include "ns_types.h"
@@ -22,103 +42,178 @@ namespace ns {
 
 constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;   // mote/train/muon.py:31
 
-__device__ __forceinline__ void decode_tile(const Launch& L, int t, int& gi, int& b, int& i0, int& j0) {
-  gi = 0;
-  while (gi + 1 < L.n_groups && t >= L.tile_start[gi + 1]) ++gi;
-  const int local = t - L.tile_start[gi];
-  const int per = L.tiles_m[gi] * L.tiles_n[gi];
-  b = local / per;
-  const int r = local - b * per;
-  const int ti = r / L.tiles_n[gi];
-  const int tj = r - ti * L.tiles_n[gi];
-  i0 = ti * BM;
-  j0 = tj * BN;
+// ---------------------------------------------------------------------------------------------------------------
+struct Tile {
+  int it, phase, src;   // iteration, phase, X buffer read by this iteration
+  int gi, b;            // group, matrix within the group
+  int i0, j0;           // output tile origin
+};
+
+__device__ __forceinline__ int tiles_per_matrix(const Launch& L, int gi, int phase) {
+  const int T = L.tiles_m[gi];
+  return phase == kUpdate ? T * L.tiles_n[gi] : T * (T + 1) / 2;
 }
 
-__device__ __forceinline__ int phase_k(const Launch& L, const Group& G) { return L.phase == kGram ? G.n : G.m; }
+__device__ __forceinline__ Tile decode_tile(const Launch& L, int t) {
+  Tile x;
+  x.it = t / L.per_iter;
+  int r = t - x.it * L.per_iter;
+  x.phase = 0;
+  while (x.phase < 2 && r >= L.phase_tiles[x.phase]) {
+    r -= L.phase_tiles[x.phase];
+    ++x.phase;
+  }
+  x.src = (L.src0 + x.it) & 1;
+  const int* ts = L.tile_start[x.phase];
+  int gi = 0;
+  while (gi + 1 < L.n_groups && r >= ts[gi + 1]) ++gi;
+  r -= ts[gi];
+  const int T = L.tiles_m[gi];
+  int ti, tj;
+  if (x.phase == kUpdate) {
+    const int per = T * L.tiles_n[gi];
+    x.b = r / per;
+    r -= x.b * per;
+    ti = r / L.tiles_n[gi];
+    tj = r - ti * L.tiles_n[gi];
+  } else {   // upper-triangle blocks, row-major
+    const int per = T * (T + 1) / 2;
+    x.b = r / per;
+    r -= x.b * per;
+    ti = 0;
+    while (r >= T - ti) {
+      r -= T - ti;
+      ++ti;
+    }
+    tj = ti + r;
+  }
+  x.gi = gi;
+  x.i0 = ti * TM;
+  x.j0 = tj * TN;
+  return x;
+}
+
+__device__ __forceinline__ int phase_k(int phase, const Group& G) { return phase == kGram ? G.n : G.m; }
+
+// Whether k-block kb of tile x reads its A operand (rows i) and its B operand (rows j, or X for kUpdate) MN-major.
+// In kPoly (A A) and kUpdate (B X) the left factor is stored only at and above the diagonal: columns k in a block
+// left of row block i come from the mirror block (k, i) as a transposed box. kPoly's right factor is A again (rows
+// j); kUpdate's is X, always MN-major.
+__device__ __forceinline__ void operand_mn(const Tile& x, int kb, bool& a_mn, bool& b_mn) {
+  const int kt = (kb * BK) / TM;
+  a_mn = x.phase != kGram && kt < x.i0 / TM;
+  b_mn = x.phase == kUpdate || (x.phase == kPoly && kt < x.j0 / TN);
+}
+
+// Persistent mode: the completion counts tile x must see before reading. kGram reads X[src] (written by the previous
+// iteration's kUpdate), kPoly reads A (this iteration's kGram), kUpdate reads B (kPoly) and X[src].
+__device__ __forceinline__ bool wait_inputs(const Launch& L, const Tile& x, const WaitCtx& ctx) {
+  const int mat = L.g[x.gi].first + x.b;
+  const int* done = L.done + mat * 3;
+  if (x.phase != kGram &&
+      !wait_counter(done + x.phase - 1, (x.it + 1) * tiles_per_matrix(L, x.gi, x.phase - 1) * kArrivalsPerTile, ctx))
+    return false;
+  if (x.phase != kPoly && x.it > 0 &&
+      !wait_counter(done + kUpdate, x.it * tiles_per_matrix(L, x.gi, kUpdate) * kArrivalsPerTile, ctx))
+    return false;
+  return true;
+}
 
 // ---------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void run_producer(const Launch& L, uint8_t* sa, uint8_t* sb, uint64_t* full, uint64_t* empty,
-                                             const WaitCtx& ctx) {
-  const int total = L.tile_start[L.n_groups];
+__device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t* sa, uint8_t* sb, uint64_t* full,
+                                         uint64_t* empty, const WaitCtx& ctx) {
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   int stage = 0;
   uint32_t phase = 0;
   long issued = 0;
   bool ok = true;
-  for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-    int gi, b, i0, j0;
-    decode_tile(L, t, gi, b, i0, j0);
-    const Group& G = L.g[gi];
-    const int nk = (phase_k(L, G) + BK - 1) / BK;
-    const CUtensorMap* amap = L.phase == kGram ? &G.xk[L.src] : (L.phase == kPoly ? &G.ak : &G.bk);
-    const CUtensorMap* bmap = L.phase == kGram ? &G.xk[L.src] : (L.phase == kPoly ? &G.ak : &G.xmn[L.src]);
+  for (int t = L.t_begin + pair; t < L.t_end && ok; t += npairs) {
+    const Tile x = decode_tile(L, t);
+    const Group& G = L.g[x.gi];
+    if (L.done != nullptr) {
+      if (!wait_inputs(L, x, ctx)) break;
+      fence_proxy_async_global();   // the TMA loads below observe the data the counters released
+    }
+    const int nk = (phase_k(x.phase, G) + BK - 1) / BK;
+    const CUtensorMap* amap = x.phase == kGram ? &G.xk[x.src] : (x.phase == kPoly ? &G.ak : &G.bk);
+    const CUtensorMap* amap_mn = x.phase == kPoly ? &G.amn : &G.bmn;
+    const CUtensorMap* bmap = x.phase == kGram ? &G.xk[x.src] : &G.ak;
+    const CUtensorMap* bmap_mn = x.phase == kPoly ? &G.amn : &G.xmn[x.src];
+    const int ia = x.i0 + HM * static_cast<int>(rank), jb = x.j0 + (TN / 2) * static_cast<int>(rank);
     for (int kb = 0; kb < nk; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, ctx)) { ok = false; break; }
-      mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+      const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+      if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
       const int k0 = kb * BK;
-      tma_load_3d(sa + stage * A_BYTES, amap, &full[stage], k0, i0, b);
-      uint8_t* dst = sb + stage * B_BYTES;
-      if (L.phase == kUpdate) {
-        // X[k0:k0+64, j0:j0+256] as four 64(k) x 64(j) boxes, each 128-byte swizzled along j
-#pragma unroll
-        for (int q = 0; q < 4; ++q) tma_load_3d(dst + q * (BK * 64 * 2), bmap, &full[stage], j0 + 64 * q, k0, b);
+      bool a_mn, b_mn;
+      operand_mn(x, kb, a_mn, b_mn);
+      uint8_t* dsta = sa + stage * A_BYTES;
+      if (a_mn) {   // rows ia..ia+127 of a block left of the diagonal = columns of the stored mirror block
+        tma_load_3d_pair(dsta, amap_mn, bar, ia, k0, x.b);
+        tma_load_3d_pair(dsta + BK * 64 * 2, amap_mn, bar, ia + 64, k0, x.b);
       } else {
-        tma_load_3d(dst, bmap, &full[stage], k0, j0, b);
-        tma_load_3d(dst + BM * BK * 2, bmap, &full[stage], k0, j0 + BM, b);
+        tma_load_3d_pair(dsta, amap, bar, k0, ia, x.b);
+      }
+      uint8_t* dstb = sb + stage * B_BYTES;
+      if (b_mn) {   // [k0:k0+64, jb:jb+128] as two 64 x 64 boxes, 128-byte swizzled along j
+        tma_load_3d_pair(dstb, bmap_mn, bar, jb, k0, x.b);
+        tma_load_3d_pair(dstb + BK * 64 * 2, bmap_mn, bar, jb + 64, k0, x.b);
+      } else {
+        tma_load_3d_pair(dstb, bmap, bar, k0, jb, x.b);
       }
       ++issued;
       if (++stage == STAGES) { stage = 0; phase ^= 1u; }
     }
   }
-  if (!ok) {
-    // unwinding: let the copies already issued land before the CTA's shared memory goes away
+  // When unwinding after a timeout, loads already issued complete on the leader's barrier; the cluster-wide barrier at
+  // the end of the kernel keeps both CTAs (and their shared memory) alive until every role has returned, and the
+  // leader's own drain below waits for its loads.
+  if (!ok && rank == 0) {
     for (int s = 0; s < STAGES; ++s) {
       if (issued <= s) break;
-      const uint32_t par = (s < stage) ? phase : (phase ^ 1u);
-      mbar_wait_drain(&full[s], par);
+      mbar_wait_drain(&full[s], (s < stage) ? phase : (phase ^ 1u));
     }
   }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-__device__ __forceinline__ void run_mma(const Launch& L, uint8_t* sa, uint8_t* sb, uint64_t* full, uint64_t* empty,
-                                        uint64_t* tfull, uint64_t* tempty, uint64_t* drain, uint32_t tmem_base,
-                                        const WaitCtx& ctx) {
-  const int total = L.tile_start[L.n_groups];
-  const bool mn_b = L.phase == kUpdate;
-  const uint32_t idesc = idesc_bf16_f32(BM, BN, false, mn_b);
+__device__ __forceinline__ void mma(const Launch& L, uint8_t* sa, uint8_t* sb, uint64_t* full, uint64_t* empty,
+                                    uint64_t* tfull, uint64_t* tempty, uint64_t* drain, uint32_t tmem_base,
+                                    const WaitCtx& ctx) {
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   int stage = 0;
   uint32_t phase = 0;
   int local = 0;
   bool ok = true;
-  for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
-    int gi, b, i0, j0;
-    decode_tile(L, t, gi, b, i0, j0);
-    const Group& G = L.g[gi];
-    const int nk = (phase_k(L, G) + BK - 1) / BK;
+  for (int t = L.t_begin + pair; t < L.t_end && ok; t += npairs, ++local) {
+    const Tile x = decode_tile(L, t);
+    const Group& G = L.g[x.gi];
+    const int nk = (phase_k(x.phase, G) + BK - 1) / BK;
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
     if (!mbar_wait(&tempty[acc], use ^ 1u, ctx)) break;
     tc_fence_after();
-    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+    const uint32_t d = tmem_base + static_cast<uint32_t>(acc * TN);
     for (int kb = 0; kb < nk; ++kb) {
       if (!mbar_wait(&full[stage], phase, ctx)) { ok = false; break; }
       tc_fence_after();
       const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
       const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+      bool a_mn, b_mn;
+      operand_mn(x, kb, a_mn, b_mn);
+      const uint32_t idesc = idesc_bf16_f32(TM, TN, a_mn, b_mn);
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t adesc = sdesc_sw128(a0 + kk * 32, 16, 1024);
-        const uint64_t bdesc = mn_b ? sdesc_sw128(b0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
-        umma_bf16(d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+        const uint64_t adesc = a_mn ? sdesc_sw128(a0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(a0 + kk * 32, 16, 1024);
+        const uint64_t bdesc = b_mn ? sdesc_sw128(b0 + kk * 16 * 128, BK * 64 * 2, 1024) : sdesc_sw128(b0 + kk * 32, 16, 1024);
+        umma_bf16_pair(d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
       }
-      umma_commit(&empty[stage]);   // frees the stage once these MMAs have read it
+      umma_commit_pair_both(&empty[stage]);   // both CTAs may refill the stage once these MMAs have read it
       if (++stage == STAGES) { stage = 0; phase ^= 1u; }
     }
-    if (ok) umma_commit(&tfull[acc]);   // accumulator complete
+    if (ok) umma_commit_pair_both(&tfull[acc]);
   }
-  // wait for every MMA this thread issued before TMEM is released
-  umma_commit(drain);
+  umma_commit_pair_local(drain);
   mbar_wait_drain(drain, 0);
 }
 
@@ -136,15 +231,17 @@ __device__ __forceinline__ uint32_t sw64(int r, int c) {
   return static_cast<uint32_t>(r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
 }
 
-// Epilogue warps 2..9: warp w reads TMEM lane quarter (w % 4), i.e. tile rows [32q, 32q+32), and owns columns
-// [128h, 128h+128) with h = (w - 2) / 4, in four 32-column chunks. Each chunk goes through one of the warp's two
-// 2 KB shared-memory subtiles: the phase's bf16 operand (A for kPoly, X for kUpdate) arrives there by TMA, each
-// thread combines its row with the accumulator and writes the result back in place, and one lane TMA-stores the
-// subtile. No per-thread global access remains, so the epilogue costs no L1 bandwidth.
-__device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, uint64_t* tempty, uint8_t* ebuf,
-                                             uint64_t* ebar, uint32_t tmem_base, const WaitCtx& ctx) {
-  constexpr int kChunks = BN / EPI_TILE / 2;
-  const int total = L.tile_start[L.n_groups];
+// The epilogue on this CTA's 128 rows of the pair tile. Warp (q, half) owns rows row0 = i0 + 128 rank + 32 q and the
+// 128 output columns of its half, in four 32 x 32 chunks; lane l owns row row0 + l. Per warp, two 2 KB subtiles
+// (64-byte swizzle): the phase's bf16 operand (A for kPoly, X for kUpdate) arrives in one by TMA, each thread combines
+// its row with the accumulator's TMEM columns and writes the result in place, one lane TMA-stores it and, once the
+// store has read it, refills it with the operand of the chunk two ahead. The accumulator release goes to the leader
+// CTA; in persistent mode each warp then waits for its stores to complete and counts the tile done for its matrix and
+// phase.
+__device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_t* tfull, uint64_t* tempty,
+                                         uint8_t* ebuf, uint64_t* ebar, uint32_t tmem_base, const WaitCtx& ctx) {
+  constexpr int kChunks = TN / EPI_TILE / 2;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ew = static_cast<int>(warp_id()) - 2;
   const int q = static_cast<int>(warp_id() & 3u);
   const int half = ew >> 2;
@@ -152,43 +249,45 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
   uint8_t* buf[2] = {ebuf + (ew * 2) * EPI_BUF_BYTES, ebuf + (ew * 2 + 1) * EPI_BUF_BYTES};
   uint64_t* bar[2] = {&ebar[ew * 2], &ebar[ew * 2 + 1]};
   uint32_t bphase[2] = {0u, 0u};
-  const bool has_aux = L.phase != kGram;
   bool ok = true;
   int local = 0;
-  for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
-    int gi, b, i0, j0;
-    decode_tile(L, t, gi, b, i0, j0);
-    const Group& G = L.g[gi];
+  for (int t = L.t_begin + pair; t < L.t_end && ok; t += npairs, ++local) {
+    const Tile x = decode_tile(L, t);
+    const Group& G = L.g[x.gi];
+    const bool has_aux = x.phase != kGram;
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
-    const int out_cols = L.phase == kUpdate ? G.n : G.m;
-    const int row0 = i0 + q * 32;
-    const bool rows_ok = row0 < G.m;   // warp-uniform: whole subtile beyond the matrix -> nothing to store
-    const int jc0 = j0 + half * (kChunks * EPI_TILE);
-    const CUtensorMap* omap = L.phase == kGram ? &G.ae : (L.phase == kPoly ? &G.be : &G.xe[L.src ^ 1]);
-    const CUtensorMap* amap = L.phase == kPoly ? &G.ae : &G.xe[L.src];
+    const int out_cols = x.phase == kUpdate ? G.n : G.m;
+    const int row0 = x.i0 + HM * static_cast<int>(rank) + q * 32;
+    const bool rows_ok = row0 < G.m;
+    const int jc0 = x.j0 + half * (kChunks * EPI_TILE);
+    const CUtensorMap* omap = x.phase == kGram ? &G.ae : (x.phase == kPoly ? &G.be : &G.xe[x.src ^ 1]);
+    const CUtensorMap* amap = x.phase == kPoly ? &G.ae : &G.xe[x.src];
     int nch = 0;
     while (nch < kChunks && jc0 + nch * EPI_TILE < out_cols) ++nch;
     const bool work = rows_ok && nch > 0;
-    // prefetch the operand subtiles of the first two chunks (the previous tile's stores must have left them)
+    int loaded = 1;
     if (lane == 0 && work) {
-      bulk_wait_read<0>();
+      bulk_wait_read<0>();   // the previous tile's stores have left both subtiles
       if (has_aux) {
-        for (int c = 0; c < 2 && c < nch; ++c) {
+        if (L.done != nullptr) {   // acquire the operand's producers (complete: the MMA operands waited for them)
+          loaded = wait_inputs(L, x, ctx) ? 1 : 0;
+          fence_proxy_async_global();
+        }
+        for (int c = 0; c < 2 && c < nch && loaded; ++c) {
           mbar_arrive_expect_tx(bar[c], EPI_BUF_BYTES);
-          tma_load_3d(buf[c], amap, bar[c], jc0 + c * EPI_TILE, row0, b);
+          tma_load_3d(buf[c], amap, bar[c], jc0 + c * EPI_TILE, row0, x.b);
         }
       }
     }
-    __syncwarp();
-    // warp-uniform outcome: the TMEM loads below are .sync.aligned
+    if (!__shfl_sync(0xffffffffu, loaded, 0)) break;
     if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], use, ctx) ? 1 : 0)) break;
     tc_fence_after();
     for (int c = 0; c < nch; ++c) {
       const int bi = c & 1;
       uint32_t r[32];
       tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                    static_cast<uint32_t>(acc * BN + half * (kChunks * EPI_TILE) + c * EPI_TILE), r);
+                    static_cast<uint32_t>(acc * TN + half * (kChunks * EPI_TILE) + c * EPI_TILE), r);
       tmem_ld_wait(r);
       if (!rows_ok) continue;
       uint8_t* row = buf[bi];
@@ -196,11 +295,11 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
         if (!__all_sync(0xffffffffu, mbar_wait(bar[bi], bphase[bi], ctx) ? 1 : 0)) { ok = false; break; }
         bphase[bi] ^= 1u;
       } else if (c >= 2) {
-        if (lane == 0) bulk_wait_read<1>();   // the store of chunk c-2 has left this buffer
+        if (lane == 0) bulk_wait_read<1>();   // the store of chunk c-2 has left this subtile
         __syncwarp();
       }
       uint32_t out[16];
-      if (L.phase == kGram) {
+      if (x.phase == kGram) {
 #pragma unroll
         for (int k = 0; k < 16; ++k) out[k] = pack_bf16x2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
       } else {
@@ -210,7 +309,7 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
           const uint4 w = *reinterpret_cast<const uint4*>(row + sw64(lane, cc));
           in[4 * cc] = w.x; in[4 * cc + 1] = w.y; in[4 * cc + 2] = w.z; in[4 * cc + 3] = w.w;
         }
-        if (L.phase == kPoly) {
+        if (x.phase == kPoly) {
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             float aa0 = __uint_as_float(r[2 * k]), aa1 = __uint_as_float(r[2 * k + 1]);
@@ -238,22 +337,33 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
       fence_async_smem();
       __syncwarp();
       if (lane == 0) {
-        tma_store_3d(omap, row, jc0 + c * EPI_TILE, row0, b);
+        tma_store_3d(omap, row, jc0 + c * EPI_TILE, row0, x.b);
         bulk_commit();
-        if (has_aux && c + 2 < nch) {   // refill this buffer with the operand of chunk c+2
+        if (has_aux && c + 2 < nch) {   // refill this subtile with the operand of chunk c+2
           bulk_wait_read<0>();
           mbar_arrive_expect_tx(bar[bi], EPI_BUF_BYTES);
-          tma_load_3d(row, amap, bar[bi], jc0 + (c + 2) * EPI_TILE, row0, b);
+          tma_load_3d(row, amap, bar[bi], jc0 + (c + 2) * EPI_TILE, row0, x.b);
         }
       }
       __syncwarp();
     }
+    if (!ok) break;
     tc_fence_before();
-    mbar_arrive(&tempty[acc]);
+    __syncwarp();
+    if (lane == 0) {
+      if (rank == 0) mbar_arrive(&tempty[acc]);   // release the accumulator to the leader's MMA: one arrival per warp
+      else mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      if (L.done != nullptr) {   // this warp's part of the tile is in global memory
+        bulk_wait<0>();
+        fence_proxy_async_global();
+        red_release_gpu_add(L.done + (G.first + x.b) * 3 + x.phase, 1);
+      }
+    }
+    __syncwarp();
   }
   if (lane == 0) {
-    bulk_wait<0>();   // stores complete before the CTA exits
-    if (!ok) {        // unwinding: operand loads still in flight land before shared memory goes away
+    bulk_wait<0>();
+    if (!ok) {
       for (int k = 0; k < 2; ++k) mbar_wait_drain(bar[k], bphase[k]);
     }
   }
@@ -261,23 +371,24 @@ __device__ __forceinline__ void run_epilogue(const Launch& L, uint64_t* tfull, u
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_constant__ Launch L) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_gemm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * A_BYTES;
-  uint8_t* ebuf = smem + STAGES * STAGE_BYTES;                        // 1024-aligned
+  uint8_t* ebuf = smem + STAGES * STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ebuf + EPI_BYTES);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint64_t* ebar = drain + 1;                                         // 2 per epilogue warp
+  uint64_t* ebar = drain + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ebar + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t warp = warp_id();
+  const uint32_t rank = cluster_ctarank();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -285,49 +396,46 @@ __global__ void __launch_bounds__(kThreads, 1) ns_phase_kernel(const __grid_cons
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps * 32);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
     }
     mbar_init(drain, 1);
     for (int e = 0; e < 2 * kEpiWarps; ++e) mbar_init(&ebar[e], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 0 && lane_id() == 0) {
-    for (int g = 0; g < L.n_groups; ++g) {
-      const Group& G = L.g[g];
-      if (L.phase == kGram) { tma_prefetch_desc(&G.xk[L.src]); tma_prefetch_desc(&G.ae); }
-      if (L.phase == kPoly) { tma_prefetch_desc(&G.ak); tma_prefetch_desc(&G.be); }
-      if (L.phase == kUpdate) {
-        tma_prefetch_desc(&G.bk); tma_prefetch_desc(&G.xmn[L.src]);
-        tma_prefetch_desc(&G.xe[0]); tma_prefetch_desc(&G.xe[1]);
-      }
-    }
+  if (warp == 0 && lane_id() < static_cast<uint32_t>(L.n_groups)) {
+    const Group& G = L.g[lane_id()];
+    const CUtensorMap* maps[] = {&G.xk[0], &G.xk[1], &G.xmn[0], &G.xmn[1], &G.ak, &G.bk, &G.amn, &G.bmn,
+                                 &G.xe[0], &G.xe[1], &G.ae, &G.be};
+#pragma unroll
+    for (int k = 0; k < 12; ++k) tma_prefetch_desc(maps[k]);
   }
+  __syncthreads();
+  cluster_sync();   // the pair's barriers exist before either CTA signals the other's
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitCtx ctx{abort_flag, L.status};
-
-  // Each role warp reconverges (__syncwarp) before the CTA-wide barrier below, which is an aligned barrier.
   if (warp == 0) {
-    if (lane_id() == 0) run_producer(L, sa, sb, full, empty, ctx);
+    if (lane_id() == 0) producer(L, rank, sa, sb, full, empty, ctx);
     __syncwarp();
   } else if (warp == 1) {
-    if (lane_id() == 0) run_mma(L, sa, sb, full, empty, tfull, tempty, drain, tmem_base, ctx);
+    if (lane_id() == 0 && rank == 0) mma(L, sa, sb, full, empty, tfull, tempty, drain, tmem_base, ctx);
     __syncwarp();
   } else {
-    run_epilogue(L, tfull, tempty, ebuf, ebar, tmem_base, ctx);
+    epilogue(L, rank, tfull, tempty, ebuf, ebar, tmem_base, ctx);
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();   // no CTA leaves while its pair still reads its shared memory or signals its barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc_pair(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(L.status, kStatusAborted);
 }

@@ -8,20 +8,21 @@
 namespace moteopt {
 namespace ns {
 
-constexpr int BM = 128;        // output rows per tile (TMEM lanes)
-constexpr int BN = 256;        // output columns per tile (TMEM columns per accumulator)
-constexpr int BK = 64;         // K per pipeline stage: one 128-byte swizzle row of bf16
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
+constexpr int TM = 256, TN = 256;   // output tile of a CTA pair (cta_group::2 MMA: M = 256, N = 256)
+constexpr int HM = 128;             // rows of the tile per CTA (its TMEM lanes), and rows of each operand it loads
+constexpr int BK = 64;              // K per pipeline stage: one 128-byte swizzle row of bf16
+constexpr int STAGES = 6;
+constexpr int A_BYTES = HM * BK * 2;          // 16 KB per CTA and stage
+constexpr int B_BYTES = (TN / 2) * BK * 2;    // 16 KB per CTA and stage
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int kEpiWarps = 8;   // two epilogue warps per TMEM lane quarter, each owning half of the columns
 constexpr int kThreads = 64 + 32 * kEpiWarps;   // warp 0: TMA producer, warp 1: MMA issuer + TMEM owner, 2-9: epilogue
 constexpr int EPI_TILE = 32;                                 // epilogue subtile: 32 rows x 32 columns, bf16
 constexpr int EPI_BUF_BYTES = EPI_TILE * EPI_TILE * 2;       // 2 KB, 64-byte swizzled
-constexpr int EPI_BYTES = kEpiWarps * 2 * EPI_BUF_BYTES;     // two buffers per epilogue warp
+constexpr int EPI_BYTES = kEpiWarps * 2 * EPI_BUF_BYTES;     // two subtiles per epilogue warp (operand in, result out)
 constexpr int kSmemBytes = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*alignment slack*/ + 512 /*barriers*/;
-constexpr uint32_t kTmemCols = 512;   // two 128 x 256 fp32 accumulators
+constexpr uint32_t kTmemCols = 512;   // two 128 x 256 fp32 accumulators per CTA
+constexpr int kArrivalsPerTile = 2 * kEpiWarps;   // completion arrivals of one pair tile (every epilogue warp)
 
 constexpr int kMaxGroups = 8;     // shape groups per launch
 constexpr int kMaxApply = 512;    // matrices per shape group
@@ -29,7 +30,7 @@ constexpr int kMaxApply = 512;    // matrices per shape group
 enum Phase : int {
   kGram = 0,     // A = X X^T                         (m x m, K = n)
   kPoly = 1,     // B = b*A + c*(A A)                 (m x m, K = m)
-  kUpdate = 2,   // X' = a*X + B X   (or the Muon apply on the last iteration)   (m x n, K = m)
+  kUpdate = 2,   // X' = a*X + B X                 (m x n, K = m)
 };
 
 // One shape group: `count` matrices that share (m, n) after the transpose rule (m <= n). Buffers are
@@ -65,14 +66,18 @@ struct MatApply {
   int has_decay;
 };
 
+// A launch walks the tile sequence [iteration][phase][group][matrix][tile] over [t_begin, t_end).
 struct Launch {
   Group g[kMaxGroups];
   int n_groups;
-  int phase;
-  int src;              // which X buffer holds the current iterate
-  int tile_start[kMaxGroups + 1];
-  int tiles_m[kMaxGroups];
-  int tiles_n[kMaxGroups];
+  int src0;                              // X buffer holding the iterate at iteration 0 (iteration i reads src0 ^ (i & 1))
+  int t_begin, t_end;
+  int per_iter;                          // tiles of one iteration, all three phases
+  int phase_tiles[3];                    // tiles of each phase in one iteration
+  int tile_start[3][kMaxGroups + 1];     // per phase: prefix over the groups
+  int tiles_m[kMaxGroups];               // row blocks of X (= both block counts of A and B)
+  int tiles_n[kMaxGroups];               // column blocks of X
+  int* done;                             // persistent mode: [matrix][phase] completion arrivals; null: one phase per launch
   int* status;
 };
 // passed by value as a __grid_constant__ kernel parameter: within the 32764-byte parameter limit of sm_70+ launches

@@ -100,6 +100,52 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Cross-CTA ordering of global data written by TMA stores (async proxy) and read by TMA loads or plain loads in
+// another CTA of the same launch. Writer: wait for its stores to complete, fence.proxy.async, then a release add on a
+// counter. Reader: acquire load of the counter, then fence.proxy.async before issuing TMA loads of the data.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// 16-byte load cached in L2 only (never a stale L1 line of data another CTA rewrote during the launch)
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Bounded wait until *counter >= target (another CTA's release adds). Gives up after the wait limit, or as soon as
+// this CTA or any other CTA of the launch has recorded a timeout.
+__device__ __forceinline__ bool wait_counter(const int* counter, int target, const WaitCtx& ctx) {
+  if (ld_acquire_gpu(counter) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu(counter) >= target) return true;
+    if ((++spins & 15u) == 0) {
+      if (*ctx.abort_smem) return false;
+      if (*reinterpret_cast<volatile int*>(ctx.status) & kStatusWaitTimeout) {
+        *ctx.abort_smem = 1;
+        return false;
+      }
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        *ctx.abort_smem = 1;
+        atomicOr(ctx.status, kStatusWaitTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // TMA: per-CTA tile loads and stores (every copy has one destination CTA)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

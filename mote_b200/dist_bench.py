@@ -151,7 +151,7 @@ def run(args, rank: int, world: int, local_rank: int):
                        else f"eager (graph capture failed: {capture_error})", "collectives":
                        "NCCL reduce-scatter (grads) + all-gather (fp32 params) + all-gather (per-rank sum of squares)",
                        "l2": "inputs larger than L2; no flush"},
-            "roofline": {"bound": "tensor", "kernel": "ns_phase_kernel2", "achieved": round(achieved, 1),
+            "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                          "traffic": None, "peak_source": f"{src} (burst bf16)", "rank": slow,
                          "ns_ms_per_step": round(ns_ms, 4)},

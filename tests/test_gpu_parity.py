@@ -78,6 +78,55 @@ def test_newton_schulz_benchmark_shapes(dev, shape):
     _status_ok(dev)
 
 
+@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (1, 1100, 1300), (3, 130, 72)])
+def test_newton_schulz_launch_modes_agree(dev, shape):
+    """One persistent cooperative launch (completion counters between phases) and one launch per phase compute
+    the same bits, for 1 and 5 iterations."""
+    from mote_b200 import _lib as L
+    from mote_b200 import ops
+    u = torch.from_numpy(ns_input(shape, 77)).to(dev)
+    prev = L.lib.moteopt_ns_set_persistent(0)
+    try:
+        a = [ops.newton_schulz(u, s) for s in (1, 5)]
+        L.lib.moteopt_ns_set_persistent(1)
+        b = [ops.newton_schulz(u, s) for s in (1, 5)]
+    finally:
+        L.lib.moteopt_ns_set_persistent(prev)
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+    _status_ok(dev)
+
+
+def test_muon_step_many_groups_launch_modes_agree(dev):
+    """More shape groups than one launch holds (8) and a 600-matrix stack (groups of <= 512): several launch sets,
+    each with its own counters, in both modes."""
+    from mote_b200 import _lib as L
+    from mote_b200.functional import MuonItem, muon_step
+    shapes = [(64, 64), (64, 96), (96, 64), (128, 64), (64, 128), (200, 72), (72, 200), (256, 256), (40, 300),
+              (600, 32, 32), (3, 520, 264)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(5)
+    base = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in shapes]
+    grads = [torch.randn(s, generator=gen, device=dev) * 1e-3 for s in shapes]
+    out = []
+    prev = L.lib.moteopt_ns_set_persistent(0)
+    try:
+        for mode in (0, 1):
+            L.lib.moteopt_ns_set_persistent(mode)
+            ps = [b.clone() for b in base]
+            bufs = [torch.zeros_like(b) for b in base]
+            items = [MuonItem(p, g, m, 0.02, 0.002) for p, g, m in zip(ps, grads, bufs)]
+            for _ in range(2):
+                muon_step(items, ns_steps=5)
+            torch.cuda.synchronize()
+            out.append(ps)
+    finally:
+        L.lib.moteopt_ns_set_persistent(prev)
+    for a, b in zip(*out):
+        assert torch.equal(a, b)
+    _status_ok(dev)
+
+
 def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
     from mote_b200 import ops
     u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
