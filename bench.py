@@ -283,8 +283,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                    "l2": "inputs (1.1 GB) larger than L2; no flush",
                    "launch": "CUDA graph of the whole step (mote_b200.CapturedStep)", "eager_ms_per_step": round(eager_ms, 4)},
         "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel", "achieved": round(achieved, 1),
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "traffic": traffic, "peak_source": f"{src} (burst bf16)",
+                     "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                     "frac": round(achieved / peaks["bf16_tflops_sustained"], 4), "traffic": traffic,
+                     "peak_source": f"{src} (sustained bf16: the kernel is timed inside back-to-back steps under the "
+                                    f"power cap)", "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
                      "ns_ms_per_step": round(ns_ms, 4), "ns_launches_per_step": 1,
                      "ns_tflop_per_step": round(ns_flops / 1e12, 5), "ref_tflop_per_step": round(ref_flops / 1e12, 5),
                      "ref_equivalent_tflops": round(ref_flops / (ns_ms * 1e-3) / 1e12, 1),
