@@ -115,6 +115,12 @@ int device_pairs() {
   return std::max(1, g_dev[dev].pairs);
 }
 
+int device_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  return std::max(1, g_dev[dev].sms);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // tensor maps
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -451,6 +457,48 @@ int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cf
   return MOTEOPT_OK;
 }
 
+// A matrix is iterated as it is stored when it has no more rows than columns and needs no padding: its X0 / final
+// iterate then has the parameter's own layout and the normalise / apply are flat passes.
+bool stored_as_iterated(const GroupPlan& g) { return !g.transposed && g.m == g.rows && g.n == g.cols; }
+
+int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float div, const float* coef,
+                     const float* den, int sms, cudaStream_t st) {
+  static thread_local FlatNormArgs A;
+  for (size_t s0 = 0; s0 < segs.size(); s0 += kMaxFlatSeg) {
+    const int cnt = static_cast<int>(std::min(segs.size() - s0, static_cast<size_t>(kMaxFlatSeg)));
+    std::memset(&A, 0, sizeof(A));
+    A.n = cnt;
+    A.has_div = has_div;
+    A.div = div;
+    A.coef = coef;
+    A.den = den;
+    for (int i = 0; i < cnt; ++i) {
+      A.seg[i] = segs[s0 + i];
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(A.seg[i].numel, kChunk));
+    }
+    ns_normalize_flat_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ns_normalize_flat_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cudaStream_t st) {
+  static thread_local FlatOutArgs A;
+  for (size_t s0 = 0; s0 < segs.size(); s0 += kMaxFlatSeg) {
+    const int cnt = static_cast<int>(std::min(segs.size() - s0, static_cast<size_t>(kMaxFlatSeg)));
+    std::memset(&A, 0, sizeof(A));
+    A.n = cnt;
+    A.apply = apply;
+    for (int i = 0; i < cnt; ++i) {
+      A.seg[i] = segs[s0 + i];
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(A.seg[i].numel, kChunk));
+    }
+    ns_out_flat_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ns_out_flat_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
 // The first half of the Muon update of `n` params: momentum and the Newton-Schulz normalisation X0.
 int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg, const Layout& L, char* ws,
              bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st) {
@@ -513,12 +561,35 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
     A.div = div;
     A.coef = coef;
     A.den = den;
-    for (int s0 = 0; s0 < nm; s0 += kMaxNormMat) {
-      const int cnt = std::min(nm - s0, kMaxNormMat);
+    std::vector<FlatNormSeg> flat;
+    std::vector<int> tiled;   // indices into mats of the matrices that need the tiled (transposing) kernel
+    for (int i = 0; i < nm; ++i) {
+      const Mat& m = mats[i];
+      const GroupPlan& g = *m.g;
+      if (stored_as_iterated(g)) {
+        FlatNormSeg S;
+        std::memset(&S, 0, sizeof(S));
+        S.g = gptr(m);
+        S.buf = m.p->momentum_buffer + elem_off(m);
+        S.x = ws + g.off_x0 + static_cast<size_t>(m.pos) * g.m * g.n * 2;
+        S.numel = static_cast<int64_t>(g.rows) * g.cols;
+        S.mom = static_cast<float>(m.p->momentum);
+        S.nesterov = m.p->nesterov != 0;
+        S.dtype = m.p->grad_dtype;
+        S.den_index = i;
+        flat.push_back(S);
+      } else {
+        tiled.push_back(i);
+      }
+    }
+    MO_TRY(launch_flat_norm(flat, has_div, div, coef, den, sms, st));
+    const int nt = static_cast<int>(tiled.size());
+    for (int s0 = 0; s0 < nt; s0 += kMaxNormMat) {
+      const int cnt = std::min(nt - s0, kMaxNormMat);
       A.n = cnt;
       int max_tiles = 0;
       for (int i = 0; i < cnt; ++i) {
-        const Mat& m = mats[s0 + i];
+        const Mat& m = mats[tiled[s0 + i]];
         const GroupPlan& g = *m.g;
         NormMat& M = A.mat[i];
         M.g = gptr(m);
@@ -532,7 +603,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
         M.dtype = m.p->grad_dtype;
         M.mom = static_cast<float>(m.p->momentum);
         M.nesterov = m.p->nesterov != 0;
-        M.den_index = s0 + i;
+        M.den_index = tiled[s0 + i];
         M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
         M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
         max_tiles = std::max(max_tiles, M.tiles);
@@ -679,9 +750,23 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
   std::memset(&A, 0, sizeof(A));
   A.apply = 1;
   std::vector<OutMat> all;
+  std::vector<FlatOutSeg> flat;
   size_t k = 0;
   for (const GroupPlan& g : L.groups)
     for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
+      if (stored_as_iterated(g)) {
+        FlatOutSeg S;
+        std::memset(&S, 0, sizeof(S));
+        S.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+        S.out = tab[k].p;
+        S.numel = static_cast<int64_t>(g.rows) * g.cols;
+        S.neg_lr = tab[k].neg_lr;
+        S.decay_mul = tab[k].decay_mul;
+        S.has_decay = tab[k].has_decay;
+        S.scale = tab[k].scale;
+        flat.push_back(S);
+        continue;
+      }
       OutMat M;
       std::memset(&M, 0, sizeof(M));
       M.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
@@ -700,6 +785,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       all.push_back(M);
     }
   (void)P;
+  MO_TRY(launch_flat_out(flat, 1, device_sms(), st));
   for (size_t s0 = 0; s0 < all.size(); s0 += kMaxOutMat) {
     const size_t cnt = std::min(all.size() - s0, static_cast<size_t>(kMaxOutMat));
     A.n = static_cast<int>(cnt);

@@ -86,24 +86,61 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// sum of squares of (g / div) per chunk
-__global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
-  __shared__ float red[kMtThreads / 32];
+// sum of squares of (g / div) per chunk. A full, 16-byte aligned chunk is read with all of a thread's 16-byte loads
+// issued before the first is used (128 B in flight per thread); ragged chunks fall back to element loads. The order of
+// the per-thread sum is fixed either way.
+__device__ __forceinline__ float sq_acc2_bf16(uint32_t w, const GradXform& X, float acc) {
+  const float a = X(bf16_lo(w)), b = X(bf16_hi(w));
+  acc = fmaf(a, a, acc);
+  return fmaf(b, b, acc);
+}
+__device__ __forceinline__ float sq_acc8_bf16(const uint4& v, const GradXform& X, float acc) {
+  acc = sq_acc2_bf16(v.x, X, acc);
+  acc = sq_acc2_bf16(v.y, X, acc);
+  acc = sq_acc2_bf16(v.z, X, acc);
+  return sq_acc2_bf16(v.w, X, acc);
+}
+__device__ __forceinline__ float sq_acc4_f32(const float4& v, const GradXform& X, float acc) {
+  const float a = X(v.x), b = X(v.y), d = X(v.z), e = X(v.w);
+  acc = fmaf(a, a, acc); acc = fmaf(b, b, acc); acc = fmaf(d, d, acc); acc = fmaf(e, e, acc);
+  return acc;
+}
+
+// kDiv: whether the grads are divided first; the division (a call on its slow path) is compiled only where used, so
+// the common path keeps all of its loads in registers.
+template <bool kDiv>
+__device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
   const int total = A.chunk_start[A.n];
+  const GradXform X{kDiv ? 1 : 0, A.div, 0, 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const SumsqSeg& S = A.seg[s];
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
-    const GradXform X{A.has_div, A.div, 0, 1.f};
     float acc = 0.f;
-    if (g_vec_ok(S.g, S.dtype)) {
-      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
-      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
-        const float4 g = load_g4(S.g, i, S.dtype);
-        const float a = X(g.x), b = X(g.y), d = X(g.z), e = X(g.w);
-        acc = fmaf(a, a, acc); acc = fmaf(b, b, acc); acc = fmaf(d, d, acc); acc = fmaf(e, e, acc);
+    if (end - begin == kChunk && aligned16(S.g)) {
+      if (S.dtype == kBF16) {   // 2048 16-byte vectors: 8 per thread
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(S.g) + begin);
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __ldg(p + threadIdx.x + k * kMtThreads);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = sq_acc8_bf16(v[k], X, acc);
+      } else {                  // 4096 16-byte vectors: 16 per thread, in two batches of 8
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(S.g) + begin);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float4 v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) v[k] = __ldg(p + threadIdx.x + (h * 8 + k) * kMtThreads);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc = sq_acc4_f32(v[k], X, acc);
+        }
       }
+    } else if (g_vec_ok(S.g, S.dtype)) {
+      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads)
+        acc = sq_acc4_f32(load_g4(S.g, i, S.dtype), X, acc);
       for (int64_t i = vend + threadIdx.x; i < end; i += kMtThreads) {
         const float a = X(load_g1(S.g, i, S.dtype));
         acc = fmaf(a, a, acc);
@@ -117,6 +154,12 @@ __global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant
     const float tot = block_sum(acc, red);
     if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
   }
+}
+
+__global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
+  __shared__ float red[kMtThreads / 32];
+  if (A.has_div) sumsq_chunks<true>(A, red);
+  else sumsq_chunks<false>(A, red);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -261,6 +304,8 @@ __device__ __forceinline__ float mom_elem(float g, float& buf, float mom, int ne
   return nesterov ? fmaf(mom, buf, g) : buf;
 }
 
+// A full chunk with 16-byte aligned buf (and 8/16-byte aligned g) is processed in two halves of 32 elements per
+// thread, with every load of a half issued before the first use (192 B in flight per thread for bf16 grads).
 __global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
   __shared__ float red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
@@ -273,18 +318,42 @@ __global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_
     float acc = 0.f;
     int64_t i0 = begin;
     if (aligned16(S.buf) && g_vec_ok(S.g, S.dtype)) {
-      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
-      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
-        float4 b = *reinterpret_cast<float4*>(S.buf + i);
-        const float4 g = load_g4(S.g, i, S.dtype);
-        const float u0 = mom_elem(X(g.x), b.x, S.mom, S.nesterov);
-        const float u1 = mom_elem(X(g.y), b.y, S.mom, S.nesterov);
-        const float u2 = mom_elem(X(g.z), b.z, S.mom, S.nesterov);
-        const float u3 = mom_elem(X(g.w), b.w, S.mom, S.nesterov);
-        *reinterpret_cast<float4*>(S.buf + i) = b;
-        acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+      if (end - begin == kChunk) {   // 4096 float4 of buf: 16 per thread, two halves of 8
+        float4* bp = reinterpret_cast<float4*>(S.buf + begin);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float4 b[8], g[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int j = threadIdx.x + (h * 8 + k) * kMtThreads;
+            b[k] = bp[j];
+            g[k] = load_g4(S.g, begin + 4 * static_cast<int64_t>(j), S.dtype);
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float u0 = mom_elem(X(g[k].x), b[k].x, S.mom, S.nesterov);
+            const float u1 = mom_elem(X(g[k].y), b[k].y, S.mom, S.nesterov);
+            const float u2 = mom_elem(X(g[k].z), b[k].z, S.mom, S.nesterov);
+            const float u3 = mom_elem(X(g[k].w), b[k].w, S.mom, S.nesterov);
+            bp[threadIdx.x + (h * 8 + k) * kMtThreads] = b[k];
+            acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+          }
+        }
+        i0 = end;
+      } else {
+        const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+        for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
+          float4 b = *reinterpret_cast<float4*>(S.buf + i);
+          const float4 g = load_g4(S.g, i, S.dtype);
+          const float u0 = mom_elem(X(g.x), b.x, S.mom, S.nesterov);
+          const float u1 = mom_elem(X(g.y), b.y, S.mom, S.nesterov);
+          const float u2 = mom_elem(X(g.z), b.z, S.mom, S.nesterov);
+          const float u3 = mom_elem(X(g.w), b.w, S.mom, S.nesterov);
+          *reinterpret_cast<float4*>(S.buf + i) = b;
+          acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+        }
+        i0 = vend;
       }
-      i0 = vend;
     }
     for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
       float b = S.buf[i];
@@ -309,6 +378,106 @@ __global__ void __launch_bounds__(256) mat_denom_kernel(const __grid_constant__ 
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) A.den[A.base + mat] = __fadd_rn(static_cast<float>(sqrt(s)), A.eps);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// X0 = bf16(u / (||u||_F + eps)) for a matrix iterated as it is stored: a flat pass over 16K-element chunks, four
+// quarters of 16 elements per thread with every load of a quarter issued before the first use. u is recomputed from
+// the grad and the updated momentum buffer exactly as the momentum kernel computed it (direct mode: u = G).
+__device__ __forceinline__ float flat_u(float g, float b, const FlatNormSeg& S, bool has_buf) {
+  return has_buf ? (S.nesterov ? fmaf(S.mom, b, g) : b) : g;
+}
+
+__global__ void __launch_bounds__(kMtThreads, 4) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
+  const int total = A.chunk_start[A.n];
+  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const FlatNormSeg& S = A.seg[s];
+    const SharedDivisor den = shared_divisor(A.den[S.den_index]);
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    const bool has_buf = S.buf != nullptr;
+    __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(S.x);
+    int64_t i0 = begin;
+    if (end - begin == kChunk && g_vec_ok(S.g, S.dtype) && (!has_buf || aligned16(S.buf)) && aligned8(x)) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float4 g[4], b[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + (h * 4 + k) * kMtThreads);
+          g[k] = load_g4(S.g, i, S.dtype);
+          b[k] = has_buf ? *reinterpret_cast<const float4*>(S.buf + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + (h * 4 + k) * kMtThreads);
+          const float u0 = flat_u(X(g[k].x), b[k].x, S, has_buf), u1 = flat_u(X(g[k].y), b[k].y, S, has_buf);
+          const float u2 = flat_u(X(g[k].z), b[k].z, S, has_buf), u3 = flat_u(X(g[k].w), b[k].w, S, has_buf);
+          *reinterpret_cast<uint2*>(x + i) = make_uint2(pack_bf16x2(den.div(u0), den.div(u1)),
+                                                        pack_bf16x2(den.div(u2), den.div(u3)));
+        }
+      }
+      i0 = end;
+    }
+    for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
+      const float u = flat_u(X(load_g1(S.g, i, S.dtype)), has_buf ? S.buf[i] : 0.f, S, has_buf);
+      x[i] = __float2bfloat16_rn(den.div(u));
+    }
+  }
+}
+
+// The flat counterpart of ns_out_kernel: the Muon apply of muon.py:97-99 (p = p*(1-decay) if decay;
+// p += -lr*(O*scale)) into the fp32 parameter, or a copy of the bf16 iterate to the output.
+__global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_constant__ FlatOutArgs A) {
+  const int total = A.chunk_start[A.n];
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const FlatOutSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(S.x);
+    int64_t i0 = begin;
+    if (A.apply) {
+      float* p = reinterpret_cast<float*>(S.out);
+      if (end - begin == kChunk && aligned8(x) && aligned16(p)) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint2 w[8];
+          float4 q[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + (h * 8 + k) * kMtThreads);
+            w[k] = *reinterpret_cast<const uint2*>(x + i);
+            q[k] = *reinterpret_cast<const float4*>(p + i);
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + (h * 8 + k) * kMtThreads);
+            const float o[4] = {bf16_lo(w[k].x), bf16_hi(w[k].x), bf16_lo(w[k].y), bf16_hi(w[k].y)};
+            float* qe = reinterpret_cast<float*>(&q[k]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float v = qe[e];
+              if (S.has_decay) v = __fmul_rn(v, S.decay_mul);
+              qe[e] = fmaf(S.neg_lr, __fmul_rn(o[e], S.scale), v);
+            }
+            *reinterpret_cast<float4*>(p + i) = q[k];
+          }
+        }
+        i0 = end;
+      }
+      for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
+        float v = p[i];
+        if (S.has_decay) v = __fmul_rn(v, S.decay_mul);
+        p[i] = fmaf(S.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
+      }
+    } else {
+      __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out);
+      for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) o[i] = x[i];
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------------------------------------------

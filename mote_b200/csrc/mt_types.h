@@ -133,6 +133,29 @@ struct NormArgs {
   NormMat mat[kMaxNormMat];
 };
 
+// ---- the same normalisation for matrices that are iterated as they are stored (rows <= cols, no padding): X0 has
+// the source's layout, so a matrix is a flat run of chunks and needs no transpose
+constexpr int kMaxFlatSeg = 320;
+struct FlatNormSeg {
+  const void* g;             // grad (momentum mode) or G (direct mode)
+  const float* buf;          // momentum buffer after this step's update, or null (direct mode)
+  void* x;                   // X0 (bf16), same layout as the source
+  int64_t numel;
+  float mom;
+  int nesterov;
+  int dtype;
+  int den_index;
+};
+struct FlatNormArgs {
+  int n;
+  int has_div;
+  float div;
+  const float* coef;
+  const float* den;
+  int chunk_start[kMaxFlatSeg + 1];
+  FlatNormSeg seg[kMaxFlatSeg];
+};
+
 // ---- per-matrix Frobenius norm from the sum-of-squares partials: den = fp32(sqrt(sum)) + eps
 constexpr int kMaxDenom = 4096;
 struct DenomArgs {
@@ -160,6 +183,21 @@ struct OutArgs {
   int n;
   int apply;
   OutMat mat[kMaxOutMat];
+};
+
+// ---- copy-out / apply for matrices iterated as they are stored (the flat counterpart of OutArgs)
+struct FlatOutSeg {
+  const void* x;             // final iterate (bf16), same layout as the output
+  void* out;                 // bf16 output, or the fp32 parameter in apply mode
+  int64_t numel;
+  float neg_lr, decay_mul, scale;
+  int has_decay;
+};
+struct FlatOutArgs {
+  int n;
+  int apply;
+  int chunk_start[kMaxFlatSeg + 1];
+  FlatOutSeg seg[kMaxFlatSeg];
 };
 
 // ---- in-place clip of the grads (standalone clip_grad_norm_)

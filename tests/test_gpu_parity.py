@@ -127,6 +127,31 @@ def test_muon_step_many_groups_launch_modes_agree(dev):
     _status_ok(dev)
 
 
+def test_muon_step_forty_shapes_matches_oracle(dev):
+    """40 distinct shapes, wide (flat normalise / apply) and tall (tiled, transposing) mixed, through muon_step,
+    against the oracle's Muon step after one Newton-Schulz iteration."""
+    from mote_b200.functional import MuonItem, muon_step
+    rng = np.random.default_rng(11)
+    shapes = [(8 + 3 * k, 16 + 5 * (k % 7)) if k % 2 else (24 + 5 * (k % 9), 8 + 3 * k) for k in range(40)]
+    shapes += [(64, 16384 + 64), (16384 + 64, 64)]   # more than one 16K-element chunk, ragged last chunk
+    p0 = [(rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)) for sh in shapes]
+    gr = [O.bf16_round(rng.standard_normal(sh, dtype=np.float32) * np.float32(1e-3)) for sh in shapes]
+    ps = _to(dev, p0)
+    gs = _to(dev, gr)
+    bufs = [torch.zeros_like(p) for p in ps]
+    muon_step([MuonItem(p, g, b, 0.02, 0.002, 0.95, True) for p, g, b in zip(ps, gs, bufs)], ns_steps=1)
+    torch.cuda.synchronize()
+    ref = [p.copy() for p in p0]
+    rbufs = [None] * len(ref)
+    O.muon_step(ref, gr, rbufs, O.MuonGroup(lr=0.02, weight_decay=0.1, ns_steps=1))
+    for i in range(len(shapes)):
+        d_gpu = ps[i].cpu().numpy() - p0[i]
+        d_ref = ref[i] - p0[i]
+        assert O.rel_frob(d_gpu, d_ref) <= 2e-3, (shapes[i], O.rel_frob(d_gpu, d_ref))
+        assert _close(bufs[i].cpu().numpy(), rbufs[i], 1e-6) == 0
+    _status_ok(dev)
+
+
 def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
     from mote_b200 import ops
     u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
