@@ -139,6 +139,22 @@ MOTEOPT_API int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon,
                                                  double grad_divisor, const float* grad_coef, void* workspace,
                                                  size_t workspace_bytes, moteopt_stream_t stream);
 
+/* The sharded step's exchange of Muon updates (no counterpart in the reference, which has no multi-GPU step: owners
+ * compute, every rank applies). moteopt_optimizer_step_with_coef_out is moteopt_optimizer_step_with_coef except that
+ * each Muon parameter's orthogonalised update O (bf16, the parameter's own shape and orientation, the value the
+ * reference casts to fp32 at mote/train/muon.py:99) is written to muon_updates[i] instead of being applied; the
+ * momentum buffers are updated as usual. moteopt_muon_apply applies such updates, p = p*(1-decay) (if decay);
+ * p += -lr*(O*scale) with scale = rms_scale*sqrt(max(rows, cols)) (muon.py:82, :97-99), to n parameters (grad and
+ * momentum_buffer are not read); it needs no workspace. Together they give the same bits as the in-step apply. */
+MOTEOPT_API int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* muon, int n_muon,
+                                                     const moteopt_muon_config* muon_cfg,
+                                                     const moteopt_adamw_tensor* adamw, int n_adamw,
+                                                     const moteopt_adamw_hparams* adamw_hp, double grad_divisor,
+                                                     const float* grad_coef, void* const* muon_updates, void* workspace,
+                                                     size_t workspace_bytes, moteopt_stream_t stream);
+MOTEOPT_API int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* muon_cfg,
+                                   const void* const* updates, moteopt_stream_t stream);
+
 /* ---- Muon.step() of one or more param groups (mote/train/muon.py:52-100). Parameters whose grad is NULL are
  *      skipped by the caller (muon.py:61-62). `grad_scale` (device, may be NULL) multiplies every grad first. */
 MOTEOPT_API size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps);

@@ -23,6 +23,7 @@ EXPORTS = (
     "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count",
     "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_with_coef",
+    "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply",
     "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
     "moteopt_adamw_step",
@@ -79,6 +80,10 @@ def _load() -> C.CDLL:
         "moteopt_optimizer_step_with_coef": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
                                                    C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp, vp, sz,
                                                    vp]),
+        "moteopt_optimizer_step_with_coef_out": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
+                                                       C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp,
+                                                       C.POINTER(vp), vp, sz, vp]),
+        "moteopt_muon_apply": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(vp), vp]),
         "moteopt_grad_sumsq_workspace_size": (sz, [C.POINTER(C.c_int64), i32]),
         "moteopt_grad_sumsq": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp, sz, vp]),
         "moteopt_clip_coef_from_sums": (i32, [vp, i32, i32, dbl, vp, vp]),

@@ -800,6 +800,58 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
   return MOTEOPT_OK;
 }
 
+// The final iterate of every matrix copied out (bf16, the parameter's orientation) to out[param] at the matrix's
+// slice, instead of being applied: the sharded step's owners produce the updates that the ranks all-gather.
+int run_copy_out(const moteopt_muon_param* P, const Layout& L, char* ws, int src, void* const* out, int sms,
+                 cudaStream_t st) {
+  static thread_local OutArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.apply = 0;
+  std::vector<OutMat> all;
+  std::vector<FlatOutSeg> flat;
+  for (const GroupPlan& g : L.groups)
+    for (size_t pos = 0; pos < g.mats.size(); ++pos) {
+      const MatRef& r = g.mats[pos];
+      const moteopt_muon_param& p = P[r.src];
+      void* dst = static_cast<char*>(out[r.src]) + static_cast<size_t>(r.slice) * p.rows * p.cols * 2;
+      const void* x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+      if (stored_as_iterated(g)) {
+        FlatOutSeg S;
+        std::memset(&S, 0, sizeof(S));
+        S.x = x;
+        S.out = dst;
+        S.numel = static_cast<int64_t>(g.rows) * g.cols;
+        flat.push_back(S);
+        continue;
+      }
+      OutMat M;
+      std::memset(&M, 0, sizeof(M));
+      M.x = x;
+      M.out = dst;
+      M.rows = g.rows;
+      M.cols = g.cols;
+      M.m_pad = g.m;
+      M.n_pad = g.n;
+      M.transposed = g.transposed;
+      M.tiles_x = static_cast<int>(cdiv(g.cols, kNormTile));
+      M.tiles = M.tiles_x * static_cast<int>(cdiv(g.rows, kNormTile));
+      all.push_back(M);
+    }
+  MO_TRY(launch_flat_out(flat, 0, sms, st));
+  for (size_t s0 = 0; s0 < all.size(); s0 += kMaxOutMat) {
+    const size_t cnt = std::min(all.size() - s0, static_cast<size_t>(kMaxOutMat));
+    A.n = static_cast<int>(cnt);
+    int max_tiles = 0;
+    for (size_t i = 0; i < cnt; ++i) {
+      A.mat[i] = all[s0 + i];
+      max_tiles = std::max(max_tiles, A.mat[i].tiles);
+    }
+    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ns_out_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
 int check_ws(void* ws, size_t have, size_t need) {
   if (ws == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");
   if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(MOTEOPT_ERR_INVALID, "workspace must be 256-byte aligned");
@@ -816,8 +868,9 @@ std::vector<std::tuple<int64_t, int64_t, int64_t>> muon_shapes(const moteopt_muo
 
 // The whole step: (optional) grad norm + clip coefficient, AdamW, Muon.
 int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* mcfg, const moteopt_adamw_tensor* adam,
-             int n_adam, const moteopt_adamw_hparams* ahp, const moteopt_grad_config* gcfg, const float* ext_scale,
-             float* out_norm, void* workspace, size_t ws_bytes, cudaStream_t st) {
+             int n_adam, const moteopt_adamw_hparams* adamw_hp, const moteopt_grad_config* gcfg, const float* ext_scale,
+             float* out_norm, void* workspace, size_t ws_bytes, cudaStream_t st, void* const* muon_out = nullptr) {
+  const moteopt_adamw_hparams* ahp = adamw_hp;
   MO_TRY(check_muon(muon, n_muon, mcfg));
   MO_TRY(check_adamw(adam, n_adam, ahp));
   int sms = 0;
@@ -858,7 +911,8 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
       MO_TRY(run_ns(L, ws, mcfg->ns_steps, status, sms, st, &final_src));
       if (t_ns_ev[1] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[1], st));
     }
-    MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st));
+    if (muon_out != nullptr) MO_TRY(run_copy_out(muon, L, ws, final_src, muon_out, sms, st));
+    else MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st));
   }
   return MOTEOPT_OK;
 }
@@ -928,6 +982,47 @@ int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon,
   gc.grad_divisor = grad_divisor;
   return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, &gc, grad_coef, nullptr, workspace,
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* muon, int n_muon,
+                                         const moteopt_muon_config* muon_cfg, const moteopt_adamw_tensor* adamw,
+                                         int n_adamw, const moteopt_adamw_hparams* adamw_hp, double grad_divisor,
+                                         const float* grad_coef, void* const* muon_updates, void* workspace,
+                                         size_t workspace_bytes, moteopt_stream_t stream) {
+  if (n_muon > 0 && muon_updates == nullptr) return fail(MOTEOPT_ERR_INVALID, "muon_updates is null");
+  for (int i = 0; i < n_muon; ++i)
+    if (muon_updates[i] == nullptr) return fail(MOTEOPT_ERR_INVALID, "muon_updates[" + std::to_string(i) + "] is null");
+  moteopt_grad_config gc;
+  gc.clip = 0;
+  gc.max_norm = 0.0;
+  gc.grad_divisor = grad_divisor;
+  return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, &gc, grad_coef, nullptr, workspace,
+                  workspace_bytes, reinterpret_cast<cudaStream_t>(stream), muon_updates);
+}
+
+int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
+                       const void* const* updates, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (muon == nullptr || updates == nullptr)) || cfg == nullptr)
+    return fail(MOTEOPT_ERR_INVALID, "moteopt_muon_apply: null argument");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  std::vector<FlatOutSeg> segs;
+  for (int i = 0; i < n; ++i) {
+    const moteopt_muon_param& p = muon[i];
+    if (p.param == nullptr || updates[i] == nullptr || p.batch < 1 || p.rows < 1 || p.cols < 1)
+      return fail(MOTEOPT_ERR_INVALID, "moteopt_muon_apply: bad entry " + std::to_string(i));
+    FlatOutSeg S;   // the same scalars as the in-step apply (muon_apply_table)
+    std::memset(&S, 0, sizeof(S));
+    S.x = updates[i];
+    S.out = p.param;
+    S.numel = p.batch * p.rows * p.cols;
+    S.neg_lr = static_cast<float>(-p.lr);
+    S.has_decay = p.decay != 0.0;
+    S.decay_mul = static_cast<float>(1.0 - p.decay);
+    S.scale = static_cast<float>(cfg->rms_scale * std::pow(static_cast<double>(std::max(p.rows, p.cols)), 0.5));
+    segs.push_back(S);
+  }
+  return launch_flat_out(segs, 1, sms, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t moteopt_grad_sumsq_workspace_size(const int64_t* numels, int n) {

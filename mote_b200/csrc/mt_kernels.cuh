@@ -475,7 +475,17 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
       }
     } else {
       __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out);
-      for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) o[i] = x[i];
+      if (end - begin == kChunk && aligned16(x) && aligned16(o)) {   // 2048 16-byte vectors: 8 per thread
+        const uint4* xs = reinterpret_cast<const uint4*>(x + begin);
+        uint4* os = reinterpret_cast<uint4*>(o + begin);
+        uint4 v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = xs[threadIdx.x + k * kMtThreads];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) os[threadIdx.x + k * kMtThreads] = v[k];
+        i0 = end;
+      }
+      for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) o[i] = x[i];
     }
   }
 }

@@ -12,8 +12,12 @@ Step (grads: each rank's local, unreduced grads in the grad regions):
   1. reduce-scatter (sum) of both grad regions: rank r receives the reduced grads of its own segments;
   2. rank r's sum of (g / divisor)^2 over what it owns, all-gathered and summed in rank order -> the global norm and
      clip coefficient (bitwise identical on every rank);
-  3. rank r runs AdamW on its slice and Muon (momentum, Newton-Schulz, apply) on its matrices;
-  4. all-gather of both param regions: every rank holds the updated model.
+  3. rank r runs AdamW on its slice and, for its matrices, Muon's momentum and Newton-Schulz, writing the
+     orthogonalised updates O (bf16) into its segment of an update region laid out like the Muon param region;
+  4. all-gather of the update region (bf16) and of the AdamW param region (fp32);
+  5. every rank applies every O to its copy of the Muon params (the same arithmetic on identical inputs, so all
+     ranks hold the same bits). The bf16 O is exactly what the reference applies (muon.py:99 casts it to fp32), and
+     gathering it moves half the bytes of gathering the fp32 params.
 Collectives go through torch.distributed (NCCL on GPUs; gloo works for the host-side tests). The compute steps are
 injected (`Compute`), so the same choreography runs with the CUDA library or with a CPU stand-in.
 """
@@ -119,10 +123,13 @@ def make_plan(muon_shapes, adam_shapes, world: int, ns_steps: int = 5) -> ShardP
 class Compute:
     """The step's compute, injected: `sumsq(views, divisor) -> 0-dim fp64 tensor` (sum of (g/divisor)^2 over the
     views), `coef(sums, max_norm) -> 2-element fp32 tensor [norm, coef]`, `update(muon_items, adam_items, coef,
-    divisor)` with items as in mote_b200.functional."""
+    divisor, muon_out)` with items as in mote_b200.functional (AdamW applied; Muon's update O written to the bf16
+    tensors `muon_out`, one per Muon item), and `apply(muon_items, updates)`: p = p*(1-decay); p += -lr*(O*scale) for
+    every item (grad and momentum buffer unused)."""
     sumsq: Callable
     coef: Callable
     update: Callable
+    apply: Callable
 
 
 def _reduce_scatter(out: torch.Tensor, flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
@@ -162,6 +169,7 @@ class ShardedStep:
         self.bufs = {i: torch.zeros(plan.muon_shapes[i], dtype=torch.float32, device=params_m.device) for i in self.mine}
         self.pieces = plan.adam_pieces(rank)
         self.gm_seg = torch.zeros(plan.m_seg, dtype=grads_m.dtype, device=grads_m.device)
+        self.om = torch.zeros(plan.muon_len, dtype=torch.bfloat16, device=params_m.device)   # Muon updates O
         self.ga_seg = torch.zeros(plan.a_seg, dtype=grads_a.dtype, device=grads_a.device)
         self.m_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
         self.v_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
@@ -210,9 +218,14 @@ class ShardedStep:
             o = plan.adam_off[i] + start
             adam.append(AdamWItem(self.pa[o:o + n], self.reduced_adam_grad(i, start, n), self.m_state[o - base:o - base + n],
                                   self.v_state[o - base:o - base + n], self.adam_lr, self.adam_wd[i], self.steps))
-        self.compute.update(muon, adam, norm_coef[1:2] if max_norm is not None else None, grad_divisor)
-        _all_gather_inplace(self.pm, plan.m_seg, r, self.group)
+        self.compute.update(muon, adam, norm_coef[1:2] if max_norm is not None else None, grad_divisor,
+                            [self.muon_view(self.om, i) for i in self.mine])
+        _all_gather_inplace(self.om, plan.m_seg, r, self.group)
         _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
+        every = range(len(plan.muon_shapes))
+        self.compute.apply([MuonItem(self.muon_view(self.pm, i), None, None, self.muon_lr,
+                                     self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
+                            for i in every], [self.muon_view(self.om, i) for i in every])
         return norm_coef[0]
 
 
@@ -262,7 +275,7 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
 
     counter = {}
 
-    def update(muon, adam, coef_t, divisor):
+    def update(muon, adam, coef_t, divisor, muon_out):
         dev = (muon[0].param if muon else adam[0].param).device if (muon or adam) else None
         if dev is None:
             return
@@ -273,9 +286,28 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
         ws = workspace(dev, nbytes)
         cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
         hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps), counter[dev].data_ptr())
-        L.check(L.lib.moteopt_optimizer_step_with_coef(
+        outs = L.array(C.c_void_p, [o.data_ptr() for o in muon_out])
+        L.check(L.lib.moteopt_optimizer_step_with_coef_out(
             m_arr, len(muon), C.byref(cfg), a_arr, len(adam), C.byref(hp), float(divisor or 0.0),
-            C.c_void_p(coef_t.data_ptr() if coef_t is not None else 0), C.c_void_p(ws.data_ptr()), ws.numel(),
-            C.c_void_p(stream_handle(dev))), "moteopt_optimizer_step_with_coef")
+            C.c_void_p(coef_t.data_ptr() if coef_t is not None else 0), outs, C.c_void_p(ws.data_ptr()),
+            ws.numel(), C.c_void_p(stream_handle(dev))), "moteopt_optimizer_step_with_coef_out")
 
-    return Compute(sumsq, coef, update)
+    def apply(muon, updates):
+        if not muon:
+            return
+        dev = muon[0].param.device
+        arr = (L.MuonParam * len(muon))()
+        for k, (it, o) in enumerate(zip(muon, updates)):
+            p = it.param
+            if o.dtype != torch.bfloat16 or o.shape != p.shape or not o.is_contiguous():
+                raise ValueError("Muon updates must be contiguous bf16 tensors shaped like their params")
+            e = arr[k]
+            e.param = p.data_ptr()
+            e.batch, e.rows, e.cols = (p.shape[0] if p.ndim == 3 else 1), p.shape[-2], p.shape[-1]
+            e.lr, e.decay, e.momentum = float(it.lr), float(it.decay), float(it.momentum)
+        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
+        ptrs = L.array(C.c_void_p, [o.data_ptr() for o in updates])
+        L.check(L.lib.moteopt_muon_apply(arr, len(muon), C.byref(cfg), ptrs, C.c_void_p(stream_handle(dev))),
+                "moteopt_muon_apply")
+
+    return Compute(sumsq, coef, update, apply)

@@ -50,7 +50,7 @@ def oracle_compute(w):
         norm, c = _coef(float(sum(sums.tolist())), max_norm)
         return torch.tensor([norm, c], dtype=torch.float32)
 
-    def update(muon, adam, coef_t, divisor):
+    def update(muon, adam, coef_t, divisor, muon_out):
         c = np.float32(coef_t.item()) if coef_t is not None else None
 
         def eff(g):
@@ -63,12 +63,18 @@ def oracle_compute(w):
         for it in adam:
             O.adamw_update(it.param.numpy(), eff(it.grad), it.exp_avg.numpy(), it.exp_avg_sq.numpy(), it.lr,
                            w.betas[0], w.betas[1], w.eps, it.weight_decay, it.step)
-        for it in muon:   # the item carries decay = lr * wd (muon.py:78); hand the oracle the matching wd
-            grp = O.MuonGroup(lr=it.lr, momentum=it.momentum, nesterov=it.nesterov,
-                              weight_decay=it.decay / it.lr if it.decay else 0.0, ns_steps=w.ns_steps)
-            bufs = [it.momentum_buffer.numpy()]
-            O.muon_step([it.param.numpy()], [eff(it.grad)], bufs, grp)
-    return Compute(sumsq, coef, update)
+        for it, out in zip(muon, muon_out):   # momentum + Newton-Schulz; the update O goes to `out`
+            u = O.muon_momentum(it.momentum_buffer.numpy(), eff(it.grad), it.momentum, it.nesterov)
+            m, n = it.param.shape[-2], it.param.shape[-1]
+            o = O.newton_schulz(u.reshape(-1, m, n), steps=w.ns_steps).reshape(it.param.shape)
+            out.copy_(torch.from_numpy(np.ascontiguousarray(o, dtype=np.float32)).to(torch.bfloat16))
+
+    def apply(muon, updates):   # the item carries decay = lr * wd (muon.py:78)
+        for it, o in zip(muon, updates):
+            m, n = it.param.shape[-2], it.param.shape[-1]
+            decay = it.lr * (it.decay / it.lr) if it.decay else 0.0   # as muon_lr_decay forms lr * wd
+            O.muon_apply(it.param.numpy(), o.float().numpy(), 0.2 * max(m, n) ** 0.5, it.lr, decay)
+    return Compute(sumsq, coef, update, apply)
 
 
 def small_workload():

@@ -152,6 +152,41 @@ def test_muon_step_forty_shapes_matches_oracle(dev):
     _status_ok(dev)
 
 
+def test_update_out_then_apply_equals_in_step_apply(dev):
+    """The sharded step's exchange: Muon updates written out (moteopt_optimizer_step_with_coef_out) and applied by
+    moteopt_muon_apply give the same bits as moteopt_optimizer_step's own apply (wide, tall, padded, 3-D)."""
+    from mote_b200.distributed import cuda_compute
+    from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    shapes = [(40, 96), (96, 40), (37, 53), (2, 48, 64), (768, 3072), (3072, 768)]
+    p0 = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in shapes]
+    g = [(torch.randn(s, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for s in shapes]
+    a0 = torch.randn(300, generator=gen, device=dev) * 0.02
+    ag = (torch.randn(300, generator=gen, device=dev) * 1e-3).to(torch.bfloat16)
+
+    def items(ps, bufs, pa, m, v):
+        return ([MuonItem(p, gr, b, 0.02, 0.002) for p, gr, b in zip(ps, g, bufs)],
+                [AdamWItem(pa, ag, m, v, 3e-4, 0.1, 1)])
+    ps1, bufs1 = [p.clone() for p in p0], [torch.zeros_like(p) for p in p0]
+    pa1, m1, v1 = a0.clone(), torch.zeros_like(a0), torch.zeros_like(a0)
+    mu, ad = items(ps1, bufs1, pa1, m1, v1)
+    optimizer_step(mu, ad, betas=(0.9, 0.95))
+    ps2, bufs2 = [p.clone() for p in p0], [torch.zeros_like(p) for p in p0]
+    pa2, m2, v2 = a0.clone(), torch.zeros_like(a0), torch.zeros_like(a0)
+    mu2, ad2 = items(ps2, bufs2, pa2, m2, v2)
+    outs = [torch.empty(s, dtype=torch.bfloat16, device=dev) for s in shapes]
+    comp = cuda_compute(betas=(0.9, 0.95))
+    comp.update(mu2, ad2, None, None, outs)
+    for p, q in zip(ps2, p0):   # the params are not touched before the apply
+        assert torch.equal(p, q)
+    comp.apply(mu2, outs)
+    torch.cuda.synchronize()
+    for x, y in zip(ps1 + bufs1 + [pa1, m1, v1], ps2 + bufs2 + [pa2, m2, v2]):
+        assert torch.equal(x, y)
+    _status_ok(dev)
+
+
 def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
     from mote_b200 import ops
     u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
