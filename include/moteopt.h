@@ -155,6 +155,16 @@ MOTEOPT_API int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* m
 MOTEOPT_API int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* muon_cfg,
                                    const void* const* updates, moteopt_stream_t stream);
 
+/* Peer mappings for the sharded step (no counterpart in the reference). A rank exports the device allocation that
+ * holds `ptr` (a CUDA IPC handle of MOTEOPT_IPC_HANDLE_BYTES bytes, plus ptr's byte offset inside it); another process
+ * on the same node imports the handle (base pointer of the mapping; add the offset) and may then pass pointers into
+ * it, e.g. a peer's Muon updates to moteopt_muon_apply, which reads them over NVLink with plain loads. The exporter's
+ * allocation must stay alive until every importer has closed its mapping. */
+#define MOTEOPT_IPC_HANDLE_BYTES 64
+MOTEOPT_API int moteopt_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out);
+MOTEOPT_API int moteopt_ipc_import(const void* handle, void** base_out);
+MOTEOPT_API int moteopt_ipc_close(void* base);
+
 /* ---- Muon.step() of one or more param groups (mote/train/muon.py:52-100). Parameters whose grad is NULL are
  *      skipped by the caller (muon.py:61-62). `grad_scale` (device, may be NULL) multiplies every grad first. */
 MOTEOPT_API size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps);

@@ -24,6 +24,7 @@ EXPORTS = (
     "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_with_coef",
     "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply",
+    "moteopt_ipc_export", "moteopt_ipc_import", "moteopt_ipc_close",
     "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
     "moteopt_adamw_step",
@@ -84,6 +85,9 @@ def _load() -> C.CDLL:
                                                        C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp,
                                                        C.POINTER(vp), vp, sz, vp]),
         "moteopt_muon_apply": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(vp), vp]),
+        "moteopt_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
+        "moteopt_ipc_import": (i32, [vp, C.POINTER(vp)]),
+        "moteopt_ipc_close": (i32, [vp]),
         "moteopt_grad_sumsq_workspace_size": (sz, [C.POINTER(C.c_int64), i32]),
         "moteopt_grad_sumsq": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp, sz, vp]),
         "moteopt_clip_coef_from_sums": (i32, [vp, i32, i32, dbl, vp, vp]),

@@ -127,6 +127,20 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+typedef CUresult (*AddrRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+AddrRangeFn addr_range_fn() {
+  static AddrRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddrRangeFn>(p);
+  });
+  return fn;
+}
+
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   static std::once_flag once;
@@ -935,6 +949,37 @@ int moteopt_profile_ns_events(void* start_event, void* end_event) {
 }
 
 const char* moteopt_last_error(void) { return t_err.c_str(); }
+
+int moteopt_ipc_export(const void* ptr, void* handle_out, uint64_t* offset_out) {
+  if (ptr == nullptr || handle_out == nullptr || offset_out == nullptr)
+    return fail(MOTEOPT_ERR_INVALID, "moteopt_ipc_export: null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == MOTEOPT_IPC_HANDLE_BYTES, "IPC handle size");
+  AddrRangeFn range = addr_range_fn();
+  if (range == nullptr) return fail(MOTEOPT_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(MOTEOPT_ERR_CUDA, "cuMemGetAddressRange failed (" + std::to_string(r) + ")");
+  cudaIpcMemHandle_t h;
+  MO_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  std::memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return MOTEOPT_OK;
+}
+
+int moteopt_ipc_import(const void* handle, void** base_out) {
+  if (handle == nullptr || base_out == nullptr) return fail(MOTEOPT_ERR_INVALID, "moteopt_ipc_import: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  MO_CUDA(cudaIpcOpenMemHandle(base_out, h, cudaIpcMemLazyEnablePeerAccess));
+  return MOTEOPT_OK;
+}
+
+int moteopt_ipc_close(void* base) {
+  if (base == nullptr) return fail(MOTEOPT_ERR_INVALID, "moteopt_ipc_close: null argument");
+  MO_CUDA(cudaIpcCloseMemHandle(base));
+  return MOTEOPT_OK;
+}
 
 int moteopt_ns_set_persistent(int enable) { return g_ns_persistent.exchange(enable ? 1 : 0); }
 

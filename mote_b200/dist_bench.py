@@ -54,6 +54,11 @@ def run(args, rank: int, world: int, local_rank: int):
         st.gm.copy_(torch.randn(plan.muon_len, generator=gen, device=dev) * 1e-3)
         st.ga.copy_(torch.randn(plan.adam_len, generator=gen, device=dev) * 1e-3)
         stream = torch.cuda.current_stream(dev)
+        peer_error = ""
+        try:
+            st.enable_peer_updates()
+        except Exception as exc:  # noqa: BLE001  (recorded in the JSON line; the all-gather exchange is used instead)
+            peer_error = f"{type(exc).__name__}: {exc}"[:200]
 
         for _ in range(args.warmup):
             st.step(max_norm=w.clip)
@@ -149,7 +154,10 @@ def run(args, rank: int, world: int, local_rank: int):
             "config": {"workload": w.name, "parallelism": f"muon-owner+zero1 x{world}",
                        "launch": "CUDA graph of the whole sharded step" if graph is not None
                        else f"eager (graph capture failed: {capture_error})", "collectives":
-                       "NCCL reduce-scatter (grads) + all-gather (fp32 params) + all-gather (per-rank sum of squares)",
+                       "NCCL reduce-scatter (grads), all-gather (per-rank sums of squares), all-gather (AdamW fp32 "
+                       "params); Muon updates: " + ("every rank's bf16 O read over NVLink by the apply kernel (CUDA "
+                       "IPC mappings, one-element all-reduce as the ordering barrier)" if st.peer_ptrs is not None
+                       else f"NCCL all-gather of bf16 O ({peer_error or 'peer mapping off'})"),
                        "l2": "inputs larger than L2; no flush"},
             "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
@@ -163,6 +171,7 @@ def run(args, rank: int, world: int, local_rank: int):
             "gpu_launches": int(allv[:, 3].sum()),
         }
         del graph, run_step, norm_t
+        st.close()
         return line
     finally:
         torch.cuda.synchronize(dev)

@@ -18,6 +18,10 @@ Step (grads: each rank's local, unreduced grads in the grad regions):
   5. every rank applies every O to its copy of the Muon params (the same arithmetic on identical inputs, so all
      ranks hold the same bits). The bf16 O is exactly what the reference applies (muon.py:99 casts it to fp32), and
      gathering it moves half the bytes of gathering the fp32 params.
+With peer updates enabled (`enable_peer_updates`, NCCL only), steps 4-5 for the Muon region become one pass: every
+rank maps the other ranks' update regions (CUDA IPC, once), a one-element all-reduce orders the owners' writes
+before the reads, and the apply kernel reads each owner's O straight over NVLink while it updates the local params,
+so no gathered copy of O is ever written.
 Collectives go through torch.distributed (NCCL on GPUs; gloo works for the host-side tests). The compute steps are
 injected (`Compute`), so the same choreography runs with the CUDA library or with a CPU stand-in.
 """
@@ -175,6 +179,47 @@ class ShardedStep:
         self.v_state = torch.zeros(plan.a_seg, dtype=torch.float32, device=params_a.device)
         self.steps = 0
         self.graph = None
+        self.peer_ptrs: Optional[List[int]] = None   # update region of every rank, mapped into this process
+        self._peer_bases: List[int] = []
+        self._flag = None
+
+    def enable_peer_updates(self) -> None:
+        """Map every rank's update region into this process (CUDA IPC through libmoteopt); collective, eager, once."""
+        import ctypes as C
+
+        from . import _lib as L
+        handle = (C.c_ubyte * 64)()
+        off = C.c_uint64(0)
+        L.check(L.lib.moteopt_ipc_export(C.c_void_p(self.om.data_ptr()), handle, C.byref(off)), "moteopt_ipc_export")
+        mine = (bytes(handle), int(off.value))
+        allh: List[Tuple[bytes, int]] = [None] * self.plan.world   # type: ignore[list-item]
+        dist.all_gather_object(allh, mine, group=self.group)
+        ptrs = []
+        for r, (h, o) in enumerate(allh):
+            if r == self.rank:
+                ptrs.append(self.om.data_ptr())
+                continue
+            base = C.c_void_p(0)
+            L.check(L.lib.moteopt_ipc_import(bytes(h), C.byref(base)), "moteopt_ipc_import")
+            self._peer_bases.append(int(base.value))
+            ptrs.append(int(base.value) + o)
+        self.peer_ptrs = ptrs
+        self._flag = torch.zeros(1, dtype=torch.float32, device=self.om.device)
+        torch.cuda.synchronize(self.om.device)
+        dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        """Unmap the peers' update regions (collective: no rank frees its region while another still maps it)."""
+        import ctypes as C
+
+        from . import _lib as L
+        if self.peer_ptrs is None:
+            return
+        torch.cuda.synchronize(self.om.device)
+        for b in self._peer_bases:
+            L.check(L.lib.moteopt_ipc_close(C.c_void_p(b)), "moteopt_ipc_close")
+        self._peer_bases, self.peer_ptrs = [], None
+        dist.barrier(group=self.group)
 
     def muon_view(self, flat: torch.Tensor, i: int) -> torch.Tensor:
         o, s = self.plan.muon_off[i], self.plan.muon_shapes[i]
@@ -220,12 +265,17 @@ class ShardedStep:
                                   self.v_state[o - base:o - base + n], self.adam_lr, self.adam_wd[i], self.steps))
         self.compute.update(muon, adam, norm_coef[1:2] if max_norm is not None else None, grad_divisor,
                             [self.muon_view(self.om, i) for i in self.mine])
-        _all_gather_inplace(self.om, plan.m_seg, r, self.group)
-        _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
         every = range(len(plan.muon_shapes))
+        if self.peer_ptrs is not None:   # the owners' O, read in place over NVLink once every owner has written it
+            dist.all_reduce(self._flag, group=self.group)
+            updates = [self.peer_ptrs[plan.owner[i]] + 2 * plan.muon_off[i] for i in every]   # bf16 elements
+        else:
+            _all_gather_inplace(self.om, plan.m_seg, r, self.group)
+            updates = [self.muon_view(self.om, i) for i in every]
+        _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
         self.compute.apply([MuonItem(self.muon_view(self.pm, i), None, None, self.muon_lr,
                                      self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
-                            for i in every], [self.muon_view(self.om, i) for i in every])
+                            for i in every], updates)
         return norm_coef[0]
 
 
@@ -299,14 +349,14 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
         arr = (L.MuonParam * len(muon))()
         for k, (it, o) in enumerate(zip(muon, updates)):
             p = it.param
-            if o.dtype != torch.bfloat16 or o.shape != p.shape or not o.is_contiguous():
+            if not isinstance(o, int) and (o.dtype != torch.bfloat16 or o.shape != p.shape or not o.is_contiguous()):
                 raise ValueError("Muon updates must be contiguous bf16 tensors shaped like their params")
             e = arr[k]
             e.param = p.data_ptr()
             e.batch, e.rows, e.cols = (p.shape[0] if p.ndim == 3 else 1), p.shape[-2], p.shape[-1]
             e.lr, e.decay, e.momentum = float(it.lr), float(it.decay), float(it.momentum)
         cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
-        ptrs = L.array(C.c_void_p, [o.data_ptr() for o in updates])
+        ptrs = L.array(C.c_void_p, [o if isinstance(o, int) else o.data_ptr() for o in updates])
         L.check(L.lib.moteopt_muon_apply(arr, len(muon), C.byref(cfg), ptrs, C.c_void_p(stream_handle(dev))),
                 "moteopt_muon_apply")
 

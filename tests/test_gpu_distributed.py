@@ -30,7 +30,7 @@ def _workload():
                             [(271, 64)], [(64,)] * 3)
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, peer):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
@@ -48,6 +48,8 @@ def _rank(rank, world, port, out):
         nd = len(w.adam_decay_shapes)
         st = ShardedStep(plan, rank, pm, pa, gm, ga, cuda_compute(betas=w.betas), muon_lr=w.muon_lr, muon_wd=w.muon_wd,
                          adam_lr=w.adam_lr, adam_wd=[w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))])
+        if peer:
+            st.enable_peer_updates()
         for i, p in enumerate(inp.muon_params):
             st.muon_view(pm, i).copy_(torch.from_numpy(p))
         for i, p in enumerate(inp.adam_params):
@@ -61,8 +63,9 @@ def _rank(rank, world, port, out):
                 st.adam_view(ga, i).copy_(torch.from_numpy(g))
             norms.append(st.step(max_norm=0.05, grad_divisor=2.0).item())
         torch.cuda.synchronize()
-        np.savez(os.path.join(out, f"r{rank}.npz"), pm=pm.cpu().numpy(), pa=pa.cpu().numpy(), norms=np.array(norms),
-                 moff=np.array(plan.muon_off), aoff=np.array(plan.adam_off))
+        st.close()
+        np.savez(os.path.join(out, f"r{rank}_{int(peer)}.npz"), pm=pm.cpu().numpy(), pa=pa.cpu().numpy(),
+                 norms=np.array(norms), moff=np.array(plan.muon_off), aoff=np.array(plan.adam_off))
     finally:
         dist.destroy_process_group()
 
@@ -74,9 +77,13 @@ def test_two_gpu_sharded_step_matches_single_gpu(tmp_path):
     from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
     from oracle import moteopt_oracle as O
     world = 2
-    mp.spawn(_rank, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
-    r0, r1 = (np.load(tmp_path / f"r{r}.npz") for r in range(world))
+    for peer in (False, True):   # NCCL all-gather of the updates, then the peer (NVLink) reads of them
+        mp.spawn(_rank, args=(world, _port(), str(tmp_path), peer), nprocs=world, join=True)
+    r0, r1 = (np.load(tmp_path / f"r{r}_0.npz") for r in range(world))
     assert np.array_equal(r0["pm"], r1["pm"]) and np.array_equal(r0["pa"], r1["pa"])
+    for r in range(world):   # the two exchanges give the same bits
+        q = np.load(tmp_path / f"r{r}_1.npz")
+        assert np.array_equal(q["pm"], r0["pm"]) and np.array_equal(q["pa"], r0["pa"])
     # one GPU, grads summed over the ranks (bf16 sum, as NCCL's bf16 reduction of two values)
     w = _workload()
     dev = torch.device("cuda", 0)
