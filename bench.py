@@ -246,6 +246,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     adam_ms = a0.elapsed_time(a1) / 10
     del fp, fg, fm, fv
 
+    # the fused extras (EMA of the weights, Muon param norms) against the separate torch passes the reference runs
+    # after its step (train.py:950-953 _foreach_lerp_, elr.py:85-87 stacked norms), on the same c1 tensors
+    extras = _time_extras(step, muon_items, adam_fixed, w, stream, counter)
+
     # end to end through the public API with host buffers: grads copied in from pinned memory, norm read back
     host_grads = flat.cpu().pin_memory()
     host_norm = torch.empty((), dtype=torch.float32).pin_memory()
@@ -297,11 +301,52 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 "d2h_bytes_per_step": 4},
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
+        "extras": extras,
     }
     return line
 
 
 # ---------------------------------------------------------------------------------------------------------------
+def _time_extras(step, muon_items, adam_items, w, stream, counter, reps: int = 10) -> dict:
+    """ms per step of: the plain eager step; the step with the fused EMA; the step with the fused norms; and the
+    reference's separate passes on the GPU (torch._foreach_lerp_ over every param; stacked per-matrix norms)."""
+    import torch
+
+    from mote_b200.functional import optimizer_step
+    params = [it.param for it in adam_items] + [it.param for it in muon_items]
+    ema = [p.clone() for p in params]
+    norms = torch.empty(len(muon_items), dtype=torch.float32, device=params[0].device)
+
+    def fused(**kw):
+        counter["step"] += 1
+        for it in adam_items:
+            it.step = counter["step"]
+        optimizer_step(muon_items, adam_items, ns_steps=w.ns_steps, betas=w.betas, eps=w.eps, max_norm=w.clip, **kw)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    base = timed(step)
+    with_ema = timed(lambda: fused(ema=ema, ema_weight=1e-3))
+    with_norms = timed(lambda: fused(muon_norms=norms))
+    sep_ema = timed(lambda: torch._foreach_lerp_(ema, params, 1e-3))
+    mp = [it.param for it in muon_items]
+    sep_norms = timed(lambda: torch.stack([p.float().norm() for p in mp]))
+    return {"unit": "ms/step", "step": round(base, 4),
+            "ema_fused_extra": round(with_ema - base, 4), "ema_separate_torch": round(sep_ema, 4),
+            "norms_fused_extra": round(with_norms - base, 4), "norms_separate_torch": round(sep_norms, 4),
+            "note": "fused: added time of the step with the extra; separate: torch pass on the same device tensors"}
+
+
 def run_reference(args, rank: int, world: int):
     """The reference's arithmetic (oracle/ numpy restatement) on the host CPU, one bounded sample per step."""
     import numpy as np

@@ -90,6 +90,20 @@ typedef struct moteopt_grad_config {
   double grad_divisor;          /* train.py:945: grads /= total_n first; 0 or 1 = no division */
 } moteopt_grad_config;
 
+/* Optional work fused into moteopt_optimizer_step_ex (no counterpart in the reference's step, which does this work
+ * in separate passes after it).
+ *   ema:        per tensor, in call order (the n_adamw AdamW tensors, then the n_muon Muon params), an fp32 buffer
+ *               shaped like the param, or NULL: e = lerp(e, p_new, ema_weight) in the pass that writes p, i.e.
+ *               mote/train/train.py:950-953 (_foreach_lerp_(ema, params, 1 - decay)) for the stepped params.
+ *               NULL array: no EMA.
+ *   muon_norms: n_muon device floats, or NULL: ||p_new||_F of each Muon param (mote/train/elr.py:85-87, the
+ *               NormTracker sample), reduced in a fixed order from the apply pass. */
+typedef struct {
+  float* const* ema;
+  double ema_weight;
+  float* muon_norms;
+} moteopt_step_extras;
+
 MOTEOPT_API int moteopt_version(void);
 MOTEOPT_API const char* moteopt_last_error(void);
 
@@ -119,6 +133,13 @@ MOTEOPT_API int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muo
                            const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* adamw_hp,
                            const moteopt_grad_config* grad_cfg, float* out_norm, void* workspace,
                            size_t workspace_bytes, moteopt_stream_t stream);
+/* moteopt_optimizer_step plus the fused extras above (extras may be NULL). Same workspace size. */
+MOTEOPT_API int moteopt_optimizer_step_ex(const moteopt_muon_param* muon, int n_muon,
+                                          const moteopt_muon_config* muon_cfg, const moteopt_adamw_tensor* adamw,
+                                          int n_adamw, const moteopt_adamw_hparams* adamw_hp,
+                                          const moteopt_grad_config* grad_cfg, const moteopt_step_extras* extras,
+                                          float* out_norm, void* workspace, size_t workspace_bytes,
+                                          moteopt_stream_t stream);
 
 /* ---- the sharded (multi-GPU) step of the same path, which the reference does not have: each rank updates only the
  *      parameters it owns, so the global clip is assembled from per-rank sums of squares.

@@ -22,7 +22,8 @@ STATUS_NONFINITE = 4
 EXPORTS = (
     "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count",
     "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
-    "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_with_coef",
+    "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_ex",
+    "moteopt_optimizer_step_with_coef",
     "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply",
     "moteopt_ipc_export", "moteopt_ipc_import", "moteopt_ipc_close",
     "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
@@ -58,6 +59,10 @@ class GradConfig(C.Structure):
     _fields_ = [("clip", C.c_int), ("max_norm", C.c_double), ("grad_divisor", C.c_double)]
 
 
+class StepExtras(C.Structure):
+    _fields_ = [("ema", C.POINTER(C.c_void_p)), ("ema_weight", C.c_double), ("muon_norms", C.c_void_p)]
+
+
 class MoteoptError(RuntimeError):
     pass
 
@@ -81,6 +86,9 @@ def _load() -> C.CDLL:
         "moteopt_optimizer_step_with_coef": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
                                                    C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp, vp, sz,
                                                    vp]),
+        "moteopt_optimizer_step_ex": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(AdamWTensor), i32,
+                                            C.POINTER(AdamWHparams), C.POINTER(GradConfig), C.POINTER(StepExtras), vp,
+                                            vp, sz, vp]),
         "moteopt_optimizer_step_with_coef_out": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
                                                        C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp,
                                                        C.POINTER(vp), vp, sz, vp]),

@@ -189,7 +189,8 @@ struct Layout {
   std::vector<GroupPlan> groups;          // Newton-Schulz shape groups, in launch order
   std::vector<int> mat_chunk_start;       // per matrix (group-major order): sum-of-squares chunk prefix
   std::vector<int> norm_tensor_chunk_start;
-  size_t off_norm = 0, off_mom = 0, off_den = 0, off_done = 0, bytes = 0;
+  std::vector<int> param_apply_start;     // per Muon param: its apply-pass partials (norm tracking), in slice order
+  size_t off_norm = 0, off_mom = 0, off_den = 0, off_done = 0, off_apply = 0, bytes = 0;
 };
 
 constexpr int kMaxMatsPerGroup = ns::kMaxApply;
@@ -200,6 +201,13 @@ struct ShapeKey {
 };
 
 // shapes: per source (batch, rows, cols); norm_numels: the tensors of the global grad norm (may be empty)
+// Partials one matrix's apply pass writes: one per 16K-element chunk when the matrix is iterated as stored (no
+// transpose, no padding: the flat kernel), else one per 64 x 64 tile (the tiled kernel).
+int64_t apply_partials_per_slice(int64_t r, int64_t c) {
+  const bool flat = r <= c && r % 8 == 0 && c % 8 == 0;
+  return flat ? cdiv(r * c, kChunk) : cdiv(c, kNormTile) * cdiv(r, kNormTile);
+}
+
 int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shapes, const std::vector<int64_t>& norm_numels,
                  int ns_steps, Layout* L) {
   L->groups.clear();
@@ -252,7 +260,14 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
   L->off_den = off;
   off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 256);
   L->off_done = off;   // persistent Newton-Schulz: per matrix of a launch set and phase, completion arrivals
-  off = align_up(off + 4 * 3 * static_cast<size_t>(ns::kMaxApply), 1024);
+  off = align_up(off + 4 * 3 * static_cast<size_t>(ns::kMaxApply), 256);
+  L->param_apply_start.assign(1, 0);   // the apply pass's sums of squares, contiguous per Muon param
+  for (const auto& sh : shapes) {
+    const int64_t b = std::get<0>(sh), r = std::get<1>(sh), c = std::get<2>(sh);
+    L->param_apply_start.push_back(L->param_apply_start.back() + static_cast<int>(b * apply_partials_per_slice(r, c)));
+  }
+  L->off_apply = off;
+  off = align_up(off + 4 * static_cast<size_t>(L->param_apply_start.back()), 1024);
   for (GroupPlan& g : L->groups) {
     const size_t cnt = g.mats.size();
     const size_t xb = cnt * g.m * g.n * 2, ab = cnt * g.m * g.m * 2;
@@ -388,10 +403,22 @@ int launch_finalize(const std::vector<int>& tensor_chunk_start, const float* par
   return MOTEOPT_OK;
 }
 
+// torch's lerp constants for a Python-float weight on fp32 tensors: w and 1 - w in fp32, |w| < 0.5 picks the form
+EmaConsts ema_consts(double weight) {
+  EmaConsts E;
+  std::memset(&E, 0, sizeof(E));
+  E.w = static_cast<float>(weight);
+  E.omw = 1.0f - E.w;
+  E.small = std::fabs(E.w) < 0.5f;
+  return E;
+}
+
+// ema: per AdamW tensor, an EMA buffer or null (null array: none)
 int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp, bool has_div, float div,
-                 const float* coef, int sms, cudaStream_t st) {
-  AdamArgs A;
+                 const float* coef, int sms, cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0) {
+  static thread_local AdamArgs A;
   std::memset(&A, 0, sizeof(A));
+  A.ema = ema_consts(ema_weight);
   A.has_div = has_div;
   A.div = div;
   A.coef = coef;
@@ -431,6 +458,7 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       S.decay_mul = static_cast<float>(1.0 - x.lr * x.weight_decay);
       S.lr = x.lr;
       S.wd = x.weight_decay;
+      S.ema = ema != nullptr ? ema[s0 + i] : nullptr;
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kChunk));
     }
     if (A.chunk_start[cnt] == 0) continue;
@@ -471,6 +499,8 @@ int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cf
   return MOTEOPT_OK;
 }
 
+EmaConsts ema_consts(double weight);
+
 // A matrix is iterated as it is stored when it has no more rows than columns and needs no padding: its X0 / final
 // iterate then has the parameter's own layout and the normalise / apply are flat passes.
 bool stored_as_iterated(const GroupPlan& g) { return !g.transposed && g.m == g.rows && g.n == g.cols; }
@@ -496,13 +526,14 @@ int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float di
   return MOTEOPT_OK;
 }
 
-int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cudaStream_t st) {
+int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cudaStream_t st, double ema_weight = 0.0) {
   static thread_local FlatOutArgs A;
   for (size_t s0 = 0; s0 < segs.size(); s0 += kMaxFlatSeg) {
     const int cnt = static_cast<int>(std::min(segs.size() - s0, static_cast<size_t>(kMaxFlatSeg)));
     std::memset(&A, 0, sizeof(A));
     A.n = cnt;
     A.apply = apply;
+    A.ema = ema_consts(ema_weight);
     for (int i = 0; i < cnt; ++i) {
       A.seg[i] = segs[s0 + i];
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(A.seg[i].numel, kChunk));
@@ -757,17 +788,28 @@ std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const mo
 }
 
 // The Muon apply (muon.py:97-99) from the final iterate: X0 when ns_steps == 0, else the last phase's output.
+// ema: per Muon param, an EMA buffer or null (null array: none)
+// norms: n_muon outputs (||p_new||_F per Muon param), or null
 int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int src,
-              cudaStream_t st) {
+              cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0, float* norms = nullptr) {
+  float* apply_partials = reinterpret_cast<float*>(ws + L.off_apply);
   const std::vector<ns::MatApply> tab = muon_apply_table(P, cfg, L);
-  OutArgs A;
+  static thread_local OutArgs A;
   std::memset(&A, 0, sizeof(A));
   A.apply = 1;
+  A.ema = ema_consts(ema_weight);
   std::vector<OutMat> all;
   std::vector<FlatOutSeg> flat;
   size_t k = 0;
   for (const GroupPlan& g : L.groups)
     for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
+      const MatRef& ref = g.mats[pos];
+      const moteopt_muon_param& pp = P[ref.src];
+      float* e = nullptr;   // this matrix's slice of its param's EMA
+      if (ema != nullptr && ema[ref.src] != nullptr) e = ema[ref.src] + static_cast<int64_t>(ref.slice) * pp.rows * pp.cols;
+      float* part = norms == nullptr ? nullptr
+                                     : apply_partials + L.param_apply_start[ref.src] +
+                                           static_cast<int64_t>(ref.slice) * apply_partials_per_slice(pp.rows, pp.cols);
       if (stored_as_iterated(g)) {
         FlatOutSeg S;
         std::memset(&S, 0, sizeof(S));
@@ -778,6 +820,8 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
         S.decay_mul = tab[k].decay_mul;
         S.has_decay = tab[k].has_decay;
         S.scale = tab[k].scale;
+        S.ema = e;
+        S.partials = part;
         flat.push_back(S);
         continue;
       }
@@ -785,6 +829,8 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       std::memset(&M, 0, sizeof(M));
       M.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
       M.out = tab[k].p;
+      M.ema = e;
+      M.partials = part;
       M.rows = g.rows;
       M.cols = g.cols;
       M.m_pad = g.m;
@@ -798,8 +844,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       M.scale = tab[k].scale;
       all.push_back(M);
     }
-  (void)P;
-  MO_TRY(launch_flat_out(flat, 1, device_sms(), st));
+  MO_TRY(launch_flat_out(flat, 1, device_sms(), st, ema_weight));
   for (size_t s0 = 0; s0 < all.size(); s0 += kMaxOutMat) {
     const size_t cnt = std::min(all.size() - s0, static_cast<size_t>(kMaxOutMat));
     A.n = static_cast<int>(cnt);
@@ -810,6 +855,22 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
     }
     ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_out_kernel");
+  }
+  if (norms != nullptr) {   // ||p_new||_F per param: fixed-order fp64 sum of its partials (eps 0)
+    const int np = static_cast<int>(L.param_apply_start.size()) - 1;
+    static thread_local DenomArgs D;
+    std::memset(&D, 0, sizeof(D));
+    D.eps = 0.f;
+    D.partials = apply_partials;
+    D.den = norms;
+    for (int s0 = 0; s0 < np; s0 += kMaxDenom) {
+      const int cnt = std::min(np - s0, kMaxDenom);
+      D.n = cnt;
+      D.base = s0;
+      for (int i = 0; i <= cnt; ++i) D.chunk_start[i] = L.param_apply_start[s0 + i];
+      mat_denom_kernel<<<(cnt + 7) / 8, 256, 0, st>>>(D);
+      MO_LAUNCHED("mat_denom_kernel");
+    }
   }
   return MOTEOPT_OK;
 }
@@ -883,8 +944,11 @@ std::vector<std::tuple<int64_t, int64_t, int64_t>> muon_shapes(const moteopt_muo
 // The whole step: (optional) grad norm + clip coefficient, AdamW, Muon.
 int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* mcfg, const moteopt_adamw_tensor* adam,
              int n_adam, const moteopt_adamw_hparams* adamw_hp, const moteopt_grad_config* gcfg, const float* ext_scale,
-             float* out_norm, void* workspace, size_t ws_bytes, cudaStream_t st, void* const* muon_out = nullptr) {
+             float* out_norm, void* workspace, size_t ws_bytes, cudaStream_t st, void* const* muon_out = nullptr,
+             const moteopt_step_extras* ex = nullptr) {
   const moteopt_adamw_hparams* ahp = adamw_hp;
+  float* const* ema = ex != nullptr ? ex->ema : nullptr;
+  const double ema_w = ex != nullptr ? ex->ema_weight : 0.0;
   MO_TRY(check_muon(muon, n_muon, mcfg));
   MO_TRY(check_adamw(adam, n_adam, ahp));
   int sms = 0;
@@ -916,7 +980,7 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     coef = &hdr->coef;
     if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
   }
-  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st));
+  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w));
   if (n_muon > 0) {
     MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st));
     int final_src = 0;
@@ -926,7 +990,8 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
       if (t_ns_ev[1] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[1], st));
     }
     if (muon_out != nullptr) MO_TRY(run_copy_out(muon, L, ws, final_src, muon_out, sms, st));
-    else MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st));
+    else MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st, ema != nullptr ? ema + n_adam : nullptr, ema_w,
+                          ex != nullptr ? ex->muon_norms : nullptr));
   }
   return MOTEOPT_OK;
 }
@@ -1015,6 +1080,14 @@ int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muon, const mot
                            size_t workspace_bytes, moteopt_stream_t stream) {
   return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, grad_cfg, nullptr, out_norm, workspace,
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moteopt_optimizer_step_ex(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,
+                              const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* adamw_hp,
+                              const moteopt_grad_config* grad_cfg, const moteopt_step_extras* extras, float* out_norm,
+                              void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, grad_cfg, nullptr, out_norm, workspace,
+                  workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr, extras);
 }
 
 int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,

@@ -238,6 +238,11 @@ struct AdamConsts {
   int lerp_small;
 };
 
+__device__ __forceinline__ float ema_lerp(float e, float p, const EmaConsts& E) {
+  const float d = __fsub_rn(p, e);
+  return E.small ? fmaf(E.w, d, e) : fmaf(-E.omw, d, p);
+}
+
 __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v, const AdamSeg& S, const AdamConsts& K) {
   if (S.has_decay) p = __fmul_rn(p, S.decay_mul);
   const float d = __fsub_rn(g, m);
@@ -264,7 +269,8 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
     }
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
-    const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype);
+    const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype) &&
+                     (S.ema == nullptr || aligned16(S.ema));
     int64_t i0 = begin;
     if (vec) {
       const int64_t vend = begin + ((end - begin) & ~int64_t(3));
@@ -280,6 +286,12 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
         *reinterpret_cast<float4*>(S.p + i) = p;
         *reinterpret_cast<float4*>(S.m + i) = m;
         *reinterpret_cast<float4*>(S.v + i) = v;
+        if (S.ema != nullptr) {
+          float4 e = *reinterpret_cast<float4*>(S.ema + i);
+          e.x = ema_lerp(e.x, p.x, A.ema); e.y = ema_lerp(e.y, p.y, A.ema);
+          e.z = ema_lerp(e.z, p.z, A.ema); e.w = ema_lerp(e.w, p.w, A.ema);
+          *reinterpret_cast<float4*>(S.ema + i) = e;
+        }
       }
       i0 = vend;
     }
@@ -287,6 +299,7 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
       float p = S.p[i], m = S.m[i], v = S.v[i];
       adam_elem(p, X(load_g1(S.g, i, S.dtype)), m, v, S, K);
       S.p[i] = p; S.m[i] = m; S.v[i] = v;
+      if (S.ema != nullptr) S.ema[i] = ema_lerp(S.ema[i], p, A.ema);
     }
   }
 }
@@ -431,17 +444,19 @@ __global__ void __launch_bounds__(kMtThreads, 4) ns_normalize_flat_kernel(const 
 // The flat counterpart of ns_out_kernel: the Muon apply of muon.py:97-99 (p = p*(1-decay) if decay;
 // p += -lr*(O*scale)) into the fp32 parameter, or a copy of the bf16 iterate to the output.
 __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_constant__ FlatOutArgs A) {
+  __shared__ float red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const FlatOutSeg& S = A.seg[s];
+    float sq = 0.f;   // sum of the updated param's squares (norm tracking), fixed per-thread order
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(S.x);
     int64_t i0 = begin;
     if (A.apply) {
       float* p = reinterpret_cast<float*>(S.out);
-      if (end - begin == kChunk && aligned8(x) && aligned16(p)) {
+      if (end - begin == kChunk && aligned8(x) && aligned16(p) && (S.ema == nullptr || aligned16(S.ema))) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint2 w[8];
@@ -464,6 +479,14 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
               qe[e] = fmaf(S.neg_lr, __fmul_rn(o[e], S.scale), v);
             }
             *reinterpret_cast<float4*>(p + i) = q[k];
+            sq = fmaf(q[k].x, q[k].x, sq); sq = fmaf(q[k].y, q[k].y, sq);
+            sq = fmaf(q[k].z, q[k].z, sq); sq = fmaf(q[k].w, q[k].w, sq);
+            if (S.ema != nullptr) {   // the EMA follows the updated param in the same pass
+              float4 e = *reinterpret_cast<float4*>(S.ema + i);
+              e.x = ema_lerp(e.x, q[k].x, A.ema); e.y = ema_lerp(e.y, q[k].y, A.ema);
+              e.z = ema_lerp(e.z, q[k].z, A.ema); e.w = ema_lerp(e.w, q[k].w, A.ema);
+              *reinterpret_cast<float4*>(S.ema + i) = e;
+            }
           }
         }
         i0 = end;
@@ -471,7 +494,14 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
       for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
         float v = p[i];
         if (S.has_decay) v = __fmul_rn(v, S.decay_mul);
-        p[i] = fmaf(S.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
+        v = fmaf(S.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
+        p[i] = v;
+        sq = fmaf(v, v, sq);
+        if (S.ema != nullptr) S.ema[i] = ema_lerp(S.ema[i], v, A.ema);
+      }
+      if (S.partials != nullptr) {   // block-uniform: every thread of the block works on this chunk
+        const float tot = block_sum(sq, red);
+        if (threadIdx.x == 0) S.partials[c - A.chunk_start[s]] = tot;
       }
     } else {
       __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(S.out);
@@ -602,7 +632,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
   }
-  const bool vec = (M.cols % 4 == 0) && aligned16(M.out);
+  const bool vec = (M.cols % 4 == 0) && aligned16(M.out) && (M.ema == nullptr || aligned16(M.ema));
+  float sq = 0.f;   // apply mode: sum of the updated param's squares over this thread's elements
 #pragma unroll
   for (int k = 0; k < 4; ++k) {   // output rows r0 + ty + 16k, columns c0 + 4tx .. +3
     const int orow = r0 + ty + kTileRowsPerPass * k, ocol = c0 + 4 * tx;
@@ -620,13 +651,23 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
           pe[e] = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
         }
         *reinterpret_cast<float4*>(p + idx) = pv;
+        sq = fmaf(pv.x, pv.x, sq); sq = fmaf(pv.y, pv.y, sq); sq = fmaf(pv.z, pv.z, sq); sq = fmaf(pv.w, pv.w, sq);
+        if (M.ema != nullptr) {
+          float4 ev = *reinterpret_cast<float4*>(M.ema + idx);
+          ev.x = ema_lerp(ev.x, pv.x, A.ema); ev.y = ema_lerp(ev.y, pv.y, A.ema);
+          ev.z = ema_lerp(ev.z, pv.z, A.ema); ev.w = ema_lerp(ev.w, pv.w, A.ema);
+          *reinterpret_cast<float4*>(M.ema + idx) = ev;
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
           if (ocol + e < M.cols) {
             float q = p[idx + e];
             if (M.has_decay) q = __fmul_rn(q, M.decay_mul);
-            p[idx + e] = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+            q = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+            p[idx + e] = q;
+            sq = fmaf(q, q, sq);
+            if (M.ema != nullptr) M.ema[idx + e] = ema_lerp(M.ema[idx + e], q, A.ema);
           }
       }
     } else {
@@ -635,6 +676,11 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
       for (int e = 0; e < 4; ++e)
         if (ocol + e < M.cols) o[idx + e] = __float2bfloat16_rn(v[k][e]);
     }
+  }
+  if (A.apply && M.partials != nullptr) {   // block-uniform (one matrix per grid row)
+    __shared__ float red[kMtThreads / 32];
+    const float tot = block_sum(sq, red);
+    if (threadIdx.x == 0) M.partials[blockIdx.x] = tot;
   }
 }
 

@@ -51,6 +51,14 @@ struct CoefArgs {
   int* status;
 };
 
+// ---- the weights' EMA (mote/train/train.py:950-953: _foreach_lerp_(ema, params, w) after the step), fused into the
+// passes that write the params: e = e + w*(p - e) for |w| < 0.5, else p - (p - e)*(1 - w), as torch's lerp
+struct EmaConsts {
+  float w, omw;              // weight, 1 - weight (fp32, as torch's opmath)
+  int small;
+  int pad_;
+};
+
 // ---- AdamW (torch.optim.AdamW single-tensor update, constructed at mote/train/train.py:98)
 constexpr int kMaxAdamSeg = 320;
 struct AdamSeg {
@@ -66,6 +74,7 @@ struct AdamSeg {
   int has_decay;
   int pad_;
   double lr, wd;             // for the device-step mode, which recomputes the three scalars above per step
+  float* ema;                // EMA of the param, lerped toward the updated param in the same pass, or null
 };
 struct AdamArgs {
   int n;
@@ -80,6 +89,7 @@ struct AdamArgs {
   float eps;
   const float* dstep;        // device step counter (already incremented for this step), or null: host scalars
   double beta1d, beta2d;
+  EmaConsts ema;
   int chunk_start[kMaxAdamSeg + 1];
   AdamSeg seg[kMaxAdamSeg];
 };
@@ -178,10 +188,13 @@ struct OutMat {
   int tiles_x, tiles;
   float neg_lr, decay_mul, scale;
   int has_decay;
+  float* ema;                // apply mode: EMA of the parameter ([R][C], fp32), or null
+  float* partials;           // apply mode: per tile, the sum of the updated param's squares, or null
 };
 struct OutArgs {
   int n;
   int apply;
+  EmaConsts ema;
   OutMat mat[kMaxOutMat];
 };
 
@@ -192,10 +205,13 @@ struct FlatOutSeg {
   int64_t numel;
   float neg_lr, decay_mul, scale;
   int has_decay;
+  float* ema;                // apply mode: EMA of the parameter (same layout), or null
+  float* partials;           // apply mode: per chunk of the segment, the sum of the updated param's squares, or null
 };
 struct FlatOutArgs {
   int n;
   int apply;
+  EmaConsts ema;
   int chunk_start[kMaxFlatSeg + 1];
   FlatOutSeg seg[kMaxFlatSeg];
 };

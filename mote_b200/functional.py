@@ -101,11 +101,18 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
                    rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
                    max_norm: Optional[float] = None, grad_divisor: Optional[float] = None,
                    out_norm: Optional[torch.Tensor] = None,
-                   device_step: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+                   device_step: Optional[torch.Tensor] = None,
+                   ema: Optional[Sequence[Optional[torch.Tensor]]] = None, ema_weight: float = 0.0,
+                   muon_norms: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
     AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
     max_norm is given. With `device_step` (a 0-dim fp32 CUDA tensor) AdamW's step count is that counter, which the
-    call increments on the device (the AdamItems' `step` is then ignored)."""
+    call increments on the device (the AdamItems' `step` is then ignored).
+
+    Fused extras (the work train.py:950-953 and elr.py:85-87 do in separate passes after the step):
+    `ema` - one fp32 buffer (or None) per AdamW item, then per Muon item, updated as
+    torch._foreach_lerp_(ema, params, ema_weight) in the pass that writes the params; `muon_norms` - an fp32 CUDA
+    tensor of len(muon) that receives ||p||_F of every Muon param after the update."""
     dev = _device(muon, adamw)
     m_arr, a_arr = muon_array(muon), adamw_array(adamw)
     nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adamw))
@@ -118,10 +125,31 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     gc = L.GradConfig(int(max_norm is not None), float(max_norm or 0.0), float(grad_divisor or 0.0))
     if max_norm is not None and out_norm is None:
         out_norm = torch.empty((), dtype=torch.float32, device=dev)
-    L.check(L.lib.moteopt_optimizer_step(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp), C.byref(gc),
-                                         C.c_void_p(out_norm.data_ptr() if out_norm is not None else 0),
-                                         C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
-            "moteopt_optimizer_step")
+    onorm = C.c_void_p(out_norm.data_ptr() if out_norm is not None else 0)
+    stream = C.c_void_p(stream_handle(dev))
+    if ema is None and muon_norms is None:
+        L.check(L.lib.moteopt_optimizer_step(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp),
+                                             C.byref(gc), onorm, C.c_void_p(ws.data_ptr()), ws.numel(), stream),
+                "moteopt_optimizer_step")
+        return out_norm
+    ex = L.StepExtras(None, float(ema_weight), None)
+    if ema is not None:
+        items = list(adamw) + list(muon)
+        if len(ema) != len(items):
+            raise ValueError(f"ema: {len(ema)} buffers for {len(items)} tensors (AdamW items, then Muon items)")
+        for e, it in zip(ema, items):
+            if e is not None:
+                _check_param(e, "EMA buffer")
+                if e.shape != it.param.shape:
+                    raise ValueError("EMA buffer shape mismatch")
+        ex.ema = L.array(C.c_void_p, [e.data_ptr() if e is not None else None for e in ema])
+    if muon_norms is not None:
+        if not (muon_norms.is_cuda and muon_norms.dtype == torch.float32 and muon_norms.numel() >= len(muon)):
+            raise ValueError("muon_norms must be an fp32 CUDA tensor with one element per Muon item")
+        ex.muon_norms = muon_norms.data_ptr()
+    L.check(L.lib.moteopt_optimizer_step_ex(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp),
+                                            C.byref(gc), C.byref(ex), onorm, C.c_void_p(ws.data_ptr()), ws.numel(),
+                                            stream), "moteopt_optimizer_step_ex")
     return out_norm
 
 

@@ -193,7 +193,8 @@ def set_lr(opt, lr: float):
 
 # -----------------------------------------------------------------------------------------------------------------
 @torch.no_grad()
-def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None) -> Optional[torch.Tensor]:
+def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Optional[dict] = None,
+               ema_decay: float = 0.0) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one library call:
 
         torch._foreach_div_(grads, total_n); gnorm = clip_grad_norm_(model.parameters(), clip); opt.step()
@@ -202,7 +203,10 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None) -> Opti
     the update kernels: the grads are read once for the norm and once for the update and never rewritten. Returns
     the pre-clip total grad norm (0-dim fp32 CUDA tensor) when max_norm is given. Only the parameters the optimizers
     own enter the norm; the reference passes model.parameters(), which is the same set when every trainable
-    parameter is in the optimizer (train.py:82-83 skips requires_grad=False ones, which have no grad)."""
+    parameter is in the optimizer (train.py:82-83 skips requires_grad=False ones, which have no grad).
+
+    `ema` ({param: fp32 EMA buffer}) with `ema_decay` folds train.py:950-953 (_foreach_lerp_(ema, params,
+    1 - ema_decay)) into the same step for the stepped params; the caller lerps any other params itself."""
     opts = getattr(opt, "opts", [opt])
     muon_sets: Dict[Tuple[int, float], List[MuonItem]] = {}
     adam_items: List[AdamWItem] = []
@@ -224,8 +228,11 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None) -> Opti
     div = None
     if grad_divisor is not None:
         div = float(grad_divisor.item()) if isinstance(grad_divisor, torch.Tensor) else float(grad_divisor)
+    bufs = None
+    if ema is not None:
+        bufs = [ema.get(it.param) for it in adam_items] + [ema.get(it.param) for it in muon_items]
     norm = F.optimizer_step(muon_items, adam_items, ns_steps=ns, rms_scale=rms, betas=betas, eps=eps,
-                            max_norm=max_norm, grad_divisor=div)
+                            max_norm=max_norm, grad_divisor=div, ema=bufs, ema_weight=1.0 - float(ema_decay))
     for o, bumped in bumps:
         o._bump(bumped)
     return norm

@@ -75,8 +75,11 @@ def test_workspace_sizes_follow_the_layout():
     n = lib.moteopt_newton_schulz_workspace_size(48, 768, 768)
     per = 48 * 768 * 768 * 2
     assert n >= 4 * per and n < 4 * per + 64 * 1024
-    # a transposed shape needs the same buffers as its transpose
-    assert lib.moteopt_newton_schulz_workspace_size(2, 3072, 768) == lib.moteopt_newton_schulz_workspace_size(2, 768, 3072)
+    # a transposed shape needs the same iteration buffers as its transpose; only the apply pass's norm partials
+    # differ (one per 16K-element chunk when iterated as stored, one per 64 x 64 tile when transposed)
+    a = lib.moteopt_newton_schulz_workspace_size(2, 3072, 768)
+    b = lib.moteopt_newton_schulz_workspace_size(2, 768, 3072)
+    assert abs(a - b) <= 4 * 2 * (3072 // 64) * (768 // 64) + 1024
     # invalid shapes report 0
     assert lib.moteopt_newton_schulz_workspace_size(0, 8, 8) == 0
     assert lib.moteopt_newton_schulz_workspace_size(1, -1, 8) == 0
