@@ -134,6 +134,7 @@ class Compute:
     coef: Callable
     update: Callable
     apply: Callable
+    set_step: Optional[Callable] = None   # set_step(device, n): AdamW's step count, when the compute keeps one
 
 
 def _reduce_scatter(out: torch.Tensor, flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
@@ -220,6 +221,72 @@ class ShardedStep:
             L.check(L.lib.moteopt_ipc_close(C.c_void_p(b)), "moteopt_ipc_close")
         self._peer_bases, self.peer_ptrs = [], None
         dist.barrier(group=self.group)
+
+    @torch.no_grad()
+    def state_dict(self) -> dict:
+        """The optimizer state in the trainer's checkpoint layout, {"multi": [adamw_sd, muon_sd]} (train.py:68-73;
+        each in torch.optim's state_dict form, AdamW state {step, exp_avg, exp_avg_sq}, Muon {momentum_buffer},
+        params numbered in plan order). Assembled on the devices with collectives: the ZeRO-1 slices of exp_avg /
+        exp_avg_sq are all-gathered, the momentum buffers go from their owners through an all-gather of an fp32
+        copy of the Muon region. Collective; every rank gets the whole dict, its tensors views of device buffers."""
+        plan, r = self.plan, self.rank
+        dev = self.pa.device
+        m_full = torch.zeros(plan.adam_len, dtype=torch.float32, device=dev)
+        v_full = torch.zeros(plan.adam_len, dtype=torch.float32, device=dev)
+        m_full[r * plan.a_seg:(r + 1) * plan.a_seg].copy_(self.m_state)
+        v_full[r * plan.a_seg:(r + 1) * plan.a_seg].copy_(self.v_state)
+        _all_gather_inplace(m_full, plan.a_seg, r, self.group)
+        _all_gather_inplace(v_full, plan.a_seg, r, self.group)
+        mb = torch.zeros(plan.muon_len, dtype=torch.float32, device=self.pm.device)
+        for i in self.mine:
+            self.muon_view(mb, i).copy_(self.bufs[i])
+        _all_gather_inplace(mb, plan.m_seg, r, self.group)
+        groups, order = {}, []
+        for i, wd in enumerate(self.adam_wd):
+            if wd not in groups:
+                groups[wd] = []
+                order.append(wd)
+            groups[wd].append(i)
+        adam_groups, idx, adam_state = [], 0, {}
+        for wd in order:   # torch numbers a state_dict's params in group order
+            ids = []
+            for i in groups[wd]:
+                adam_state[idx] = {"step": torch.tensor(float(self.steps)), "exp_avg": self.adam_view(m_full, i),
+                                   "exp_avg_sq": self.adam_view(v_full, i)}
+                ids.append(idx)
+                idx += 1
+            adam_groups.append({"lr": self.adam_lr, "weight_decay": wd, "params": ids, "plan_index": groups[wd]})
+        muon_state = {i: {"momentum_buffer": self.muon_view(mb, i)} for i in range(len(plan.muon_shapes))}
+        muon_groups = [{"lr": self.muon_lr, "momentum": self.momentum, "nesterov": self.nesterov,
+                        "weight_decay": self.muon_wd, "params": list(range(len(plan.muon_shapes)))}]
+        return {"multi": [{"state": adam_state, "param_groups": adam_groups},
+                          {"state": muon_state, "param_groups": muon_groups}]}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd: dict) -> None:
+        """Resume from state_dict()'s layout (on any device or the CPU): each rank takes its ZeRO-1 slices and the
+        momentum buffers of the matrices it owns. Local, no collectives."""
+        adam_sd, muon_sd = sd["multi"]
+        plan = self.plan
+        by_plan = {}
+        for g in adam_sd["param_groups"]:
+            for k, i in zip(g["params"], g.get("plan_index", g["params"])):
+                by_plan[i] = adam_sd["state"][k]
+        base = self.rank * plan.a_seg
+        steps = None
+        for i, start, n in self.pieces:
+            st = by_plan[i]
+            o = plan.adam_off[i] + start - base
+            self.m_state[o:o + n].copy_(st["exp_avg"].reshape(-1)[start:start + n])
+            self.v_state[o:o + n].copy_(st["exp_avg_sq"].reshape(-1)[start:start + n])
+            steps = int(float(st["step"]))
+        if steps is None and by_plan:
+            steps = int(float(next(iter(by_plan.values()))["step"]))
+        self.steps = steps or 0
+        for i in self.mine:
+            self.bufs[i].copy_(muon_sd["state"][i]["momentum_buffer"].reshape(self.bufs[i].shape))
+        if self.compute.set_step is not None:
+            self.compute.set_step(self.pa.device, self.steps)
 
     def muon_view(self, flat: torch.Tensor, i: int) -> torch.Tensor:
         o, s = self.plan.muon_off[i], self.plan.muon_shapes[i]
@@ -360,4 +427,9 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
         L.check(L.lib.moteopt_muon_apply(arr, len(muon), C.byref(cfg), ptrs, C.c_void_p(stream_handle(dev))),
                 "moteopt_muon_apply")
 
-    return Compute(sumsq, coef, update, apply)
+    def set_step(dev, n):
+        if dev not in counter:
+            counter[dev] = torch.zeros((), dtype=torch.float32, device=dev)
+        counter[dev].fill_(float(n))
+
+    return Compute(sumsq, coef, update, apply, set_step)

@@ -109,8 +109,29 @@ def _rank_main(rank, world, port, out_dir):
             for i, g in enumerate(ag):
                 st.adam_view(ga, i).copy_(torch.from_numpy(g))
             norms.append(float(st.step(max_norm=CLIP, grad_divisor=DIV)))
-        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), pm=pm.numpy(), pa=pa.numpy(), norms=np.array(norms),
-                 muon_off=np.array(plan.muon_off), adam_off=np.array(plan.adam_off))
+        # the sharded checkpoint: the whole state on every rank, then a fresh step object resumed from it must
+        # continue bit for bit like the original
+        pm_after, pa_after = pm.clone(), pa.clone()
+        sd = st.state_dict()
+        adam_sd, muon_sd = sd["multi"]
+        idx = {i: k for g in adam_sd["param_groups"] for k, i in zip(g["params"], g["plan_index"])}
+        ckpt = {f"m{i}": adam_sd["state"][idx[i]]["exp_avg"].numpy().copy() for i in range(len(w.adam_shapes))}
+        ckpt.update({f"v{i}": adam_sd["state"][idx[i]]["exp_avg_sq"].numpy().copy() for i in range(len(w.adam_shapes))})
+        ckpt.update({f"b{i}": muon_sd["state"][i]["momentum_buffer"].numpy().copy() for i in range(len(w.muon_shapes))})
+        st2 = ShardedStep(plan, rank, pm.clone(), pa.clone(), gm, ga, oracle_compute(w), muon_lr=w.muon_lr,
+                          muon_wd=w.muon_wd, adam_lr=w.adam_lr,
+                          adam_wd=[w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))])
+        st2.load_state_dict(sd)
+        ag, mg = configs.make_grads(w, seed=100 + rank, step=STEPS)
+        for i, g in enumerate(mg):
+            st.muon_view(gm, i).copy_(torch.from_numpy(g))
+        for i, g in enumerate(ag):
+            st.adam_view(ga, i).copy_(torch.from_numpy(g))
+        st.step(max_norm=CLIP, grad_divisor=DIV)
+        st2.step(max_norm=CLIP, grad_divisor=DIV)
+        resumed = bool(torch.equal(st.pm, st2.pm) and torch.equal(st.pa, st2.pa))
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), pm=pm_after.numpy(), pa=pa_after.numpy(), norms=np.array(norms),
+                 muon_off=np.array(plan.muon_off), adam_off=np.array(plan.adam_off), resumed=resumed, **ckpt)
     finally:
         dist.destroy_process_group()
 
@@ -140,7 +161,7 @@ def _reference(world):
         O.muon_step(inp.muon_params, allg[len(inp.adam_params):], bufs,
                     O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=(w.muon_lr * w.muon_wd) / w.muon_lr,
                                 ns_steps=w.ns_steps))
-    return inp, norms
+    return inp, norms, ms, vs, bufs
 
 
 def test_plan_owns_every_matrix_once_and_balances_cost():
@@ -165,7 +186,7 @@ def test_two_cpu_ranks_match_one_process(tmp_path):
     outs = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     assert np.array_equal(outs[0]["pm"], outs[1]["pm"]) and np.array_equal(outs[0]["pa"], outs[1]["pa"])
     assert np.array_equal(outs[0]["norms"], outs[1]["norms"])
-    inp, norms = _reference(world)
+    inp, norms, ms, vs, bufs = _reference(world)
     assert np.allclose(outs[0]["norms"], norms, rtol=1e-6, atol=0)
     w = small_workload()
     for i, (p, s) in enumerate(zip(inp.muon_params, w.muon_shapes)):
@@ -175,3 +196,10 @@ def test_two_cpu_ranks_match_one_process(tmp_path):
     for i, (p, s) in enumerate(zip(inp.adam_params, w.adam_shapes)):
         o = int(outs[0]["adam_off"][i])
         assert np.array_equal(outs[0]["pa"][o:o + p.size].reshape(s), p), i
+    # the sharded checkpoint holds the single-process optimizer state, and resuming from it is bitwise
+    for r in range(world):
+        assert bool(outs[r]["resumed"])
+        for i in range(len(w.adam_shapes)):
+            assert np.array_equal(outs[r][f"m{i}"], ms[i]) and np.array_equal(outs[r][f"v{i}"], vs[i]), i
+        for i in range(len(w.muon_shapes)):
+            assert np.array_equal(outs[r][f"b{i}"], bufs[i]), i
