@@ -163,33 +163,39 @@ __global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// per-tensor norms -> total norm (the norm of the per-tensor norms, as torch's get_total_norm) -> clip coefficient
+// per-tensor norms -> total norm (the norm of the per-tensor norms, as torch's get_total_norm) -> clip coefficient.
+// One warp per tensor (lanes sum strided chunk partials in fp64, then a fixed xor tree), the per-tensor norms kept in
+// shared memory, then warp 0 sums their squares in the same fixed way: deterministic, and no serial chain of loads.
 __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_constant__ FinalizeArgs A) {
-  __shared__ double red[32];
-  double acc = 0.0;
-  for (int t = threadIdx.x; t < A.n_tensors; t += blockDim.x) {
+  __shared__ float tnorm[kMaxFinalTensors];
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  const int nwarps = static_cast<int>(blockDim.x >> 5);
+  for (int t = warp; t < A.n_tensors; t += nwarps) {
     double s = 0.0;
-    for (int c = A.tensor_chunk_start[t]; c < A.tensor_chunk_start[t + 1]; ++c) s += static_cast<double>(A.partials[c]);
-    const float nt = static_cast<float>(sqrt(s));
-    acc += static_cast<double>(nt) * static_cast<double>(nt);
-  }
+    for (int c = A.tensor_chunk_start[t] + lane; c < A.tensor_chunk_start[t + 1]; c += 32)
+      s += static_cast<double>(A.partials[c]);
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) tnorm[t] = static_cast<float>(sqrt(s));
+  }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    double s = 0.0;
-    for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += red[k];
-    const float total = static_cast<float>(sqrt(s));
-    float coef = 1.0f;
-    if (A.has_clip) {
-      // clamp(max_norm / (total + 1e-6), max=1) in fp32; a NaN norm gives a NaN coefficient, as in torch
-      const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
-      coef = (c > 1.0f) ? 1.0f : c;
+  if (warp == 0) {
+    double acc = 0.0;
+    for (int t = lane; t < A.n_tensors; t += 32) acc += static_cast<double>(tnorm[t]) * static_cast<double>(tnorm[t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      const float total = static_cast<float>(sqrt(acc));
+      float coef = 1.0f;
+      if (A.has_clip) {
+        // clamp(max_norm / (total + 1e-6), max=1) in fp32; a NaN norm gives a NaN coefficient, as in torch
+        const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
+        coef = (c > 1.0f) ? 1.0f : c;
+      }
+      A.out[0] = total;
+      A.out[1] = coef;
+      if (!isfinite(total)) atomicOr(A.status, kStatusNonFinite);
     }
-    A.out[0] = total;
-    A.out[1] = coef;
-    if (!isfinite(total)) atomicOr(A.status, kStatusNonFinite);
   }
 }
 
