@@ -114,10 +114,11 @@ MOTEOPT_API const char* moteopt_last_error(void);
 MOTEOPT_API unsigned long long moteopt_launch_count(void);
 MOTEOPT_API int moteopt_profile_ns_events(void* start_event, void* end_event);
 
-/* Newton-Schulz launch mode (no counterpart in the reference). 1 (the default): all iterations of a step run as one
- * cooperative launch whose tiles wait on per-matrix completion counters; 0: one launch per phase and iteration.
- * Both compute the same bits. Process-wide; returns the previous mode. */
-MOTEOPT_API int moteopt_ns_set_persistent(int enable);
+/* Newton-Schulz launch mode (no counterpart in the reference). 1: all iterations of a step run as one cooperative
+ * launch whose tiles wait on per-matrix completion counters; 0: one launch per phase and iteration; -1 (the
+ * default): the persistent launch for problems of up to 48 waves of tiles per iteration, per-phase launches above.
+ * All compute the same bits. Process-wide; returns the previous mode. */
+MOTEOPT_API int moteopt_ns_set_persistent(int mode);
 
 /* Read (and optionally clear) the workspace's status word and the last [total norm, clip coefficient].
  * Synchronises `stream`. Either output may be NULL. */

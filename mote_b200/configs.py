@@ -66,6 +66,16 @@ class Workload:
             tot += batch * self.ns_steps * (2.0 * upper * b + 2.0 * upper * a + 2.0 * a * a * b)
         return tot
 
+    def ns_tiles_per_iter(self, tile: int = 256) -> int:
+        """256 x 256 output tiles of one Newton-Schulz iteration (upper-triangle Gram and A A blocks, full B X)."""
+        tot = 0
+        for s in self.muon_shapes:
+            batch = int(np.prod(s[:-2])) if len(s) > 2 else 1
+            a, b = min(s[-2], s[-1]), max(s[-2], s[-1])
+            t, u = -(-a // tile), -(-b // tile)
+            tot += batch * (t * (t + 1) + t * u)
+        return tot
+
     def state_bytes(self) -> float:
         """Algorithmic HBM bytes per step: Muon 20 B/element (bf16 grad read twice, fp32 momentum and param read
         and written), AdamW 28 B/element (bf16 grad twice, fp32 param, exp_avg, exp_avg_sq read and written)."""

@@ -35,7 +35,11 @@ int fail(int code, const std::string& msg) {
   } while (0)
 
 std::atomic<unsigned long long> g_launches{0};
-std::atomic<int> g_ns_persistent{1};   // Newton-Schulz launch mode (moteopt_ns_set_persistent)
+std::atomic<int> g_ns_persistent{-1};   // Newton-Schulz launch mode (moteopt_ns_set_persistent): 1, 0, or -1 = auto
+// Auto mode: one persistent launch while an iteration is at most this many waves of CTA-pair tiles; above it the
+// per-phase launches' ramps are amortised and their leaner tiles win (measured: c1 at 32 waves favours the
+// persistent launch, c2 at 197 waves the per-phase launches by ~10 %).
+constexpr int kPersistentMaxWaves = 48;
 thread_local cudaEvent_t t_ns_ev[2] = {nullptr, nullptr};
 
 #define MO_LAUNCHED(what)                                                                      \
@@ -735,7 +739,8 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
       Lh.per_iter += Lh.phase_tiles[ph];
     }
     const int pairs = device_pairs();
-    if (g_ns_persistent.load(std::memory_order_relaxed)) {
+    const int mode = g_ns_persistent.load(std::memory_order_relaxed);
+    if (mode == 1 || (mode < 0 && Lh.per_iter <= kPersistentMaxWaves * pairs)) {
       // one cooperative launch for every iteration; the completion counters start at zero
       MO_CUDA(cudaMemsetAsync(done, 0, sizeof(int) * 3 * static_cast<size_t>(first), st));
       Lh.done = done;
@@ -1046,7 +1051,7 @@ int moteopt_ipc_close(void* base) {
   return MOTEOPT_OK;
 }
 
-int moteopt_ns_set_persistent(int enable) { return g_ns_persistent.exchange(enable ? 1 : 0); }
+int moteopt_ns_set_persistent(int mode) { return g_ns_persistent.exchange(mode < 0 ? -1 : (mode ? 1 : 0)); }
 
 int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream) {
   if (workspace == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");
