@@ -77,6 +77,16 @@ def run(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
         ns_local = statistics.mean(a.elapsed_time(b) for a, b in ns_ev) if st.mine else 0.0
+        # per-phase breakdown of eager steps (CUDA events between the phases of ShardedStep.step)
+        phases = ["reduce_scatter", "grad_norm", "owned_update", "exchange", "apply_all"]
+        per = {k: [] for k in phases}
+        for _ in range(5):
+            marks = []
+            st.step(max_norm=w.clip, marks=marks)
+            torch.cuda.synchronize(dev)
+            for (_, a), (name, b) in zip(marks, marks[1:]):
+                per[name].append(a.elapsed_time(b))
+        breakdown = [statistics.median(per[k]) for k in phases]
         # the whole sharded step (NCCL collectives + kernels) captured in a CUDA graph and replayed
         graph = None
         capture_error = ""
@@ -136,7 +146,8 @@ def run(args, rank: int, world: int, local_rank: int):
         e2e_local = h0.elapsed_time(h1) / e2e_steps
 
         my_flops = sum(w.ns_steps * _ns_flops_issued(w.muon_shapes[i]) for i in st.mine)
-        vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops], dtype=torch.float64, device=dev)
+        vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops] + breakdown, dtype=torch.float64,
+                            device=dev)
         allv = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(allv, vals)
         allv = torch.stack(allv).cpu()
@@ -169,6 +180,8 @@ def run(args, rank: int, world: int, local_rank: int):
                     "h2d_bytes_per_step": int((st.gm.numel() + st.ga.numel()) * 2), "d2h_bytes_per_step": 4},
             "clocks": clk.summary(),
             "gpu_launches": int(allv[:, 3].sum()),
+            "breakdown_ms": {"eager step phases, max over ranks": True,
+                             **{k: round(float(allv[:, 5 + i].max()), 4) for i, k in enumerate(phases)}},
         }
         del graph, run_step, norm_t
         st.close()

@@ -311,15 +311,27 @@ class ShardedStep:
         return views
 
     @torch.no_grad()
-    def step(self, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None) -> torch.Tensor:
+    def step(self, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None,
+             marks: Optional[list] = None) -> torch.Tensor:
+        """One sharded step. `marks` (eager use only): a list that receives (phase name, CUDA event) pairs recorded on
+        the current stream after each phase, for a per-phase time breakdown."""
         from .functional import AdamWItem, MuonItem
         plan, r = self.plan, self.rank
+
+        def mark(name):
+            if marks is not None:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                marks.append((name, e))
+        mark("start")
         _reduce_scatter(self.gm_seg, self.gm, plan.m_seg, r, self.group)
         _reduce_scatter(self.ga_seg, self.ga, plan.a_seg, r, self.group)
+        mark("reduce_scatter")
         mine = self.compute.sumsq(self.owned_grad_views(), grad_divisor)
         sums = torch.empty(plan.world, dtype=torch.float64, device=mine.device)
         dist.all_gather_into_tensor(sums, mine.reshape(1), group=self.group)
         norm_coef = self.compute.coef(sums, max_norm)
+        mark("grad_norm")
         self.steps += 1
         muon = [MuonItem(self.muon_view(self.pm, i), self.reduced_muon_grad(i), self.bufs[i], self.muon_lr,
                          self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
@@ -332,6 +344,7 @@ class ShardedStep:
                                   self.v_state[o - base:o - base + n], self.adam_lr, self.adam_wd[i], self.steps))
         self.compute.update(muon, adam, norm_coef[1:2] if max_norm is not None else None, grad_divisor,
                             [self.muon_view(self.om, i) for i in self.mine])
+        mark("owned_update")
         every = range(len(plan.muon_shapes))
         if self.peer_ptrs is not None:   # the owners' O, read in place over NVLink once every owner has written it
             dist.all_reduce(self._flag, group=self.group)
@@ -340,9 +353,11 @@ class ShardedStep:
             _all_gather_inplace(self.om, plan.m_seg, r, self.group)
             updates = [self.muon_view(self.om, i) for i in every]
         _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
+        mark("exchange")
         self.compute.apply([MuonItem(self.muon_view(self.pm, i), None, None, self.muon_lr,
                                      self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
                             for i in every], updates)
+        mark("apply_all")
         return norm_coef[0]
 
 
