@@ -25,7 +25,7 @@ METRIC = "ms/optimizer step (96M set)"
 
 
 def run(args, rank: int, world: int, local_rank: int):
-    from bench import ClockSampler, load_peaks   # the driver-facing helpers live in bench.py
+    from bench import ClockSampler, load_peaks, streamed_e2e   # the driver-facing helpers live in bench.py
     from . import _lib as L
     from .ops import read_status
 
@@ -124,26 +124,16 @@ def run(args, rank: int, world: int, local_rank: int):
         e2e_steps = max(5, min(30, args.steps // 6))
         norm_t = _norm if graph is not None else None
 
-        def e2e_step():
-            st.gm.copy_(host_m, non_blocking=True)
-            st.ga.copy_(host_a, non_blocking=True)
-            if graph is not None:
-                graph.replay()
-                host_norm.copy_(norm_t, non_blocking=True)
-            else:
-                host_norm.copy_(st.step(max_norm=w.clip), non_blocking=True)
+        run_e2e = (graph.replay if graph is not None else (lambda: st.step(max_norm=w.clip)))
 
-        for _ in range(2):
-            e2e_step()
-        torch.cuda.synchronize(dev)
+        def e2e_step():
+            r = run_e2e()
+            return norm_t if graph is not None else r
+
+        pairs = [(st.gm, host_m), (st.ga, host_a)]
+        streamed_e2e(e2e_step, pairs, host_norm, 2, stream)
         dist.barrier()
-        h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h0.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        h1.record(stream)
-        torch.cuda.synchronize(dev)
-        e2e_local = h0.elapsed_time(h1) / e2e_steps
+        e2e_local = streamed_e2e(e2e_step, pairs, host_norm, e2e_steps, stream)
 
         my_flops = sum(w.ns_steps * _ns_flops_issued(w.muon_shapes[i]) for i in st.mine)
         vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops] + breakdown, dtype=torch.float64,
@@ -177,7 +167,9 @@ def run(args, rank: int, world: int, local_rank: int):
                          "rank": slow,
                          "ns_ms_per_step": round(ns_ms, 4)},
             "e2e": {"value": round(e2e, 4), "unit": "ms/step",
-                    "h2d_bytes_per_step": int((st.gm.numel() + st.ga.numel()) * 2), "d2h_bytes_per_step": 4},
+                    "h2d_bytes_per_step": int((st.gm.numel() + st.ga.numel()) * 2), "d2h_bytes_per_step": 4,
+                    "how": "host-fed loop per rank: each step's local grads uploaded from pinned memory on a copy "
+                           "stream while the previous step computes, then moved to the grad regions; norm read back"},
             "clocks": clk.summary(),
             "gpu_launches": int(allv[:, 3].sum()),
             "breakdown_ms": {"eager step phases, max over ranks": True,
