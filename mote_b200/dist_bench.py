@@ -2,8 +2,9 @@
 GPU (launched by torch.distributed.run), NCCL over NVLink.
 
 Each rank holds the whole c1 model in its flat param regions and its own local bf16 grads; one step is the
-reduce-scatter of the grads, the global clip from per-rank sums, the owned updates and the all-gather of the params.
-Time is measured with CUDA events on each rank and the maximum over ranks is reported.
+reduce-scatter of the grads, the global clip from per-rank sums, the owned updates, and the exchange and apply of
+the Muon updates (read from their owners over NVLink) with the AdamW slices all-gathered. Time is measured with CUDA
+events on each rank and the maximum over ranks is reported.
 """
 
 from __future__ import annotations
@@ -33,6 +34,7 @@ def run(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
                             device_id=dev)
+    held = {"graph": None}   # the only reference to the captured graph: dropped before destroy_process_group
     try:
         w = configs.CONFIGS[args.config]()
         plan = make_plan(w.muon_shapes, w.adam_shapes, world, ns_steps=w.ns_steps)
@@ -77,27 +79,23 @@ def run(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         L.check(L.lib.moteopt_profile_ns_events(None, None), "events")
         ns_local = statistics.mean(a.elapsed_time(b) for a, b in ns_ev) if st.mine else 0.0
-        # per-phase breakdown of eager steps (CUDA events between the phases of ShardedStep.step)
-        phases = ["reduce_scatter", "grad_norm", "owned_update", "exchange", "apply_all"]
-        per = {k: [] for k in phases}
-        for _ in range(5):
-            marks = []
-            st.step(max_norm=w.clip, marks=marks)
-            torch.cuda.synchronize(dev)
-            for (_, a), (name, b) in zip(marks, marks[1:]):
-                per[name].append(a.elapsed_time(b))
-        breakdown = [statistics.median(per[k]) for k in phases]
         # the whole sharded step (NCCL collectives + kernels) captured in a CUDA graph and replayed
-        graph = None
         capture_error = ""
+        _norm = None
         l0 = L.lib.moteopt_launch_count()
         try:
-            graph, _norm = capture(st, max_norm=w.clip)
+            held["graph"], _norm = capture(st, max_norm=w.clip)
         except Exception as exc:  # noqa: BLE001  (recorded in the JSON line; the eager step is timed instead)
-            graph = None
+            held["graph"] = None
             capture_error = f"{type(exc).__name__}: {exc}"[:200]
         per_step = L.lib.moteopt_launch_count() - l0
-        run_step = graph.replay if graph is not None else (lambda: st.step(max_norm=w.clip))
+        captured = held["graph"] is not None
+
+        def run_step():
+            if captured:
+                held["graph"].replay()
+                return _norm
+            return st.step(max_norm=w.clip)
         for _ in range(3):
             run_step()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -111,7 +109,7 @@ def run(args, rank: int, world: int, local_rank: int):
                 run_step()
             e1.record(stream)
             torch.cuda.synchronize(dev)
-        launches = per_step * args.steps if graph is not None else L.lib.moteopt_launch_count() - l1
+        launches = per_step * args.steps if captured else L.lib.moteopt_launch_count() - l1
         ms_local = e0.elapsed_time(e1) / args.steps
         status, _ = read_status(dev)
         if status & 3:
@@ -122,22 +120,13 @@ def run(args, rank: int, world: int, local_rank: int):
         host_a = st.ga.cpu().pin_memory()
         host_norm = torch.empty((), dtype=torch.float32).pin_memory()
         e2e_steps = max(5, min(30, args.steps // 6))
-        norm_t = _norm if graph is not None else None
-
-        run_e2e = (graph.replay if graph is not None else (lambda: st.step(max_norm=w.clip)))
-
-        def e2e_step():
-            r = run_e2e()
-            return norm_t if graph is not None else r
-
         pairs = [(st.gm, host_m), (st.ga, host_a)]
-        streamed_e2e(e2e_step, pairs, host_norm, 2, stream)
+        streamed_e2e(run_step, pairs, host_norm, 2, stream)
         dist.barrier()
-        e2e_local = streamed_e2e(e2e_step, pairs, host_norm, e2e_steps, stream)
+        e2e_local = streamed_e2e(run_step, pairs, host_norm, e2e_steps, stream)
 
         my_flops = sum(w.ns_steps * _ns_flops_issued(w.muon_shapes[i]) for i in st.mine)
-        vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops] + breakdown, dtype=torch.float64,
-                            device=dev)
+        vals = torch.tensor([ms_local, e2e_local, ns_local, float(launches), my_flops], dtype=torch.float64, device=dev)
         allv = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(allv, vals)
         allv = torch.stack(allv).cpu()
@@ -153,7 +142,7 @@ def run(args, rank: int, world: int, local_rank: int):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded params N(0,0.02^2) fp32 (same on every rank), local grads N(0,1e-3^2) bf16 per rank",
             "config": {"workload": w.name, "parallelism": f"muon-owner+zero1 x{world}",
-                       "launch": "CUDA graph of the whole sharded step" if graph is not None
+                       "launch": "CUDA graph of the whole sharded step" if captured
                        else f"eager (graph capture failed: {capture_error})", "collectives":
                        "NCCL reduce-scatter (grads), all-gather (per-rank sums of squares), all-gather (AdamW fp32 "
                        "params); Muon updates: " + ("every rank's bf16 O read over NVLink by the apply kernel (CUDA "
@@ -172,13 +161,11 @@ def run(args, rank: int, world: int, local_rank: int):
                            "stream while the previous step computes, then moved to the grad regions; norm read back"},
             "clocks": clk.summary(),
             "gpu_launches": int(allv[:, 3].sum()),
-            "breakdown_ms": {"eager step phases, max over ranks": True,
-                             **{k: round(float(allv[:, 5 + i].max()), 4) for i, k in enumerate(phases)}},
         }
-        del graph, run_step, norm_t
         st.close()
         return line
     finally:
+        held["graph"] = None   # a graph holding NCCL calls must be gone before destroy_process_group, or the exit waits
         torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()

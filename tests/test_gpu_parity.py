@@ -187,6 +187,27 @@ def test_update_out_then_apply_equals_in_step_apply(dev):
     _status_ok(dev)
 
 
+def test_muon_step_without_iterations_matches_oracle(dev):
+    """ns_steps = 0: Muon applies the normalised momentum itself (muon.py:32-36 with no iteration), wide, tall, padded
+    and 3-D parameters."""
+    from mote_b200.functional import MuonItem, muon_step
+    rng = np.random.default_rng(21)
+    shapes = [(64, 96), (96, 64), (37, 53), (2, 40, 72)]
+    p0 = [(rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02)) for sh in shapes]
+    gr = [O.bf16_round(rng.standard_normal(sh, dtype=np.float32) * np.float32(1e-3)) for sh in shapes]
+    ps, gs = _to(dev, p0), _to(dev, gr)
+    bufs = [torch.zeros_like(p) for p in ps]
+    muon_step([MuonItem(p, g, b, 0.02, 0.002, 0.95, True) for p, g, b in zip(ps, gs, bufs)], ns_steps=0)
+    torch.cuda.synchronize()
+    ref = [p.copy() for p in p0]
+    rbufs = [None] * len(ref)
+    O.muon_step(ref, gr, rbufs, O.MuonGroup(lr=0.02, weight_decay=0.1, ns_steps=0))
+    for i in range(len(shapes)):
+        d_gpu, d_ref = ps[i].cpu().numpy() - p0[i], ref[i] - p0[i]
+        assert O.rel_frob(d_gpu, d_ref) <= 1e-3, (shapes[i], O.rel_frob(d_gpu, d_ref))   # bf16 X0: a norm ulp can flip a rounding
+    _status_ok(dev)
+
+
 def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
     from mote_b200 import ops
     u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
