@@ -102,6 +102,16 @@ typedef struct {
   float* const* ema;
   double ema_weight;
   float* muon_norms;
+  /* lr:          DEVICE array of n_adamw + n_muon doubles, each tensor's lr for this step (AdamW tensors, then Muon
+   *              params), read by the kernels instead of the structs' lr: a learning-rate schedule (train.py:177-179
+   *              set_lr, elr.py param_lr) then needs no new launch parameters, so a captured step can replay it.
+   *              AdamW's decay is lr * weight_decay; a Muon param's decay is lr * muon_wd[i], or
+   *              (lr * lr / muon_lr_max[i]) * muon_wd[i] when muon_lr_max[i] > 0 (Muon-SW, muon.py:76-79).
+   *              NULL: the structs' lr and decay.
+   * muon_wd, muon_lr_max: HOST arrays of n_muon doubles, required with lr when n_muon > 0. */
+  const double* lr;
+  const double* muon_wd;
+  const double* muon_lr_max;
 } moteopt_step_extras;
 
 MOTEOPT_API int moteopt_version(void);

@@ -60,7 +60,8 @@ class GradConfig(C.Structure):
 
 
 class StepExtras(C.Structure):
-    _fields_ = [("ema", C.POINTER(C.c_void_p)), ("ema_weight", C.c_double), ("muon_norms", C.c_void_p)]
+    _fields_ = [("ema", C.POINTER(C.c_void_p)), ("ema_weight", C.c_double), ("muon_norms", C.c_void_p),
+                ("lr", C.c_void_p), ("muon_wd", C.POINTER(C.c_double)), ("muon_lr_max", C.POINTER(C.c_double))]
 
 
 class MoteoptError(RuntimeError):

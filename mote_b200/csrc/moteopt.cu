@@ -418,8 +418,10 @@ EmaConsts ema_consts(double weight) {
 }
 
 // ema: per AdamW tensor, an EMA buffer or null (null array: none)
+// ema: per AdamW tensor, an EMA buffer or null; lr_dev: device array, one lr per tensor, or null
 int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp, bool has_div, float div,
-                 const float* coef, int sms, cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0) {
+                 const float* coef, int sms, cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0,
+                 const double* lr_dev = nullptr) {
   static thread_local AdamArgs A;
   std::memset(&A, 0, sizeof(A));
   A.ema = ema_consts(ema_weight);
@@ -463,6 +465,8 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       S.lr = x.lr;
       S.wd = x.weight_decay;
       S.ema = ema != nullptr ? ema[s0 + i] : nullptr;
+      S.lr_dev = lr_dev != nullptr ? lr_dev + s0 + i : nullptr;
+      S.bc1 = bc1;
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kChunk));
     }
     if (A.chunk_start[cnt] == 0) continue;
@@ -794,9 +798,11 @@ std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const mo
 
 // The Muon apply (muon.py:97-99) from the final iterate: X0 when ns_steps == 0, else the last phase's output.
 // ema: per Muon param, an EMA buffer or null (null array: none)
-// norms: n_muon outputs (||p_new||_F per Muon param), or null
+// norms: n_muon outputs (||p_new||_F per Muon param), or null; lr_dev: device array of one lr per Muon param, with
+// the host arrays wd / lr_max (see moteopt_step_extras), or null
 int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int src,
-              cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0, float* norms = nullptr) {
+              cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0, float* norms = nullptr,
+              const double* lr_dev = nullptr, const double* wd = nullptr, const double* lr_max = nullptr) {
   float* apply_partials = reinterpret_cast<float*>(ws + L.off_apply);
   const std::vector<ns::MatApply> tab = muon_apply_table(P, cfg, L);
   static thread_local OutArgs A;
@@ -827,6 +833,11 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
         S.scale = tab[k].scale;
         S.ema = e;
         S.partials = part;
+        if (lr_dev != nullptr) {
+          S.lr_dev = lr_dev + ref.src;
+          S.wd = wd[ref.src];
+          S.lr_max = lr_max[ref.src];
+        }
         flat.push_back(S);
         continue;
       }
@@ -836,6 +847,11 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       M.out = tab[k].p;
       M.ema = e;
       M.partials = part;
+      if (lr_dev != nullptr) {
+        M.lr_dev = lr_dev + ref.src;
+        M.wd = wd[ref.src];
+        M.lr_max = lr_max[ref.src];
+      }
       M.rows = g.rows;
       M.cols = g.cols;
       M.m_pad = g.m;
@@ -985,7 +1001,8 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     coef = &hdr->coef;
     if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
   }
-  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w));
+  const double* lr_dev = ex != nullptr ? ex->lr : nullptr;
+  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w, lr_dev));
   if (n_muon > 0) {
     MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st));
     int final_src = 0;
@@ -996,7 +1013,8 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     }
     if (muon_out != nullptr) MO_TRY(run_copy_out(muon, L, ws, final_src, muon_out, sms, st));
     else MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st, ema != nullptr ? ema + n_adam : nullptr, ema_w,
-                          ex != nullptr ? ex->muon_norms : nullptr));
+                          ex != nullptr ? ex->muon_norms : nullptr, lr_dev != nullptr ? lr_dev + n_adam : nullptr,
+                          ex != nullptr ? ex->muon_wd : nullptr, ex != nullptr ? ex->muon_lr_max : nullptr));
   }
   return MOTEOPT_OK;
 }
@@ -1091,6 +1109,9 @@ int moteopt_optimizer_step_ex(const moteopt_muon_param* muon, int n_muon, const 
                               const moteopt_adamw_tensor* adamw, int n_adamw, const moteopt_adamw_hparams* adamw_hp,
                               const moteopt_grad_config* grad_cfg, const moteopt_step_extras* extras, float* out_norm,
                               void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  if (extras != nullptr && extras->lr != nullptr && n_muon > 0 &&
+      (extras->muon_wd == nullptr || extras->muon_lr_max == nullptr))
+    return fail(MOTEOPT_ERR_INVALID, "extras->lr needs muon_wd and muon_lr_max for the Muon params");
   return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, grad_cfg, nullptr, out_norm, workspace,
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr, extras);
 }

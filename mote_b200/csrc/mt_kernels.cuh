@@ -244,6 +244,21 @@ struct AdamConsts {
   int lerp_small;
 };
 
+// The Muon apply's scalars for this step (mote/train/muon.py:76-79, :97-99) when the lr is read on the device:
+// decay = (lr*lr/lr_max if Muon-SW else lr) * wd in fp64, as the reference's Python floats; then fp32 casts of
+// -lr and 1 - decay, as torch's scalar arguments.
+struct ApplyScalars {
+  float neg_lr, decay_mul;
+  int has_decay;
+};
+__device__ __forceinline__ ApplyScalars apply_scalars(const double* lr_dev, double wd, double lr_max, float neg_lr,
+                                                      float decay_mul, int has_decay) {
+  if (lr_dev == nullptr) return ApplyScalars{neg_lr, decay_mul, has_decay};
+  const double e = *lr_dev;
+  const double d = wd == 0.0 ? 0.0 : (lr_max > 0.0 ? (e * e / lr_max) * wd : e * wd);
+  return ApplyScalars{static_cast<float>(-e), static_cast<float>(1.0 - d), d != 0.0};
+}
+
 __device__ __forceinline__ float ema_lerp(float e, float p, const EmaConsts& E) {
   const float d = __fsub_rn(p, e);
   return E.small ? fmaf(E.w, d, e) : fmaf(-E.omw, d, p);
@@ -267,12 +282,16 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     AdamSeg S = A.seg[s];
+    const double lr = S.lr_dev != nullptr ? *S.lr_dev : S.lr;   // this step's lr (device-read under a schedule)
     if (A.dstep != nullptr) {   // the host computes these in fp64 from its step count; the same formulas here
       const double bc1 = 1.0 - pow(A.beta1d, dstep);
       const double bc2 = 1.0 - pow(A.beta2d, dstep);
-      S.neg_step_size = static_cast<float>(-(S.lr / bc1));
+      S.neg_step_size = static_cast<float>(-(lr / bc1));
       S.bc2_sqrt = static_cast<float>(pow(bc2, 0.5));
+    } else if (S.lr_dev != nullptr) {
+      S.neg_step_size = static_cast<float>(-(lr / S.bc1));
     }
+    if (S.lr_dev != nullptr) S.decay_mul = static_cast<float>(1.0 - lr * S.wd);
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype) &&
@@ -462,6 +481,7 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
     int64_t i0 = begin;
     if (A.apply) {
       float* p = reinterpret_cast<float*>(S.out);
+      const ApplyScalars K = apply_scalars(S.lr_dev, S.wd, S.lr_max, S.neg_lr, S.decay_mul, S.has_decay);
       if (end - begin == kChunk && aligned8(x) && aligned16(p) && (S.ema == nullptr || aligned16(S.ema))) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -481,8 +501,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               float v = qe[e];
-              if (S.has_decay) v = __fmul_rn(v, S.decay_mul);
-              qe[e] = fmaf(S.neg_lr, __fmul_rn(o[e], S.scale), v);
+              if (K.has_decay) v = __fmul_rn(v, K.decay_mul);
+              qe[e] = fmaf(K.neg_lr, __fmul_rn(o[e], S.scale), v);
             }
             *reinterpret_cast<float4*>(p + i) = q[k];
             sq = fmaf(q[k].x, q[k].x, sq); sq = fmaf(q[k].y, q[k].y, sq);
@@ -499,8 +519,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
       }
       for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) {
         float v = p[i];
-        if (S.has_decay) v = __fmul_rn(v, S.decay_mul);
-        v = fmaf(S.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
+        if (K.has_decay) v = __fmul_rn(v, K.decay_mul);
+        v = fmaf(K.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
         p[i] = v;
         sq = fmaf(v, v, sq);
         if (S.ema != nullptr) S.ema[i] = ema_lerp(S.ema[i], v, A.ema);
@@ -639,6 +659,7 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
       for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
   }
   const bool vec = (M.cols % 4 == 0) && aligned16(M.out) && (M.ema == nullptr || aligned16(M.ema));
+  const ApplyScalars K = apply_scalars(A.apply ? M.lr_dev : nullptr, M.wd, M.lr_max, M.neg_lr, M.decay_mul, M.has_decay);
   float sq = 0.f;   // apply mode: sum of the updated param's squares over this thread's elements
 #pragma unroll
   for (int k = 0; k < 4; ++k) {   // output rows r0 + ty + 16k, columns c0 + 4tx .. +3
@@ -653,8 +674,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float q = pe[e];
-          if (M.has_decay) q = __fmul_rn(q, M.decay_mul);
-          pe[e] = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+          if (K.has_decay) q = __fmul_rn(q, K.decay_mul);
+          pe[e] = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
         }
         *reinterpret_cast<float4*>(p + idx) = pv;
         sq = fmaf(pv.x, pv.x, sq); sq = fmaf(pv.y, pv.y, sq); sq = fmaf(pv.z, pv.z, sq); sq = fmaf(pv.w, pv.w, sq);
@@ -669,8 +690,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
         for (int e = 0; e < 4; ++e)
           if (ocol + e < M.cols) {
             float q = p[idx + e];
-            if (M.has_decay) q = __fmul_rn(q, M.decay_mul);
-            q = fmaf(M.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+            if (K.has_decay) q = __fmul_rn(q, K.decay_mul);
+            q = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
             p[idx + e] = q;
             sq = fmaf(q, q, sq);
             if (M.ema != nullptr) M.ema[idx + e] = ema_lerp(M.ema[idx + e], q, A.ema);

@@ -60,7 +60,7 @@ struct EmaConsts {
 };
 
 // ---- AdamW (torch.optim.AdamW single-tensor update, constructed at mote/train/train.py:98)
-constexpr int kMaxAdamSeg = 320;
+constexpr int kMaxAdamSeg = 256;
 struct AdamSeg {
   float* p;
   const void* g;
@@ -75,6 +75,8 @@ struct AdamSeg {
   int pad_;
   double lr, wd;             // for the device-step mode, which recomputes the three scalars above per step
   float* ema;                // EMA of the param, lerped toward the updated param in the same pass, or null
+  const double* lr_dev;      // this step's lr read on the device (schedules under graph capture), or null: lr
+  double bc1;                // 1 - beta1^t (host step mode), for the device-lr step size
 };
 struct AdamArgs {
   int n;
@@ -178,7 +180,7 @@ struct DenomArgs {
 };
 
 // ---- copy the final iterate out of the workspace (standalone newton_schulz), or apply it (ns_steps == 0)
-constexpr int kMaxOutMat = 320;
+constexpr int kMaxOutMat = 256;
 struct OutMat {
   const void* x;             // [m_pad][n_pad] bf16 iterate
   void* out;                 // bf16 [R][C] output, or the fp32 parameter in apply mode
@@ -190,6 +192,8 @@ struct OutMat {
   int has_decay;
   float* ema;                // apply mode: EMA of the parameter ([R][C], fp32), or null
   float* partials;           // apply mode: per tile, the sum of the updated param's squares, or null
+  const double* lr_dev;      // apply mode: this step's lr read on the device, or null (neg_lr / decay_mul above)
+  double wd, lr_max;         // with lr_dev: decay = lr*wd, or (lr*lr/lr_max)*wd when lr_max > 0 (Muon-SW)
 };
 struct OutArgs {
   int n;
@@ -207,6 +211,8 @@ struct FlatOutSeg {
   int has_decay;
   float* ema;                // apply mode: EMA of the parameter (same layout), or null
   float* partials;           // apply mode: per chunk of the segment, the sum of the updated param's squares, or null
+  const double* lr_dev;      // apply mode: this step's lr read on the device, or null (neg_lr / decay_mul above)
+  double wd, lr_max;         // with lr_dev: decay = lr*wd, or (lr*lr/lr_max)*wd when lr_max > 0 (Muon-SW)
 };
 struct FlatOutArgs {
   int n;

@@ -21,7 +21,10 @@ from .ops import grad_dtype_code, stream_handle, workspace
 @dataclass
 class MuonItem:
     """One Muon parameter for one step (mote/train/muon.py:60-79): `lr` is already the effective rate (param_lr
-    override resolved) and `decay` the decoupled decay of muon.py:78 (0 for none)."""
+    override resolved) and `decay` the decoupled decay of muon.py:78 (0 for none). For a step whose lr is read on
+    the device (`optimizer_step(lr_device=...)`, `CapturedStep(dynamic_lr=True)`), `wd` and `lr_max` give the decay
+    rule instead: decay = lr * wd, or (lr * lr / lr_max) * wd with Muon-SW (lr_max > 0); `wd` None derives it from
+    decay / lr."""
     param: torch.Tensor
     grad: torch.Tensor
     momentum_buffer: torch.Tensor
@@ -29,6 +32,8 @@ class MuonItem:
     decay: float = 0.0
     momentum: float = 0.95
     nesterov: bool = True
+    wd: Optional[float] = None
+    lr_max: float = 0.0
 
 
 @dataclass
@@ -103,7 +108,8 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
                    out_norm: Optional[torch.Tensor] = None,
                    device_step: Optional[torch.Tensor] = None,
                    ema: Optional[Sequence[Optional[torch.Tensor]]] = None, ema_weight: float = 0.0,
-                   muon_norms: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+                   muon_norms: Optional[torch.Tensor] = None,
+                   lr_device: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
     AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
     max_norm is given. With `device_step` (a 0-dim fp32 CUDA tensor) AdamW's step count is that counter, which the
@@ -112,7 +118,9 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     Fused extras (the work train.py:950-953 and elr.py:85-87 do in separate passes after the step):
     `ema` - one fp32 buffer (or None) per AdamW item, then per Muon item, updated as
     torch._foreach_lerp_(ema, params, ema_weight) in the pass that writes the params; `muon_norms` - an fp32 CUDA
-    tensor of len(muon) that receives ||p||_F of every Muon param after the update."""
+    tensor of len(muon) that receives ||p||_F of every Muon param after the update; `lr_device` - an fp64 CUDA tensor
+    of len(adamw) + len(muon) lrs (AdamW items, then Muon items) read by the kernels at run time instead of the items'
+    `lr` (a schedule under graph capture; see MuonItem for the decay rule)."""
     dev = _device(muon, adamw)
     m_arr, a_arr = muon_array(muon), adamw_array(adamw)
     nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adamw))
@@ -127,7 +135,7 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
         out_norm = torch.empty((), dtype=torch.float32, device=dev)
     onorm = C.c_void_p(out_norm.data_ptr() if out_norm is not None else 0)
     stream = C.c_void_p(stream_handle(dev))
-    if ema is None and muon_norms is None:
+    if ema is None and muon_norms is None and lr_device is None:
         L.check(L.lib.moteopt_optimizer_step(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp),
                                              C.byref(gc), onorm, C.c_void_p(ws.data_ptr()), ws.numel(), stream),
                 "moteopt_optimizer_step")
@@ -147,6 +155,15 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
         if not (muon_norms.is_cuda and muon_norms.dtype == torch.float32 and muon_norms.numel() >= len(muon)):
             raise ValueError("muon_norms must be an fp32 CUDA tensor with one element per Muon item")
         ex.muon_norms = muon_norms.data_ptr()
+    keep = []
+    if lr_device is not None:
+        if not (lr_device.is_cuda and lr_device.dtype == torch.float64 and lr_device.is_contiguous()
+                and lr_device.numel() >= len(adamw) + len(muon)):
+            raise ValueError("lr_device must be a contiguous fp64 CUDA tensor with one lr per AdamW and Muon item")
+        ex.lr = lr_device.data_ptr()
+        wds = [it.wd if it.wd is not None else (it.decay / it.lr if it.lr else 0.0) for it in muon]
+        keep = [L.array(C.c_double, wds or [0.0]), L.array(C.c_double, [float(it.lr_max) for it in muon] or [0.0])]
+        ex.muon_wd, ex.muon_lr_max = keep
     L.check(L.lib.moteopt_optimizer_step_ex(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw), C.byref(hp),
                                             C.byref(gc), C.byref(ex), onorm, C.c_void_p(ws.data_ptr()), ws.numel(),
                                             stream), "moteopt_optimizer_step_ex")
@@ -198,7 +215,8 @@ class CapturedStep:
 
     def __init__(self, muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (), *, ns_steps: int = 5,
                  rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
-                 max_norm: Optional[float] = None, grad_divisor: Optional[float] = None, start_step: int = 0):
+                 max_norm: Optional[float] = None, grad_divisor: Optional[float] = None, start_step: int = 0,
+                 dynamic_lr: bool = False):
         self.dev = _device(muon, adamw)
         self.kw = dict(ns_steps=ns_steps, rms_scale=rms_scale, ns_eps=ns_eps, betas=betas, eps=eps,
                        max_norm=max_norm, grad_divisor=grad_divisor)
@@ -208,9 +226,25 @@ class CapturedStep:
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.calls = 0
         self.launches_per_step = 0
+        self.lr_device: Optional[torch.Tensor] = None
+        if dynamic_lr:   # the kernels read every tensor's lr here at replay time (set_lrs)
+            self.lr_device = torch.tensor([it.lr for it in self.adamw] + [it.lr for it in self.muon],
+                                          dtype=torch.float64, device=self.dev)
+
+    def set_lrs(self, adamw_lrs: Sequence[float], muon_lrs: Sequence[float]) -> None:
+        """This step's lrs (dynamic_lr=True): one per AdamW item and one per Muon item, as set_lr / param_lr give them
+        (train.py:177-179); the decay follows each item's rule. A synchronous host-to-device copy of a few bytes, so
+        it is safe to call between replays."""
+        if self.lr_device is None:
+            raise RuntimeError("CapturedStep was built without dynamic_lr")
+        vals = [float(x) for x in adamw_lrs] + [float(x) for x in muon_lrs]
+        if len(vals) != self.lr_device.numel():
+            raise ValueError(f"set_lrs: {len(vals)} lrs for {self.lr_device.numel()} tensors")
+        self.lr_device.copy_(torch.tensor(vals, dtype=torch.float64))
 
     def _run(self):
-        optimizer_step(self.muon, self.adamw, out_norm=self.out_norm, device_step=self.device_step, **self.kw)
+        optimizer_step(self.muon, self.adamw, out_norm=self.out_norm, device_step=self.device_step,
+                       lr_device=self.lr_device, **self.kw)
 
     @torch.no_grad()
     def __call__(self) -> torch.Tensor:

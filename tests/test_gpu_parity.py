@@ -208,6 +208,48 @@ def test_muon_step_without_iterations_matches_oracle(dev):
     _status_ok(dev)
 
 
+def test_captured_step_with_a_learning_rate_schedule(dev):
+    """CapturedStep(dynamic_lr=True): one graph replayed under a changing lr (set_lrs before each replay, plain and
+    Muon-SW decay rules) == eager steps built with each step's lr and decay as the reference computes them
+    (muon.py:76-79), bit for bit."""
+    from mote_b200.functional import AdamWItem, CapturedStep, MuonItem, optimizer_step
+    w = configs.c0()
+    sets = []
+    for _ in range(2):
+        inp = configs.make_params(w, seed=4)
+        mp, ap = _to(dev, inp.muon_params), _to(dev, inp.adam_params)
+        ag_np, mg_np = configs.make_grads(w, seed=4, step=0)
+        mg = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in mg_np]
+        ag = [torch.from_numpy(x).to(dev).to(torch.bfloat16) for x in ag_np]
+        sets.append((mp, ap, mg, ag, [torch.zeros_like(p) for p in mp], [torch.zeros_like(p) for p in ap],
+                     [torch.zeros_like(p) for p in ap]))
+    wd, lr_max = 0.1, 0.05
+    sw = [i % 2 == 1 for i in range(len(w.muon_shapes))]   # every other Muon param on the Muon-SW rule
+    sched = [(0.02, 3e-4), (0.015, 2e-4), (0.03, 1e-4), (0.005, 5e-5)]
+
+    def decay(e, i):
+        return (e * e / lr_max if sw[i] else e) * wd
+
+    mp, ap, mg, ag, mb, am, av = sets[0]
+    for k, (lm, la) in enumerate(sched):
+        optimizer_step([MuonItem(p, g, b, lm, decay(lm, i)) for i, (p, g, b) in enumerate(zip(mp, mg, mb))],
+                       [AdamWItem(p, g, m, v, la, 0.1, k + 1) for p, g, m, v in zip(ap, ag, am, av)],
+                       betas=(0.9, 0.95), max_norm=0.01)
+    mp2, ap2, mg2, ag2, mb2, am2, av2 = sets[1]
+    lm0, la0 = sched[0]
+    cs = CapturedStep([MuonItem(p, g, b, lm0, decay(lm0, i), wd=wd, lr_max=lr_max if sw[i] else 0.0)
+                       for i, (p, g, b) in enumerate(zip(mp2, mg2, mb2))],
+                      [AdamWItem(p, g, m, v, la0, 0.1, 0) for p, g, m, v in zip(ap2, ag2, am2, av2)],
+                      betas=(0.9, 0.95), max_norm=0.01, dynamic_lr=True)
+    for lm, la in sched:
+        cs.set_lrs([la] * len(ap2), [lm] * len(mp2))
+        cs()
+    torch.cuda.synchronize()
+    assert cs.graph is not None
+    for a, b in zip(mp + ap + mb + am + av, mp2 + ap2 + mb2 + am2 + av2):
+        assert torch.equal(a, b)
+
+
 def test_newton_schulz_fp32_and_bf16_inputs_agree(dev):
     from mote_b200 import ops
     u = torch.from_numpy(O.bf16_round(ns_input((3, 96, 200), 9))).to(dev)
