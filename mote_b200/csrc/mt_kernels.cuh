@@ -356,24 +356,35 @@ __global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_
     float acc = 0.f;
     int64_t i0 = begin;
     if (aligned16(S.buf) && g_vec_ok(S.g, S.dtype)) {
-      if (end - begin == kChunk) {   // 4096 float4 of buf: 16 per thread, two halves of 8
-        float4* bp = reinterpret_cast<float4*>(S.buf + begin);
+      if (end - begin == kChunk) {   // 4096 float4 of buf: 16 per thread, four quarters of 4, software-pipelined:
+        float4* bp = reinterpret_cast<float4*>(S.buf + begin);   // quarter q+1's loads go out before quarter q's math
+        float4 b[2][4], g[2][4];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float4 b[8], g[8];
+        for (int k = 0; k < 4; ++k) {
+          const int j = threadIdx.x + k * kMtThreads;
+          b[0][k] = bp[j];
+          g[0][k] = load_g4(S.g, begin + 4 * static_cast<int64_t>(j), S.dtype);
+        }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int j = threadIdx.x + (h * 8 + k) * kMtThreads;
-            b[k] = bp[j];
-            g[k] = load_g4(S.g, begin + 4 * static_cast<int64_t>(j), S.dtype);
+        for (int q = 0; q < 4; ++q) {
+          const int cur = q & 1;
+          if (q + 1 < 4) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int j = threadIdx.x + ((q + 1) * 4 + k) * kMtThreads;
+              b[cur ^ 1][k] = bp[j];
+              g[cur ^ 1][k] = load_g4(S.g, begin + 4 * static_cast<int64_t>(j), S.dtype);
+            }
           }
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float u0 = mom_elem(X(g[k].x), b[k].x, S.mom, S.nesterov);
-            const float u1 = mom_elem(X(g[k].y), b[k].y, S.mom, S.nesterov);
-            const float u2 = mom_elem(X(g[k].z), b[k].z, S.mom, S.nesterov);
-            const float u3 = mom_elem(X(g[k].w), b[k].w, S.mom, S.nesterov);
-            bp[threadIdx.x + (h * 8 + k) * kMtThreads] = b[k];
+          for (int k = 0; k < 4; ++k) {
+            float4& bb = b[cur][k];
+            const float4& gg = g[cur][k];
+            const float u0 = mom_elem(X(gg.x), bb.x, S.mom, S.nesterov);
+            const float u1 = mom_elem(X(gg.y), bb.y, S.mom, S.nesterov);
+            const float u2 = mom_elem(X(gg.z), bb.z, S.mom, S.nesterov);
+            const float u3 = mom_elem(X(gg.w), bb.w, S.mom, S.nesterov);
+            bp[threadIdx.x + (q * 4 + k) * kMtThreads] = bb;
             acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
           }
         }
@@ -569,34 +580,59 @@ __global__ void __launch_bounds__(kMtThreads) ns_normalize_kernel(const __grid_c
   const int sr0 = M.transposed ? j0 : i0, sc0 = M.transposed ? i0 : j0;
   const bool vec = (M.cols % 4 == 0) && aligned16(M.buf == nullptr ? M.g : M.buf) && g_vec_ok(M.g, M.dtype);
   float v[4][4];
+  if (vec && sr0 + kNormTile <= M.rows && sc0 + kNormTile <= M.cols) {
+    // interior tile: all eight 16-byte loads of the thread are issued before the first use
+    float4 g4[4], b4[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {   // source rows sr0 + ty + 16k, columns sc0 + 4tx .. +3
-    const int sr = sr0 + ty + kTileRowsPerPass * k, sc = sc0 + 4 * tx;
-    const int64_t idx = static_cast<int64_t>(sr) * M.cols + sc;
-    float gv[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
-    if (sr < M.rows) {
-      if (vec && sc + 3 < M.cols) {
-        const float4 g4 = load_g4(M.g, idx, M.dtype);
-        gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
-        if (M.buf != nullptr) {
-          const float4 b4 = *reinterpret_cast<const float4*>(M.buf + idx);
-          bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
-        }
-      } else {
+    for (int k = 0; k < 4; ++k)
+      g4[k] = load_g4(M.g, static_cast<int64_t>(sr0 + ty + kTileRowsPerPass * k) * M.cols + sc0 + 4 * tx, M.dtype);
+    if (M.buf != nullptr) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (sc + e < M.cols) {
-            gv[e] = load_g1(M.g, idx + e, M.dtype);
-            if (M.buf != nullptr) bv[e] = M.buf[idx + e];
-          }
-      }
+      for (int k = 0; k < 4; ++k)
+        b4[k] = *reinterpret_cast<const float4*>(
+            M.buf + static_cast<int64_t>(sr0 + ty + kTileRowsPerPass * k) * M.cols + sc0 + 4 * tx);
     }
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float u = X(gv[e]);
-      if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, bv[e], u) : bv[e];
-      const bool ok = sr < M.rows && sc + e < M.cols;
-      v[k][e] = ok ? bf16_round_f(den.div(u)) : 0.f;
+    for (int k = 0; k < 4; ++k) {
+      const float* gv = reinterpret_cast<const float*>(&g4[k]);
+      const float* bv = reinterpret_cast<const float*>(&b4[k]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u = X(gv[e]);
+        if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, bv[e], u) : bv[e];
+        v[k][e] = bf16_round_f(den.div(u));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {   // source rows sr0 + ty + 16k, columns sc0 + 4tx .. +3
+      const int sr = sr0 + ty + kTileRowsPerPass * k, sc = sc0 + 4 * tx;
+      const int64_t idx = static_cast<int64_t>(sr) * M.cols + sc;
+      float gv[4] = {0.f, 0.f, 0.f, 0.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
+      if (sr < M.rows) {
+        if (vec && sc + 3 < M.cols) {
+          const float4 g4 = load_g4(M.g, idx, M.dtype);
+          gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+          if (M.buf != nullptr) {
+            const float4 b4 = *reinterpret_cast<const float4*>(M.buf + idx);
+            bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (sc + e < M.cols) {
+              gv[e] = load_g1(M.g, idx + e, M.dtype);
+              if (M.buf != nullptr) bv[e] = M.buf[idx + e];
+            }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u = X(gv[e]);
+        if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, bv[e], u) : bv[e];
+        const bool ok = sr < M.rows && sc + e < M.cols;
+        v[k][e] = ok ? bf16_round_f(den.div(u)) : 0.f;
+      }
     }
   }
   __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(M.x);
@@ -636,6 +672,23 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(M.x);
   const int xr0 = M.transposed ? c0 : r0, xc0 = M.transposed ? r0 : c0;
+  const bool vec = (M.cols % 4 == 0) && aligned16(M.out) && (M.ema == nullptr || aligned16(M.ema));
+  const ApplyScalars K = apply_scalars(A.apply ? M.lr_dev : nullptr, M.wd, M.lr_max, M.neg_lr, M.decay_mul, M.has_decay);
+  // interior tile of an apply: the param (and EMA) loads go out first, ahead of the X loads and the transpose
+  const bool pre = A.apply && vec && r0 + kNormTile <= M.rows && c0 + kNormTile <= M.cols;
+  float4 pp[4], pe[4];
+  if (pre) {
+    const float* p = reinterpret_cast<const float*>(M.out);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      pp[k] = *reinterpret_cast<const float4*>(p + static_cast<int64_t>(r0 + ty + kTileRowsPerPass * k) * M.cols + c0 + 4 * tx);
+    if (M.ema != nullptr) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        pe[k] = *reinterpret_cast<const float4*>(
+            M.ema + static_cast<int64_t>(r0 + ty + kTileRowsPerPass * k) * M.cols + c0 + 4 * tx);
+    }
+  }
   float v[4][4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) {   // X rows xr0 + ty + 16k, columns xc0 + 4tx .. +3 (n_pad is a multiple of 8)
@@ -658,8 +711,6 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
   }
-  const bool vec = (M.cols % 4 == 0) && aligned16(M.out) && (M.ema == nullptr || aligned16(M.ema));
-  const ApplyScalars K = apply_scalars(A.apply ? M.lr_dev : nullptr, M.wd, M.lr_max, M.neg_lr, M.decay_mul, M.has_decay);
   float sq = 0.f;   // apply mode: sum of the updated param's squares over this thread's elements
 #pragma unroll
   for (int k = 0; k < 4; ++k) {   // output rows r0 + ty + 16k, columns c0 + 4tx .. +3
@@ -669,18 +720,18 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_kernel(const __grid_constan
     if (A.apply) {
       float* p = reinterpret_cast<float*>(M.out);
       if (vec) {
-        float4 pv = *reinterpret_cast<float4*>(p + idx);
-        float* pe = reinterpret_cast<float*>(&pv);
+        float4 pv = pre ? pp[k] : *reinterpret_cast<float4*>(p + idx);
+        float* pf = reinterpret_cast<float*>(&pv);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float q = pe[e];
+          float q = pf[e];
           if (K.has_decay) q = __fmul_rn(q, K.decay_mul);
-          pe[e] = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
+          pf[e] = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
         }
         *reinterpret_cast<float4*>(p + idx) = pv;
         sq = fmaf(pv.x, pv.x, sq); sq = fmaf(pv.y, pv.y, sq); sq = fmaf(pv.z, pv.z, sq); sq = fmaf(pv.w, pv.w, sq);
         if (M.ema != nullptr) {
-          float4 ev = *reinterpret_cast<float4*>(M.ema + idx);
+          float4 ev = pre ? pe[k] : *reinterpret_cast<float4*>(M.ema + idx);
           ev.x = ema_lerp(ev.x, pv.x, A.ema); ev.y = ema_lerp(ev.y, pv.y, A.ema);
           ev.z = ema_lerp(ev.z, pv.z, A.ema); ev.w = ema_lerp(ev.w, pv.w, A.ema);
           *reinterpret_cast<float4*>(M.ema + idx) = ev;
