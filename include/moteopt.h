@@ -234,6 +234,20 @@ MOTEOPT_API size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t r
 MOTEOPT_API int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, int64_t rows, int64_t cols,
                           int steps, double eps, void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
 
+/* ---- the lossfree MoE router's bias step after the optimizer step: MoESwiGLU.update_bias
+ *      (mote/model/moe.py:147-159), called for every MoE layer at mote/train/train.py:948-949. One launch for all
+ *      layers and no host round trip (the reference's `load.sum() <= 0` test reads the sum back on the host).
+ *      Per layer: if the loads sum to <= 0 nothing changes; else bias += gamma * (sgn - mean(sgn)) with
+ *      sgn = sign((mean(load) - load) / max(mean(load), 1e-9)), and the loads are zeroed. The caller passes only
+ *      layers whose router is "lossfree" with gamma > 0 (moe.py:151-152 returns before touching the others). */
+typedef struct moteopt_moe_bias {
+  float* load_acc;      /* [n_experts] fp32 token counts accumulated since the last step (_load_acc) */
+  float* expert_bias;   /* [n_experts] fp32 routing bias (expert_bias), updated in place */
+  int n_experts;        /* >= 0; 0 skips the layer */
+  float gamma;          /* bias_gamma, rounded to fp32 as torch does for a Python scalar times an fp32 tensor */
+} moteopt_moe_bias;
+MOTEOPT_API int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, moteopt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

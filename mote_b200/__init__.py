@@ -11,7 +11,7 @@ _LAZY = {
     "split_muon_params": "optim", "fused_step": "optim", "set_lr": "optim",
     "clip_grad_norm_": "ops", "newton_schulz": "ops",
     "optimizer_step": "functional", "MuonItem": "functional", "AdamWItem": "functional",
-    "CapturedStep": "functional",
+    "CapturedStep": "functional", "moe_update_bias": "functional",
 }
 
 

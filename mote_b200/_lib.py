@@ -31,6 +31,7 @@ EXPORTS = (
     "moteopt_adamw_step",
     "moteopt_clip_grad_norm_workspace_size", "moteopt_clip_grad_norm", "moteopt_clip_grad_norm_noalloc",
     "moteopt_newton_schulz_workspace_size", "moteopt_newton_schulz",
+    "moteopt_moe_update_bias",
 )
 
 
@@ -62,6 +63,10 @@ class GradConfig(C.Structure):
 class StepExtras(C.Structure):
     _fields_ = [("ema", C.POINTER(C.c_void_p)), ("ema_weight", C.c_double), ("muon_norms", C.c_void_p),
                 ("lr", C.c_void_p), ("muon_wd", C.POINTER(C.c_double)), ("muon_lr_max", C.POINTER(C.c_double))]
+
+
+class MoeBias(C.Structure):
+    _fields_ = [("load_acc", C.c_void_p), ("expert_bias", C.c_void_p), ("n_experts", C.c_int), ("gamma", C.c_float)]
 
 
 class MoteoptError(RuntimeError):
@@ -108,6 +113,7 @@ def _load() -> C.CDLL:
         "moteopt_clip_grad_norm_noalloc": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int), i32, dbl, vp, vp]),
         "moteopt_newton_schulz_workspace_size": (sz, [i64, i64, i64]),
         "moteopt_newton_schulz": (i32, [vp, i32, vp, i64, i64, i64, i32, dbl, vp, sz, vp]),
+        "moteopt_moe_update_bias": (i32, [C.POINTER(MoeBias), i32, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

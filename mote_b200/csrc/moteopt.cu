@@ -467,7 +467,7 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       S.ema = ema != nullptr ? ema[s0 + i] : nullptr;
       S.lr_dev = lr_dev != nullptr ? lr_dev + s0 + i : nullptr;
       S.bc1 = bc1;
-      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kChunk));
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kAdamChunk));
     }
     if (A.chunk_start[cnt] == 0) continue;
     adamw_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
@@ -487,7 +487,7 @@ int check_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparam
       return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": grad dtype must be fp32 or bf16");
     if (x.step < 1 && hp->device_step == nullptr)
       return fail(MOTEOPT_ERR_INVALID, "AdamW tensor " + std::to_string(i) + ": step must be >= 1");
-    if (cdiv(x.numel, kChunk) > (1 << 30)) return fail(MOTEOPT_ERR_LIMIT, "AdamW tensor too large");
+    if (cdiv(x.numel, kAdamChunk) > (1 << 30)) return fail(MOTEOPT_ERR_LIMIT, "AdamW tensor too large");
   }
   return MOTEOPT_OK;
 }
@@ -1237,6 +1237,34 @@ int moteopt_adamw_step(const moteopt_adamw_tensor* adamw, int n_adamw, const mot
   r = device_setup(&sms);
   if (r != MOTEOPT_OK) return r;
   return launch_adamw(adamw, n_adamw, hp, false, 1.0f, grad_scale, sms, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && layers == nullptr)) return fail(MOTEOPT_ERR_INVALID, "bad MoE layer list");
+  for (int i = 0; i < n; ++i) {
+    const moteopt_moe_bias& x = layers[i];
+    if (x.n_experts < 0) return fail(MOTEOPT_ERR_INVALID, "MoE layer " + std::to_string(i) + ": negative n_experts");
+    if (x.n_experts > 0 && (x.load_acc == nullptr || x.expert_bias == nullptr))
+      return fail(MOTEOPT_ERR_INVALID, "MoE layer " + std::to_string(i) + ": null pointer");
+  }
+  int sms = 0;
+  int r = device_setup(&sms);
+  if (r != MOTEOPT_OK) return r;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  static thread_local MoeBiasArgs A;
+  A.n = 0;
+  for (int i = 0; i <= n; ++i) {
+    if (i == n || A.n == kMaxMoeLayers) {   // flush a full argument block, and the last one
+      if (A.n > 0) {
+        moe_bias_kernel<<<A.n, kMtThreads, 0, st>>>(A);
+        MO_LAUNCHED("moe_bias_kernel");
+      }
+      A.n = 0;
+    }
+    if (i < n && layers[i].n_experts > 0)
+      A.layer[A.n++] = MoeLayer{layers[i].load_acc, layers[i].expert_bias, layers[i].n_experts, layers[i].gamma};
+  }
+  return MOTEOPT_OK;
 }
 
 size_t moteopt_clip_grad_norm_workspace_size(const int64_t* numels, int n) {

@@ -1,7 +1,7 @@
 // Memory-bound kernels of the optimizer step (sm_100a). Each is a grid-stride loop over fixed 16K-element chunks
-// of a segment list, with 128-bit loads where the pointers allow. Reductions are deterministic: a fixed per-thread
-// order, a fixed warp-shuffle tree and a fixed cross-warp order per chunk, one partial per chunk, and a fixed-order
-// second pass, so results are bitwise identical from run to run.
+// (2K for AdamW) of a segment list, with 128-bit loads where the pointers allow. Reductions are deterministic: a
+// fixed per-thread order, a fixed warp-shuffle tree and a fixed cross-warp order per chunk, one partial per chunk,
+// and a fixed-order second pass, so results are bitwise identical from run to run.
 //
 // Rounding follows the reference's torch ops one by one (see the per-kernel comments); __fmul_rn / __fadd_rn /
 // __fdiv_rn keep the compiler from contracting what torch rounds separately, fmaf is used where torch fuses.
@@ -163,6 +163,23 @@ __global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Sum of partials[begin, end) over a warp in fp64: lane l adds elements l, l+32, ... in that order, then a fixed xor
+// tree. Loads go out eight at a time before their adds (out-of-range ones read as 0, and s + 0 = s for the
+// non-negative sums here), so a tensor of a few hundred chunks costs one or two load round trips. Result in every lane.
+__device__ __forceinline__ double warp_sum_partials(const float* partials, int begin, int end, int lane) {
+  double s = 0.0;
+  for (int base = begin + lane; base < end; base += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = base + 32 * k < end ? partials[base + 32 * k] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += static_cast<double>(v[k]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
 // per-tensor norms -> total norm (the norm of the per-tensor norms, as torch's get_total_norm) -> clip coefficient.
 // One warp per tensor (lanes sum strided chunk partials in fp64, then a fixed xor tree), the per-tensor norms kept in
 // shared memory, then warp 0 sums their squares in the same fixed way: deterministic, and no serial chain of loads.
@@ -171,11 +188,7 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
   const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
   const int nwarps = static_cast<int>(blockDim.x >> 5);
   for (int t = warp; t < A.n_tensors; t += nwarps) {
-    double s = 0.0;
-    for (int c = A.tensor_chunk_start[t] + lane; c < A.tensor_chunk_start[t + 1]; c += 32)
-      s += static_cast<double>(A.partials[c]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const double s = warp_sum_partials(A.partials, A.tensor_chunk_start[t], A.tensor_chunk_start[t + 1], lane);
     if (lane == 0) tnorm[t] = static_cast<float>(sqrt(s));
   }
   __syncthreads();
@@ -204,7 +217,14 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
 __global__ void __launch_bounds__(1024) partials_total_kernel(const float* partials, int n, double* out) {
   __shared__ double red[32];
   double acc = 0.0;
-  for (int c = threadIdx.x; c < n; c += blockDim.x) acc += static_cast<double>(partials[c]);
+  const int stride = static_cast<int>(blockDim.x);
+  for (int base = threadIdx.x; base < n; base += 8 * stride) {   // thread order c, c + stride, ...; loads batched by 8
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = base + stride * k < n ? partials[base + stride * k] : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += static_cast<double>(v[k]);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -279,24 +299,58 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
   const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
   const double dstep = A.dstep != nullptr ? static_cast<double>(*A.dstep) : 0.0;
+  int s_cur = -1;
+  AdamSeg S;
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
-    AdamSeg S = A.seg[s];
-    const double lr = S.lr_dev != nullptr ? *S.lr_dev : S.lr;   // this step's lr (device-read under a schedule)
-    if (A.dstep != nullptr) {   // the host computes these in fp64 from its step count; the same formulas here
-      const double bc1 = 1.0 - pow(A.beta1d, dstep);
-      const double bc2 = 1.0 - pow(A.beta2d, dstep);
-      S.neg_step_size = static_cast<float>(-(lr / bc1));
-      S.bc2_sqrt = static_cast<float>(pow(bc2, 0.5));
-    } else if (S.lr_dev != nullptr) {
-      S.neg_step_size = static_cast<float>(-(lr / S.bc1));
+    if (s != s_cur) {   // the segment's scalars, recomputed only when the block moves to another tensor
+      s_cur = s;
+      S = A.seg[s];
+      const double lr = S.lr_dev != nullptr ? *S.lr_dev : S.lr;   // this step's lr (device-read under a schedule)
+      if (A.dstep != nullptr) {   // the host computes these in fp64 from its step count; the same formulas here
+        const double bc1 = 1.0 - pow(A.beta1d, dstep);
+        const double bc2 = 1.0 - pow(A.beta2d, dstep);
+        S.neg_step_size = static_cast<float>(-(lr / bc1));
+        S.bc2_sqrt = static_cast<float>(pow(bc2, 0.5));
+      } else if (S.lr_dev != nullptr) {
+        S.neg_step_size = static_cast<float>(-(lr / S.bc1));
+      }
+      if (S.lr_dev != nullptr) S.decay_mul = static_cast<float>(1.0 - lr * S.wd);
     }
-    if (S.lr_dev != nullptr) S.decay_mul = static_cast<float>(1.0 - lr * S.wd);
-    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
-    const int64_t end = min(begin + kChunk, S.numel);
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kAdamChunk;
+    const int64_t end = min(begin + kAdamChunk, S.numel);
     const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype) &&
                      (S.ema == nullptr || aligned16(S.ema));
     int64_t i0 = begin;
+    if (vec && end - begin == kAdamChunk) {   // a full chunk: both vectors' loads go out before the first use
+      float4 p[2], m[2], v[2], g[2], e[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + k * kMtThreads);
+        p[k] = *reinterpret_cast<const float4*>(S.p + i);
+        m[k] = *reinterpret_cast<const float4*>(S.m + i);
+        v[k] = *reinterpret_cast<const float4*>(S.v + i);
+        g[k] = load_g4(S.g, i, S.dtype);
+        if (S.ema != nullptr) e[k] = *reinterpret_cast<const float4*>(S.ema + i);
+      }
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + k * kMtThreads);
+        adam_elem(p[k].x, X(g[k].x), m[k].x, v[k].x, S, K);
+        adam_elem(p[k].y, X(g[k].y), m[k].y, v[k].y, S, K);
+        adam_elem(p[k].z, X(g[k].z), m[k].z, v[k].z, S, K);
+        adam_elem(p[k].w, X(g[k].w), m[k].w, v[k].w, S, K);
+        *reinterpret_cast<float4*>(S.p + i) = p[k];
+        *reinterpret_cast<float4*>(S.m + i) = m[k];
+        *reinterpret_cast<float4*>(S.v + i) = v[k];
+        if (S.ema != nullptr) {
+          e[k].x = ema_lerp(e[k].x, p[k].x, A.ema); e[k].y = ema_lerp(e[k].y, p[k].y, A.ema);
+          e[k].z = ema_lerp(e[k].z, p[k].z, A.ema); e[k].w = ema_lerp(e[k].w, p[k].w, A.ema);
+          *reinterpret_cast<float4*>(S.ema + i) = e[k];
+        }
+      }
+      continue;
+    }
     if (vec) {
       const int64_t vend = begin + ((end - begin) & ~int64_t(3));
       for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
@@ -422,10 +476,7 @@ __global__ void __launch_bounds__(256) mat_denom_kernel(const __grid_constant__ 
   const int mat = blockIdx.x * 8 + static_cast<int>(threadIdx.x >> 5);
   if (mat >= A.n) return;
   const int lane = threadIdx.x & 31;
-  double s = 0.0;
-  for (int c = A.chunk_start[mat] + lane; c < A.chunk_start[mat + 1]; c += 32) s += static_cast<double>(A.partials[c]);
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const double s = warp_sum_partials(A.partials, A.chunk_start[mat], A.chunk_start[mat + 1], lane);
   if (lane == 0) A.den[A.base + mat] = __fadd_rn(static_cast<float>(sqrt(s)), A.eps);
 }
 
@@ -781,6 +832,64 @@ __global__ void __launch_bounds__(kMtThreads) clip_scale_kernel(const __grid_con
         g[i] = __fmul_rn(g[i], coef);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// MoESwiGLU.update_bias (mote/model/moe.py:147-159) for every MoE layer of the model in one launch, one block per
+// layer, fp32 tensor ops as the reference:
+//   if load.sum() <= 0: return
+//   e = (load.mean() - load) / load.mean().clamp_min(1e-9); sgn = sign(e)   (sign(NaN) = 0, as torch)
+//   bias += fp32(gamma) * (sgn - sgn.mean()); load.zero_()
+// The loads are token counts (integers), so their sum, formed in fp64 and rounded once, is the reference's fp32 sum
+// in any order; the sum of the signs is an exact integer. No host round trip: the reference's `load.sum() <= 0`
+// test becomes a per-block branch.
+__global__ void __launch_bounds__(kMtThreads) moe_bias_kernel(const __grid_constant__ MoeBiasArgs A) {
+  __shared__ double red_d[kMtThreads / 32];
+  __shared__ int red_i[kMtThreads / 32];
+  __shared__ float sh_mean;
+  __shared__ int sh_skip, sh_count;
+  const MoeLayer& L = A.layer[blockIdx.x];
+  const int E = L.experts;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  double s = 0.0;
+  for (int i = threadIdx.x; i < E; i += kMtThreads) s += static_cast<double>(L.load[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+  if (lane == 0) red_d[warp] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < kMtThreads / 32; ++w) t += red_d[w];
+    const float total = static_cast<float>(t);
+    sh_skip = total <= 0.f;   // a NaN sum goes on, as `load.sum() <= 0` is false for it
+    sh_mean = __fdiv_rn(total, static_cast<float>(E));
+  }
+  __syncthreads();
+  if (sh_skip) return;
+  const float mean = sh_mean;
+  const float den = mean < 1e-9f ? 1e-9f : mean;   // clamp_min keeps a NaN
+  int cnt = 0;
+  for (int i = threadIdx.x; i < E; i += kMtThreads) {
+    const float e = __fdiv_rn(__fsub_rn(mean, L.load[i]), den);
+    cnt += (e > 0.f) - (e < 0.f);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_down_sync(0xffffffffu, cnt, o);
+  if (lane == 0) red_i[warp] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int t = 0;
+    for (int w = 0; w < kMtThreads / 32; ++w) t += red_i[w];
+    sh_count = t;
+  }
+  __syncthreads();
+  const float sgn_mean = __fdiv_rn(static_cast<float>(sh_count), static_cast<float>(E));
+  for (int i = threadIdx.x; i < E; i += kMtThreads) {   // each thread rewrites only the elements it read above
+    const float e = __fdiv_rn(__fsub_rn(mean, L.load[i]), den);
+    const float sgn = static_cast<float>((e > 0.f) - (e < 0.f));
+    L.bias[i] = __fadd_rn(L.bias[i], __fmul_rn(L.gamma, __fsub_rn(sgn, sgn_mean)));
+    L.load[i] = 0.f;
   }
 }
 

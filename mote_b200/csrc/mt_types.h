@@ -9,6 +9,9 @@ namespace moteopt {
 
 constexpr int kChunk = 16384;          // elements per work unit of the multi-tensor kernels
 constexpr int kMtThreads = 256;
+// AdamW's work unit: two 16-byte vectors per thread, so that a few hundred thousand AdamW elements (a trainer's
+// embeddings and norms) still spread over every SM, one load round trip per chunk
+constexpr int kAdamChunk = 8 * kMtThreads;
 
 enum DType : int { kF32 = 0, kBF16 = 1 };
 
@@ -228,6 +231,19 @@ struct ScaleArgs {
   const float* coef;
   int chunk_start[kMaxNormSeg + 1];
   SumsqSeg seg[kMaxNormSeg];
+};
+
+// ---- the lossfree MoE router's bias step after the optimizer step (mote/model/moe.py:147-159), one block per layer
+constexpr int kMaxMoeLayers = 512;
+struct MoeLayer {
+  float* load;               // [experts] token counts since the last step (_load_acc), zeroed by the step
+  float* bias;               // [experts] routing bias (expert_bias), updated in place
+  int experts;
+  float gamma;               // bias_gamma as fp32 (torch multiplies the fp32 tensor by the Python float in fp32)
+};
+struct MoeBiasArgs {
+  int n;
+  MoeLayer layer[kMaxMoeLayers];
 };
 
 }  // namespace moteopt

@@ -4,6 +4,7 @@ descriptor arrays. The optimizer classes (optim.py), the tests and bench.py all 
     optimizer_step(muon=[MuonItem...], adamw=[AdamWItem...], ...)   # mote/train/train.py:944-947
     muon_step(...)                                                  # mote/train/muon.py:52-100
     adamw_step(...)                                                 # torch.optim.AdamW.step (train.py:98)
+    moe_update_bias(moe_layers)                                     # mote/model/moe.py:147-159 (train.py:948-949)
 """
 
 from __future__ import annotations
@@ -201,6 +202,37 @@ def adamw_step(adamw: Sequence[AdamWItem], *, betas=(0.9, 0.999), eps: float = 1
     L.check(L.lib.moteopt_adamw_step(arr, len(adamw), C.byref(hp),
                                      C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
                                      C.c_void_p(stream_handle(dev))), "moteopt_adamw_step")
+
+
+def moe_update_bias(layers: Sequence) -> None:
+    """MoESwiGLU.update_bias (mote/model/moe.py:147-159) of every given MoE layer in one launch, as the trainer calls
+    it after the optimizer step (mote/train/train.py:948-949). `layers` holds MoE modules (anything with the
+    reference module's `router_kind`, `bias_gamma`, `_load_acc` and `expert_bias`) or (load_acc, expert_bias, gamma)
+    tuples. Layers whose router is not "lossfree" or whose gamma is <= 0 are skipped, as moe.py:151-152 does. No
+    host synchronisation, so the call can sit inside a captured CUDA graph."""
+    rows = []
+    for m in layers:
+        if isinstance(m, tuple):
+            load, bias, gamma = m
+        else:
+            if getattr(m, "router_kind", None) != "lossfree" or float(m.bias_gamma) <= 0:
+                continue
+            load, bias, gamma = m._load_acc, m.expert_bias, float(m.bias_gamma)
+        if float(gamma) <= 0:
+            continue
+        for t, what in ((load, "load_acc"), (bias, "expert_bias")):
+            if not (t.is_cuda and t.dtype == torch.float32 and t.is_contiguous()):
+                raise TypeError(f"moe_update_bias: {what} must be a contiguous fp32 CUDA tensor")
+        if load.numel() != bias.numel() or load.device != bias.device:
+            raise ValueError("moe_update_bias: load_acc and expert_bias must match in size and device")
+        rows.append((load, bias, float(gamma)))
+    if not rows:
+        return
+    dev = rows[0][0].device
+    if any(r[0].device != dev for r in rows):
+        raise ValueError("moe_update_bias: all layers must be on one device")
+    arr = (L.MoeBias * len(rows))(*[L.MoeBias(ld.data_ptr(), b.data_ptr(), ld.numel(), g) for ld, b, g in rows])
+    L.check(L.lib.moteopt_moe_update_bias(arr, len(rows), C.c_void_p(stream_handle(dev))), "moteopt_moe_update_bias")
 
 
 class CapturedStep:

@@ -18,7 +18,7 @@ tensors; there is no CPU fallback.
 from __future__ import annotations
 
 from collections import defaultdict
-from typing import Dict, List, Optional, Tuple
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 
@@ -194,7 +194,7 @@ def set_lr(opt, lr: float):
 # -----------------------------------------------------------------------------------------------------------------
 @torch.no_grad()
 def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Optional[dict] = None,
-               ema_decay: float = 0.0) -> Optional[torch.Tensor]:
+               ema_decay: float = 0.0, moe: Optional[Sequence] = None) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one library call:
 
         torch._foreach_div_(grads, total_n); gnorm = clip_grad_norm_(model.parameters(), clip); opt.step()
@@ -206,7 +206,10 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Op
     parameter is in the optimizer (train.py:82-83 skips requires_grad=False ones, which have no grad).
 
     `ema` ({param: fp32 EMA buffer}) with `ema_decay` folds train.py:950-953 (_foreach_lerp_(ema, params,
-    1 - ema_decay)) into the same step for the stepped params; the caller lerps any other params itself."""
+    1 - ema_decay)) into the same step for the stepped params; the caller lerps any other params itself.
+
+    `moe` (the trainer's MoE layers) runs their routers' bias step after the optimizer step, as train.py:948-949
+    (`for m in self._moe: m.update_bias()`), in one launch (functional.moe_update_bias)."""
     opts = getattr(opt, "opts", [opt])
     muon_sets: Dict[Tuple[int, float], List[MuonItem]] = {}
     adam_items: List[AdamWItem] = []
@@ -235,6 +238,8 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Op
                             max_norm=max_norm, grad_divisor=div, ema=bufs, ema_weight=1.0 - float(ema_decay))
     for o, bumped in bumps:
         o._bump(bumped)
+    if moe:
+        F.moe_update_bias(moe)
     return norm
 
 

@@ -13,6 +13,7 @@ What it restates (paths relative to the reference project noahsabaj/mote):
                                 documented single-tensor update (the path torch takes for CPU tensors), which is
                                 the published decoupled-weight-decay Adam of Loshchilov & Hutter.
 * `clip_grad_norm`           -- torch.nn.utils.clip_grad_norm_ as called at mote/train/train.py:946
+* `moe_update_bias`          -- mote/model/moe.py:147-159 (the lossfree router's bias step, train.py:948-949)
 * `optimizer_step`           -- mote/train/train.py:944-947 followed by MultiOpt.step (train.py:64-66: AdamW, then Muon)
 
 Rounding model. Each elementwise op rounds to the tensor's dtype exactly where the reference's tensor op does.
@@ -255,6 +256,30 @@ def clip_grad_norm(grads: List[np.ndarray], max_norm: float) -> np.float32:
     for g in grads:
         g[...] = np.asarray(g * coef, np.float32)
     return total
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# the MoE router's bias step after the optimizer step
+def moe_update_bias(load: np.ndarray, bias: np.ndarray, gamma: float) -> None:
+    """mote/model/moe.py:147-159 (MoESwiGLU.update_bias, called at mote/train/train.py:948-949), in place, for a
+    "lossfree" router with gamma > 0 (the other cases return before touching anything, moe.py:151-152).
+
+    fp32 tensor ops as the reference: mean = sum/E; e = (mean - load) / clamp_min(mean, 1e-9); sgn = sign(e) (0 for
+    NaN); bias += fp32(gamma) * (sgn - sgn.mean()); load = 0. Nothing happens when load.sum() <= 0 (moe.py:154-155).
+    The loads are token counts (integers), so their fp32 sum is exact in any order; it is formed in fp64 here."""
+    E = load.size
+    total = np.float32(np.sum(load.astype(np.float64)))
+    if E == 0 or total <= 0:
+        return
+    mean = np.float32(total / np.float32(E))
+    den = mean if not mean < np.float32(1e-9) else np.float32(1e-9)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        e = ((mean - load.astype(np.float32)).astype(np.float32) / den).astype(np.float32)
+    sgn = (e > 0).astype(np.float32) - (e < 0).astype(np.float32)
+    sgn_mean = np.float32(np.float32(np.sum(sgn, dtype=np.float64)) / np.float32(E))
+    t = (sgn - sgn_mean).astype(np.float32)
+    bias[...] = (bias + (np.float32(gamma) * t).astype(np.float32)).astype(np.float32)
+    load[...] = 0
 
 
 # ----------------------------------------------------------------------------------------------------------------

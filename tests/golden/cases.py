@@ -35,3 +35,42 @@ def sample_index(numel: int, k: int = SAMPLES) -> np.ndarray:
     """Fixed element indices of one tensor that the c0 fixture stores."""
     rng = np.random.default_rng(numel)
     return np.sort(rng.choice(numel, size=min(k, numel), replace=False))
+
+
+# the lossfree router's bias step (mote/model/moe.py:147-159): (name, experts, load kind, seed); gamma per case below
+MOE_CASES = [
+    ("zipf64", 64, "zipf", 21),
+    ("balanced8", 8, "equal", 22),
+    ("odd12", 12, "uniform", 23),
+    ("idle16", 16, "zero", 24),
+    ("onehot5", 5, "onehot", 25),
+    ("ties4", 4, "ties", 26),
+    ("wide256", 256, "uniform", 27),
+    ("pair2", 2, "uniform", 28),
+]
+MOE_GAMMA = 1e-3
+MOE_STEPS = 3
+
+
+def moe_loads(experts: int, kind: str, seed: int, step: int) -> np.ndarray:
+    """Token counts per expert for one step of a MOE_CASES case (integers stored as fp32, as the router's _load_acc)."""
+    rng = np.random.default_rng(seed * 100 + step)
+    if kind == "zipf":
+        x = np.minimum(rng.zipf(1.3, size=experts), 50000)
+    elif kind == "equal":
+        x = np.full(experts, 4096)
+    elif kind == "zero":
+        x = np.zeros(experts)
+    elif kind == "onehot":
+        x = np.zeros(experts)
+        x[step % experts] = 2048
+    elif kind == "ties":
+        x = np.array([1, 2, 3, 2][:experts]) * (step + 1)
+    else:
+        x = rng.integers(0, 5000, size=experts)
+    return x.astype(np.float32)
+
+
+def moe_bias0(experts: int, seed: int) -> np.ndarray:
+    """The expert bias a case starts from."""
+    return np.random.default_rng(seed).uniform(-0.05, 0.05, size=experts).astype(np.float32)

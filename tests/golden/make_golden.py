@@ -11,7 +11,8 @@ What is run (reference file:line):
   * `mote.train.muon.Muon` (muon.py:46-100): the batched-step case of tests/test_muon_batched.py:46-67, the 3-D stack
     of tests/test_moe.py:105-123 and the per-matrix-lr cases of tests/test_elr.py:145-182;
   * `torch.optim.AdamW` (constructed as at train.py:98) and `torch.nn.utils.clip_grad_norm_` (train.py:946);
-  * the whole step of train.py:944-947 (grads /= n, clip, AdamW then Muon) on the c0 workload for 10 steps.
+  * the whole step of train.py:944-947 (grads /= n, clip, AdamW then Muon) on the c0 workload for 10 steps;
+  * `mote.model.moe.MoESwiGLU.update_bias` (moe.py:147-159), the lossfree router's bias step of train.py:948-949.
 """
 
 from __future__ import annotations
@@ -32,8 +33,8 @@ sys.path.insert(0, REF)
 from mote.train.muon import Muon, newton_schulz  # noqa: E402  (the reference)
 
 from mote_b200 import configs  # noqa: E402
-from tests.golden.cases import (ADAM_SHAPES, C0_DIVISOR, NS_CASES, NS_STEPS, ns_input,  # noqa: E402
-                                sample_index)
+from tests.golden.cases import (ADAM_SHAPES, C0_DIVISOR, MOE_CASES, MOE_GAMMA, MOE_STEPS, NS_CASES,  # noqa: E402
+                                NS_STEPS, moe_bias0, moe_loads, ns_input, sample_index)
 
 torch.set_num_threads(max(1, min(8, os.cpu_count() or 1)))
 
@@ -166,10 +167,30 @@ def make_c0():
     np.savez_compressed(HERE / "c0_reference.npz", **out)
 
 
+# ---------------------------------------------------------------------------------------------------------------
+def make_moe():
+    """mote/model/moe.py:147-159 (MoESwiGLU.update_bias) on the MOE_CASES loads, MOE_STEPS steps per case."""
+    from mote.model.moe import MoESwiGLU   # the reference
+    out = {}
+    for name, experts, kind, seed in MOE_CASES:
+        torch.manual_seed(0)
+        m = MoESwiGLU(16, 32, experts, top_k=1, router="lossfree", bias_gamma=MOE_GAMMA)
+        with torch.no_grad():
+            m.expert_bias.copy_(torch.from_numpy(moe_bias0(experts, seed)))
+        for step in range(MOE_STEPS):
+            with torch.no_grad():
+                m._load_acc.copy_(torch.from_numpy(moe_loads(experts, kind, seed, step)))
+            m.update_bias()
+            out[f"{name}_bias{step}"] = m.expert_bias.numpy().copy()
+            out[f"{name}_load{step}"] = m._load_acc.numpy().copy()
+    np.savez_compressed(HERE / "moe_reference.npz", **out)
+
+
 if __name__ == "__main__":
     make_ns()
     make_muon()
     make_adamw_clip()
     make_c0()
+    make_moe()
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

@@ -22,7 +22,8 @@ import pytest
 from tests.conftest import golden
 from oracle import moteopt_oracle as O
 
-from tests.golden.cases import ADAM_SHAPES, ADAM_WDS, C0_DIVISOR, NS_CASES, ns_input, sample_index
+from tests.golden.cases import (ADAM_SHAPES, ADAM_WDS, C0_DIVISOR, MOE_CASES, MOE_GAMMA, MOE_STEPS, NS_CASES, moe_bias0,
+                                moe_loads, ns_input, sample_index)
 from mote_b200 import configs
 
 
@@ -177,3 +178,15 @@ def test_reference_noise_floor_is_recorded():
     a = O.newton_schulz(u, 5)
     b = np.swapaxes(O.newton_schulz(np.ascontiguousarray(np.swapaxes(u, -1, -2)), 5), -1, -2)
     assert O.rel_frob(a, b) > 1e-3   # not bitwise: the noise floor is real
+
+
+@pytest.mark.parametrize("name,experts,kind,seed", MOE_CASES)
+def test_moe_update_bias_matches_reference(name, experts, kind, seed):
+    """The lossfree router's bias step (mote/model/moe.py:147-159), MOE_STEPS steps: bit for bit, bias and load."""
+    ref = golden("moe_reference")
+    bias = moe_bias0(experts, seed)
+    for step in range(MOE_STEPS):
+        load = moe_loads(experts, kind, seed, step)
+        O.moe_update_bias(load, bias, MOE_GAMMA)
+        assert np.array_equal(bias.view(np.uint32), ref[f"{name}_bias{step}"].view(np.uint32)), (name, step)
+        assert np.array_equal(load.view(np.uint32), ref[f"{name}_load{step}"].view(np.uint32)), (name, step)
