@@ -186,6 +186,19 @@ MOTEOPT_API int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* m
                                                      size_t workspace_bytes, moteopt_stream_t stream);
 MOTEOPT_API int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* muon_cfg,
                                    const void* const* updates, moteopt_stream_t stream);
+/* moteopt_muon_apply with the trainer's two after-step reads of the weights fused into the same pass:
+ * ema[i] (fp32, the param's shape; the array or an entry may be NULL) = lerp(ema[i], p_new, ema_weight), as
+ * torch._foreach_lerp_ at mote/train/train.py:950-953; norms (device, n floats, may be NULL) receives ||p_new||_F of
+ * each param (mote/train/elr.py:85-87, NormTracker.sample), summed in fp64 in a fixed order. The norms need a
+ * workspace of moteopt_muon_apply_workspace_size bytes (256-byte aligned); without norms it may be NULL. */
+MOTEOPT_API size_t moteopt_muon_apply_workspace_size(const moteopt_muon_param* muon, int n);
+MOTEOPT_API int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_muon_config* muon_cfg,
+                                      const void* const* updates, float* const* ema, double ema_weight, float* norms,
+                                      void* workspace, size_t workspace_bytes, moteopt_stream_t stream);
+/* ema[i] = lerp(ema[i], params[i], weight) over n fp32 tensors: torch._foreach_lerp_(ema, params, weight), the EMA
+ * update of mote/train/train.py:950-953 (weight = 1 - ema_decay), bit for bit, for params that no fused pass writes. */
+MOTEOPT_API int moteopt_ema_lerp(float* const* ema, const float* const* params, const int64_t* numels, int n,
+                                 double weight, moteopt_stream_t stream);
 
 /* Peer mappings for the sharded step (no counterpart in the reference). A rank exports the device allocation that
  * holds `ptr` (a CUDA IPC handle of MOTEOPT_IPC_HANDLE_BYTES bytes, plus ptr's byte offset inside it); another process

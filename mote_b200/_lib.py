@@ -24,7 +24,8 @@ EXPORTS = (
     "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_ex",
     "moteopt_optimizer_step_with_coef",
-    "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply",
+    "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply", "moteopt_muon_apply_workspace_size",
+    "moteopt_muon_apply_ex", "moteopt_ema_lerp",
     "moteopt_ipc_export", "moteopt_ipc_import", "moteopt_ipc_close",
     "moteopt_grad_sumsq_workspace_size", "moteopt_grad_sumsq", "moteopt_clip_coef_from_sums",
     "moteopt_muon_step_workspace_size", "moteopt_muon_step",
@@ -99,6 +100,10 @@ def _load() -> C.CDLL:
                                                        C.POINTER(AdamWTensor), i32, C.POINTER(AdamWHparams), dbl, vp,
                                                        C.POINTER(vp), vp, sz, vp]),
         "moteopt_muon_apply": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(vp), vp]),
+        "moteopt_muon_apply_workspace_size": (sz, [C.POINTER(MuonParam), i32]),
+        "moteopt_muon_apply_ex": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(vp), C.POINTER(vp),
+                                        dbl, vp, vp, sz, vp]),
+        "moteopt_ema_lerp": (i32, [C.POINTER(vp), C.POINTER(vp), C.POINTER(C.c_int64), i32, dbl, vp]),
         "moteopt_ipc_export": (i32, [vp, vp, C.POINTER(C.c_uint64)]),
         "moteopt_ipc_import": (i32, [vp, C.POINTER(vp)]),
         "moteopt_ipc_close": (i32, [vp]),

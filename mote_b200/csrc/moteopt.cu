@@ -417,7 +417,6 @@ EmaConsts ema_consts(double weight) {
   return E;
 }
 
-// ema: per AdamW tensor, an EMA buffer or null (null array: none)
 // ema: per AdamW tensor, an EMA buffer or null; lr_dev: device array, one lr per tensor, or null
 int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp, bool has_div, float div,
                  const float* coef, int sms, cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0,
@@ -446,6 +445,10 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
     const int cnt = std::min(n - s0, kMaxAdamSeg);
     A.n = cnt;
     A.chunk_start[0] = 0;
+    int64_t elems = 0;
+    for (int i = 0; i < cnt; ++i) elems += t[s0 + i].numel;
+    const bool small = cdiv(elems, kChunk) < 4 * static_cast<int64_t>(sms);
+    const int unit = small ? kAdamChunk : kChunk;
     for (int i = 0; i < cnt; ++i) {
       const moteopt_adamw_tensor& x = t[s0 + i];
       AdamSeg& S = A.seg[i];
@@ -467,10 +470,11 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       S.ema = ema != nullptr ? ema[s0 + i] : nullptr;
       S.lr_dev = lr_dev != nullptr ? lr_dev + s0 + i : nullptr;
       S.bc1 = bc1;
-      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, kAdamChunk));
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, unit));
     }
     if (A.chunk_start[cnt] == 0) continue;
-    adamw_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    if (small) adamw_kernel<true><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    else adamw_kernel<false><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("adamw_kernel");
   }
   return MOTEOPT_OK;
@@ -1144,13 +1148,30 @@ int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* muon, int n_m
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream), muon_updates);
 }
 
-int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
-                       const void* const* updates, moteopt_stream_t stream) {
+size_t moteopt_muon_apply_workspace_size(const moteopt_muon_param* muon, int n) {
+  if (n < 0 || (n > 0 && muon == nullptr)) return 0;
+  int64_t chunks = 0;
+  for (int i = 0; i < n; ++i) chunks += cdiv(std::max<int64_t>(muon[i].batch * muon[i].rows * muon[i].cols, 0), kChunk);
+  return static_cast<size_t>(std::max<int64_t>(chunks, 1)) * sizeof(float);
+}
+
+int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
+                          const void* const* updates, float* const* ema, double ema_weight, float* norms,
+                          void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
   if (n < 0 || (n > 0 && (muon == nullptr || updates == nullptr)) || cfg == nullptr)
     return fail(MOTEOPT_ERR_INVALID, "moteopt_muon_apply: null argument");
+  if (n > kMaxDenom && norms != nullptr)
+    return fail(MOTEOPT_ERR_LIMIT, "moteopt_muon_apply: norms of more than 4096 params in one call");
   int sms = 0;
   MO_TRY(device_setup(&sms));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* partials = nullptr;
+  if (norms != nullptr && n > 0) {
+    MO_TRY(check_ws(workspace, workspace_bytes, moteopt_muon_apply_workspace_size(muon, n)));
+    partials = static_cast<float*>(workspace);
+  }
   std::vector<FlatOutSeg> segs;
+  std::vector<int> start(1, 0);
   for (int i = 0; i < n; ++i) {
     const moteopt_muon_param& p = muon[i];
     if (p.param == nullptr || updates[i] == nullptr || p.batch < 1 || p.rows < 1 || p.cols < 1)
@@ -1164,9 +1185,59 @@ int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon
     S.has_decay = p.decay != 0.0;
     S.decay_mul = static_cast<float>(1.0 - p.decay);
     S.scale = static_cast<float>(cfg->rms_scale * std::pow(static_cast<double>(std::max(p.rows, p.cols)), 0.5));
+    S.ema = ema != nullptr ? ema[i] : nullptr;
+    S.partials = partials != nullptr ? partials + start.back() : nullptr;
+    start.push_back(start.back() + static_cast<int>(cdiv(S.numel, kChunk)));
     segs.push_back(S);
   }
-  return launch_flat_out(segs, 1, sms, reinterpret_cast<cudaStream_t>(stream));
+  MO_TRY(launch_flat_out(segs, 1, sms, st, ema_weight));
+  if (partials != nullptr) {   // ||p_new||_F per param: fixed-order fp64 sum of its chunk partials
+    static thread_local DenomArgs D;
+    std::memset(&D, 0, sizeof(D));
+    D.n = n;
+    D.base = 0;
+    D.eps = 0.f;
+    D.partials = partials;
+    D.den = norms;
+    for (int i = 0; i <= n; ++i) D.chunk_start[i] = start[i];
+    mat_denom_kernel<<<(n + 7) / 8, 256, 0, st>>>(D);
+    MO_LAUNCHED("mat_denom_kernel");
+  }
+  return MOTEOPT_OK;
+}
+
+int moteopt_muon_apply(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
+                       const void* const* updates, moteopt_stream_t stream) {
+  return moteopt_muon_apply_ex(muon, n, cfg, updates, nullptr, 0.0, nullptr, nullptr, 0, stream);
+}
+
+int moteopt_ema_lerp(float* const* ema, const float* const* params, const int64_t* numels, int n, double weight,
+                     moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (ema == nullptr || params == nullptr || numels == nullptr)))
+    return fail(MOTEOPT_ERR_INVALID, "moteopt_ema_lerp: null argument");
+  for (int i = 0; i < n; ++i)
+    if (numels[i] < 0 || (numels[i] > 0 && (ema[i] == nullptr || params[i] == nullptr)))
+      return fail(MOTEOPT_ERR_INVALID, "moteopt_ema_lerp: bad tensor " + std::to_string(i));
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  static thread_local LerpArgs A;
+  for (int s0 = 0; s0 < n; s0 += kMaxLerpSeg) {
+    const int cnt = std::min(n - s0, kMaxLerpSeg);
+    std::memset(&A, 0, sizeof(A));
+    A.n = cnt;
+    A.ema = ema_consts(weight);
+    for (int i = 0; i < cnt; ++i) {
+      A.seg[i] = LerpSeg{ema[s0 + i], params[s0 + i], numels[s0 + i]};
+      if (cdiv(numels[s0 + i], kChunk) > (1 << 30) - A.chunk_start[i])
+        return fail(MOTEOPT_ERR_LIMIT, "moteopt_ema_lerp: too many elements in one call");
+      A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(numels[s0 + i], kChunk));
+    }
+    if (A.chunk_start[cnt] == 0) continue;
+    ema_lerp_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    MO_LAUNCHED("ema_lerp_kernel");
+  }
+  return MOTEOPT_OK;
 }
 
 size_t moteopt_grad_sumsq_workspace_size(const int64_t* numels, int n) {

@@ -294,6 +294,10 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
   p = __fadd_rn(p, __fdiv_rn(__fmul_rn(S.neg_step_size, m), den));
 }
 
+// kSmall: kAdamChunk work units with both of a thread's vectors loaded up front (launches too small to fill the
+// GPU in kChunk units); else kChunk units walked one vector per thread at a time, which needs half the registers
+// and so runs twice the blocks per SM. A separate instantiation each, so each gets its own register allocation.
+template <bool kSmall>
 __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant__ AdamArgs A) {
   const int total = A.chunk_start[A.n];
   const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
@@ -317,12 +321,13 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
       }
       if (S.lr_dev != nullptr) S.decay_mul = static_cast<float>(1.0 - lr * S.wd);
     }
-    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kAdamChunk;
-    const int64_t end = min(begin + kAdamChunk, S.numel);
+    constexpr int kUnit = kSmall ? kAdamChunk : kChunk;
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kUnit;
+    const int64_t end = min(begin + kUnit, S.numel);
     const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype) &&
                      (S.ema == nullptr || aligned16(S.ema));
     int64_t i0 = begin;
-    if (vec && end - begin == kAdamChunk) {   // a full chunk: both vectors' loads go out before the first use
+    if (kSmall && vec && end - begin == kAdamChunk) {   // a full unit: both vectors' loads go out before the first use
       float4 p[2], m[2], v[2], g[2], e[2];
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
@@ -832,6 +837,43 @@ __global__ void __launch_bounds__(kMtThreads) clip_scale_kernel(const __grid_con
         g[i] = __fmul_rn(g[i], coef);
       }
     }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// ema = lerp(ema, p, w) over a segment list (torch._foreach_lerp_, train.py:950-953), torch's rounding as ema_lerp.
+// A full aligned chunk goes in four quarters of four 16-byte vectors per thread, each quarter's eight loads issued
+// before its math.
+__global__ void __launch_bounds__(kMtThreads) ema_lerp_kernel(const __grid_constant__ LerpArgs A) {
+  const int total = A.chunk_start[A.n];
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const LerpSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    int64_t i0 = begin;
+    if (end - begin == kChunk && aligned16(S.ema) && aligned16(S.p)) {
+      float4* ep = reinterpret_cast<float4*>(S.ema + begin);
+      const float4* pp = reinterpret_cast<const float4*>(S.p + begin);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 e[4], p[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int j = threadIdx.x + (q * 4 + k) * kMtThreads;
+          e[k] = ep[j];
+          p[k] = pp[j];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          e[k].x = ema_lerp(e[k].x, p[k].x, A.ema); e[k].y = ema_lerp(e[k].y, p[k].y, A.ema);
+          e[k].z = ema_lerp(e[k].z, p[k].z, A.ema); e[k].w = ema_lerp(e[k].w, p[k].w, A.ema);
+          ep[threadIdx.x + (q * 4 + k) * kMtThreads] = e[k];
+        }
+      }
+      i0 = end;
+    }
+    for (int64_t i = i0 + threadIdx.x; i < end; i += kMtThreads) S.ema[i] = ema_lerp(S.ema[i], S.p[i], A.ema);
   }
 }
 

@@ -9,8 +9,9 @@ namespace moteopt {
 
 constexpr int kChunk = 16384;          // elements per work unit of the multi-tensor kernels
 constexpr int kMtThreads = 256;
-// AdamW's work unit: two 16-byte vectors per thread, so that a few hundred thousand AdamW elements (a trainer's
-// embeddings and norms) still spread over every SM, one load round trip per chunk
+// AdamW's small work unit: two 16-byte vectors per thread, so that a few hundred thousand AdamW elements (a
+// trainer's embeddings and norms) still spread over every SM, one load round trip per chunk. Launches with enough
+// elements to fill the GPU in kChunk units use those instead (fewer registers, more blocks per SM).
 constexpr int kAdamChunk = 8 * kMtThreads;
 
 enum DType : int { kF32 = 0, kBF16 = 1 };
@@ -231,6 +232,21 @@ struct ScaleArgs {
   const float* coef;
   int chunk_start[kMaxNormSeg + 1];
   SumsqSeg seg[kMaxNormSeg];
+};
+
+// ---- the weights' EMA as a pass of its own (mote/train/train.py:950-953, torch._foreach_lerp_(ema, params, w)),
+// for params that no fused pass writes (the sharded step's all-gathered AdamW region)
+constexpr int kMaxLerpSeg = 512;
+struct LerpSeg {
+  float* ema;
+  const float* p;
+  int64_t numel;
+};
+struct LerpArgs {
+  int n;
+  EmaConsts ema;
+  int chunk_start[kMaxLerpSeg + 1];
+  LerpSeg seg[kMaxLerpSeg];
 };
 
 // ---- the lossfree MoE router's bias step after the optimizer step (mote/model/moe.py:147-159), one block per layer

@@ -128,13 +128,16 @@ class Compute:
     """The step's compute, injected: `sumsq(views, divisor) -> 0-dim fp64 tensor` (sum of (g/divisor)^2 over the
     views), `coef(sums, max_norm) -> 2-element fp32 tensor [norm, coef]`, `update(muon_items, adam_items, coef,
     divisor, muon_out)` with items as in mote_b200.functional (AdamW applied; Muon's update O written to the bf16
-    tensors `muon_out`, one per Muon item), and `apply(muon_items, updates)`: p = p*(1-decay); p += -lr*(O*scale) for
-    every item (grad and momentum buffer unused)."""
+    tensors `muon_out`, one per Muon item), and `apply(muon_items, updates, ema=None, ema_weight=0.0, norms=None)`:
+    p = p*(1-decay); p += -lr*(O*scale) for every item (grad and momentum buffer unused), then, when given,
+    ema[k] = lerp(ema[k], p, ema_weight) and norms[k] = ||p||_F in the same pass. `ema(emas, params, weight)` lerps
+    tensors that no pass writes (the all-gathered AdamW region)."""
     sumsq: Callable
     coef: Callable
     update: Callable
     apply: Callable
     set_step: Optional[Callable] = None   # set_step(device, n): AdamW's step count, when the compute keeps one
+    ema: Optional[Callable] = None
 
 
 def _reduce_scatter(out: torch.Tensor, flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
@@ -183,6 +186,19 @@ class ShardedStep:
         self.peer_ptrs: Optional[List[int]] = None   # update region of every rank, mapped into this process
         self._peer_bases: List[int] = []
         self._flag = None
+        self.ema_decay: Optional[float] = None
+        self.em: Optional[torch.Tensor] = None   # EMA of the Muon and AdamW param regions (every rank, replicated)
+        self.ea: Optional[torch.Tensor] = None
+
+    def enable_ema(self, decay: float) -> None:
+        """Keep the weights' EMA of train.py:950-953 (ema = lerp(ema, p, 1 - decay) after every step), starting from
+        the params as they are now (train.py keeps `[p.detach().clone() for p in params]`). Every rank holds the
+        whole EMA: the Muon region's is lerped in the apply pass that writes the params, the AdamW region's in one
+        pass after its all-gather, so each is a pure function of the replicated params and stays identical across
+        ranks. The EMA of param i is `muon_view(step.em, i)` / `adam_view(step.ea, i)`."""
+        self.ema_decay = float(decay)
+        self.em = self.pm.detach().clone()
+        self.ea = self.pa.detach().clone()
 
     def enable_peer_updates(self) -> None:
         """Map every rank's update region into this process (CUDA IPC through libmoteopt); collective, eager, once."""
@@ -312,9 +328,11 @@ class ShardedStep:
 
     @torch.no_grad()
     def step(self, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None,
-             marks: Optional[list] = None) -> torch.Tensor:
-        """One sharded step. `marks` (eager use only): a list that receives (phase name, CUDA event) pairs recorded on
-        the current stream after each phase, for a per-phase time breakdown."""
+             marks: Optional[list] = None, norms: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One sharded step. `norms` (fp32, one per Muon param, on the device) receives ||p||_F of every Muon param
+        after the update (the ELR tracker's NormTracker.sample, elr.py:85-87), computed in the apply pass. `marks`
+        (eager use only): a list that receives (phase name, CUDA event) pairs recorded on the current stream after
+        each phase, for a per-phase time breakdown."""
         from .functional import AdamWItem, MuonItem
         plan, r = self.plan, self.rank
 
@@ -354,9 +372,14 @@ class ShardedStep:
             updates = [self.muon_view(self.om, i) for i in every]
         _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
         mark("exchange")
+        w = 1.0 - self.ema_decay if self.em is not None else 0.0
         self.compute.apply([MuonItem(self.muon_view(self.pm, i), None, None, self.muon_lr,
                                      self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
-                            for i in every], updates)
+                            for i in every], updates,
+                           ema=[self.muon_view(self.em, i) for i in every] if self.em is not None else None,
+                           ema_weight=w, norms=norms)
+        if self.ea is not None:
+            self.compute.ema([self.ea], [self.pa], w)
         mark("apply_all")
         return norm_coef[0]
 
@@ -424,7 +447,7 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
             C.c_void_p(coef_t.data_ptr() if coef_t is not None else 0), outs, C.c_void_p(ws.data_ptr()),
             ws.numel(), C.c_void_p(stream_handle(dev))), "moteopt_optimizer_step_with_coef_out")
 
-    def apply(muon, updates):
+    def apply(muon, updates, ema=None, ema_weight=0.0, norms=None):
         if not muon:
             return
         dev = muon[0].param.device
@@ -439,12 +462,25 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
             e.lr, e.decay, e.momentum = float(it.lr), float(it.decay), float(it.momentum)
         cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
         ptrs = L.array(C.c_void_p, [o if isinstance(o, int) else o.data_ptr() for o in updates])
-        L.check(L.lib.moteopt_muon_apply(arr, len(muon), C.byref(cfg), ptrs, C.c_void_p(stream_handle(dev))),
-                "moteopt_muon_apply")
+        emas = L.array(C.c_void_p, [e.data_ptr() for e in ema]) if ema is not None else None
+        if norms is not None and (norms.dtype != torch.float32 or norms.numel() < len(muon) or not norms.is_cuda):
+            raise ValueError("norms must be an fp32 CUDA tensor with one entry per Muon param")
+        ws = None
+        if norms is not None:
+            ws = workspace(dev, L.lib.moteopt_muon_apply_workspace_size(arr, len(muon)))
+        L.check(L.lib.moteopt_muon_apply_ex(arr, len(muon), C.byref(cfg), ptrs, emas, float(ema_weight),
+                                            C.c_void_p(norms.data_ptr() if norms is not None else 0),
+                                            C.c_void_p(ws.data_ptr() if ws is not None else 0),
+                                            ws.numel() if ws is not None else 0, C.c_void_p(stream_handle(dev))),
+                "moteopt_muon_apply_ex")
+
+    def ema(emas, params, weight):
+        from .functional import ema_lerp
+        ema_lerp([e.reshape(-1) for e in emas], [p.reshape(-1) for p in params], weight)
 
     def set_step(dev, n):
         if dev not in counter:
             counter[dev] = torch.zeros((), dtype=torch.float32, device=dev)
         counter[dev].fill_(float(n))
 
-    return Compute(sumsq, coef, update, apply, set_step)
+    return Compute(sumsq, coef, update, apply, set_step, ema)

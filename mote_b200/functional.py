@@ -5,6 +5,7 @@ descriptor arrays. The optimizer classes (optim.py), the tests and bench.py all 
     muon_step(...)                                                  # mote/train/muon.py:52-100
     adamw_step(...)                                                 # torch.optim.AdamW.step (train.py:98)
     moe_update_bias(moe_layers)                                     # mote/model/moe.py:147-159 (train.py:948-949)
+    ema_lerp(emas, params, 1 - decay)                               # train.py:950-953
 """
 
 from __future__ import annotations
@@ -202,6 +203,26 @@ def adamw_step(adamw: Sequence[AdamWItem], *, betas=(0.9, 0.999), eps: float = 1
     L.check(L.lib.moteopt_adamw_step(arr, len(adamw), C.byref(hp),
                                      C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
                                      C.c_void_p(stream_handle(dev))), "moteopt_adamw_step")
+
+
+def ema_lerp(emas: Sequence[torch.Tensor], params: Sequence[torch.Tensor], weight: float) -> None:
+    """torch._foreach_lerp_(emas, params, weight) (the EMA update of mote/train/train.py:950-953, weight = 1 -
+    ema_decay) in one library launch, bit for bit torch's lerp. For params that no fused pass writes; the optimizer
+    step itself takes `ema=` for the params it updates."""
+    if len(emas) != len(params):
+        raise ValueError("ema_lerp: one EMA buffer per param")
+    if not emas:
+        return
+    for e, p in zip(emas, params):
+        if not (e.is_cuda and p.is_cuda and e.dtype == torch.float32 and p.dtype == torch.float32
+                and e.is_contiguous() and p.is_contiguous() and e.numel() == p.numel() and e.device == p.device):
+            raise TypeError("ema_lerp: EMA buffers and params must be contiguous fp32 CUDA tensors of equal size")
+    dev = emas[0].device
+    n = len(emas)
+    L.check(L.lib.moteopt_ema_lerp(L.array(C.c_void_p, [e.data_ptr() for e in emas]),
+                                   L.array(C.c_void_p, [p.data_ptr() for p in params]),
+                                   L.array(C.c_int64, [p.numel() for p in params]), n, float(weight),
+                                   C.c_void_p(stream_handle(dev))), "moteopt_ema_lerp")
 
 
 def moe_update_bias(layers: Sequence) -> None:

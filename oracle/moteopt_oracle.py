@@ -14,6 +14,7 @@ What it restates (paths relative to the reference project noahsabaj/mote):
                                 the published decoupled-weight-decay Adam of Loshchilov & Hutter.
 * `clip_grad_norm`           -- torch.nn.utils.clip_grad_norm_ as called at mote/train/train.py:946
 * `moe_update_bias`          -- mote/model/moe.py:147-159 (the lossfree router's bias step, train.py:948-949)
+* `ema_lerp`, `frob_norm32`  -- train.py:950-953 (the weights' EMA) and elr.py:85-87 (the ELR tracker's norms)
 * `optimizer_step`           -- mote/train/train.py:944-947 followed by MultiOpt.step (train.py:64-66: AdamW, then Muon)
 
 Rounding model. Each elementwise op rounds to the tensor's dtype exactly where the reference's tensor op does.
@@ -256,6 +257,24 @@ def clip_grad_norm(grads: List[np.ndarray], max_norm: float) -> np.float32:
     for g in grads:
         g[...] = np.asarray(g * coef, np.float32)
     return total
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# the weights' EMA and the ELR tracker's norms after the optimizer step
+def ema_lerp(ema: np.ndarray, p: np.ndarray, weight: float) -> None:
+    """mote/train/train.py:950-953, torch._foreach_lerp_(ema, params, weight), in place: torch's fp32 lerp,
+    e + w*(p - e) for |w| < 0.5 and p - (p - e)*(1 - w) otherwise, each one fused multiply-add."""
+    w = np.float32(weight)
+    d = (np.asarray(p, np.float32) - ema).astype(np.float32)
+    if abs(w) < np.float32(0.5):
+        ema[...] = fma32(w, d, ema)
+    else:
+        ema[...] = fma32(-(np.float32(1.0) - w), d, p)
+
+
+def frob_norm32(p: np.ndarray) -> np.float32:
+    """mote/train/elr.py:85-87 (NormTracker.sample: p.detach().float().norm()) as an fp32 value from an fp64 sum."""
+    return np.float32(np.sqrt(np.sum(np.asarray(p, np.float64) ** 2)))
 
 
 # ----------------------------------------------------------------------------------------------------------------

@@ -18,6 +18,7 @@ from oracle import moteopt_oracle as O
 DIV = 3.0
 CLIP = 0.02
 STEPS = 3
+EMA_DECAY = 0.75   # weight 0.25: the lerp's small-weight branch; the GPU tests cover the other
 
 
 def _free_port():
@@ -69,12 +70,20 @@ def oracle_compute(w):
             o = O.newton_schulz(u.reshape(-1, m, n), steps=w.ns_steps).reshape(it.param.shape)
             out.copy_(torch.from_numpy(np.ascontiguousarray(o, dtype=np.float32)).to(torch.bfloat16))
 
-    def apply(muon, updates):   # the item carries decay = lr * wd (muon.py:78)
-        for it, o in zip(muon, updates):
+    def apply(muon, updates, ema=None, ema_weight=0.0, norms=None):   # the item carries decay = lr * wd (muon.py:78)
+        for k, (it, o) in enumerate(zip(muon, updates)):
             m, n = it.param.shape[-2], it.param.shape[-1]
             decay = it.lr * (it.decay / it.lr) if it.decay else 0.0   # as muon_lr_decay forms lr * wd
             O.muon_apply(it.param.numpy(), o.float().numpy(), 0.2 * max(m, n) ** 0.5, it.lr, decay)
-    return Compute(sumsq, coef, update, apply)
+            if ema is not None:
+                O.ema_lerp(ema[k].numpy(), it.param.numpy(), ema_weight)
+            if norms is not None:
+                norms[k] = float(O.frob_norm32(it.param.numpy()))
+
+    def ema(emas, params, weight):
+        for e, p in zip(emas, params):
+            O.ema_lerp(e.numpy(), p.numpy(), weight)
+    return Compute(sumsq, coef, update, apply, None, ema)
 
 
 def small_workload():
@@ -101,14 +110,18 @@ def _rank_main(rank, world, port, out_dir):
             st.muon_view(pm, i).copy_(torch.from_numpy(p))
         for i, p in enumerate(inp.adam_params):
             st.adam_view(pa, i).copy_(torch.from_numpy(p))
+        st.enable_ema(EMA_DECAY)
         norms = []
+        wnorms = torch.zeros(len(w.muon_shapes))
         for step in range(STEPS):
             ag, mg = configs.make_grads(w, seed=100 + rank, step=step)   # local grads differ per rank
             for i, g in enumerate(mg):
                 st.muon_view(gm, i).copy_(torch.from_numpy(g))
             for i, g in enumerate(ag):
                 st.adam_view(ga, i).copy_(torch.from_numpy(g))
-            norms.append(float(st.step(max_norm=CLIP, grad_divisor=DIV)))
+            norms.append(float(st.step(max_norm=CLIP, grad_divisor=DIV, norms=wnorms)))
+        ema = {f"em{i}": st.muon_view(st.em, i).numpy().copy() for i in range(len(w.muon_shapes))}
+        ema.update({f"ea{i}": st.adam_view(st.ea, i).numpy().copy() for i in range(len(w.adam_shapes))})
         # the sharded checkpoint: the whole state on every rank, then a fresh step object resumed from it must
         # continue bit for bit like the original
         pm_after, pa_after = pm.clone(), pa.clone()
@@ -131,7 +144,8 @@ def _rank_main(rank, world, port, out_dir):
         st2.step(max_norm=CLIP, grad_divisor=DIV)
         resumed = bool(torch.equal(st.pm, st2.pm) and torch.equal(st.pa, st2.pa))
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), pm=pm_after.numpy(), pa=pa_after.numpy(), norms=np.array(norms),
-                 muon_off=np.array(plan.muon_off), adam_off=np.array(plan.adam_off), resumed=resumed, **ckpt)
+                 muon_off=np.array(plan.muon_off), adam_off=np.array(plan.adam_off), resumed=resumed,
+                 wnorms=wnorms.numpy().copy(), **ckpt, **ema)
     finally:
         dist.destroy_process_group()
 
@@ -143,6 +157,7 @@ def _reference(world):
     nd = len(w.adam_decay_shapes)
     ms, vs = [np.zeros_like(p) for p in inp.adam_params], [np.zeros_like(p) for p in inp.adam_params]
     bufs = [None] * len(inp.muon_params)
+    emas = [p.copy() for p in inp.adam_params + inp.muon_params]
     norms = []
     for step in range(STEPS):
         tot_a = [np.zeros_like(p) for p in inp.adam_params]
@@ -161,7 +176,9 @@ def _reference(world):
         O.muon_step(inp.muon_params, allg[len(inp.adam_params):], bufs,
                     O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=(w.muon_lr * w.muon_wd) / w.muon_lr,
                                 ns_steps=w.ns_steps))
-    return inp, norms, ms, vs, bufs
+        for e, p in zip(emas, inp.adam_params + inp.muon_params):   # train.py:950-953 after the step
+            O.ema_lerp(e, p, 1.0 - EMA_DECAY)
+    return inp, norms, ms, vs, bufs, emas
 
 
 def test_plan_owns_every_matrix_once_and_balances_cost():
@@ -181,12 +198,14 @@ def test_plan_owns_every_matrix_once_and_balances_cost():
 
 @pytest.mark.timeout(300)
 def test_two_cpu_ranks_match_one_process(tmp_path):
+    """Two gloo ranks with the oracle as the compute: params, optimizer state, checkpoint/resume, the weights' EMA
+    and the per-matrix norms all equal the single-process oracle step on the summed grads, bit for bit."""
     world = 2
     mp.spawn(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
     outs = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
     assert np.array_equal(outs[0]["pm"], outs[1]["pm"]) and np.array_equal(outs[0]["pa"], outs[1]["pa"])
     assert np.array_equal(outs[0]["norms"], outs[1]["norms"])
-    inp, norms, ms, vs, bufs = _reference(world)
+    inp, norms, ms, vs, bufs, emas = _reference(world)
     assert np.allclose(outs[0]["norms"], norms, rtol=1e-6, atol=0)
     w = small_workload()
     for i, (p, s) in enumerate(zip(inp.muon_params, w.muon_shapes)):
@@ -196,6 +215,14 @@ def test_two_cpu_ranks_match_one_process(tmp_path):
     for i, (p, s) in enumerate(zip(inp.adam_params, w.adam_shapes)):
         o = int(outs[0]["adam_off"][i])
         assert np.array_equal(outs[0]["pa"][o:o + p.size].reshape(s), p), i
+    # the EMA (train.py:950-953) and the ELR norms (elr.py:85-87) kept by the sharded step, on every rank
+    na = len(w.adam_shapes)
+    for r in range(world):
+        for i in range(na):
+            assert np.array_equal(outs[r][f"ea{i}"], emas[i]), (r, i)
+        for i, p in enumerate(inp.muon_params):
+            assert np.array_equal(outs[r][f"em{i}"], emas[na + i]), (r, i)
+            assert outs[r]["wnorms"][i] == O.frob_norm32(p), (r, i)
     # the sharded checkpoint holds the single-process optimizer state, and resuming from it is bitwise
     for r in range(world):
         assert bool(outs[r]["resumed"])

@@ -1,6 +1,7 @@
 """The sharded step on 2 GPUs (NCCL): both ranks end with identical params, and they match the single-GPU fused step
 run on the summed grads (AdamW to 1e-5; Muon to the Newton-Schulz noise floor, 1e-2 relative Frobenius, since the
 sharded clip sums squares in another order and a one-ulp coefficient change is amplified by the bf16 iteration).
+The step also keeps the weights' EMA and the per-matrix norms, checked against torch's lerp and fp64 norms.
 Skipped with fewer than 2 GPUs."""
 
 import datetime
@@ -14,6 +15,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
+EMA_DECAY = 0.3   # weight 0.7: the lerp's large-weight branch
 
 
 def _port():
@@ -54,6 +56,9 @@ def _rank(rank, world, port, out, peer):
             st.muon_view(pm, i).copy_(torch.from_numpy(p))
         for i, p in enumerate(inp.adam_params):
             st.adam_view(pa, i).copy_(torch.from_numpy(p))
+        st.enable_ema(EMA_DECAY)
+        snaps = {"pm_init": pm.cpu().numpy(), "pa_init": pa.cpu().numpy()}
+        wnorms = torch.zeros(len(w.muon_shapes), device=dev)
         norms = []
         for step in range(3):
             ag, mg = configs.make_grads(w, seed=50 + rank, step=step)
@@ -61,11 +66,13 @@ def _rank(rank, world, port, out, peer):
                 st.muon_view(gm, i).copy_(torch.from_numpy(g))
             for i, g in enumerate(ag):
                 st.adam_view(ga, i).copy_(torch.from_numpy(g))
-            norms.append(st.step(max_norm=0.05, grad_divisor=2.0).item())
+            norms.append(st.step(max_norm=0.05, grad_divisor=2.0, norms=wnorms).item())
+            snaps[f"pm{step}"], snaps[f"pa{step}"] = pm.cpu().numpy(), pa.cpu().numpy()
         torch.cuda.synchronize()
         st.close()
         np.savez(os.path.join(out, f"r{rank}_{int(peer)}.npz"), pm=pm.cpu().numpy(), pa=pa.cpu().numpy(),
-                 norms=np.array(norms), moff=np.array(plan.muon_off), aoff=np.array(plan.adam_off))
+                 norms=np.array(norms), moff=np.array(plan.muon_off), aoff=np.array(plan.adam_off),
+                 em=st.em.cpu().numpy(), ea=st.ea.cpu().numpy(), wnorms=wnorms.cpu().numpy(), **snaps)
     finally:
         dist.destroy_process_group()
 
@@ -84,8 +91,28 @@ def test_two_gpu_sharded_step_matches_single_gpu(tmp_path):
     for r in range(world):   # the two exchanges give the same bits
         q = np.load(tmp_path / f"r{r}_1.npz")
         assert np.array_equal(q["pm"], r0["pm"]) and np.array_equal(q["pa"], r0["pa"])
-    # one GPU, grads summed over the ranks (bf16 sum, as NCCL's bf16 reduction of two values)
+    # the weights' EMA (train.py:950-953) and the ELR norms (elr.py:85-87) kept by the sharded step: the same on every
+    # rank and exchange, the EMA bit for bit torch's lerp of each step's params, the norms those of the final params
     w = _workload()
+    for r in range(world):
+        for peer in (0, 1):
+            q = np.load(tmp_path / f"r{r}_{peer}.npz")
+            for key in ("em", "ea", "wnorms"):
+                assert np.array_equal(q[key], r0[key]), (r, peer, key)
+    em = torch.from_numpy(r0["pm_init"].copy())
+    ea = torch.from_numpy(r0["pa_init"].copy())
+    for step in range(3):
+        torch._foreach_lerp_([em, ea], [torch.from_numpy(r0[f"pm{step}"]), torch.from_numpy(r0[f"pa{step}"])],
+                             1.0 - EMA_DECAY)
+    for i, s in enumerate(w.muon_shapes):
+        o, n = int(r0["moff"][i]), int(np.prod(s))
+        assert np.array_equal(r0["em"][o:o + n], em.numpy()[o:o + n]), i
+        exact = float(np.linalg.norm(r0["pm"][o:o + n].astype(np.float64)))
+        assert abs(float(r0["wnorms"][i]) - exact) <= 1e-6 * exact, i
+    for i, s in enumerate(w.adam_shapes):
+        o, n = int(r0["aoff"][i]), int(np.prod(s))
+        assert np.array_equal(r0["ea"][o:o + n], ea.numpy()[o:o + n]), i
+    # one GPU, grads summed over the ranks (bf16 sum, as NCCL's bf16 reduction of two values)
     dev = torch.device("cuda", 0)
     inp = configs.make_params(w, seed=0)
     mp_ = [torch.from_numpy(p).to(dev) for p in inp.muon_params]

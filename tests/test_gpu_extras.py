@@ -71,3 +71,53 @@ def test_fused_muon_norms_match_the_updated_params(dev):
         assert abs(n - exact) <= 1e-6 * exact, (tuple(it.param.shape), n, exact)
         tn = float(torch.linalg.vector_norm(it.param.cpu()))   # what NormTracker computes (fp32)
         assert abs(n - tn) <= 1e-5 * tn
+
+
+@pytest.mark.parametrize("weight", [0.01, 0.7])
+def test_standalone_ema_lerp_equals_torch(dev, weight):
+    """moteopt_ema_lerp (the EMA pass for params no fused pass writes): full 16K chunks, ragged tails and a tensor
+    starting off the 16-byte grid, bit for bit torch._foreach_lerp_ on the CPU."""
+    from mote_b200.functional import ema_lerp
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+    sizes = [16384 * 3, 16384 * 2 + 77, 5, 1]
+    ps = [torch.randn(n, generator=gen, device=dev) * 0.02 for n in sizes]
+    es = [torch.randn(n, generator=gen, device=dev) * 0.02 for n in sizes]
+    base = torch.randn(16384 + 1, generator=gen, device=dev)
+    ps.append(base[1:])   # 4-byte aligned only: the element path
+    es.append(torch.randn(16384, generator=gen, device=dev)[:16384])
+    ref = [e.cpu() for e in es]
+    torch._foreach_lerp_(ref, [p.cpu() for p in ps], weight)
+    ema_lerp(es, ps, weight)
+    torch.cuda.synchronize()
+    for e, r in zip(es, ref):
+        assert torch.equal(e.cpu(), r)
+
+
+@pytest.mark.parametrize("weight", [0.01, 0.7])
+def test_muon_apply_with_ema_and_norms(dev, weight):
+    """moteopt_muon_apply_ex (the sharded step's apply): the same params as the plain apply, the EMA bit for bit
+    torch's lerp of the updated params, and the norms within 1e-6 of the fp64 norms."""
+    from mote_b200.distributed import cuda_compute
+    from mote_b200.functional import MuonItem
+    comp = cuda_compute()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(12)
+    shapes = [(96, 160), (160, 96), (37, 53), (2, 48, 64), (256, 2048)]
+    p0 = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in shapes]
+    us = [(torch.randn(s, generator=gen, device=dev) * 0.05).to(torch.bfloat16) for s in shapes]
+    e0 = [p + torch.randn(p.shape, generator=gen, device=dev) * 1e-3 for p in p0]
+    pa = [p.clone() for p in p0]
+    pb = [p.clone() for p in p0]
+    eb = [e.clone() for e in e0]
+    comp.apply([MuonItem(p, None, None, 0.02, 0.002) for p in pa], us)
+    norms = torch.full((len(shapes),), -1.0, device=dev)
+    comp.apply([MuonItem(p, None, None, 0.02, 0.002) for p in pb], us, ema=eb, ema_weight=weight, norms=norms)
+    torch.cuda.synchronize()
+    for a, b, e, e_old, n in zip(pa, pb, eb, e0, norms.cpu().tolist()):
+        assert torch.equal(a, b)
+        ref = [e_old.cpu()]
+        torch._foreach_lerp_(ref, [b.cpu()], weight)
+        assert torch.equal(e.cpu(), ref[0])
+        exact = float(np.linalg.norm(b.cpu().numpy().astype(np.float64)))
+        assert abs(n - exact) <= 1e-6 * exact

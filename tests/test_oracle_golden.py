@@ -190,3 +190,16 @@ def test_moe_update_bias_matches_reference(name, experts, kind, seed):
         O.moe_update_bias(load, bias, MOE_GAMMA)
         assert np.array_equal(bias.view(np.uint32), ref[f"{name}_bias{step}"].view(np.uint32)), (name, step)
         assert np.array_equal(load.view(np.uint32), ref[f"{name}_load{step}"].view(np.uint32)), (name, step)
+
+
+@pytest.mark.parametrize("weight", [0.001, 0.25, 0.5, 0.9])
+def test_ema_lerp_matches_torch(weight):
+    """train.py:950-953 is torch._foreach_lerp_ (third-party, run here on the CPU): both of its weight branches."""
+    import torch
+    rng = np.random.default_rng(int(weight * 1000))
+    e = rng.standard_normal(4099).astype(np.float32) * np.float32(0.02)
+    p = rng.standard_normal(4099).astype(np.float32) * np.float32(0.02)
+    ref = torch.from_numpy(e.copy())
+    torch._foreach_lerp_([ref], [torch.from_numpy(p)], weight)
+    O.ema_lerp(e, p, weight)
+    assert np.array_equal(e.view(np.uint32), ref.numpy().view(np.uint32))
