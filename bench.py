@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c1")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-adamw-sweep", action="store_true", help="skip the c4 AdamW sweep (1e6..2e9 elements)")
     return ap.parse_args()
 
 
@@ -282,6 +283,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     adam_ms = a0.elapsed_time(a1) / 10
     del fp, fg, fm, fv
 
+    sweep = None if args.no_adamw_sweep else _adamw_sweep(dev, gen, w.betas, load_peaks()[0]["hbm_gbs"], stream)
+
     # the fused extras (EMA of the weights, Muon param norms) against the separate torch passes the reference runs
     # after its step (train.py:950-953 _foreach_lerp_, elr.py:85-87 stacked norms), on the same c1 tensors
     extras = _time_extras(step, muon_items, adam_fixed, w, stream, counter)
@@ -304,6 +307,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if prof.exists():
         traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
     adam_gbs = 28.0 * n_flat / (adam_ms * 1e-3) / 1e9
+    step_roof = step_roofline(ref_flops, w.state_bytes(), 0.0, peaks, ms)
     line = {
         "metric": METRIC, "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
@@ -324,6 +328,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                      "ref_equivalent_tflops": round(ref_flops / (ns_ms * 1e-3) / 1e12, 1),
                      "timed": "library events around the Newton-Schulz launch(es) of each eager step (one persistent "
                               "cooperative launch for all iterations, or one launch per phase for large problems)"},
+        "step_roofline": step_roof,
         "adamw_hbm": {"achieved": round(adam_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                       "frac": round(adam_gbs / peaks["hbm_gbs"], 4), "elems": n_flat, "ms": round(adam_ms, 4)},
         "e2e": {"value": round(e2e_ms, 4), "unit": "ms/step", "h2d_bytes_per_step": int(flat.numel() * 2),
@@ -332,8 +337,65 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         "clocks": clk.summary(),
         "gpu_launches": int(launches),
         "extras": extras,
+        "adamw_sweep": sweep,
     }
     return line
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def step_roofline(flops: float, state_bytes: float, exchange_bytes: float, peaks: dict, ms: float,
+                  link_gbs: float = 770.0) -> dict:
+    """The step-level roofline the target is stated against: the slower of the reference algorithm's GEMM FLOPs at
+    the bf16 peak and the optimizer-state bytes at HBM bandwidth, plus the bytes a GPU receives in the exchange at
+    the NVLink rate (the pool's measured peer copy, 770 GB/s per direction), per GPU. Given for the measured
+    sustained and burst bf16 peaks; `frac` = roofline time / measured step time."""
+    out = {"unit": "ms", "gemm_tflop": round(flops / 1e12, 4), "state_gb": round(state_bytes / 1e9, 4),
+           "exchange_gb": round(exchange_bytes / 1e9, 4)}
+    link_ms = exchange_bytes / (link_gbs * 1e9) * 1e3
+    hbm_ms = state_bytes / (peaks["hbm_gbs"] * 1e9) * 1e3
+    for key, tf in (("sustained", peaks["bf16_tflops_sustained"]), ("burst", peaks["bf16_tflops"])):
+        roof = max(flops / (tf * 1e12) * 1e3, hbm_ms) + link_ms
+        out[key] = {"roofline_ms": round(roof, 4), "frac": round(roof / ms, 4)}
+    return out
+
+
+# ---------------------------------------------------------------------------------------------------------------
+def _adamw_sweep(dev, gen, betas, hbm_gbs, stream) -> dict:
+    """The AdamW-only bandwidth sweep (config c4): flat fp32 params of 1e6 to 2e9 elements, bf16 grads
+    N(0, 1e-3^2), m/v from a 5-step warm-up, each step the global clip (norm pass) plus AdamW, captured as a CUDA
+    graph. Reported per size: ms per step and GB/s at 28 B/elem (grad read by the norm and by the update, p, m, v
+    read and written)."""
+    import torch
+
+    from mote_b200.functional import AdamWItem, CapturedStep
+    sizes = [1_000_000, 10_000_000, 100_000_000, 1_000_000_000, 2_000_000_000]
+    free = torch.cuda.mem_get_info(dev)[0]
+    sizes = [n for n in sizes if 16 * n < free * 0.8]   # p, m, v fp32 + g bf16 = 14 B/elem, with headroom
+    nmax = sizes[-1]
+    p = torch.empty(nmax, device=dev).normal_(0.0, 0.02, generator=gen)
+    g = torch.empty(nmax, device=dev).normal_(0.0, 1e-3, generator=gen).to(torch.bfloat16)
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    rows = []
+    for n in sizes:
+        cs = CapturedStep((), [AdamWItem(p[:n], g[:n], m[:n], v[:n], 3e-4, 0.1, 1)], betas=betas, max_norm=1.0)
+        for _ in range(5):   # the m/v warm-up; the first call runs eagerly, the second captures
+            cs()
+        reps = 20 if n <= 100_000_000 else 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        e0.record(stream)
+        for _ in range(reps):
+            cs()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        gbs = 28.0 * n / (ms * 1e-3) / 1e9
+        rows.append({"elems": n, "ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / hbm_gbs, 4)})
+        del cs
+    del p, g, m, v
+    torch.cuda.empty_cache()
+    return {"unit": "ms/step, GB/s", "bytes_per_elem": 28, "step": "clip_grad_norm_ + AdamW (CUDA graph)",
+            "l2": "sizes above 4.5e6 elements exceed L2; smaller ones are L2-resident between steps", "rows": rows}
 
 
 # ---------------------------------------------------------------------------------------------------------------

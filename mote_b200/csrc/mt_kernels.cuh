@@ -187,9 +187,36 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
   __shared__ float tnorm[kMaxFinalTensors];
   const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
   const int nwarps = static_cast<int>(blockDim.x >> 5);
-  for (int t = warp; t < A.n_tensors; t += nwarps) {
-    const double s = warp_sum_partials(A.partials, A.tensor_chunk_start[t], A.tensor_chunk_start[t + 1], lane);
-    if (lane == 0) tnorm[t] = static_cast<float>(sqrt(s));
+  // three tensors per warp at a time: the first eight partials per lane of all three are loaded before any is summed
+  // (a tensor's sum is the same as warp_sum_partials': lane l adds elements l, l+32, ... in order)
+  for (int t0 = warp; t0 < A.n_tensors; t0 += 3 * nwarps) {
+    float v[3][8];
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+      const int t = t0 + u * nwarps;
+      const int b = t < A.n_tensors ? A.tensor_chunk_start[t] : 0, e = t < A.n_tensors ? A.tensor_chunk_start[t + 1] : 0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[u][k] = b + lane + 32 * k < e ? A.partials[b + lane + 32 * k] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 3; ++u) {
+      const int t = t0 + u * nwarps;
+      if (t >= A.n_tensors) break;
+      const int b = A.tensor_chunk_start[t], e = A.tensor_chunk_start[t + 1];
+      double s = 0.0;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += static_cast<double>(v[u][k]);
+      for (int base = b + lane + 8 * 32; base < e; base += 8 * 32) {   // tensors of more than 256 chunks
+        float w[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) w[k] = base + 32 * k < e ? A.partials[base + 32 * k] : 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += static_cast<double>(w[k]);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) tnorm[t] = static_cast<float>(sqrt(s));
+    }
   }
   __syncthreads();
   if (warp == 0) {

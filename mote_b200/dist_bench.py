@@ -26,7 +26,7 @@ METRIC = "ms/optimizer step (96M set)"
 
 
 def run(args, rank: int, world: int, local_rank: int):
-    from bench import ClockSampler, load_peaks, streamed_e2e   # the driver-facing helpers live in bench.py
+    from bench import ClockSampler, load_peaks, step_roofline, streamed_e2e   # driver-facing helpers live in bench.py
     from . import _lib as L
     from .ops import read_status
 
@@ -136,6 +136,9 @@ def run(args, rank: int, world: int, local_rank: int):
         peaks, src = load_peaks()
         ns_ms = float(allv[slow, 2])
         achieved = float(allv[slow, 4]) / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
+        # per GPU: 1/N of the reference FLOPs and state bytes; received in the exchange: the other ranks' bf16 O
+        o_bytes = 2.0 * w.numel()[0]
+        roof = step_roofline(w.ns_flops() / world, w.state_bytes() / world, o_bytes * (world - 1) / world, peaks, ms)
         line = {
             "metric": METRIC, "value": round(ms, 4), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": False, "scaling": "strong",
@@ -155,6 +158,7 @@ def run(args, rank: int, world: int, local_rank: int):
                          "peak_source": f"{src} (sustained bf16)", "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
                          "rank": slow,
                          "ns_ms_per_step": round(ns_ms, 4)},
+            "step_roofline": roof,
             "e2e": {"value": round(e2e, 4), "unit": "ms/step",
                     "h2d_bytes_per_step": int((st.gm.numel() + st.ga.numel()) * 2), "d2h_bytes_per_step": 4,
                     "how": "host-fed loop per rank: each step's local grads uploaded from pinned memory on a copy "
