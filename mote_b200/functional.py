@@ -264,15 +264,22 @@ class CapturedStep:
     decay, betas, clip, divisor) are the ones given here, fixed at capture (build a new CapturedStep to change
     them). AdamW's step count is a device counter starting at `start_step`. The first call runs the step eagerly
     (it also warms the library up), the second captures it and replays it, every later call replays. Returns the
-    pre-clip grad norm tensor (overwritten by every call)."""
+    pre-clip grad norm tensor (overwritten by every call).
+
+    The trainer's after-step work can ride in the same graph (train.py:948-953, elr.py:85-87): `ema` (one fp32 EMA
+    buffer or None per AdamW item, then per Muon item) with `ema_weight` = 1 - ema_decay, `muon_norms` (fp32, one
+    per Muon item, receives each param's norm) and `moe` (MoE layers, as moe_update_bias takes them)."""
 
     def __init__(self, muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (), *, ns_steps: int = 5,
                  rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
                  max_norm: Optional[float] = None, grad_divisor: Optional[float] = None, start_step: int = 0,
-                 dynamic_lr: bool = False):
+                 dynamic_lr: bool = False, ema: Optional[Sequence[Optional[torch.Tensor]]] = None,
+                 ema_weight: float = 0.0, muon_norms: Optional[torch.Tensor] = None, moe: Optional[Sequence] = None):
         self.dev = _device(muon, adamw)
         self.kw = dict(ns_steps=ns_steps, rms_scale=rms_scale, ns_eps=ns_eps, betas=betas, eps=eps,
-                       max_norm=max_norm, grad_divisor=grad_divisor)
+                       max_norm=max_norm, grad_divisor=grad_divisor, ema=ema, ema_weight=ema_weight,
+                       muon_norms=muon_norms)
+        self.moe = list(moe) if moe else []
         self.muon, self.adamw = list(muon), list(adamw)
         self.device_step = torch.full((), float(start_step), dtype=torch.float32, device=self.dev)
         self.out_norm = torch.zeros((), dtype=torch.float32, device=self.dev)
@@ -298,6 +305,8 @@ class CapturedStep:
     def _run(self):
         optimizer_step(self.muon, self.adamw, out_norm=self.out_norm, device_step=self.device_step,
                        lr_device=self.lr_device, **self.kw)
+        if self.moe:
+            moe_update_bias(self.moe)
 
     @torch.no_grad()
     def __call__(self) -> torch.Tensor:

@@ -121,3 +121,42 @@ def test_muon_apply_with_ema_and_norms(dev, weight):
         assert torch.equal(e.cpu(), ref[0])
         exact = float(np.linalg.norm(b.cpu().numpy().astype(np.float64)))
         assert abs(n - exact) <= 1e-6 * exact
+
+
+def test_captured_step_with_ema_norms_and_moe_equals_eager(dev):
+    """CapturedStep carrying the trainer's after-step work (EMA, per-matrix norms, MoE bias step) in its graph:
+    three replays give the same bits as three eager steps with the same extras."""
+    import types
+
+    from mote_b200.functional import CapturedStep, moe_update_bias, optimizer_step
+
+    def mk(seed):
+        muon, adam = _setup(dev, seed)
+        ema = [it.param.clone() for it in adam + muon]
+        norms = torch.zeros(len(muon), device=dev)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(3)
+        layer = types.SimpleNamespace(router_kind="lossfree", bias_gamma=1e-3,
+                                      _load_acc=torch.zeros(16, device=dev), expert_bias=torch.zeros(16, device=dev))
+        loads = [torch.randint(0, 500, (16,), generator=gen, device=dev).float() for _ in range(3)]
+        return muon, adam, ema, norms, layer, loads
+    ma, aa, ea, na, la, lda = mk(21)
+    mb, ab, eb, nb, lb, ldb = mk(21)
+    for k in range(3):
+        la._load_acc.copy_(lda[k])
+        optimizer_step(ma, aa, ns_steps=2, betas=(0.9, 0.95), max_norm=1.0, ema=ea, ema_weight=0.3, muon_norms=na,
+                       device_step=torch.full((), float(k), device=dev))
+        moe_update_bias([la])
+    cs = CapturedStep(mb, ab, ns_steps=2, betas=(0.9, 0.95), max_norm=1.0, ema=eb, ema_weight=0.3, muon_norms=nb,
+                      moe=[lb])
+    for k in range(3):
+        lb._load_acc.copy_(ldb[k])
+        cs()
+    torch.cuda.synchronize()
+    assert cs.graph is not None
+    for x, y in zip(aa + ma, ab + mb):
+        assert torch.equal(x.param, y.param)
+    for x, y in zip(ea, eb):
+        assert torch.equal(x, y)
+    assert torch.equal(na, nb)
+    assert torch.equal(la.expert_bias, lb.expert_bias) and float(lb._load_acc.abs().sum()) == 0.0

@@ -132,3 +132,21 @@ def test_captured_in_a_cuda_graph(dev):
     assert np.array_equal(_bits(g_bias), _bits(eager_bias))
     assert float(g_load.abs().sum()) == 0.0
     del graph
+
+
+def test_fused_step_runs_the_bias_step_after_the_optimizer(dev):
+    """fused_step(opt, ..., moe=layers) = the optimizer step, then every layer's update_bias (train.py:947-949)."""
+    from mote_b200 import AdamW, fused_step
+    p = torch.nn.Parameter(torch.randn(64, device=dev) * 0.02)
+    p.grad = torch.randn(64, device=dev) * 1e-3
+    opt = AdamW([p], lr=3e-4)
+    loads = [np.array([10.0, 2.0, 2.0, 2.0], np.float32), np.arange(12, dtype=np.float32)]
+    biases = [np.zeros(4, np.float32), np.linspace(-0.01, 0.01, 12).astype(np.float32)]
+    mods = [_module(dev, ld, b) for ld, b in zip(loads, biases)] + [_module(dev, loads[0], biases[0], router="aux")]
+    fused_step(opt, max_norm=1.0, moe=mods)
+    for m, ld, b in zip(mods[:2], loads, biases):
+        ld, b = ld.copy(), b.copy()
+        O.moe_update_bias(ld, b, MOE_GAMMA)
+        assert np.array_equal(_bits(m.expert_bias), b.view(np.uint32))
+        assert np.array_equal(_bits(m._load_acc), ld.view(np.uint32))
+    assert np.array_equal(mods[2]._load_acc.cpu().numpy(), loads[0])   # not lossfree: untouched
