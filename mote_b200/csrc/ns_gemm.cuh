@@ -105,6 +105,12 @@ __device__ __forceinline__ void operand_mn(const Tile& x, int kb, bool& a_mn, bo
   b_mn = x.phase == kUpdate || (x.phase == kPoly && kt < x.j0 / TN);
 }
 
+// A diagonal block of the symmetric products (kGram X X^T, kPoly A A): its two operands are the same rows, read the
+// same way in every k-block (operand_mn gives a_mn == b_mn, from the same tensor maps), and the pair splits them the
+// same way (CTA r holds rows 128r..128r+127 of both). They are loaded once and the MMA reads the A stage as B too,
+// which saves the block's second operand stream (a quarter to a third of the Gram and polynomial operand bytes).
+__device__ __forceinline__ bool on_diagonal(const Tile& x) { return x.phase != kUpdate && x.i0 == x.j0; }
+
 // Persistent mode: the completion counts tile x must see before reading. kGram reads X[src] (written by the previous
 // iteration's kUpdate), kPoly reads A (this iteration's kGram), kUpdate reads B (kPoly) and X[src].
 __device__ __forceinline__ bool wait_inputs(const Launch& L, const Tile& x, const WaitCtx& ctx) {
@@ -140,10 +146,11 @@ __device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t
     const CUtensorMap* bmap = x.phase == kGram ? &G.xk[x.src] : &G.ak;
     const CUtensorMap* bmap_mn = x.phase == kPoly ? &G.amn : &G.xmn[x.src];
     const int ia = x.i0 + HM * static_cast<int>(rank), jb = x.j0 + (TN / 2) * static_cast<int>(rank);
+    const bool diag = on_diagonal(x);   // B = A: the stage holds one operand, which the MMA reads as both
     for (int kb = 0; kb < nk; ++kb) {
       if (!mbar_wait(&empty[stage], phase ^ 1u, ctx)) { ok = false; break; }
       const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-      if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * STAGE_BYTES);
+      if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (diag ? A_BYTES : STAGE_BYTES));
       const int k0 = kb * BK;
       bool a_mn, b_mn;
       operand_mn(x, kb, a_mn, b_mn);
@@ -155,11 +162,13 @@ __device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t
         tma_load_3d_pair(dsta, amap, bar, k0, ia, x.b);
       }
       uint8_t* dstb = sb + stage * B_BYTES;
-      if (b_mn) {   // [k0:k0+64, jb:jb+128] as two 64 x 64 boxes, 128-byte swizzled along j
-        tma_load_3d_pair(dstb, bmap_mn, bar, jb, k0, x.b);
-        tma_load_3d_pair(dstb + BK * 64 * 2, bmap_mn, bar, jb + 64, k0, x.b);
-      } else {
-        tma_load_3d_pair(dstb, bmap, bar, k0, jb, x.b);
+      if (!diag) {
+        if (b_mn) {   // [k0:k0+64, jb:jb+128] as two 64 x 64 boxes, 128-byte swizzled along j
+          tma_load_3d_pair(dstb, bmap_mn, bar, jb, k0, x.b);
+          tma_load_3d_pair(dstb + BK * 64 * 2, bmap_mn, bar, jb + 64, k0, x.b);
+        } else {
+          tma_load_3d_pair(dstb, bmap, bar, k0, jb, x.b);
+        }
       }
       ++issued;
       if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -198,7 +207,7 @@ __device__ __forceinline__ void mma(const Launch& L, uint8_t* sa, uint8_t* sb, u
       if (!mbar_wait(&full[stage], phase, ctx)) { ok = false; break; }
       tc_fence_after();
       const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
-      const uint32_t b0 = smem_u32(sb + stage * B_BYTES);
+      const uint32_t b0 = on_diagonal(x) ? a0 : smem_u32(sb + stage * B_BYTES);
       bool a_mn, b_mn;
       operand_mn(x, kb, a_mn, b_mn);
       const uint32_t idesc = idesc_bf16_f32(TM, TN, a_mn, b_mn);
