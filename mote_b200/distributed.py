@@ -190,15 +190,19 @@ class ShardedStep:
         self.em: Optional[torch.Tensor] = None   # EMA of the Muon and AdamW param regions (every rank, replicated)
         self.ea: Optional[torch.Tensor] = None
 
-    def enable_ema(self, decay: float) -> None:
-        """Keep the weights' EMA of train.py:950-953 (ema = lerp(ema, p, 1 - decay) after every step), starting from
-        the params as they are now (train.py keeps `[p.detach().clone() for p in params]`). Every rank holds the
-        whole EMA: the Muon region's is lerped in the apply pass that writes the params, the AdamW region's in one
-        pass after its all-gather, so each is a pure function of the replicated params and stays identical across
-        ranks. The EMA of param i is `muon_view(step.em, i)` / `adam_view(step.ea, i)`."""
+    def enable_ema(self, decay: float, zero_init: bool = True) -> None:
+        """Keep the weights' EMA of train.py:950-953 (ema = lerp(ema, p, 1 - decay) after every step). It starts at
+        zero, as train.py:716-721 keeps it (a reader divides by 1 - decay^steps, hnet.ema_scale), or from the params
+        as they are now with `zero_init=False` (the average of checkpoints written before that change); a resumed
+        average is copied into `step.em` / `step.ea` after this call. Every rank holds the whole EMA: the Muon
+        region's is lerped in the apply pass that writes the params, the AdamW region's in one pass after its
+        all-gather, so each is a pure function of the replicated params and stays identical across ranks. The EMA of
+        param i is `muon_view(step.em, i)` / `adam_view(step.ea, i)`."""
+        if self.compute.ema is None:
+            raise ValueError("enable_ema: the step's Compute has no `ema` pass")
         self.ema_decay = float(decay)
-        self.em = self.pm.detach().clone()
-        self.ea = self.pa.detach().clone()
+        self.em = torch.zeros_like(self.pm) if zero_init else self.pm.detach().clone()
+        self.ea = torch.zeros_like(self.pa) if zero_init else self.pa.detach().clone()
 
     def enable_peer_updates(self) -> None:
         """Map every rank's update region into this process (CUDA IPC through libmoteopt); collective, eager, once."""
@@ -372,14 +376,16 @@ class ShardedStep:
             updates = [self.muon_view(self.om, i) for i in every]
         _all_gather_inplace(self.pa, plan.a_seg, r, self.group)
         mark("exchange")
-        w = 1.0 - self.ema_decay if self.em is not None else 0.0
+        extras = {}   # passed only when asked for, so a Compute without them keeps working
+        if self.em is not None:
+            extras.update(ema=[self.muon_view(self.em, i) for i in every], ema_weight=1.0 - self.ema_decay)
+        if norms is not None:
+            extras["norms"] = norms
         self.compute.apply([MuonItem(self.muon_view(self.pm, i), None, None, self.muon_lr,
                                      self.muon_lr * self.muon_wd if self.muon_wd else 0.0, self.momentum, self.nesterov)
-                            for i in every], updates,
-                           ema=[self.muon_view(self.em, i) for i in every] if self.em is not None else None,
-                           ema_weight=w, norms=norms)
+                            for i in every], updates, **extras)
         if self.ea is not None:
-            self.compute.ema([self.ea], [self.pa], w)
+            self.compute.ema([self.ea], [self.pa], 1.0 - self.ema_decay)
         mark("apply_all")
         return norm_coef[0]
 

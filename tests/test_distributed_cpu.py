@@ -157,7 +157,7 @@ def _reference(world):
     nd = len(w.adam_decay_shapes)
     ms, vs = [np.zeros_like(p) for p in inp.adam_params], [np.zeros_like(p) for p in inp.adam_params]
     bufs = [None] * len(inp.muon_params)
-    emas = [p.copy() for p in inp.adam_params + inp.muon_params]
+    emas = [np.zeros_like(p) for p in inp.adam_params + inp.muon_params]   # train.py:721 starts the average at 0
     norms = []
     for step in range(STEPS):
         tot_a = [np.zeros_like(p) for p in inp.adam_params]

@@ -99,8 +99,8 @@ def test_two_gpu_sharded_step_matches_single_gpu(tmp_path):
             q = np.load(tmp_path / f"r{r}_{peer}.npz")
             for key in ("em", "ea", "wnorms"):
                 assert np.array_equal(q[key], r0[key]), (r, peer, key)
-    em = torch.from_numpy(r0["pm_init"].copy())
-    ea = torch.from_numpy(r0["pa_init"].copy())
+    em = torch.zeros(r0["pm_init"].shape)   # train.py:721 starts the average at 0
+    ea = torch.zeros(r0["pa_init"].shape)
     for step in range(3):
         torch._foreach_lerp_([em, ea], [torch.from_numpy(r0[f"pm{step}"]), torch.from_numpy(r0[f"pa{step}"])],
                              1.0 - EMA_DECAY)
