@@ -44,6 +44,7 @@ def test_ctypes_structs_match_the_c_layout():
 #define O(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
 int main(void) {
   P(moteopt_muon_param) P(moteopt_muon_config) P(moteopt_adamw_tensor) P(moteopt_adamw_hparams) P(moteopt_grad_config)
+  P(moteopt_moe_bias) O(moteopt_moe_bias, expert_bias) O(moteopt_moe_bias, n_experts) O(moteopt_moe_bias, gamma)
   O(moteopt_muon_param, lr) O(moteopt_muon_param, nesterov) O(moteopt_muon_param, grad_dtype)
   O(moteopt_adamw_tensor, numel) O(moteopt_adamw_tensor, step) O(moteopt_adamw_tensor, grad_dtype)
   O(moteopt_muon_config, rms_scale) O(moteopt_grad_config, max_norm) O(moteopt_adamw_hparams, device_step)
@@ -59,7 +60,7 @@ int main(void) {
                                                                 check=True).stdout.splitlines())
     m = {"moteopt_muon_param": _lib.MuonParam, "moteopt_muon_config": _lib.MuonConfig,
          "moteopt_adamw_tensor": _lib.AdamWTensor, "moteopt_adamw_hparams": _lib.AdamWHparams,
-         "moteopt_grad_config": _lib.GradConfig}
+         "moteopt_grad_config": _lib.GradConfig, "moteopt_moe_bias": _lib.MoeBias}
     for k, v in got.items():
         if "." in k:
             t, f = k.split(".")
@@ -93,3 +94,14 @@ def test_entry_points_reject_bad_arguments_without_touching_a_device():
     assert rc == -1 and b"null" in lib.moteopt_last_error()
     rc = lib.moteopt_profile_ns_events(C.c_void_p(1), None)
     assert rc == -1
+    # the after-step entry points check their lists before any device call
+    assert lib.moteopt_moe_update_bias(None, -1, None) == -1
+    assert lib.moteopt_moe_update_bias(None, 2, None) == -1 and b"MoE" in lib.moteopt_last_error()
+    bad = (_lib.MoeBias * 1)(_lib.MoeBias(None, None, 4, 1e-3))
+    assert lib.moteopt_moe_update_bias(bad, 1, None) == -1 and b"null" in lib.moteopt_last_error()
+    assert lib.moteopt_ema_lerp(None, None, None, 1, 0.1, None) == -1
+    numel = (C.c_int64 * 1)(-5)
+    ptrs = (C.c_void_p * 1)(1)
+    assert lib.moteopt_ema_lerp(ptrs, ptrs, numel, 1, 0.1, None) == -1 and b"bad tensor" in lib.moteopt_last_error()
+    assert lib.moteopt_muon_apply_ex(None, 1, None, None, None, 0.0, None, None, 0, None) == -1
+    assert lib.moteopt_muon_apply_workspace_size(None, 3) == 0
