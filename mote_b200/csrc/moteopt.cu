@@ -532,10 +532,18 @@ int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float di
       A.seg[i] = segs[s0 + i];
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(A.seg[i].numel, kChunk));
     }
-    ns_normalize_flat_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    if (A.has_div) ns_normalize_flat_kernel<true><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    else ns_normalize_flat_kernel<false><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_normalize_flat_kernel");
   }
   return MOTEOPT_OK;
+}
+
+// Whether any matrix of a tiled copy-out / apply launch lerps an EMA (picks the kernel instantiation).
+bool out_has_ema(const OutArgs& A, size_t cnt) {
+  for (size_t i = 0; i < cnt; ++i)
+    if (A.mat[i].ema != nullptr) return true;
+  return false;
 }
 
 int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cudaStream_t st, double ema_weight = 0.0) {
@@ -665,7 +673,8 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
         M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
         max_tiles = std::max(max_tiles, M.tiles);
       }
-      ns_normalize_kernel<<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+      if (A.has_div) ns_normalize_kernel<true><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+      else ns_normalize_kernel<false><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
       MO_LAUNCHED("ns_normalize_kernel");
     }
   }
@@ -878,7 +887,8 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       A.mat[i] = all[s0 + i];
       max_tiles = std::max(max_tiles, A.mat[i].tiles);
     }
-    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    if (out_has_ema(A, cnt)) ns_out_kernel<true><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    else ns_out_kernel<false><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_out_kernel");
   }
   if (norms != nullptr) {   // ||p_new||_F per param: fixed-order fp64 sum of its partials (eps 0)
@@ -946,7 +956,8 @@ int run_copy_out(const moteopt_muon_param* P, const Layout& L, char* ws, int src
       A.mat[i] = all[s0 + i];
       max_tiles = std::max(max_tiles, A.mat[i].tiles);
     }
-    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    if (out_has_ema(A, cnt)) ns_out_kernel<true><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
+    else ns_out_kernel<false><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_out_kernel");
   }
   return MOTEOPT_OK;
@@ -1563,7 +1574,8 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
       M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
       max_tiles = std::max(max_tiles, M.tiles);
     }
-    ns_normalize_kernel<<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+    if (A.has_div) ns_normalize_kernel<true><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
+    else ns_normalize_kernel<false><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_normalize_kernel");
   }
   int final_src = 0;
@@ -1598,7 +1610,8 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
       O.mat[i] = all[s0 + i];
       max_tiles = std::max(max_tiles, O.mat[i].tiles);
     }
-    ns_out_kernel<<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(O);
+    if (out_has_ema(O, cnt)) ns_out_kernel<true><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(O);
+    else ns_out_kernel<false><<<dim3(max_tiles, static_cast<unsigned>(cnt)), kMtThreads, 0, st>>>(O);
     MO_LAUNCHED("ns_out_kernel");
   }
   return MOTEOPT_OK;
