@@ -27,7 +27,9 @@ import torch
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
 sys.path.insert(0, str(ROOT))
-REF = os.environ.get("MOTE_REFERENCE", "/root/reference")
+REF = os.environ.get("MOTE_REFERENCE")
+if not REF:
+    raise SystemExit("set MOTE_REFERENCE to a checkout of noahsabaj/mote (the generator runs the reference itself)")
 sys.path.insert(0, REF)
 
 from mote.train.muon import Muon, newton_schulz  # noqa: E402  (the reference)
