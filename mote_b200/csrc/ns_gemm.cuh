@@ -112,17 +112,17 @@ __device__ __forceinline__ void operand_mn(const Tile& x, int kb, bool& a_mn, bo
 __device__ __forceinline__ bool on_diagonal(const Tile& x) { return x.phase != kUpdate && x.i0 == x.j0; }
 
 // Persistent mode: the completion counts tile x must see before reading. kGram reads X[src] (written by the previous
-// iteration's kUpdate), kPoly reads A (this iteration's kGram), kUpdate reads B (kPoly) and X[src].
+// iteration's kUpdate), kPoly reads A (this iteration's kGram), kUpdate reads B (kPoly) and X[src]. kUpdate checks
+// only kPoly: this iteration's kPoly tiles of the matrix started after its kGram tiles completed, and those after the
+// previous kUpdate completed, so a complete kPoly count already orders X[src] (and the end of every read of X[src^1],
+// which kUpdate overwrites) before the tile, through the same release/acquire chain that orders the overwrites.
 __device__ __forceinline__ bool wait_inputs(const Launch& L, const Tile& x, const WaitCtx& ctx) {
   const int mat = L.g[x.gi].first + x.b;
   const int* done = L.done + mat * 3;
-  if (x.phase != kGram &&
-      !wait_counter(done + x.phase - 1, (x.it + 1) * tiles_per_matrix(L, x.gi, x.phase - 1) * kArrivalsPerTile, ctx))
-    return false;
-  if (x.phase != kPoly && x.it > 0 &&
-      !wait_counter(done + kUpdate, x.it * tiles_per_matrix(L, x.gi, kUpdate) * kArrivalsPerTile, ctx))
-    return false;
-  return true;
+  if (x.phase != kGram)
+    return wait_counter(done + x.phase - 1, (x.it + 1) * tiles_per_matrix(L, x.gi, x.phase - 1) * kArrivalsPerTile,
+                        ctx);
+  return x.it == 0 || wait_counter(done + kUpdate, x.it * tiles_per_matrix(L, x.gi, kUpdate) * kArrivalsPerTile, ctx);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
