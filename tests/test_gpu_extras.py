@@ -160,3 +160,17 @@ def test_captured_step_with_ema_norms_and_moe_equals_eager(dev):
         assert torch.equal(x, y)
     assert torch.equal(na, nb)
     assert torch.equal(la.expert_bias, lb.expert_bias) and float(lb._load_acc.abs().sum()) == 0.0
+
+
+def test_standalone_ema_lerp_over_many_tensors(dev):
+    """More tensors than one argument block holds (600 > 512): the lerp is split over launches, same bits as torch."""
+    from mote_b200.functional import ema_lerp
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    ps = [torch.randn(int(n), generator=gen, device=dev) for n in torch.randint(1, 3000, (600,), generator=gen, device=dev).tolist()]
+    es = [torch.randn(p.shape, generator=gen, device=dev) for p in ps]
+    ref = [e.cpu() for e in es]
+    torch._foreach_lerp_(ref, [p.cpu() for p in ps], 0.02)
+    ema_lerp(es, ps, 0.02)
+    torch.cuda.synchronize()
+    assert all(torch.equal(e.cpu(), r) for e, r in zip(es, ref))

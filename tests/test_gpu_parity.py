@@ -425,3 +425,29 @@ def test_captured_step_replays_equal_eager_steps(dev):
     for a, b in zip(mp + ap + mb + am + av, mp2 + ap2 + mb2 + am2 + av2):
         assert torch.equal(a, b)
     assert cs.device_step.item() == 4.0
+
+
+def test_adamw_large_launch_equals_small_launches(dev):
+    """AdamW picks its work unit per launch: 16K-element units when the launch fills the GPU in them, 2K otherwise.
+    A 10.5M-element tensor in one call (16K units) and the same tensor in four calls of 2.6M (2K units) must give
+    the same bits, with a grad divisor and the fused EMA, over three steps."""
+    from mote_b200.functional import AdamWItem, optimizer_step
+    n, parts = 10_500_000, 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31)
+    p0 = torch.randn(n, generator=gen, device=dev) * 0.02
+    ga = [(torch.randn(n, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for _ in range(3)]
+    big = [p0.clone(), torch.zeros(n, device=dev), torch.zeros(n, device=dev), p0.clone()]
+    small = [t.clone() for t in big]
+    cut = [k * (n // parts) for k in range(parts)] + [n]
+    for step in range(3):
+        p, m, v, e = big
+        optimizer_step((), [AdamWItem(p, ga[step], m, v, 3e-4, 0.1, step + 1)], betas=(0.9, 0.95),
+                       grad_divisor=3.0, ema=[e], ema_weight=0.1)
+        for a, b in zip(cut, cut[1:]):
+            p, m, v, e = (t[a:b] for t in small)
+            optimizer_step((), [AdamWItem(p, ga[step][a:b], m, v, 3e-4, 0.1, step + 1)], betas=(0.9, 0.95),
+                           grad_divisor=3.0, ema=[e], ema_weight=0.1)
+    torch.cuda.synchronize()
+    for x, y in zip(big, small):
+        assert torch.equal(x, y)
