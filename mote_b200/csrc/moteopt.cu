@@ -612,7 +612,8 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
         A.chunk_start[i] = L.mat_chunk_start[s0 + i] - A.chunk_base;
       }
       A.chunk_start[cnt] = L.mat_chunk_start[s0 + cnt] - A.chunk_base;
-      muon_momentum_kernel<<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+      if (A.has_div) muon_momentum_kernel<true><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+      else muon_momentum_kernel<false><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
       MO_LAUNCHED("muon_momentum_kernel");
     }
   }

@@ -430,10 +430,13 @@ __device__ __forceinline__ float mom_elem(float g, float& buf, float mom, int ne
 
 // A full chunk with 16-byte aligned buf (and 8/16-byte aligned g) is processed in two halves of 32 elements per
 // thread, with every load of a half issued before the first use (192 B in flight per thread for bf16 grads).
-__global__ void __launch_bounds__(kMtThreads) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
+// kDiv: whether the grads are divided first. Without the division (and its slow path) the kernel fits four blocks
+// per SM and runs at the copy bandwidth (c1: 165 -> 144 us); the dividing instantiation is compute-heavier (205 us).
+template <bool kDiv>
+__global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
   __shared__ float red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
-  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{kDiv ? A.has_div : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const MomSeg& S = A.seg[s];
