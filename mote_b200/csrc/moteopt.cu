@@ -364,7 +364,8 @@ int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chu
     }
     A.chunk_start[n] = chunk_start[s0 + n] - A.chunk_base;
     if (A.chunk_start[n] == 0) continue;
-    sumsq_kernel<<<grid_for(A.chunk_start[n], sms), kMtThreads, 0, st>>>(A);
+    if (A.has_div) sumsq_kernel<true><<<grid_for(A.chunk_start[n], sms), kMtThreads, 0, st>>>(A);
+    else sumsq_kernel<false><<<grid_for(A.chunk_start[n], sms), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("sumsq_kernel");
   }
   return MOTEOPT_OK;
@@ -1488,7 +1489,8 @@ int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, co
     }
     S.chunk_start[cnt] = F.tensor_chunk_start[s0 + cnt] - S.chunk_base;
     if (S.chunk_start[cnt] == 0) continue;
-    sumsq_kernel<<<grid_for(S.chunk_start[cnt], sms), kMtThreads, 0, st>>>(S);
+    if (S.has_div) sumsq_kernel<true><<<grid_for(S.chunk_start[cnt], sms), kMtThreads, 0, st>>>(S);
+    else sumsq_kernel<false><<<grid_for(S.chunk_start[cnt], sms), kMtThreads, 0, st>>>(S);
     MO_LAUNCHED("sumsq_kernel");
   }
   norm_finalize_kernel<<<1, 1024, 0, st>>>(F);

@@ -156,10 +156,11 @@ __device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
   }
 }
 
-__global__ void __launch_bounds__(kMtThreads) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
+// One instantiation per divisor mode (each gets its own register allocation): 48 registers, five blocks per SM.
+template <bool kDiv>
+__global__ void __launch_bounds__(kMtThreads, 5) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
   __shared__ float red[kMtThreads / 32];
-  if (A.has_div) sumsq_chunks<true>(A, red);
-  else sumsq_chunks<false>(A, red);
+  sumsq_chunks<kDiv>(A, red);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
