@@ -230,3 +230,60 @@ def test_two_cpu_ranks_match_one_process(tmp_path):
             assert np.array_equal(outs[r][f"m{i}"], ms[i]) and np.array_equal(outs[r][f"v{i}"], vs[i]), i
         for i in range(len(w.muon_shapes)):
             assert np.array_equal(outs[r][f"b{i}"], bufs[i]), i
+
+
+def _rank_fault(rank, world, port, out_dir, mode):
+    """One step on both ranks, then rank 1 either dies before the second step ("dead") or enters it late ("late")."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=15))
+    w = small_workload()
+    plan = make_plan(w.muon_shapes, w.adam_shapes, world, ns_steps=w.ns_steps)
+    inp = configs.make_params(w, seed=0)
+    pm, pa = torch.zeros(plan.muon_len), torch.zeros(plan.adam_len)
+    gm, ga = torch.zeros(plan.muon_len), torch.zeros(plan.adam_len)
+    nd = len(w.adam_decay_shapes)
+    st = ShardedStep(plan, rank, pm, pa, gm, ga, oracle_compute(w), muon_lr=w.muon_lr, muon_wd=w.muon_wd,
+                     adam_lr=w.adam_lr, adam_wd=[w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))])
+    for i, p in enumerate(inp.muon_params):
+        st.muon_view(pm, i).copy_(torch.from_numpy(p))
+    for i, p in enumerate(inp.adam_params):
+        st.adam_view(pa, i).copy_(torch.from_numpy(p))
+    for step in range(2):
+        ag, mg = configs.make_grads(w, seed=100 + rank, step=step)
+        for i, g in enumerate(mg):
+            st.muon_view(gm, i).copy_(torch.from_numpy(g))
+        for i, g in enumerate(ag):
+            st.adam_view(ga, i).copy_(torch.from_numpy(g))
+        if step == 1 and rank == 1:
+            if mode == "dead":
+                os._exit(0)   # leaves between steps, with nothing in flight
+            time.sleep(2.0)
+        t0 = time.time()
+        try:
+            st.step(max_norm=CLIP, grad_divisor=DIV)
+        except Exception as exc:  # noqa: BLE001  (the surviving rank records how its collective ended)
+            with open(os.path.join(out_dir, f"fault{rank}.txt"), "w") as f:
+                f.write(f"error {type(exc).__name__} {time.time() - t0:.1f}")
+            os._exit(0)   # the group is broken: no destroy_process_group
+    np.save(os.path.join(out_dir, f"late{rank}.npy"), pm.numpy())
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(180)
+def test_a_dead_rank_ends_the_step_with_an_error_not_a_hang(tmp_path):
+    """Failure detection on the host: a rank that leaves between steps makes the survivor's next
+    collective fail within the process group's timeout (15 s here) instead of waiting forever."""
+    mp.spawn(_rank_fault, args=(2, _free_port(), str(tmp_path), "dead"), nprocs=2, join=True)
+    msg = (tmp_path / "fault0.txt").read_text().split()
+    assert msg[0] == "error" and float(msg[2]) < 60.0, msg
+
+
+@pytest.mark.timeout(180)
+def test_a_late_rank_only_delays_the_step(tmp_path):
+    """A rank that enters the step 2 s late: the collectives wait for it and both ranks end with the same params."""
+    mp.spawn(_rank_fault, args=(2, _free_port(), str(tmp_path), "late"), nprocs=2, join=True)
+    a, b = np.load(tmp_path / "late0.npy"), np.load(tmp_path / "late1.npy")
+    assert np.array_equal(a, b)
