@@ -3,8 +3,10 @@
  * Every entry point takes plain device pointers, element counts, host-side hyperparameters and the CUDA stream to
  * enqueue on; none allocates device memory, none synchronises the host. Scratch memory is the caller's
  * `workspace` (query its size with the matching *_workspace_size function; it must stay allocated until the work
- * enqueued on `stream` has finished; 256-byte aligned). The first bytes of the workspace hold a status word and the last grad norm,
- * which moteopt_read_status() reads back.
+ * enqueued on `stream` has finished; 256-byte aligned). The first 256 bytes of the workspace are a header: the status
+ * word and the grad norm and clip coefficient of the last call that uses them (a step, a clip or a Newton-Schulz call
+ * resets the header when it starts), which moteopt_read_status() reads back. Entry points that use a workspace only
+ * for partial sums (moteopt_muon_apply_ex) leave the header alone.
  *
  * Every function returns MOTEOPT_OK (0) or a negative error code; moteopt_last_error() describes the last failure
  * of the calling thread. References below are to the reference project noahsabaj/mote, path:line.
@@ -123,6 +125,13 @@ MOTEOPT_API const char* moteopt_last_error(void);
  * first Newton-Schulz launch and the second after its last, on the step's stream. */
 MOTEOPT_API unsigned long long moteopt_launch_count(void);
 MOTEOPT_API int moteopt_profile_ns_events(void* start_event, void* end_event);
+
+/* Index checks (no counterpart in the reference; the stand-in for a memory checker, which this library's GPUs do not
+ * run). Built with -DMOTE_OPT_CHECKS (libmoteopt_checked.so), every kernel checks the tensor, chunk, tile and TMEM
+ * indices it derives and counts the failures on the device; the count of the current device is returned (and
+ * cleared with `clear`), after synchronising the device. A release build compiles no check and returns 0; -1 means
+ * a CUDA error (moteopt_last_error). */
+MOTEOPT_API long long moteopt_check_count(int clear);
 
 /* Newton-Schulz launch mode (no counterpart in the reference). 1: all iterations of a step run as one cooperative
  * launch whose tiles wait on per-matrix completion counters; 0: one launch per phase and iteration; -1 (the

@@ -20,7 +20,7 @@ STATUS_NONFINITE = 4
 
 # every exported symbol of include/moteopt.h
 EXPORTS = (
-    "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count",
+    "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count", "moteopt_check_count",
     "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_ex",
     "moteopt_optimizer_step_with_coef",
@@ -84,6 +84,7 @@ def _load() -> C.CDLL:
         "moteopt_version": (i32, []),
         "moteopt_last_error": (C.c_char_p, []),
         "moteopt_launch_count": (C.c_ulonglong, []),
+        "moteopt_check_count": (C.c_longlong, [i32]),
         "moteopt_profile_ns_events": (i32, [vp, vp]),
         "moteopt_ns_set_persistent": (i32, [i32]),
         "moteopt_read_status": (i32, [vp, C.POINTER(C.c_int), f32p, i32, vp]),

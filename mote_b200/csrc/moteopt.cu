@@ -1045,6 +1045,26 @@ int moteopt_version(void) { return 1; }
 
 unsigned long long moteopt_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
+long long moteopt_check_count(int clear) {
+#ifdef MOTE_OPT_CHECKS
+  unsigned long long v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_check_fails, sizeof(v));
+  if (e == cudaSuccess && clear) {
+    const unsigned long long z = 0;
+    e = cudaMemcpyToSymbol(g_check_fails, &z, sizeof(z));
+  }
+  if (e != cudaSuccess) {
+    fail(MOTEOPT_ERR_CUDA, std::string("moteopt_check_count: ") + cudaGetErrorString(e));
+    return -1;
+  }
+  return static_cast<long long>(v);
+#else
+  (void)clear;
+  return 0;
+#endif
+}
+
 int moteopt_profile_ns_events(void* start_event, void* end_event) {
   if ((start_event == nullptr) != (end_event == nullptr))
     return fail(MOTEOPT_ERR_INVALID, "give both events or neither");
@@ -1165,7 +1185,7 @@ size_t moteopt_muon_apply_workspace_size(const moteopt_muon_param* muon, int n) 
   if (n < 0 || (n > 0 && muon == nullptr)) return 0;
   int64_t chunks = 0;
   for (int i = 0; i < n; ++i) chunks += cdiv(std::max<int64_t>(muon[i].batch * muon[i].rows * muon[i].cols, 0), kChunk);
-  return static_cast<size_t>(std::max<int64_t>(chunks, 1)) * sizeof(float);
+  return sizeof(Header) + static_cast<size_t>(std::max<int64_t>(chunks, 1)) * sizeof(float);   // header, partials
 }
 
 int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
@@ -1181,7 +1201,7 @@ int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_m
   float* partials = nullptr;
   if (norms != nullptr && n > 0) {
     MO_TRY(check_ws(workspace, workspace_bytes, moteopt_muon_apply_workspace_size(muon, n)));
-    partials = static_cast<float*>(workspace);
+    partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + sizeof(Header));   // the header stays intact
   }
   std::vector<FlatOutSeg> segs;
   std::vector<int> start(1, 0);

@@ -117,6 +117,7 @@ __device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
     const SumsqSeg& S = A.seg[s];
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     float acc = 0.f;
     if (end - begin == kChunk && aligned16(S.g)) {
       if (S.dtype == kBF16) {   // 2048 16-byte vectors: 8 per thread
@@ -204,6 +205,7 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
       const int t = t0 + u * nwarps;
       if (t >= A.n_tensors) break;
       const int b = A.tensor_chunk_start[t], e = A.tensor_chunk_start[t + 1];
+      MO_CHECK(b <= e);
       double s = 0.0;
 #pragma unroll
       for (int k = 0; k < 8; ++k) s += static_cast<double>(v[u][k]);
@@ -352,6 +354,7 @@ __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant
     constexpr int kUnit = kSmall ? kAdamChunk : kChunk;
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kUnit;
     const int64_t end = min(begin + kUnit, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     const bool vec = aligned16(S.p) && aligned16(S.m) && aligned16(S.v) && g_vec_ok(S.g, S.dtype) &&
                      (S.ema == nullptr || aligned16(S.ema));
     int64_t i0 = begin;
@@ -443,6 +446,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel
     const MomSeg& S = A.seg[s];
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     float acc = 0.f;
     int64_t i0 = begin;
     if (aligned16(S.buf) && g_vec_ok(S.g, S.dtype)) {
@@ -512,6 +516,7 @@ __global__ void __launch_bounds__(256) mat_denom_kernel(const __grid_constant__ 
   const int mat = blockIdx.x * 8 + static_cast<int>(threadIdx.x >> 5);
   if (mat >= A.n) return;
   const int lane = threadIdx.x & 31;
+  MO_CHECK(A.chunk_start[mat] <= A.chunk_start[mat + 1]);
   const double s = warp_sum_partials(A.partials, A.chunk_start[mat], A.chunk_start[mat + 1], lane);
   if (lane == 0) A.den[A.base + mat] = __fadd_rn(static_cast<float>(sqrt(s)), A.eps);
 }
@@ -535,6 +540,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) ns_normalize_flat_ke
     const SharedDivisor den = shared_divisor(A.den[S.den_index]);
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     const bool has_buf = S.buf != nullptr;
     __nv_bfloat16* x = reinterpret_cast<__nv_bfloat16*>(S.x);
     int64_t i0 = begin;
@@ -577,6 +583,7 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
     float sq = 0.f;   // sum of the updated param's squares (norm tracking), fixed per-thread order
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(S.x);
     int64_t i0 = begin;
     if (A.apply) {
@@ -664,6 +671,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 5) ns_normalize_kernel(
   if (static_cast<int>(blockIdx.x) >= M.tiles) return;
   const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
   const int i0 = ti * kNormTile, j0 = tj * kNormTile;   // destination tile origin (X rows i, cols j)
+  MO_CHECK(i0 < M.m_pad && j0 < M.n_pad);
   const SharedDivisor den = shared_divisor(A.den[M.den_index]);
   const GradXform X{kDiv ? 1 : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;   // 16 x 16 threads, 4 columns each
@@ -765,6 +773,7 @@ __global__ void __launch_bounds__(kMtThreads, kEma ? 1 : 5) ns_out_kernel(const 
   if (static_cast<int>(blockIdx.x) >= M.tiles) return;
   const int ti = blockIdx.x / M.tiles_x, tj = blockIdx.x % M.tiles_x;
   const int r0 = ti * kNormTile, c0 = tj * kNormTile;      // output tile origin (rows r, cols c of R x C)
+  MO_CHECK(r0 < M.rows && c0 < M.cols);
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(M.x);
   const int xr0 = M.transposed ? c0 : r0, xc0 = M.transposed ? r0 : c0;
@@ -868,6 +877,7 @@ __global__ void __launch_bounds__(kMtThreads) clip_scale_kernel(const __grid_con
     const SumsqSeg& S = A.seg[s];
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) {
       if (S.dtype == kBF16) {
         __nv_bfloat16* g = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(S.g));
@@ -891,6 +901,7 @@ __global__ void __launch_bounds__(kMtThreads) ema_lerp_kernel(const __grid_const
     const LerpSeg& S = A.seg[s];
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
     int64_t i0 = begin;
     if (end - begin == kChunk && aligned16(S.ema) && aligned16(S.p)) {
       float4* ep = reinterpret_cast<float4*>(S.ema + begin);
@@ -933,6 +944,7 @@ __global__ void __launch_bounds__(kMtThreads) moe_bias_kernel(const __grid_const
   __shared__ int sh_skip, sh_count;
   const MoeLayer& L = A.layer[blockIdx.x];
   const int E = L.experts;
+  MO_CHECK(static_cast<int>(blockIdx.x) < A.n && E > 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   double s = 0.0;
   for (int i = threadIdx.x; i < E; i += kMtThreads) s += static_cast<double>(L.load[i]);

@@ -7,6 +7,19 @@
 
 namespace moteopt {
 
+// Index checks (-DMOTE_OPT_CHECKS builds only): a failed MO_CHECK counts in g_check_fails and the kernel goes on.
+#ifdef MOTE_OPT_CHECKS
+__device__ unsigned long long g_check_fails;
+#define MO_CHECK(cond)                                     \
+  do {                                                     \
+    if (!(cond)) atomicAdd(&::moteopt::g_check_fails, 1ull); \
+  } while (0)
+#else
+#define MO_CHECK(cond) \
+  do {                 \
+  } while (0)
+#endif
+
 constexpr int kChunk = 16384;          // elements per work unit of the multi-tensor kernels
 constexpr int kMtThreads = 256;
 // AdamW's small work unit: two 16-byte vectors per thread, so that a few hundred thousand AdamW elements (a

@@ -34,6 +34,7 @@
 //   tempty[a] leader only: one arrival per epilogue warp of both CTAs (the peer's arrive remotely).
 #pragma once
 
+#include "mt_types.h"
 #include "ns_types.h"
 #include "ptx.cuh"
 
@@ -141,6 +142,8 @@ __device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t
       fence_proxy_async_global();   // the TMA loads below observe the data the counters released
     }
     const int nk = (phase_k(x.phase, G) + BK - 1) / BK;
+    MO_CHECK(x.gi >= 0 && x.gi < L.n_groups && x.b >= 0 && x.b < G.count && x.i0 < G.m &&
+             x.j0 < (x.phase == kUpdate ? G.n : G.m) && (x.phase == kUpdate || x.i0 <= x.j0) && nk > 0);
     const CUtensorMap* amap = x.phase == kGram ? &G.xk[x.src] : (x.phase == kPoly ? &G.ak : &G.bk);
     const CUtensorMap* amap_mn = x.phase == kPoly ? &G.amn : &G.bmn;
     const CUtensorMap* bmap = x.phase == kGram ? &G.xk[x.src] : &G.ak;
@@ -295,6 +298,7 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
     for (int c = 0; c < nch; ++c) {
       const int bi = c & 1;
       uint32_t r[32];
+      MO_CHECK(acc * TN + half * (kChunks * EPI_TILE) + (c + 1) * EPI_TILE <= static_cast<int>(kTmemCols));
       tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
                     static_cast<uint32_t>(acc * TN + half * (kChunks * EPI_TILE) + c * EPI_TILE), r);
       tmem_ld_wait(r);

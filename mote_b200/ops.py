@@ -30,13 +30,23 @@ def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+HEADER_BYTES = 256   # the workspace header of include/moteopt.h
+
+
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     """A grow-only scratch buffer per device (allocated through PyTorch's caching allocator, 512-byte aligned).
-    Calls on one device share it, so they must be issued on one stream at a time."""
+    Calls on one device share it, so they must be issued on one stream at a time. Its first 256 bytes are the
+    library's header (the last call's status word, norm and clip coefficient): zeroed when first allocated and
+    copied when the buffer grows, so read_status still returns the last call's header after a growth."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _workspaces.get(idx)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.empty(max(int(nbytes), 1024), dtype=torch.uint8, device=torch.device("cuda", idx))
+        new = torch.empty(max(int(nbytes), 1024), dtype=torch.uint8, device=torch.device("cuda", idx))
+        if ws is None:
+            new[:HEADER_BYTES].zero_()
+        else:
+            new[:HEADER_BYTES].copy_(ws[:HEADER_BYTES])
+        ws = new
         _workspaces[idx] = ws
     return ws
 
