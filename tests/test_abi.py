@@ -33,6 +33,20 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(_lib.lib, name)
 
 
+def test_checked_library_exports_the_same_symbols_and_release_counts_nothing():
+    """libmoteopt_checked.so (the -DMOTE_OPT_CHECKS build) has the release library's ABI; the release library's
+    moteopt_check_count compiles no check and returns 0 without touching a device."""
+    from mote_b200 import _lib
+    checked = ROOT / "mote_b200" / "libmoteopt_checked.so"
+    if not checked.exists():
+        pytest.skip("libmoteopt_checked.so not built (python -m mote_b200.build --checked)")
+    out = subprocess.run(["nm", "-D", "--defined-only", str(checked)], capture_output=True, text=True,
+                         check=True).stdout
+    syms = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert set(declared()) <= syms
+    assert _lib.lib.moteopt_check_count(0) == 0
+
+
 def test_ctypes_structs_match_the_c_layout():
     import ctypes as C
     from mote_b200 import _lib
