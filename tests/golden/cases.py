@@ -74,3 +74,83 @@ def moe_loads(experts: int, kind: str, seed: int, step: int) -> np.ndarray:
 def moe_bias0(experts: int, seed: int) -> np.ndarray:
     """The expert bias a case starts from."""
     return np.random.default_rng(seed).uniform(-0.05, 0.05, size=experts).astype(np.float32)
+
+
+# optimizer construction (mote/train/train.py:76-105 build_optimizer, mote/train/muon.py:103-126 split_muon_params,
+# train.py:177-179 set_lr): a model with one parameter of every kind the split distinguishes, in three stages
+GROUP_LR = 3e-3
+GROUP_WD = 0.1
+GROUP_MULTS = [2.0, 1.0, 0.5]
+GROUP_KINDS = ("adamw", "muon", "muonsw")
+GROUP_SET_LR = 1.5e-3
+
+
+def mixer_parts(mod) -> None:
+    """The two projections of a Mamba-3 mixer that the split looks at: `in_proj` goes to AdamW, `out_proj` to Muon.
+    Both the test's stand-in class and the generator's subclass of the reference's Mamba3Mixer call this."""
+    import torch
+    mod.in_proj = torch.nn.Linear(16, 40, bias=False)
+    mod.out_proj = torch.nn.Linear(20, 16, bias=False)
+
+
+def group_model(mixer_cls):
+    """Embeddings with a tied head, a Mamba-3 mixer, a 3-D MoE expert stack (`_muon_stack`), a router
+    (`_no_muon`), a 2-D `_no_weight_decay` gain, a 3-D conv kernel without the stack flag, vectors, a frozen matrix,
+    and a stage with no matrix for Muon."""
+    import torch
+
+    class GroupModel(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.embeddings = torch.nn.Embedding(50, 16)
+            self.lm_head = torch.nn.Linear(16, 50, bias=False)
+            self.lm_head.weight = self.embeddings.weight
+            self.norm0 = torch.nn.Parameter(torch.ones(16))
+            self.mixer = mixer_cls()
+            self.conv = torch.nn.Parameter(torch.zeros(4, 1, 8))
+            self.gain = torch.nn.Parameter(torch.ones(1, 16))
+            self.gain._no_weight_decay = True
+            self.w1 = torch.nn.Linear(16, 32)
+            self.w2 = torch.nn.Linear(32, 16, bias=False)
+            self.experts = torch.nn.Parameter(torch.zeros(4, 16, 24))
+            self.experts._muon_stack = True
+            self.router = torch.nn.Parameter(torch.zeros(4, 16))
+            self.router._no_muon = True
+            self.frozen = torch.nn.Parameter(torch.zeros(8, 8), requires_grad=False)
+            self.head_norm = torch.nn.Parameter(torch.ones(16))
+            self.scale = torch.nn.Parameter(torch.ones(()))
+
+        def stage_param_groups(self):
+            return {0: [self.embeddings.weight, self.norm0, self.mixer.in_proj.weight, self.mixer.out_proj.weight,
+                        self.conv, self.gain],
+                    1: [self.w1.weight, self.w1.bias, self.w2.weight, self.experts, self.router, self.frozen],
+                    2: [self.head_norm, self.scale]}
+
+    torch.manual_seed(0)
+    return GroupModel()
+
+
+def _jsonable(v):
+    if isinstance(v, (list, tuple)):
+        return [_jsonable(x) for x in v]
+    if isinstance(v, dict):
+        return {k: _jsonable(x) for k, x in v.items()}
+    if hasattr(v, "item"):   # a 0-dim tensor (lr, betas given as tensors)
+        return float(v.item())
+    return v
+
+
+def describe_optimizer(opt, model) -> dict:
+    """What a drop-in must reproduce of a freshly built optimizer: whether it is a MultiOpt, and per optimizer its kind,
+    every param group (parameter names in order and every other key) and the param_groups of its state_dict (what a
+    checkpoint stores)."""
+    names = {id(p): n for n, p in model.named_parameters()}
+    opts = opt.opts if hasattr(opt, "opts") else [opt]
+    out = {"multi": hasattr(opt, "opts"), "opts": []}
+    for o in opts:
+        groups = [{"params": [names[id(p)] for p in g["params"]],
+                   **{k: _jsonable(v) for k, v in sorted(g.items()) if k != "params"}} for g in o.param_groups]
+        sd = o.state_dict()
+        out["opts"].append({"kind": "muon" if "ns_steps" in o.defaults else "adamw", "groups": groups,
+                            "state_dict_groups": _jsonable(sd["param_groups"]), "state": len(sd["state"])})
+    return out

@@ -3,8 +3,9 @@ checkout) on seeded inputs. Run in a container that has the reference checkout:
 
     MOTE_REFERENCE=/path/to/mote python tests/golden/make_golden.py
 
-It writes `tests/golden/*.npz`. The fixtures pin `oracle/moteopt_oracle.py` (tests/test_oracle_golden.py) and are
-the reference side of the GPU parity tests. The reference is never needed at test time.
+It writes `tests/golden/*.npz` and `groups_reference.json`. The fixtures pin `oracle/moteopt_oracle.py`
+(tests/test_oracle_golden.py) and are the reference side of the GPU parity tests and of the optimizer-construction
+test (tests/test_host_optim.py). The reference is never needed at test time.
 
 What is run (reference file:line):
   * `mote.train.muon.newton_schulz` (muon.py:26-43) on assorted shapes at 1, 2 and 5 iterations;
@@ -12,7 +13,9 @@ What is run (reference file:line):
     of tests/test_moe.py:105-123 and the per-matrix-lr cases of tests/test_elr.py:145-182;
   * `torch.optim.AdamW` (constructed as at train.py:98) and `torch.nn.utils.clip_grad_norm_` (train.py:946);
   * the whole step of train.py:944-947 (grads /= n, clip, AdamW then Muon) on the c0 workload for 10 steps;
-  * `mote.model.moe.MoESwiGLU.update_bias` (moe.py:147-159), the lossfree router's bias step of train.py:948-949.
+  * `mote.model.moe.MoESwiGLU.update_bias` (moe.py:147-159), the lossfree router's bias step of train.py:948-949;
+  * `split_muon_params` (muon.py:103-126), `build_optimizer` (train.py:76-105) and `set_lr` (train.py:177-179) on a
+    model with every kind of parameter the split distinguishes (groups_reference.json).
 """
 
 from __future__ import annotations
@@ -35,8 +38,10 @@ sys.path.insert(0, REF)
 from mote.train.muon import Muon, newton_schulz  # noqa: E402  (the reference)
 
 from mote_b200 import configs  # noqa: E402
-from tests.golden.cases import (ADAM_SHAPES, C0_DIVISOR, MOE_CASES, MOE_GAMMA, MOE_STEPS, NS_CASES,  # noqa: E402
-                                NS_STEPS, moe_bias0, moe_loads, ns_input, sample_index)
+from tests.golden.cases import (ADAM_SHAPES, C0_DIVISOR, GROUP_KINDS, GROUP_LR, GROUP_MULTS,  # noqa: E402
+                                GROUP_SET_LR, GROUP_WD, MOE_CASES, MOE_GAMMA, MOE_STEPS, NS_CASES, NS_STEPS,
+                                describe_optimizer, group_model, mixer_parts, moe_bias0, moe_loads, ns_input,
+                                sample_index)
 
 torch.set_num_threads(max(1, min(8, os.cpu_count() or 1)))
 
@@ -188,7 +193,37 @@ def make_moe():
     np.savez_compressed(HERE / "moe_reference.npz", **out)
 
 
+# ---------------------------------------------------------------------------------------------------------------
+def make_groups():
+    """The reference's split_muon_params (muon.py:103-126), build_optimizer (train.py:76-105) and set_lr
+    (train.py:177-179) on cases.group_model for each optimizer kind: which parameter lands in which group, every
+    group key, and the param_groups a checkpoint stores. Written as JSON (tests/golden/groups_reference.json)."""
+    import json
+    from mote.model.mamba3 import Mamba3Mixer as RefMixer   # the reference
+    from mote.train.muon import split_muon_params
+    from mote.train.train import build_optimizer, set_lr
+
+    class Mamba3Mixer(RefMixer):   # an instance of the reference's class, without its full construction
+        def __init__(self):
+            torch.nn.Module.__init__(self)
+            mixer_parts(self)
+
+    model = group_model(Mamba3Mixer)
+    names = {id(p): n for n, p in model.named_parameters()}
+    muon, other = split_muon_params(model)
+    out = {"split": {"muon": [names[id(p)] for p in muon], "other": [names[id(p)] for p in other]},
+           "cuda": torch.cuda.is_available()}
+    for kind in GROUP_KINDS:
+        opt = build_optimizer(model, GROUP_LR, GROUP_WD, GROUP_MULTS, optimizer=kind)
+        d = describe_optimizer(opt, model)
+        set_lr(opt, GROUP_SET_LR)
+        d["set_lr"] = [g["lr"] for g in opt.param_groups]
+        out[kind] = d
+    (HERE / "groups_reference.json").write_text(json.dumps(out, indent=1, sort_keys=True) + "\n")
+
+
 if __name__ == "__main__":
+    make_groups()
     make_ns()
     make_muon()
     make_adamw_clip()
