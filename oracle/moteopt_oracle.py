@@ -16,6 +16,10 @@ What it restates (paths relative to the reference project noahsabaj/mote):
 * `moe_update_bias`          -- mote/model/moe.py:147-159 (the lossfree router's bias step, train.py:948-949)
 * `ema_lerp`, `frob_norm32`  -- train.py:950-953 (the weights' EMA) and elr.py:85-87 (the ELR tracker's norms)
 * `optimizer_step`           -- mote/train/train.py:944-947 followed by MultiOpt.step (train.py:64-66: AdamW, then Muon)
+* `gram_newton_schulz`       -- NOT in the reference's code: the Gram Newton-Schulz variant its research notes propose
+                                (docs/research/efficiency-campaign-2026-08-23.md:903-911), the specification of an
+                                opt-in variant; checked by its exact-arithmetic identity with the reference iteration
+                                and against the reference's own Newton-Schulz outputs (tests/test_oracle_gram_ns.py)
 
 Rounding model. Each elementwise op rounds to the tensor's dtype exactly where the reference's tensor op does.
 Where torch's CPU kernels fuse a multiply-add (``add(alpha=)``, ``lerp_``, ``addcmul_``) the oracle fuses too; this
@@ -122,6 +126,90 @@ def newton_schulz_f64(G: np.ndarray, steps: int = 5, eps: float = 1e-7) -> np.nd
         A = X @ np.swapaxes(X, -1, -2)
         B = NS_B * A + NS_C * (A @ A)
         X = NS_A * X + B @ X
+    if transposed:
+        X = np.swapaxes(X, -1, -2)
+    return X
+
+
+# ----------------------------------------------------------------------------------------------------------------
+# Gram Newton-Schulz: an opt-in variant, NOT the reference's iteration (no product kernel implements it yet)
+#
+# The reference's research notes (docs/research/efficiency-campaign-2026-08-23.md:903-911) propose it as a drop-in
+# for muon.py's newton_schulz: since polar(X) = (X X^T)^(-1/2) X, iterate on the small m x m Gram matrix and touch
+# the rectangular X only twice. Every iterate of the quintic iteration is X_k = Q_k X_0 with Q_k a polynomial in
+# R_0 = X_0 X_0^T, so all of Q_k, R_k = X_k X_k^T and P_k = aI + bR_k + cR_k^2 commute and
+#     X_{k+1} = P_k X_k  ->  Q_{k+1} = P_k Q_k,   R_{k+1} = P_k R_k P_k = P_k (P_k R_k).
+# The schedule below (steps >= 1): R_0 = X X^T; per iteration B_k = bR_k + cR_k^2 (the polynomial phase),
+# Q_1 = aI + B_0, Q_{k+1} = aQ_k + B_k Q_k, and, while another iteration follows, T = aR_k + B_k R_k,
+# R_{k+1} = aT + B_k T with its upper triangle mirrored (R is symmetric); finally X = Q_steps X_0. Each product is
+# one of the three kinds the Newton-Schulz kernel already runs (Gram, polynomial, a*Y + B Y), on m x m operands.
+
+def gram_ns_eligible(m: int, n: int) -> bool:
+    """Shapes the variant is for: the long side at least twice the short one. Square matrices gain no FLOPs (the
+    m x m iterate costs more products than X does) and lose accuracy in bf16 (R squares X's condition number)."""
+    s, l = min(m, n), max(m, n)
+    return l >= 2 * s
+
+
+def gram_ns_flops(m: int, n: int, steps: int = 5) -> float:
+    """Algorithmic FLOPs of the schedule above: two rectangular products (4 s^2 l) and 4*steps - 3 square ones
+    (steps polynomial, steps - 1 Q updates, 2 (steps - 1) R updates), 2 s^3 each."""
+    s, l = min(m, n), max(m, n)
+    return 4.0 * s * s * l + (4.0 * steps - 3.0) * 2.0 * s ** 3
+
+
+def _fused_round(x: np.ndarray) -> np.ndarray:
+    return bf16_round(np.asarray(x, np.float32))
+
+
+def gram_newton_schulz(G: np.ndarray, steps: int = 5, eps: float = 1e-7) -> np.ndarray:
+    """The schedule above in bf16 with fused epilogues: every product accumulates in fp32 and its output, including
+    the a*Y / b*R terms added in fp32, is rounded once to bf16, as a GEMM epilogue writes it. (With the reference's
+    rounding of every elementwise op the variant lands farther from the exact polar factor than the reference's own
+    iteration; with one rounding per product it lands closer.) G: [..., m, n]; returns fp32 holding bf16 values."""
+    if steps < 1:
+        raise ValueError("steps must be >= 1")
+    X = ns_normalize(G, eps)
+    transposed = X.shape[-2] > X.shape[-1]
+    if transposed:
+        X = np.ascontiguousarray(np.swapaxes(X, -1, -2))
+    a, b, c = f32(NS_A), f32(NS_B), f32(NS_C)
+    m = X.shape[-2]
+    eye = np.eye(m, dtype=np.float32)
+    R = _fused_round(np.matmul(X, np.swapaxes(X, -1, -2)))
+    Q = None
+    for k in range(steps):
+        B = _fused_round(b * R + c * np.matmul(R, R))
+        Q = _fused_round(a * eye + B) if Q is None else _fused_round(a * Q + np.matmul(B, Q))
+        if k < steps - 1:
+            T = _fused_round(a * R + np.matmul(B, R))
+            R = _fused_round(a * T + np.matmul(B, T))
+            R = np.triu(R) + np.swapaxes(np.triu(R, 1), -1, -2)
+    X = _fused_round(np.matmul(Q, X))
+    if transposed:
+        X = np.ascontiguousarray(np.swapaxes(X, -1, -2))
+    return X
+
+
+def gram_newton_schulz_f64(G: np.ndarray, steps: int = 5, eps: float = 1e-7) -> np.ndarray:
+    """The same schedule in fp64 with no rounding; in exact arithmetic it equals newton_schulz_f64."""
+    if steps < 1:
+        raise ValueError("steps must be >= 1")
+    X = np.asarray(G, np.float64)
+    X = X / (np.sqrt((X * X).sum(axis=(-2, -1), keepdims=True)) + eps)
+    transposed = X.shape[-2] > X.shape[-1]
+    if transposed:
+        X = np.swapaxes(X, -1, -2)
+    eye = np.eye(X.shape[-2])
+    R = X @ np.swapaxes(X, -1, -2)
+    Q = None
+    for k in range(steps):
+        B = NS_B * R + NS_C * (R @ R)
+        Q = NS_A * eye + B if Q is None else NS_A * Q + B @ Q
+        if k < steps - 1:
+            T = NS_A * R + B @ R
+            R = NS_A * T + B @ T
+    X = Q @ X
     if transposed:
         X = np.swapaxes(X, -1, -2)
     return X
