@@ -2,14 +2,18 @@
 set_lr against the reference's own results on the same model (tests/golden/groups_reference.json, made by running
 mote/train/muon.py:103-126 and mote/train/train.py:76-105, :177-179). A checkpoint written by the reference trainer
 holds these param_groups, so a drop-in must build the same groups, in the same order, with the same keys and values,
-for its load_state_dict to line the saved state up with the right parameters."""
+for its load_state_dict to line the saved state up with the right parameters. Also: CPU tensors and a missing library
+are refused with an error, never computed some other way."""
 
 import json
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
 
-from tests.conftest import GOLDEN
+from tests.conftest import GOLDEN, ROOT
 from tests.golden.cases import (GROUP_KINDS, GROUP_LR, GROUP_MULTS, GROUP_SET_LR, GROUP_WD, describe_optimizer,
                                 group_model, mixer_parts)
 
@@ -73,3 +77,29 @@ def test_a_reference_shaped_state_dict_loads_into_the_drop_in():
     b.load_state_dict(sd)
     assert b.state_dict()["multi"][0]["param_groups"] == sd["multi"][0]["param_groups"]
     assert b.state_dict()["multi"][1]["param_groups"] == sd["multi"][1]["param_groups"]
+
+
+@pytest.mark.parametrize("call", ["muon", "adamw", "multi", "fused_step", "newton_schulz", "clip_grad_norm_"])
+def test_cpu_tensors_are_refused_not_computed(call):
+    """There is no CPU or PyTorch fallback: every entry point refuses CPU tensors with an error and leaves the
+    parameters as they were."""
+    from mote_b200 import AdamW, Muon, MultiOpt, clip_grad_norm_, fused_step, newton_schulz
+    p = torch.nn.Parameter(torch.randn(8, 16))
+    p.grad = torch.randn(8, 16)
+    v = torch.nn.Parameter(torch.randn(16))
+    v.grad = torch.randn(16)
+    before = (p.detach().clone(), v.detach().clone())
+    run = {"muon": lambda: Muon([p]).step(), "adamw": lambda: AdamW([p, v]).step(),
+           "multi": lambda: MultiOpt([AdamW([v]), Muon([p])]).step(),
+           "fused_step": lambda: fused_step(MultiOpt([AdamW([v]), Muon([p])]), max_norm=1.0, grad_divisor=2.0),
+           "newton_schulz": lambda: newton_schulz(p.grad), "clip_grad_norm_": lambda: clip_grad_norm_([p, v], 1.0)}
+    with pytest.raises(ValueError, match="GPU"):
+        run[call]()
+    assert torch.equal(p.detach(), before[0]) and torch.equal(v.detach(), before[1])
+
+
+def test_a_missing_library_is_an_import_error():
+    env = {**os.environ, "MOTEOPT_LIB": str(ROOT / "no_such_dir" / "libmoteopt.so")}
+    r = subprocess.run([sys.executable, "-c", "import mote_b200._lib"], cwd=ROOT, capture_output=True, text=True,
+                       env=env, timeout=300)
+    assert r.returncode != 0 and "ImportError" in r.stderr and "no CPU or PyTorch fallback" in r.stderr
