@@ -67,7 +67,9 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
 
 
 @pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (2, 3072, 768), (2, 512, 2048), (1, 1000, 264),
-                                   (1, 1100, 1300)])
+                                   (1, 1100, 1300),
+                                   # the c2 (1024^2, 1024 x 4096) and c3 (768 x 2048 expert) matrix shapes
+                                   (2, 1024, 1024), (1, 1024, 4096), (1, 4096, 1024), (1, 768, 2048), (1, 2048, 768)])
 def test_newton_schulz_benchmark_shapes(dev, shape):
     u = ns_input(shape, 123)
     for steps, tol in ((1, 1e-3), (5, 4e-2)):
@@ -144,6 +146,35 @@ def test_muon_step_forty_shapes_matches_oracle(dev):
     ref = [p.copy() for p in p0]
     rbufs = [None] * len(ref)
     O.muon_step(ref, gr, rbufs, O.MuonGroup(lr=0.02, weight_decay=0.1, ns_steps=1))
+    for i in range(len(shapes)):
+        d_gpu = ps[i].cpu().numpy() - p0[i]
+        d_ref = ref[i] - p0[i]
+        assert O.rel_frob(d_gpu, d_ref) <= 2e-3, (shapes[i], O.rel_frob(d_gpu, d_ref))
+        assert _close(bufs[i].cpu().numpy(), rbufs[i], 1e-6) == 0
+    _status_ok(dev)
+
+
+def test_expert_stacks_with_zipf_grads_match_oracle(dev):
+    """c3's 3-D MoE expert stacks (mote/train/muon.py:59-72 reshapes them to (-1, m, n)), both orientations, with each
+    expert's grad scaled by its Zipf(1.1) token factor, through the whole step: momentum buffers to 1e-6, param
+    deltas to 2e-3 after one Newton-Schulz iteration."""
+    from mote_b200.functional import MuonItem, muon_step
+    w = configs.c3()
+    e = 4
+    shapes = [(e,) + s[1:] for s in w.muon_shapes]
+    scale = np.asarray(w.grad_scale[:e], np.float32)[:, None, None]
+    rng = np.random.default_rng(31)
+    p0 = [rng.standard_normal(sh, dtype=np.float32) * np.float32(0.02) for sh in shapes]
+    gr = [O.bf16_round(rng.standard_normal(sh, dtype=np.float32) * np.float32(1e-3) * scale) for sh in shapes]
+    ps, gs = _to(dev, p0), _to(dev, gr)
+    bufs = [torch.zeros_like(p) for p in ps]
+    for _ in range(2):   # the second step runs on a non-zero momentum buffer
+        muon_step([MuonItem(p, g, b, 0.02, 0.002, 0.95, True) for p, g, b in zip(ps, gs, bufs)], ns_steps=1)
+    torch.cuda.synchronize()
+    ref = [p.copy() for p in p0]
+    rbufs = [None] * len(ref)
+    for _ in range(2):
+        O.muon_step(ref, gr, rbufs, O.MuonGroup(lr=0.02, weight_decay=0.1, ns_steps=1))
     for i in range(len(shapes)):
         d_gpu = ps[i].cpu().numpy() - p0[i]
         d_ref = ref[i] - p0[i]
