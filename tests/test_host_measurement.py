@@ -1,0 +1,64 @@
+"""The measurement arithmetic on the CPU: the per-step algorithmic work of each workload (the units the roofline
+figures in bench.py divide by) against the figures the reference's step is quoted with, the issued tensor-core work
+against an explicit enumeration of the kernel's tile schedule, and the step roofline's formula."""
+
+import pytest
+
+from mote_b200 import configs
+
+
+@pytest.mark.parametrize("name,tflop,gb,elems", [
+    ("c1", 1.727, 1.877, 93.3e6),    # 12 x {4 x 768^2, 768 x 3072, 3072 x 768} + 8 x 512 x 2048 Muon, ~0.36 M AdamW
+    ("c2", 14.43, 10.74, 536.9e6),   # 256 x 1024^2 + 64 x 1024 x 4096
+    ("c3", 3.67, 4.03, 201.3e6),     # 64 x 768 x 2048 + 64 x 2048 x 768 expert stacks
+])
+def test_workload_figures(name, tflop, gb, elems):
+    """FLOPs = sum 5 (4 s^2 l + 2 s^3) over the matrices (s, l = short, long side); bytes = 20 per Muon element and
+    28 per AdamW element."""
+    w = configs.CONFIGS[name]()
+    assert w.ns_flops() / 1e12 == pytest.approx(tflop, rel=1e-3)
+    assert w.state_bytes() / 1e9 == pytest.approx(gb, rel=1e-3)
+    assert w.numel()[0] == pytest.approx(elems, rel=1e-3)
+
+
+def _issued_by_enumeration(w, tile=256):
+    """Walk the kernel's schedule tile by tile: per iteration the Gram (X X^T, K = l) and polynomial (A A, K = s)
+    phases compute the output blocks on and above the diagonal, the update (B X, K = s) every block of X; a block
+    clipped at the matrix edge does only its valid rows and columns."""
+    tot = 0.0
+    for shape in w.muon_shapes:
+        batch = shape[0] if len(shape) == 3 else 1
+        s, l = min(shape[-2:]), max(shape[-2:])
+        rows = [min(tile, s - i) for i in range(0, s, tile)]
+        cols = [min(tile, l - j) for j in range(0, l, tile)]
+        for bi, r in enumerate(rows):
+            for bj, c in enumerate(rows):
+                if bj >= bi:
+                    tot += batch * w.ns_steps * (2.0 * r * c * l + 2.0 * r * c * s)
+            for c in cols:
+                tot += batch * w.ns_steps * 2.0 * r * c * s
+    return tot
+
+
+@pytest.mark.parametrize("name", ["c0", "c1", "c2", "c3"])
+def test_issued_tensor_work_matches_the_tile_schedule(name):
+    w = configs.CONFIGS[name]()
+    assert w.ns_flops_issued() == pytest.approx(_issued_by_enumeration(w), rel=1e-12)
+    assert w.ns_flops_issued() <= w.ns_flops()
+
+
+def test_c1_issued_work_and_tiles():
+    w = configs.c1()
+    assert w.ns_flops_issued() == pytest.approx(1.3878e12, rel=1e-4)   # the figure the NS profile divides by
+    assert w.ns_tiles_per_iter() == 2336
+
+
+def test_step_roofline_formula():
+    import bench
+    peaks = {"hbm_gbs": 6500.0, "bf16_tflops": 1600.0, "bf16_tflops_sustained": 1400.0}
+    r = bench.step_roofline(1.727e12, 1.877e9, 0.0, peaks, ms=2.0)
+    assert r["sustained"]["roofline_ms"] == pytest.approx(1.727e12 / 1.4e15 * 1e3, rel=1e-3)   # FLOP-bound
+    assert r["burst"]["frac"] == pytest.approx(1.727e12 / 1.6e15 * 1e3 / 2.0, rel=1e-3)
+    # an exchange adds its NVLink time (770 GB/s per direction) on top of the slower of the two bounds
+    r = bench.step_roofline(1e9, 6.5e9, 0.77e9, peaks, ms=2.0)
+    assert r["sustained"]["roofline_ms"] == pytest.approx(1.0 + 1.0, rel=1e-3)
