@@ -7,8 +7,9 @@ the embedding and vectors, Muon (momentum + 5 Newton-Schulz iterations + apply) 
 (fp32 params, bf16 grads, fp32 optimizer state; 1.1 GB) stay resident in HBM and are larger than L2, so nothing is
 flushed between steps. Prints one JSON line (rank 0).
 
---impl reference times the reference's arithmetic on the host CPU: the numpy restatement in oracle/ (the reference
-is Python and cannot be installed on the GPU host), one bounded sample per step, extrapolated to the full step.
+--impl reference times the reference's step on the host CPU: oracle/torch_port.py performs the reference's own torch
+operations (the reference is Python and is not installed on the GPU host; the port equals it bit for bit on the
+golden fixtures), one Newton-Schulz stack per step, extrapolated to the full step by stack counts.
 """
 
 from __future__ import annotations
@@ -138,45 +139,79 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------------------------
-def cpu_baseline_sample(w, seconds_cap: float = 30.0):
-    """Time the oracle (numpy restatement of the reference step) on one matrix of every Muon shape plus the full
-    AdamW set and the grad norm, on this host's cores; extrapolate to the whole step by matrix counts."""
-    import numpy as np
-    from oracle import moteopt_oracle as O
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    shapes = {}
-    for s in w.muon_shapes:
-        shapes[tuple(s)] = shapes.get(tuple(s), 0) + 1
-    t_shape = {}
-    grp = O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=w.muon_wd, ns_steps=w.ns_steps)
-    for s in shapes:
-        p = (rng.standard_normal(s, dtype=np.float32) * np.float32(0.02))
-        g = O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3))
-        bufs = [None]
+class TorchReference:
+    """The reference's step on the host CPU (oracle/torch_port.py: the reference's own torch operations, equal to it
+    bit for bit on the golden fixtures), sampled one Newton-Schulz stack at a time. `counts` maps each distinct
+    stack of the workload's Muon step (the member params' shapes; muon.py:81-90 caps a stack at 32 MiB) to how often
+    it occurs; `time_stack(key)` runs the whole Muon update of one such stack (momentum, stacked Newton-Schulz,
+    decay, apply); `time_rest()` the grad division, the clip over every grad and the AdamW step."""
+
+    def __init__(self, w):
+        import torch
+        from oracle import torch_port as TP
+        self.torch, self.TP, self.w = torch, TP, w
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        self.cores = torch.get_num_threads()
+        gen = torch.Generator().manual_seed(0)
+
+        def randn(shape, std):
+            return torch.randn(shape, generator=gen) * std
+
+        self.counts, self.stack = {}, {}
+        for _, idx in TP.stacks([tuple(s) for s in w.muon_shapes]):
+            key = tuple(tuple(w.muon_shapes[i]) for i in idx)
+            self.counts[key] = self.counts.get(key, 0) + 1
+            if key not in self.stack:
+                ps = [torch.nn.Parameter(randn(s, 0.02)) for s in key]
+                for q in ps:
+                    q.grad = randn(q.shape, 1e-3).to(torch.bfloat16).float()
+                self.stack[key] = (ps, [None] * len(ps))
+        n_muon = w.numel()[0]
+        self.flat = torch.nn.Parameter(torch.zeros(n_muon))   # every Muon grad, for the division and the clip
+        self.adam_p = [torch.nn.Parameter(randn(s, 0.02)) for s in w.adam_shapes]
+        nd = len(w.adam_decay_shapes)
+        self.adam = torch.optim.AdamW([{"params": self.adam_p[:nd], "weight_decay": w.adam_wd},
+                                       {"params": self.adam_p[nd:], "weight_decay": 0.0}], lr=w.adam_lr,
+                                      betas=w.betas, eps=w.eps, fused=torch.cuda.is_available())   # train.py:98
+        for key in self.stack:   # momentum buffers created, first-touch costs paid
+            self.time_stack(key)
+        self.time_rest()
+
+    def time_stack(self, key) -> float:
+        ps, bufs = self.stack[key]
+        w = self.w
         t0 = time.perf_counter()
-        O.muon_step([p], [g], bufs, grp)
-        t_shape[s] = time.perf_counter() - t0
-    ap = [(rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)) for s in w.adam_shapes]
-    ag = [O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3)) for s in w.adam_shapes]
-    t0 = time.perf_counter()
-    O.adamw_step(ap, ag, [None] * len(ap), [None] * len(ap), [0] * len(ap),
-                 O.AdamWGroup(lr=w.adam_lr, betas=w.betas, eps=w.eps, weight_decay=w.adam_wd))
-    t_adam = time.perf_counter() - t0
-    # grad norm over every grad: time it on the AdamW grads plus one matrix per shape, scale by element count
-    sample = ag + [O.bf16_round(rng.standard_normal(s, dtype=np.float32)) for s in shapes]
-    n_sample = sum(x.size for x in sample)
-    t0 = time.perf_counter()
-    O.grad_total_norm(sample)
-    t_norm = (time.perf_counter() - t0) * (sum(w.numel()) / n_sample)
-    total = sum(shapes[s] * t_shape[s] for s in shapes) + t_adam + t_norm
-    desc = ("oracle/moteopt_oracle.py (numpy, bf16-exact rounding) on one matrix of each Muon shape "
-            f"{sorted(shapes)}, the full AdamW set and a norm sample; scaled by matrix counts to the full step")
-    return {"value": total * 1e3, "unit": "ms/step", "cores": int(cores), "kind": "port", "sample": desc}
+        self.TP.muon_update(ps, bufs, lr=w.muon_lr, momentum=w.muon_momentum, nesterov=True,
+                            weight_decay=w.muon_wd, ns_steps=w.ns_steps)
+        return time.perf_counter() - t0
+
+    def time_rest(self) -> float:
+        torch = self.torch
+        self.flat.grad = torch.full_like(self.flat, 1e-3)
+        for q in self.adam_p:
+            q.grad = torch.full_like(q, 1e-3)
+        params = [self.flat] + self.adam_p
+        t0 = time.perf_counter()
+        torch._foreach_div_([q.grad for q in params], 1.0)
+        torch.nn.utils.clip_grad_norm_(params, self.w.clip)
+        self.adam.step()
+        return time.perf_counter() - t0
+
+    def describe(self, how: str) -> str:
+        kinds = ", ".join(f"{len(k)} x {k[0]} ({c}x)" for k, c in self.counts.items())
+        return (f"oracle/torch_port.py (the reference's torch CPU operations; bit-equal to the reference on the golden "
+                f"fixtures) on {self.cores} host threads: {how} Muon stacks of the step [{kinds}]; plus grads /= n, "
+                "clip_grad_norm_ and the AdamW step on the whole workload; summed by stack counts to the full step")
+
+
+def cpu_baseline_sample(w) -> dict:
+    """The reference's step on this host's cores (TorchReference): every stack kind timed twice after a warm-up,
+    the medians summed by stack counts, plus the clip and AdamW."""
+    ref = TorchReference(w)
+    total = sum(c * statistics.median([ref.time_stack(k) for _ in range(2)]) for k, c in ref.counts.items())
+    total += ref.time_rest()
+    return {"value": round(total * 1e3, 3), "unit": "ms/step", "cores": int(ref.cores), "kind": "port",
+            "sample": ref.describe("each of the")}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -440,68 +475,31 @@ def _time_extras(step, muon_items, adam_items, w, stream, counter, reps: int = 1
 
 
 def run_reference(args, rank: int, world: int):
-    """The reference's arithmetic (oracle/ numpy restatement) on the host CPU, one bounded sample per step."""
-    import numpy as np
+    """The reference's step on the host CPU (TorchReference), one bounded sample per step: step k runs the Muon
+    update of one Newton-Schulz stack, cycling through the workload's stack kinds; the per-kind medians summed by
+    stack counts, plus the clip and AdamW, give the full step."""
     from mote_b200 import configs
-    from oracle import moteopt_oracle as O
-    try:
-        from threadpoolctl import threadpool_info
-        cores = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
     w = configs.CONFIGS[args.config]()
-    rng = np.random.default_rng(0)
-    counts = {}
-    for s in w.muon_shapes:
-        counts[tuple(s)] = counts.get(tuple(s), 0) + 1
-    shapes = sorted(counts)
-    # one Newton-Schulz iteration of one matrix per step, cycling through the shapes; the rest of the step
-    # (momentum, normalisation, apply, AdamW, grad norm) is timed once and added
-    xs = {s: O.ns_normalize(rng.standard_normal(s, dtype=np.float32)) for s in shapes}
-    t_iter = {s: [] for s in shapes}
+    ref = TorchReference(w)
+    keys = list(ref.counts)
+    t = {k: [] for k in keys}
     for k in range(args.warmup + args.steps):
-        s = shapes[k % len(shapes)]
-        t0 = time.perf_counter()
-        O.ns_iterate(xs[s], 1)
-        dt = time.perf_counter() - t0
+        key = keys[k % len(keys)]
+        dt = ref.time_stack(key)
         if k >= args.warmup:
-            t_iter[s].append(dt)
-    for s in shapes:   # a shape not reached by a short run gets one measurement here
-        if not t_iter[s]:
-            t0 = time.perf_counter()
-            O.ns_iterate(xs[s], 1)
-            t_iter[s].append(time.perf_counter() - t0)
-    # element-wise parts on one matrix per shape: momentum, normalisation, apply
-    t_elem = 0.0
-    grp = O.MuonGroup(lr=w.muon_lr, momentum=w.muon_momentum, weight_decay=w.muon_wd, ns_steps=0)
-    for s in shapes:
-        p = rng.standard_normal(s, dtype=np.float32) * np.float32(0.02)
-        g = O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3))
-        t0 = time.perf_counter()
-        O.muon_step([p], [g], [None], grp)
-        t_elem += counts[s] * (time.perf_counter() - t0)
-    ap = [rng.standard_normal(s, dtype=np.float32) * np.float32(0.02) for s in w.adam_shapes]
-    ag = [O.bf16_round(rng.standard_normal(s, dtype=np.float32) * np.float32(1e-3)) for s in w.adam_shapes]
-    t0 = time.perf_counter()
-    O.adamw_step(ap, ag, [None] * len(ap), [None] * len(ap), [0] * len(ap),
-                 O.AdamWGroup(lr=w.adam_lr, betas=w.betas, eps=w.eps, weight_decay=w.adam_wd))
-    t_rest = time.perf_counter() - t0
-    sample = ag + [xs[s] for s in shapes]
-    t0 = time.perf_counter()
-    O.grad_total_norm(sample)
-    t_rest += (time.perf_counter() - t0) * (sum(w.numel()) / sum(x.size for x in sample))
-    total = sum(counts[s] * w.ns_steps * statistics.median(t_iter[s]) for s in shapes) + t_elem + t_rest
-    ms = total * 1e3
-    desc = (f"oracle/moteopt_oracle.py (numpy) on the host: per step one Newton-Schulz iteration of one matrix, "
-            f"cycling {shapes}; + momentum/normalise/apply per shape, full AdamW and a norm sample, once; "
-            "extrapolated to the full step by matrix counts")
+            t[key].append(dt)
+    for key in keys:   # a kind not reached by a short run gets one measurement here
+        if not t[key]:
+            t[key].append(ref.time_stack(key))
+    rest = statistics.median([ref.time_rest() for _ in range(3)])
+    ms = (sum(ref.counts[k] * statistics.median(t[k]) for k in keys) + rest) * 1e3
     return {"metric": METRIC, "value": round(ms, 3), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "impl": "reference",
-            "data": "synthetic: seeded params N(0,0.02^2) fp32, grads N(0,1e-3^2) bf16",
+            "data": "synthetic: seeded params N(0,0.02^2) fp32, grads N(0,1e-3^2) bf16-valued fp32",
             "config": {"workload": w.name, "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(ms, 3), "unit": "ms/step", "cores": int(cores), "kind": "port",
-                             "sample": desc},
+            "cpu_baseline": {"value": round(ms, 3), "unit": "ms/step", "cores": int(ref.cores), "kind": "port",
+                             "sample": ref.describe("per step one of the")},
             "e2e": {"value": round(ms, 3), "unit": "ms/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
