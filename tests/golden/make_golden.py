@@ -4,8 +4,9 @@ checkout) on seeded inputs. Run in a container that has the reference checkout:
     MOTE_REFERENCE=/path/to/mote python tests/golden/make_golden.py
 
 It writes `tests/golden/*.npz` and `groups_reference.json`. The fixtures pin `oracle/moteopt_oracle.py`
-(tests/test_oracle_golden.py) and are the reference side of the GPU parity tests and of the optimizer-construction
-test (tests/test_host_optim.py). The reference is never needed at test time.
+(tests/test_oracle_golden.py) and `oracle/torch_port.py` (tests/test_oracle_torch_port.py, bit for bit), and are the
+reference side of the GPU parity tests and of the optimizer-construction test (tests/test_host_optim.py). The
+reference is never needed at test time.
 
 What is run (reference file:line):
   * `mote.train.muon.newton_schulz` (muon.py:26-43) on assorted shapes at 1, 2 and 5 iterations;
