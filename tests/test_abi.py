@@ -119,3 +119,48 @@ def test_entry_points_reject_bad_arguments_without_touching_a_device():
     assert lib.moteopt_ema_lerp(ptrs, ptrs, numel, 1, 0.1, None) == -1 and b"bad tensor" in lib.moteopt_last_error()
     assert lib.moteopt_muon_apply_ex(None, 1, None, None, None, 0.0, None, None, 0, None) == -1
     assert lib.moteopt_muon_apply_workspace_size(None, 3) == 0
+
+
+C_HOST = r"""
+#include <stdio.h>
+#include <string.h>
+#include "moteopt.h"
+
+/* A non-Python host: the c1 workload's optimizer-step workspace, sized and checked without a device. */
+int main(void) {
+  moteopt_muon_param m[2];
+  moteopt_adamw_tensor a[1];
+  memset(m, 0, sizeof m);
+  memset(a, 0, sizeof a);
+  m[0].batch = 4; m[0].rows = 768; m[0].cols = 768; m[0].grad_dtype = MOTEOPT_DTYPE_BF16;
+  m[1].batch = 1; m[1].rows = 3072; m[1].cols = 768; m[1].grad_dtype = MOTEOPT_DTYPE_BF16;
+  a[0].numel = 271 * 768; a[0].grad_dtype = MOTEOPT_DTYPE_F32;
+  size_t ws = moteopt_optimizer_step_workspace_size(m, 2, 5, a, 1);
+  size_t ns = moteopt_newton_schulz_workspace_size(4, 768, 768);
+  moteopt_muon_config mc = {5, 0.2, 1e-7};
+  moteopt_adamw_hparams hp = {0.9, 0.95, 1e-8, NULL};
+  moteopt_grad_config gc = {1, 1.0, 0.0};
+  int rc = moteopt_optimizer_step(m, 2, &mc, a, 1, &hp, &gc, NULL, NULL, 0, NULL);   /* null pointers: refused */
+  printf("%d %zu %zu %d %s\n", moteopt_version(), ws, ns, rc, rc == MOTEOPT_ERR_INVALID ? "refused" : "?");
+  printf("%s\n", moteopt_last_error());
+  return (ws > 0 && ns > 0 && rc == MOTEOPT_ERR_INVALID) ? 0 : 1;
+}
+"""
+
+
+def test_a_c_host_compiles_links_and_calls_the_library(tmp_path):
+    """include/moteopt.h is plain C (C11, -Wall -Werror): a C program builds against it, links libmoteopt.so and
+    calls it; the host-only entry points answer without a device and a bad call returns its error code."""
+    from mote_b200 import _lib
+    src = tmp_path / "host.c"
+    src.write_text(C_HOST)
+    exe = tmp_path / "host"
+    lib_dir = Path(_lib.LIB_PATH).parent
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"), str(src),
+                    "-L", str(lib_dir), "-l:" + Path(_lib.LIB_PATH).name, "-Wl,-rpath," + str(lib_dir), "-o",
+                    str(exe)], check=True, capture_output=True, text=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+    version, ws, ns, rc, word = r.stdout.splitlines()[0].split()
+    assert int(version) == _lib.lib.moteopt_version() and int(ws) > int(ns) > 0
+    assert int(rc) == -1 and word == "refused"
