@@ -164,3 +164,41 @@ def test_a_c_host_compiles_links_and_calls_the_library(tmp_path):
     version, ws, ns, rc, word = r.stdout.splitlines()[0].split()
     assert int(version) == _lib.lib.moteopt_version() and int(ws) > int(ns) > 0
     assert int(rc) == -1 and word == "refused"
+
+
+def _kernel_resources():
+    """{kernel: (registers, spilled bytes: the larger of the spill stores and loads)} from ptxas's report of the
+    release build (mote_b200/_build/)."""
+    from mote_b200 import build
+    if not build.RESOURCES.exists():
+        pytest.skip("no ptxas report: rebuild with python -m mote_b200.build")
+    if build.RESOURCES.stat().st_mtime < build.LIB.stat().st_mtime - 5:
+        pytest.skip("the ptxas report is older than the library")
+    out, name = {}, None
+    for line in build.RESOURCES.read_text().splitlines():
+        m = re.search(r"Compiling entry function '(\w+)'", line)
+        if m:
+            name = m.group(1)
+            continue
+        m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
+        if m and name:
+            out.setdefault(name, [0, 0])[1] = max(int(m.group(1)), int(m.group(2)))
+        m = re.search(r"Used (\d+) registers", line)
+        if m and name:
+            out.setdefault(name, [0, 0])[0] = int(m.group(1))
+    return {k: tuple(v) for k, v in out.items()}
+
+
+def test_kernel_register_budgets():
+    """Registers and spills of every kernel, against the budgets their launch shapes were tuned for: the
+    Newton-Schulz kernel's 320 threads at one CTA per SM with its 96 registers; no spills anywhere except the
+    16-byte one of the division-free momentum pass, whose register cap (four blocks per SM) was measured to run at
+    the copy bandwidth with it."""
+    res = _kernel_resources()
+    assert len(res) >= 20, sorted(res)
+    ns = [v for k, v in res.items() if "ns_gemm_kernel" in k]
+    assert ns and ns[0][0] <= 96 and ns[0][1] == 0
+    for k, (regs, spill) in res.items():
+        allowed = 16 if "muon_momentum_kernelILb0E" in k else 0
+        assert spill <= allowed, (k, regs, spill)
+        assert regs <= 255, k
