@@ -483,7 +483,13 @@ def run_reference(args, rank: int, world: int):
     ref = TorchReference(w)
     keys = list(ref.counts)
     t = {k: [] for k in keys}
+    rest_t = []
     for k in range(args.warmup + args.steps):
+        if not keys:   # a workload without Muon matrices (c4): every step samples the clip + AdamW step
+            dt = ref.time_rest()
+            if k >= args.warmup:
+                rest_t.append(dt)
+            continue
         key = keys[k % len(keys)]
         dt = ref.time_stack(key)
         if k >= args.warmup:
@@ -491,7 +497,7 @@ def run_reference(args, rank: int, world: int):
     for key in keys:   # a kind not reached by a short run gets one measurement here
         if not t[key]:
             t[key].append(ref.time_stack(key))
-    rest = statistics.median([ref.time_rest() for _ in range(3)])
+    rest = statistics.median(rest_t or [ref.time_rest() for _ in range(3)])
     ms = (sum(ref.counts[k] * statistics.median(t[k]) for k in keys) + rest) * 1e3
     return {"metric": METRIC, "value": round(ms, 3), "unit": "ms/step", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
