@@ -62,3 +62,30 @@ def test_step_roofline_formula():
     # an exchange adds its NVLink time (770 GB/s per direction) on top of the slower of the two bounds
     r = bench.step_roofline(1e9, 6.5e9, 0.77e9, peaks, ms=2.0)
     assert r["sustained"]["roofline_ms"] == pytest.approx(1.0 + 1.0, rel=1e-3)
+
+
+@pytest.mark.parametrize("config", ["c0", "c4_small"])
+def test_reference_arm_line(config, monkeypatch):
+    """`bench.py --impl reference`: the reference's own torch step on the host (oracle/torch_port.py), one JSON line
+    with the contract's keys; a workload without Muon matrices samples its clip + AdamW step instead."""
+    import argparse
+
+    import bench
+    if config == "c4_small":
+        monkeypatch.setitem(configs.CONFIGS, "c4_small", lambda: configs.c4(200_000))
+    args = argparse.Namespace(steps=4, warmup=1, config=config)
+    line = bench.run_reference(args, rank=0, world=1)
+    assert line["impl"] == "reference" and line["unit"] == "ms/step" and line["higher_is_better"] is False
+    assert line["value"] > 0 and line["value"] == line["ms_per_step"] == line["e2e"]["value"]
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"] and "torch_port" in cb["sample"]
+
+
+def test_cpu_baseline_sample_sums_every_stack_kind():
+    import bench
+    w = configs.c0()
+    cb = bench.cpu_baseline_sample(w)
+    ref = bench.TorchReference(w)
+    assert sum(c * len(k) for k, c in ref.counts.items()) == len(w.muon_shapes)   # every Muon param in one stack
+    assert cb["value"] > 0 and cb["unit"] == "ms/step" and cb["kind"] == "port"
