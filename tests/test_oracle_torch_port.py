@@ -2,6 +2,8 @@
 reference's own outputs (tests/golden/, made by running mote/train/muon.py and train.py:944-947). It performs the
 reference's torch operations in the reference's order, so the outputs are equal bit for bit."""
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -10,6 +12,16 @@ from oracle import torch_port as TP
 from tests.conftest import golden
 from tests.golden.cases import C0_DIVISOR, NS_CASES, ns_input, sample_index
 from mote_b200 import configs
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _fixture_threads():
+    """The fixtures were made with min(8, cores) torch threads (make_golden.py); the CPU matmuls' blocking, and so
+    their summation order, follows the thread count, so the port runs with the same count."""
+    before = torch.get_num_threads()
+    torch.set_num_threads(max(1, min(8, os.cpu_count() or 1)))
+    yield
+    torch.set_num_threads(before)
 
 
 def _bits16(t: torch.Tensor) -> np.ndarray:
