@@ -89,3 +89,23 @@ def test_cpu_baseline_sample_sums_every_stack_kind():
     ref = bench.TorchReference(w)
     assert sum(c * len(k) for k, c in ref.counts.items()) == len(w.muon_shapes)   # every Muon param in one stack
     assert cb["value"] > 0 and cb["unit"] == "ms/step" and cb["kind"] == "port"
+
+
+def test_reference_arm_under_torchrun_prints_on_rank_zero_only():
+    """Under torchrun (N > 1) rank 0 alone times and prints the reference line; the other ranks exit 0 without work."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from tests.conftest import ROOT
+    cmd = [sys.executable, "bench.py", "--impl", "reference", "--steps", "2", "--warmup", "0", "--config", "c0"]
+    for rank in (1, 0):
+        env = {**os.environ, "RANK": str(rank), "LOCAL_RANK": str(rank), "WORLD_SIZE": "2"}
+        r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stderr[-2000:]
+        lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+        if rank:
+            assert lines == []
+        else:
+            line = json.loads(lines[-1])
+            assert line["impl"] == "reference" and line["n_gpus"] == 2
