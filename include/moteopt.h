@@ -245,7 +245,10 @@ MOTEOPT_API int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels
  *      every device that loads the library until the process exits. The first call on a device looks up the
  *      array's device address; make that first call before any CUDA graph capture on that device. Calls share the
  *      array: calls that can overlap on the GPU (different streams without ordering, or several host threads) race
- *      and must be serialised by the caller. `out_norm` (device, may be NULL) receives the total norm. */
+ *      and must be serialised by the caller. `out_norm` (device, may be NULL) receives the total norm. This call has
+ *      no workspace header for moteopt_read_status to read: a NaN or Inf grad shows only as a NaN or Inf *out_norm
+ *      (the grads are then scaled by torch's coefficient for that norm, as moteopt_clip_grad_norm does); a caller
+ *      that needs the check reads out_norm back. */
 MOTEOPT_API int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, const int* dtypes, int n,
                                                double max_norm, float* out_norm, moteopt_stream_t stream);
 
@@ -269,6 +272,23 @@ typedef struct moteopt_moe_bias {
   float gamma;          /* bias_gamma, rounded to fp32 as torch does for a Python scalar times an fp32 tensor */
 } moteopt_moe_bias;
 MOTEOPT_API int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, moteopt_stream_t stream);
+
+/* ---- self-tests of two device primitives the optimizer's kernels rely on (diagnostics with no counterpart in the
+ *      reference; nothing in the optimizer step calls them).
+ *      moteopt_selftest_divide: out[i] = a[i] / d[i] (n fp32 device values) computed the way the Newton-Schulz
+ *      normalisation divides by a shared norm (a correctly rounded reciprocal, one product, one Markstein
+ *      correction), so a caller can hold it against IEEE division.
+ *      moteopt_selftest_wait_timeout: runs the kernels' bounded waits on something that never completes and returns
+ *      once they have given up: mode 0 waits on `counter` (a device int the caller keeps below 1: a persistent
+ *      Newton-Schulz tile's input counter that nothing adds to), mode 1 on an mbarrier nothing arrives on (a pipeline
+ *      stage whose loads never land). Two CTAs wait; CTA 0 gives up after limit_seconds (1 us .. 0.25 s) and sets
+ *      MOTEOPT_STATUS_WAIT_TIMEOUT in *status (device int); CTA 1 waits with four times the limit and, in mode 0,
+ *      stops as soon as it sees that bit, as every CTA of a launch does. Each CTA that unwound sets
+ *      MOTEOPT_STATUS_ABORTED; elapsed_ns (device, 2 values) receives how long each CTA waited. The GPU context stays
+ *      usable afterwards. */
+MOTEOPT_API int moteopt_selftest_divide(const float* a, const float* d, float* out, int64_t n, moteopt_stream_t stream);
+MOTEOPT_API int moteopt_selftest_wait_timeout(int mode, double limit_seconds, int* counter, int* status,
+                                              unsigned long long* elapsed_ns, moteopt_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -33,6 +33,7 @@ EXPORTS = (
     "moteopt_clip_grad_norm_workspace_size", "moteopt_clip_grad_norm", "moteopt_clip_grad_norm_noalloc",
     "moteopt_newton_schulz_workspace_size", "moteopt_newton_schulz",
     "moteopt_moe_update_bias",
+    "moteopt_selftest_divide", "moteopt_selftest_wait_timeout",
 )
 
 
@@ -120,6 +121,8 @@ def _load() -> C.CDLL:
         "moteopt_newton_schulz_workspace_size": (sz, [i64, i64, i64]),
         "moteopt_newton_schulz": (i32, [vp, i32, vp, i64, i64, i64, i32, dbl, vp, sz, vp]),
         "moteopt_moe_update_bias": (i32, [C.POINTER(MoeBias), i32, vp]),
+        "moteopt_selftest_divide": (i32, [vp, vp, vp, i64, vp]),
+        "moteopt_selftest_wait_timeout": (i32, [i32, dbl, vp, vp, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

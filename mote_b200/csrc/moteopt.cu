@@ -1641,3 +1641,69 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
 }
 
 }  // extern "C"
+
+// ---- self-tests of two device primitives (diagnostics; no counterpart in the reference) ---------------------------
+namespace {
+
+// out[i] = a[i] / d[i] by SharedDivisor (the normalisation's quotient: reciprocal + one Markstein correction)
+__global__ void selftest_divide_kernel(const float* a, const float* d, float* out, int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = shared_divisor(d[i]).div(a[i]);
+}
+
+// Two CTAs, one waiting thread each, on something that never completes: mode 0 a completion counter nothing adds to
+// (wait_counter, as a persistent Newton-Schulz tile waits for its inputs), mode 1 an mbarrier nothing arrives on
+// (mbar_wait, as a pipeline stage waits for its loads). CTA 0 gives up after limit_ns and records the timeout; CTA 1
+// waits with four times the limit and, in mode 0, must give up as soon as it sees CTA 0's timeout in the status
+// word, as the other CTAs of a launch do. Each CTA records how long it waited (elapsed_ns[blockIdx.x]) and, like the
+// Newton-Schulz kernel at its exit, MOTEOPT_STATUS_ABORTED when it unwound.
+__global__ void selftest_wait_kernel(int* counter, int* status, int mode, unsigned long long limit_ns,
+                                     unsigned long long* elapsed_ns) {
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const WaitCtx ctx{&abort_flag, status, blockIdx.x == 0 ? limit_ns : 4 * limit_ns};
+    const unsigned long long t0 = globaltimer_ns();
+    const bool ok = mode == 0 ? wait_counter(counter, 1, ctx) : mbar_wait(&bar, 0, ctx);
+    elapsed_ns[blockIdx.x] = globaltimer_ns() - t0;
+    if (!ok) atomicOr(status, kStatusAborted);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int moteopt_selftest_divide(const float* a, const float* d, float* out, int64_t n, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!a || !d || !out))) return fail(MOTEOPT_ERR_INVALID, "moteopt_selftest_divide: bad arguments");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  if (n == 0) return MOTEOPT_OK;
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(n, 256), 8 * sms));
+  selftest_divide_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, d, out, n);
+  MO_LAUNCHED("selftest_divide_kernel");
+  return MOTEOPT_OK;
+}
+
+int moteopt_selftest_wait_timeout(int mode, double limit_seconds, int* counter, int* status,
+                                  unsigned long long* elapsed_ns, moteopt_stream_t stream) {
+  if ((mode != 0 && mode != 1) || !counter || !status || !elapsed_ns)
+    return fail(MOTEOPT_ERR_INVALID, "moteopt_selftest_wait_timeout: bad arguments");
+  if (!(limit_seconds >= 1e-6 && limit_seconds <= 0.25))
+    return fail(MOTEOPT_ERR_INVALID, "moteopt_selftest_wait_timeout: the limit must lie in [1 us, 0.25 s]");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  selftest_wait_kernel<<<2, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      counter, status, mode, static_cast<unsigned long long>(limit_seconds * 1e9), elapsed_ns);
+  MO_LAUNCHED("selftest_wait_kernel");
+  return MOTEOPT_OK;
+}
+
+}  // extern "C"

@@ -433,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_gemm
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const WaitCtx ctx{abort_flag, L.status};
+  const WaitCtx ctx{abort_flag, L.status, kWaitLimitNs};
   if (warp == 0) {
     if (lane_id() == 0) producer(L, rank, sa, sb, full, empty, ctx);
     __syncwarp();

@@ -66,10 +66,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Shared state of one CTA's bounded waits: `abort_smem` is set by whichever role gives up first, `status` is the
-// launch's global status word.
+// launch's global status word, `limit_ns` how long one wait may take (kWaitLimitNs in the optimizer's kernels; the
+// self-test of the timeout path passes a short one).
 struct WaitCtx {
   volatile int* abort_smem;
   int* status;
+  unsigned long long limit_ns;
 };
 
 // Wait until the phase with the given parity has completed. Returns false (and marks the CTA aborted) on timeout or
@@ -82,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 31u) == 0) {
       if (*ctx.abort_smem) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > ctx.limit_ns) {
         *ctx.abort_smem = 1;
         atomicOr(ctx.status, kStatusWaitTimeout);
         return false;
@@ -136,7 +138,7 @@ __device__ __forceinline__ bool wait_counter(const int* counter, int target, con
         *ctx.abort_smem = 1;
         return false;
       }
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > ctx.limit_ns) {
         *ctx.abort_smem = 1;
         atomicOr(ctx.status, kStatusWaitTimeout);
         return false;

@@ -40,8 +40,9 @@ def _lr(v) -> float:
 class Muon(_MuonBase):
     """Nesterov momentum + batched Newton-Schulz orthogonalisation + RMS-matched scale + decoupled (or Muon-SW)
     weight decay, with per-parameter `param_lr` overrides (mote/train/muon.py:46-100). Every matrix of every group
-    is orthogonalised in one batched tcgen05 launch sequence; the parameter update is fused into the last
-    Newton-Schulz launch. State: `momentum_buffer` (fp32, the parameter's shape) per parameter."""
+    is orthogonalised in one batched tcgen05 launch sequence; the decay and the scaled update are then applied in
+    one memory-bound pass over every parameter (muon.py:93-99). State: `momentum_buffer` (fp32, the parameter's
+    shape) per parameter."""
 
     def __init__(self, params, lr: float = 1e-3, momentum: float = 0.95, nesterov: bool = True,
                  weight_decay: float = 0.0, ns_steps: int = 5, rms_scale: float = 0.2, sw_decay: bool = False,
@@ -174,6 +175,13 @@ class MultiOpt:
             o.zero_grad(set_to_none=set_to_none)
 
     def step(self):
+        """train.py:64-66 (AdamW.step(), then Muon.step()). When every optimizer is this module's AdamW or Muon and
+        their groups can share one launch sequence (one ns_steps / rms_scale over the Muon groups, one betas / eps
+        over the AdamW groups), both run as ONE library call (fused_step without a clip or divisor), which gives
+        the same bits as the two separate steps; otherwise each optimizer steps in turn."""
+        if _fusable(self.opts):
+            fused_step(self)
+            return
         for o in self.opts:
             o.step()
 
@@ -183,6 +191,19 @@ class MultiOpt:
     def load_state_dict(self, sd):
         for o, s in zip(self.opts, sd["multi"]):
             o.load_state_dict(s)
+
+
+def _fusable(opts) -> bool:
+    """Whether fused_step can run these optimizers as one library call."""
+    muon_keys, adam_keys = set(), set()
+    for o in opts:
+        if isinstance(o, Muon):
+            muon_keys.update((int(g["ns_steps"]), float(g["rms_scale"])) for g in o.param_groups)
+        elif isinstance(o, AdamW):
+            adam_keys.update((tuple(float(b) for b in g["betas"]), float(g["eps"])) for g in o.param_groups)
+        else:
+            return False
+    return len(muon_keys) <= 1 and len(adam_keys) <= 1
 
 
 def set_lr(opt, lr: float):

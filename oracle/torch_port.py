@@ -96,14 +96,15 @@ def muon_update(params: Sequence[torch.Tensor], bufs: List[Optional[torch.Tensor
 
 
 @torch.no_grad()
-def optimizer_step(adam: torch.optim.Optimizer, muon_params: Sequence[torch.Tensor],
+def optimizer_step(adam: Optional[torch.optim.Optimizer], muon_params: Sequence[torch.Tensor],
                    muon_bufs: List[Optional[torch.Tensor]], all_params: Sequence[torch.Tensor], *, divisor,
-                   max_norm: float, muon_kw: dict) -> torch.Tensor:
+                   max_norm: Optional[float], muon_kw: dict) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947: grads /= divisor, clip_grad_norm_(all params), AdamW step, Muon step. Returns the
-    pre-clip total norm."""
+    pre-clip total norm. A workload without AdamW params passes adam=None; max_norm=None skips the clip."""
     grads = [p.grad for p in all_params if p.grad is not None]
     torch._foreach_div_(grads, divisor)
-    total = torch.nn.utils.clip_grad_norm_(all_params, max_norm)
-    adam.step()
+    total = torch.nn.utils.clip_grad_norm_(all_params, max_norm) if max_norm is not None else None
+    if adam is not None:
+        adam.step()
     muon_update(muon_params, muon_bufs, **muon_kw)
     return total

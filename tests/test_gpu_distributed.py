@@ -140,3 +140,140 @@ def test_two_gpu_sharded_step_matches_single_gpu(tmp_path):
         got = r0["pa"][o:o + p.numel()].reshape(s)
         ref = p.cpu().numpy()
         assert np.allclose(got, ref, rtol=1e-5, atol=1e-8), i
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# N = 2, 4, 8 GPUs: the sharded step bit for bit against one GPU, and the sharded checkpoint round trip over NCCL
+def _grid_workload():
+    from mote_b200 import configs
+    return configs.Workload("dist_grid_test", [(256, 256)] * 5 + [(256, 1024), (1024, 256), (2, 128, 384), (384, 640)],
+                            [(271, 64)], [(64,)] * 5)
+
+
+def _grid_grads(w, rank, step):
+    """fp32 grads on the 2^-20 grid with |g| < 2^-10: a sum over up to 8 ranks is exact in fp32 in any order, so
+    NCCL's reduction order cannot change a bit and one GPU can reproduce the reduced grads exactly."""
+    rng = np.random.default_rng([77, rank, step])
+    out = []
+    for s in list(w.adam_shapes) + list(w.muon_shapes):
+        out.append((rng.integers(-1023, 1024, size=s).astype(np.float32) * np.float32(2.0 ** -20)))
+    return out[: len(w.adam_shapes)], out[len(w.adam_shapes):]
+
+
+def _grid_rank(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        from mote_b200 import configs
+        from mote_b200.distributed import ShardedStep, cuda_compute, make_plan
+        w = _grid_workload()
+        plan = make_plan(w.muon_shapes, w.adam_shapes, world)
+        inp = configs.make_params(w, seed=5)
+        nd = len(w.adam_decay_shapes)
+        wds = [w.adam_wd if i < nd else 0.0 for i in range(len(w.adam_shapes))]
+
+        def new_step(pm, pa):
+            gm = torch.zeros(plan.muon_len, device=dev)
+            ga = torch.zeros(plan.adam_len, device=dev)
+            return ShardedStep(plan, rank, pm, pa, gm, ga, cuda_compute(betas=w.betas), muon_lr=w.muon_lr,
+                               muon_wd=w.muon_wd, adam_lr=w.adam_lr, adam_wd=wds)
+
+        def load_grads(st, step):
+            ag, mg = _grid_grads(w, rank, step)
+            for i, g in enumerate(mg):
+                st.muon_view(st.gm, i).copy_(torch.from_numpy(g))
+            for i, g in enumerate(ag):
+                st.adam_view(st.ga, i).copy_(torch.from_numpy(g))
+
+        pm = torch.zeros(plan.muon_len, device=dev)
+        pa = torch.zeros(plan.adam_len, device=dev)
+        st = new_step(pm, pa)
+        for i, p in enumerate(inp.muon_params):
+            st.muon_view(pm, i).copy_(torch.from_numpy(p))
+        for i, p in enumerate(inp.adam_params):
+            st.adam_view(pa, i).copy_(torch.from_numpy(p))
+        st.enable_peer_updates()   # the bench's exchange: every owner's update read over NVLink
+        for step in range(2):
+            load_grads(st, step)
+            st.step(max_norm=None)
+        sd = st.state_dict()       # collective: the ZeRO-1 slices and the owners' momentum buffers, gathered
+        # resume: a fresh step object on copies of the params takes the checkpoint (NCCL all-gather exchange)
+        st2 = new_step(pm.clone(), pa.clone())
+        st2.load_state_dict(sd)
+        for s in (st, st2):
+            load_grads(s, 2)
+            s.step(max_norm=None)
+        torch.cuda.synchronize()
+        sd3 = st.state_dict()
+        sd3b = st2.state_dict()
+        st.close()
+        flat = {"pm": pm.cpu().numpy(), "pa": pa.cpu().numpy(), "pm2": st2.pm.cpu().numpy(), "pa2": st2.pa.cpu().numpy(),
+                "moff": np.array(plan.muon_off), "aoff": np.array(plan.adam_off)}
+        for tag, d in (("sd2", sd), ("sd3", sd3), ("sd3b", sd3b)):
+            adam_sd, muon_sd = d["multi"]
+            for g in adam_sd["param_groups"]:
+                for k, i in zip(g["params"], g["plan_index"]):
+                    flat[f"{tag}_m{i}"] = adam_sd["state"][k]["exp_avg"].cpu().numpy()
+                    flat[f"{tag}_v{i}"] = adam_sd["state"][k]["exp_avg_sq"].cpu().numpy()
+                    flat[f"{tag}_step{i}"] = np.array(float(adam_sd["state"][k]["step"]))
+            for i in range(len(w.muon_shapes)):
+                flat[f"{tag}_b{i}"] = muon_sd["state"][i]["momentum_buffer"].cpu().numpy()
+        np.savez(os.path.join(out, f"grid_r{rank}.npz"), **flat)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_step_and_checkpoint_bitwise_against_one_gpu(tmp_path, world):
+    """`world` ranks over NCCL (peer-read exchange), 3 steps without clip on exact-grid fp32 grads: every rank holds
+    the same params, and they equal one GPU's optimizer_step on the summed grads bit for bit; the sharded
+    checkpoint after step 2 (ShardedStep.state_dict, train.py:68-73's {"multi": [adamw, muon]} layout) equals that
+    GPU's optimizer state bit for bit, and a fresh ShardedStep that loads it continues bit for bit (step 3)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from mote_b200 import configs
+    from mote_b200.functional import AdamWItem, MuonItem, optimizer_step
+    mp.spawn(_grid_rank, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    rs = [np.load(tmp_path / f"grid_r{r}.npz") for r in range(world)]
+    for r in rs[1:]:
+        for key in rs[0].files:
+            assert np.array_equal(r[key], rs[0][key]), key
+    r0 = rs[0]
+    assert np.array_equal(r0["pm2"], r0["pm"]) and np.array_equal(r0["pa2"], r0["pa"])   # the resumed step
+    # one GPU on the summed grads
+    w = _grid_workload()
+    dev = torch.device("cuda", 0)
+    inp = configs.make_params(w, seed=5)
+    mps = [torch.from_numpy(p).to(dev) for p in inp.muon_params]
+    aps = [torch.from_numpy(p).to(dev) for p in inp.adam_params]
+    mb = [torch.zeros_like(p) for p in mps]
+    am, av = [torch.zeros_like(p) for p in aps], [torch.zeros_like(p) for p in aps]
+    nd = len(w.adam_decay_shapes)
+    snap = {}
+    for step in range(3):
+        gs = [_grid_grads(w, r, step) for r in range(world)]
+        ag = [torch.from_numpy(sum(g[0][i] for g in gs)).to(dev) for i in range(len(aps))]
+        mg = [torch.from_numpy(sum(g[1][i] for g in gs)).to(dev) for i in range(len(mps))]
+        optimizer_step([MuonItem(p, g, b, w.muon_lr, w.muon_lr * w.muon_wd) for p, g, b in zip(mps, mg, mb)],
+                       [AdamWItem(p, g, m, v, w.adam_lr, w.adam_wd if i < nd else 0.0, step + 1)
+                        for i, (p, g, m, v) in enumerate(zip(aps, ag, am, av))], betas=w.betas)
+        if step == 1:
+            snap = {"m": [x.cpu().numpy() for x in am], "v": [x.cpu().numpy() for x in av],
+                    "b": [x.cpu().numpy() for x in mb]}
+    for tag, ref in (("sd2", snap), ("sd3", {"m": [x.cpu().numpy() for x in am], "v": [x.cpu().numpy() for x in av],
+                                             "b": [x.cpu().numpy() for x in mb]})):
+        for i in range(len(aps)):
+            assert np.array_equal(r0[f"{tag}_m{i}"], ref["m"][i]), (tag, "exp_avg", i)
+            assert np.array_equal(r0[f"{tag}_v{i}"], ref["v"][i]), (tag, "exp_avg_sq", i)
+            assert float(r0[f"{tag}_step{i}"]) == (2.0 if tag == "sd2" else 3.0)
+        for i in range(len(mps)):
+            assert np.array_equal(r0[f"{tag}_b{i}"], ref["b"][i]), (tag, "momentum_buffer", i)
+            assert np.array_equal(r0[f"sd3b_b{i}"], r0[f"sd3_b{i}"])
+    for i, (p, s) in enumerate(zip(mps, w.muon_shapes)):
+        o = int(r0["moff"][i])
+        assert np.array_equal(r0["pm"][o:o + p.numel()].reshape(s), p.cpu().numpy()), ("muon param", i)
+    for i, (p, s) in enumerate(zip(aps, w.adam_shapes)):
+        o = int(r0["aoff"][i])
+        assert np.array_equal(r0["pa"][o:o + p.numel()].reshape(s), p.cpu().numpy()), ("adamw param", i)

@@ -233,3 +233,33 @@ def test_state_dict_layout_matches_the_reference(dev):
     for k in ("lr", "momentum", "nesterov", "weight_decay", "ns_steps", "rms_scale", "sw_decay", "lr_max", "lr_mult", "stage"):
         assert k in g
     assert g["sw_decay"] is True
+
+
+def test_multiopt_step_is_one_library_call_with_the_separate_steps_bits(dev, monkeypatch):
+    """MultiOpt.step (train.py:64-66) over this package's AdamW + Muon runs as one library call (one optimizer_step:
+    AdamW, then Muon), and gives the same bits as AdamW.step() followed by Muon.step(), over 3 steps."""
+    from mote_b200 import build_optimizer
+    from mote_b200 import functional as F
+    m1, m2 = _tiny_model(dev), _tiny_model(dev)
+    o1 = build_optimizer(m1, 1e-2, 0.1, [2.0, 1.0], optimizer="muonsw")
+    o2 = build_optimizer(m2, 1e-2, 0.1, [2.0, 1.0], optimizer="muonsw")
+    calls = {"step": 0, "adamw": 0, "muon": 0}
+    real = F.optimizer_step
+
+    def counting(*a, **k):
+        calls["step"] += 1
+        return real(*a, **k)
+    monkeypatch.setattr(F, "optimizer_step", counting)
+    for step in range(3):
+        _grads(m1, step)
+        _grads(m2, step)
+        o1.step()
+        for o in o2.opts:   # the two optimizers one after the other, as the reference's MultiOpt steps them
+            o.step()
+    assert calls["step"] == 3
+    for p, q in zip(m1.parameters(), m2.parameters()):
+        assert torch.equal(p, q)
+    for s1, s2 in zip(o1.state_dict()["multi"], o2.state_dict()["multi"]):
+        for k in s1["state"]:
+            for name, t in s1["state"][k].items():
+                assert torch.equal(t, s2["state"][k][name]), (k, name)

@@ -54,20 +54,21 @@ def test_c1_issued_work_and_tiles():
 
 
 def test_step_roofline_formula():
-    import bench
+    from mote_b200.measure import step_roofline
     peaks = {"hbm_gbs": 6500.0, "bf16_tflops": 1600.0, "bf16_tflops_sustained": 1400.0}
-    r = bench.step_roofline(1.727e12, 1.877e9, 0.0, peaks, ms=2.0)
+    r = step_roofline(1.727e12, 1.877e9, 0.0, peaks, ms=2.0)
     assert r["sustained"]["roofline_ms"] == pytest.approx(1.727e12 / 1.4e15 * 1e3, rel=1e-3)   # FLOP-bound
     assert r["burst"]["frac"] == pytest.approx(1.727e12 / 1.6e15 * 1e3 / 2.0, rel=1e-3)
     # an exchange adds its NVLink time (770 GB/s per direction) on top of the slower of the two bounds
-    r = bench.step_roofline(1e9, 6.5e9, 0.77e9, peaks, ms=2.0)
+    r = step_roofline(1e9, 6.5e9, 0.77e9, peaks, ms=2.0)
     assert r["sustained"]["roofline_ms"] == pytest.approx(1.0 + 1.0, rel=1e-3)
 
 
 @pytest.mark.parametrize("config", ["c0", "c4_small"])
 def test_reference_arm_line(config, monkeypatch):
-    """`bench.py --impl reference`: the reference's own torch step on the host (oracle/torch_port.py), one JSON line
-    with the contract's keys; a workload without Muon matrices samples its clip + AdamW step instead."""
+    """`bench.py --impl reference`: the reference's own torch step on the host (oracle/torch_port.py), whole steps,
+    one JSON line with the contract's keys and the same `config` dict as the library's line for that workload; a
+    workload without Muon matrices times its clip + AdamW step."""
     import argparse
 
     import bench
@@ -80,15 +81,22 @@ def test_reference_arm_line(config, monkeypatch):
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     cb = line["cpu_baseline"]
     assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["value"] == line["value"] and "torch_port" in cb["sample"]
+    assert "4 whole steps" in cb["sample"]
+    from mote_b200.measure import bench_config
+    assert line["config"] == bench_config(configs.CONFIGS[config](), 1)
 
 
-def test_cpu_baseline_sample_sums_every_stack_kind():
+def test_cpu_baseline_times_whole_reference_steps():
+    """The GPU arm's cpu_baseline: whole reference steps over every Muon param and AdamW tensor of the workload,
+    whose momentum buffers and AdamW state exist after the step (every tensor was stepped)."""
     import bench
     w = configs.c0()
-    cb = bench.cpu_baseline_sample(w)
+    cb = bench.cpu_baseline_sample(w, steps=2)
+    assert cb["value"] > 0 and cb["unit"] == "ms/step" and cb["kind"] == "port" and "2 whole steps" in cb["sample"]
     ref = bench.TorchReference(w)
-    assert sum(c * len(k) for k, c in ref.counts.items()) == len(w.muon_shapes)   # every Muon param in one stack
-    assert cb["value"] > 0 and cb["unit"] == "ms/step" and cb["kind"] == "port"
+    ref.time_step()
+    assert all(b is not None for b in ref.bufs) and len(ref.bufs) == len(w.muon_shapes)
+    assert all(len(ref.adam.state[p]) == 3 for p in ref.adam_p)
 
 
 def test_reference_arm_under_torchrun_prints_on_rank_zero_only():

@@ -14,8 +14,6 @@ import numpy as np
 import pytest
 import torch
 
-pytestmark = pytest.mark.gpu
-
 
 def _grads(dev, seed, dt):
     rng = np.random.default_rng(seed)
@@ -35,6 +33,7 @@ def _call(lib, fn, grads, max_norm, out, ws=None):
                                       C.c_void_p(ws.data_ptr()), ws.numel(), stream)
 
 
+@pytest.mark.gpu
 def test_noalloc_clip_matches_the_workspace_entry_point_twice_in_a_row():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
@@ -59,7 +58,26 @@ def test_noalloc_clip_matches_the_workspace_entry_point_twice_in_a_row():
             assert torch.equal(x, y)
 
 
+@pytest.mark.gpu
+def test_noalloc_clip_reports_a_nonfinite_norm_through_out_norm():
+    """A NaN grad: the call has no status word for moteopt_read_status, so the non-finite norm shows as a NaN
+    out_norm, and the grads are scaled by torch's coefficient for it (NaN), as the workspace entry point does."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from mote_b200 import _lib
+    lib = _lib.lib
+    dev = torch.device("cuda", 0)
+    a = _grads(dev, 3, torch.float32)
+    a[1][4] = float("nan")
+    out = torch.zeros((), device=dev)
+    assert _call(lib, "noalloc", a, 1.0, out) == 0, lib.moteopt_last_error()
+    torch.cuda.synchronize()
+    assert np.isnan(out.item())
+    assert all(bool(torch.isnan(g).all()) for g in a)
+
+
 def test_noalloc_clip_rejects_more_than_its_scratch_holds():
+    """The size check runs on the host before any device work, so this runs without a GPU too."""
     from mote_b200 import _lib
     lib = _lib.lib
     n = 1
