@@ -241,7 +241,7 @@ MOTEOPT_API int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels
  *      point of the call: a host runtime with its own memory pool that forbids outside allocations, a region where
  *      allocation would break stream ordering, or a C caller without an allocator of its own. Limit: the grads'
  *      element counts, each rounded up to a multiple of 16384, may sum to at most 65536 x 16384 (2^30) elements,
- *      and n <= 4096; beyond that it returns MOTEOPT_ERR_LIMIT and does nothing. The array (256 KB + 256 B) lives on
+ *      and n <= 4096; beyond that it returns MOTEOPT_ERR_LIMIT and does nothing. The array (512 KB + 256 B) lives on
  *      every device that loads the library until the process exits. The first call on a device looks up the
  *      array's device address; make that first call before any CUDA graph capture on that device. Calls share the
  *      array: calls that can overlap on the GPU (different streams without ordering, or several host threads) race

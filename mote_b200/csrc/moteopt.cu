@@ -258,9 +258,9 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
   }
   size_t off = kHeaderBytes;
   L->off_norm = off;
-  off = align_up(off + 4 * static_cast<size_t>(L->norm_tensor_chunk_start.back()), 256);
+  off = align_up(off + sizeof(double) * static_cast<size_t>(L->norm_tensor_chunk_start.back()), 256);
   L->off_mom = off;
-  off = align_up(off + 4 * static_cast<size_t>(L->mat_chunk_start.back()), 256);
+  off = align_up(off + sizeof(double) * static_cast<size_t>(L->mat_chunk_start.back()), 256);
   L->off_den = off;
   off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 256);
   L->off_done = off;   // persistent Newton-Schulz: per matrix of a launch set and phase, completion arrivals
@@ -271,7 +271,7 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
     L->param_apply_start.push_back(L->param_apply_start.back() + static_cast<int>(b * apply_partials_per_slice(r, c)));
   }
   L->off_apply = off;
-  off = align_up(off + 4 * static_cast<size_t>(L->param_apply_start.back()), 1024);
+  off = align_up(off + sizeof(double) * static_cast<size_t>(L->param_apply_start.back()), 1024);
   for (GroupPlan& g : L->groups) {
     const size_t cnt = g.mats.size();
     const size_t xb = cnt * g.m * g.n * 2, ab = cnt * g.m * g.m * 2;
@@ -347,7 +347,7 @@ struct GradSource {          // one tensor of the global grad norm
   int dtype;
 };
 
-int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chunk_start, float* partials, bool has_div,
+int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chunk_start, double* partials, bool has_div,
                  float div, int sms, cudaStream_t st) {
   SumsqArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -372,7 +372,7 @@ int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chu
 }
 
 // per-matrix ||u||_F + eps from the sum-of-squares partials
-int launch_denoms(const Layout& L, const float* partials, float* den, float eps, cudaStream_t st) {
+int launch_denoms(const Layout& L, const double* partials, float* den, float eps, cudaStream_t st) {
   const int nm = static_cast<int>(L.mat_chunk_start.size()) - 1;
   DenomArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -390,7 +390,7 @@ int launch_denoms(const Layout& L, const float* partials, float* den, float eps,
   return MOTEOPT_OK;
 }
 
-int launch_finalize(const std::vector<int>& tensor_chunk_start, const float* partials, bool clip, double max_norm,
+int launch_finalize(const std::vector<int>& tensor_chunk_start, const double* partials, bool clip, double max_norm,
                     float* out, int* status, cudaStream_t st) {
   const int n = static_cast<int>(tensor_chunk_start.size()) - 1;
   if (n > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "more than 4096 tensors in one grad-norm call");
@@ -569,7 +569,7 @@ int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cud
 int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg, const Layout& L, char* ws,
              bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st) {
   if (n == 0) return MOTEOPT_OK;
-  float* mom_partials = reinterpret_cast<float*>(ws + L.off_mom);
+  double* mom_partials = reinterpret_cast<double*>(ws + L.off_mom);
   // flatten the matrices in group-major order
   struct Mat {
     const moteopt_muon_param* p;
@@ -818,7 +818,7 @@ std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const mo
 int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int src,
               cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0, float* norms = nullptr,
               const double* lr_dev = nullptr, const double* wd = nullptr, const double* lr_max = nullptr) {
-  float* apply_partials = reinterpret_cast<float*>(ws + L.off_apply);
+  double* apply_partials = reinterpret_cast<double*>(ws + L.off_apply);
   const std::vector<ns::MatApply> tab = muon_apply_table(P, cfg, L);
   static thread_local OutArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -833,7 +833,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       const moteopt_muon_param& pp = P[ref.src];
       float* e = nullptr;   // this matrix's slice of its param's EMA
       if (ema != nullptr && ema[ref.src] != nullptr) e = ema[ref.src] + static_cast<int64_t>(ref.slice) * pp.rows * pp.cols;
-      float* part = norms == nullptr ? nullptr
+      double* part = norms == nullptr ? nullptr
                                      : apply_partials + L.param_apply_start[ref.src] +
                                            static_cast<int64_t>(ref.slice) * apply_partials_per_slice(pp.rows, pp.cols);
       if (stored_as_iterated(g)) {
@@ -1012,7 +1012,7 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     for (int i = 0; i < n_adam; ++i) src.push_back(GradSource{adam[i].grad, adam[i].numel, adam[i].grad_dtype});
     for (int i = 0; i < n_muon; ++i)
       src.push_back(GradSource{muon[i].grad, muon[i].batch * muon[i].rows * muon[i].cols, muon[i].grad_dtype});
-    float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+    double* partials = reinterpret_cast<double*>(ws + L.off_norm);
     MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, div, sms, st));
     MO_TRY(launch_finalize(L.norm_tensor_chunk_start, partials, true, gcfg->max_norm, &hdr->norm, status, st));
     coef = &hdr->coef;
@@ -1185,7 +1185,7 @@ size_t moteopt_muon_apply_workspace_size(const moteopt_muon_param* muon, int n) 
   if (n < 0 || (n > 0 && muon == nullptr)) return 0;
   int64_t chunks = 0;
   for (int i = 0; i < n; ++i) chunks += cdiv(std::max<int64_t>(muon[i].batch * muon[i].rows * muon[i].cols, 0), kChunk);
-  return sizeof(Header) + static_cast<size_t>(std::max<int64_t>(chunks, 1)) * sizeof(float);   // header, partials
+  return sizeof(Header) + static_cast<size_t>(std::max<int64_t>(chunks, 1)) * sizeof(double);   // header, partials
 }
 
 int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_muon_config* cfg,
@@ -1198,10 +1198,10 @@ int moteopt_muon_apply_ex(const moteopt_muon_param* muon, int n, const moteopt_m
   int sms = 0;
   MO_TRY(device_setup(&sms));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  float* partials = nullptr;
+  double* partials = nullptr;
   if (norms != nullptr && n > 0) {
     MO_TRY(check_ws(workspace, workspace_bytes, moteopt_muon_apply_workspace_size(muon, n)));
-    partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + sizeof(Header));   // the header stays intact
+    partials = reinterpret_cast<double*>(static_cast<char*>(workspace) + sizeof(Header));   // the header stays intact
   }
   std::vector<FlatOutSeg> segs;
   std::vector<int> start(1, 0);
@@ -1294,7 +1294,7 @@ int moteopt_grad_sumsq(const void* const* grads, const int64_t* numels, const in
   char* ws = static_cast<char*>(workspace);
   std::vector<GradSource> src;
   for (int i = 0; i < n; ++i) src.push_back(GradSource{grads[i], numels[i], dtypes[i]});
-  float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+  double* partials = reinterpret_cast<double*>(ws + L.off_norm);
   const bool has_div = grad_divisor != 0.0 && grad_divisor != 1.0;
   MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, has_div ? static_cast<float>(grad_divisor) : 1.f,
                       sms, st));
@@ -1400,7 +1400,7 @@ int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int*
   MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
   std::vector<GradSource> src;
   for (int i = 0; i < n; ++i) src.push_back(GradSource{grads[i], numels[i], dtypes[i]});
-  float* partials = reinterpret_cast<float*>(ws + L.off_norm);
+  double* partials = reinterpret_cast<double*>(ws + L.off_norm);
   r = launch_sumsq(src, L.norm_tensor_chunk_start, partials, false, 1.0f, sms, st);
   if (r != MOTEOPT_OK) return r;
   r = launch_finalize(L.norm_tensor_chunk_start, partials, true, max_norm, &hdr->norm, &hdr->status, st);
@@ -1425,14 +1425,14 @@ int moteopt_clip_grad_norm(void* const* grads, const int64_t* numels, const int*
 }
 
 // ---- clip_grad_norm_ without a caller-provided workspace ------------------------------------------------------
-// Scratch of moteopt_clip_grad_norm_noalloc: one fp32 sum of squares per 16K-element chunk plus a 256-byte header
+// Scratch of moteopt_clip_grad_norm_noalloc: one fp64 sum of squares per 16K-element chunk plus a 256-byte header
 // (status, norm, clip coefficient), in a file-scope device array. Every device that loads this library holds it
-// (256 KB + 256 B) until the process exits; all calls on a device share it.
+// (512 KB + 256 B) until the process exits; all calls on a device share it.
 }  // extern "C"
 
 namespace {
 constexpr int kNoAllocMaxChunks = 65536;   // 65536 x 16384 = 2^30 grad elements per call
-constexpr size_t kNoAllocBytes = kHeaderBytes + sizeof(float) * static_cast<size_t>(kNoAllocMaxChunks);
+constexpr size_t kNoAllocBytes = kHeaderBytes + sizeof(double) * static_cast<size_t>(kNoAllocMaxChunks);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
@@ -1479,7 +1479,7 @@ int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, co
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(scratch);
   Header* hdr = reinterpret_cast<Header*>(ws);
-  float* partials = reinterpret_cast<float*>(ws + kHeaderBytes);
+  double* partials = reinterpret_cast<double*>(ws + kHeaderBytes);
   // the header carries the previous call's status bits: clear it (every partial is overwritten)
   MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
   // fixed-size argument blocks on the stack: no host or device allocation on this path
@@ -1566,7 +1566,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
       gofm.push_back(&g);
       posm.push_back(static_cast<int>(k));
     }
-  float* partials = reinterpret_cast<float*>(ws + L.off_mom);
+  double* partials = reinterpret_cast<double*>(ws + L.off_mom);
   r = launch_sumsq(src, L.mat_chunk_start, partials, false, 1.0f, sms, st);
   if (r != MOTEOPT_OK) return r;
   float* den = reinterpret_cast<float*>(ws + L.off_den);

@@ -38,22 +38,80 @@ __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_c
 __device__ __forceinline__ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 __device__ __forceinline__ bool g_vec_ok(const void* g, int dt) { return dt == kBF16 ? aligned8(g) : aligned16(g); }
 
-// a / d rounded to nearest, for a divisor shared by many numerators: with r = RN(1/d), q = RN(a*r) and the exact
-// residual e = a - q*d (one fma), RN(q + e*r) is the correctly rounded quotient (Markstein's correction step, "Computation
-// of elementary functions on the IBM RISC System/6000 processor", 1990). Checked bit for bit against IEEE division
-// on 2^30 numerator/denominator pairs of the ranges the optimizer divides (norms 1e-6..1e4, entries 1e-9..10).
+// a / d rounded to nearest (ties to even), for a divisor shared by many numerators. With r = RN(1/d), q = RN(a*r) and
+// the residual e = a - q*d (one fma), RN(q + e*r) is the correctly rounded quotient (Markstein's correction step,
+// "Computation of elementary functions on the IBM RISC System/6000 processor", 1990), provided the residual is exact
+// and nothing under- or overflows: |a| >= 2^-80, 2^-100 <= |q| < 2^126 and 2^-100 <= d < 2^100 (the common case:
+// the optimizer divides entries of 1e-9..10 by norms of 1e-7..1e4). Every other numerator is rare and takes an exact
+// inline path, no call: a = m 2^ea with |m| in [0.5, 1) and d = dm 2^ed with dm in [1, 2), so q' = RN(m / dm) by the
+// same correction lies in (0.25, 1); the quotient is q' 2^(ea-ed) scaled back with one rounding (overflow gives Inf,
+// underflow a subnormal or zero), and where that rounding falls exactly on a midpoint of the subnormal grid the
+// residual's sign picks the neighbour the exact quotient lies toward. Zeros, Inf and NaN numerators give a * r, which
+// is IEEE's a / d for them. Defined for every positive finite d; d = 0, Inf or NaN also give a * r (IEEE's result).
+// tests/test_gpu_selftest.py holds it against IEEE division bit for bit: the optimizer's ranges, their edges, tiny
+// and subnormal numerators, divisors across the whole exponent range, and special values.
+__device__ __forceinline__ float pow2f(int n) {   // 2^n for n in [-149, 127], exactly
+  return n >= -126 ? __uint_as_float(static_cast<uint32_t>(n + 127) << 23) : __uint_as_float(1u << (n + 149));
+}
+// x (|x| in (0.25, 1]) times 2^n, rounded once
+__device__ __forceinline__ float scale_once(float x, int n) {
+  if (n > 191) return copysignf(__int_as_float(0x7f800000), x);
+  if (n > 127) return __fmul_rn(__fmul_rn(x, 0x1p64f), pow2f(n - 64));
+  if (n >= -126) return __fmul_rn(x, pow2f(n));
+  if (n >= -152) return __fmul_rn(__fmul_rn(x, pow2f(n + 64)), 0x1p-64f);
+  return copysignf(0.f, x);   // |x 2^n| < 2^-152: below half the smallest subnormal
+}
+// a finite nonzero float as m 2^e with |m| in [0.5, 1) (bias 126) or [1, 2) (bias 127)
+__device__ __forceinline__ float split_exp(float a, int bias, int* e) {
+  uint32_t u = __float_as_uint(a);
+  int shift = 0;
+  if (((u >> 23) & 0xffu) == 0u) {   // subnormal: scale into the normal range first (exact)
+    u = __float_as_uint(__fmul_rn(a, 0x1p64f));
+    shift = 64;
+  }
+  *e = static_cast<int>((u >> 23) & 0xffu) - bias - shift;
+  return __uint_as_float((u & 0x807fffffu) | (static_cast<uint32_t>(bias) << 23));
+}
 struct SharedDivisor {
-  float d, r;
+  float d, r;     // d and RN(1/d)
+  float dm, rm;   // d = dm 2^ed with dm in [1, 2), and RN(1/dm)
+  int ed;
+  bool fast_d;    // 2^-100 <= d < 2^100
+  bool finite;    // d is positive and finite
+  __device__ __forceinline__ float div_rare(float a) const {
+    int ea;
+    const float m = split_exp(a, 126, &ea);
+    const float q1 = __fmul_rn(m, rm);
+    const float qm = fmaf(fmaf(-q1, dm, m), rm, q1);   // RN(m / dm), in (0.25, 1)
+    const float em = fmaf(-qm, dm, m);                  // exact: m / dm - qm has the sign of em
+    const int n = ea - ed;
+    float v = scale_once(qm, n);
+    if (fabsf(v) < 0x1p-126f && em != 0.f && n >= -152) {
+      const float w = __fmul_rn(qm, pow2f(n + 149));   // the quotient in units of 2^-149, exact
+      if (fabsf(w - truncf(w)) == 0.5f) v = __fmul_rn(em > 0.f ? ceilf(w) : floorf(w), 0x1p-149f);
+    }
+    return v;
+  }
   __device__ __forceinline__ float div(float a) const {
     const float q = __fmul_rn(a, r);
-    const float e = fmaf(-q, d, a);
-    return fmaf(e, r, q);
+    if (fast_d && fabsf(a) >= 0x1p-80f && fabsf(q) >= 0x1p-100f && fabsf(q) < 0x1p126f) {
+      const float e = fmaf(-q, d, a);
+      return fmaf(e, r, q);
+    }
+    if (a == 0.f || !finite || !(fabsf(a) <= 0x1.fffffep127f)) return q;
+    return div_rare(a);
   }
 };
 __device__ __forceinline__ SharedDivisor shared_divisor(float den) {
   SharedDivisor s;
   s.d = den;
   s.r = __frcp_rn(den);
+  s.finite = den > 0.f && den <= 0x1.fffffep127f;
+  s.fast_d = den >= 0x1p-100f && den < 0x1p100f;
+  s.ed = 0;
+  s.dm = 1.f;
+  if (s.finite) s.dm = split_exp(den, 127, &s.ed);
+  s.rm = __frcp_rn(s.dm);
   return s;
 }
 
@@ -70,14 +128,14 @@ struct GradXform {
   }
 };
 
-// Sum of a per-thread fp32 value over the block, in a fixed order. Result valid in thread 0.
-__device__ __forceinline__ float block_sum(float v, float* red) {
+// Sum of a per-thread fp64 value over the block, in a fixed order. Result valid in thread 0.
+__device__ __forceinline__ double block_sum(double v, double* red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5;
   if ((threadIdx.x & 31) == 0) red[w] = v;
   __syncthreads();
-  float s = 0.f;
+  double s = 0.0;
   if (threadIdx.x == 0) {
     for (int k = 0; k < static_cast<int>(blockDim.x >> 5); ++k) s += red[k];
   }
@@ -85,31 +143,39 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
+// acc + x^2 in fp64. The square of an fp32 value is exact in fp64 (48 significant bits), so a sum of squares
+// accumulated this way is off the exact sum by ~1e-16 relative: sqrt of it, rounded to fp32, is the correctly
+// rounded Frobenius norm (a fp64 -> fp32 rounding of a correctly rounded fp64 sqrt is innocuous, 53 >= 2 * 24 + 2).
+__device__ __forceinline__ double sqacc(float x, double acc) {
+  const double d = static_cast<double>(x);
+  return fma(d, d, acc);
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // sum of squares of (g / div) per chunk. A full, 16-byte aligned chunk is read with all of a thread's 16-byte loads
 // issued before the first is used (128 B in flight per thread); ragged chunks fall back to element loads. The order of
 // the per-thread sum is fixed either way.
-__device__ __forceinline__ float sq_acc2_bf16(uint32_t w, const GradXform& X, float acc) {
+__device__ __forceinline__ double sq_acc2_bf16(uint32_t w, const GradXform& X, double acc) {
   const float a = X(bf16_lo(w)), b = X(bf16_hi(w));
-  acc = fmaf(a, a, acc);
-  return fmaf(b, b, acc);
+  acc = sqacc(a, acc);
+  return sqacc(b, acc);
 }
-__device__ __forceinline__ float sq_acc8_bf16(const uint4& v, const GradXform& X, float acc) {
+__device__ __forceinline__ double sq_acc8_bf16(const uint4& v, const GradXform& X, double acc) {
   acc = sq_acc2_bf16(v.x, X, acc);
   acc = sq_acc2_bf16(v.y, X, acc);
   acc = sq_acc2_bf16(v.z, X, acc);
   return sq_acc2_bf16(v.w, X, acc);
 }
-__device__ __forceinline__ float sq_acc4_f32(const float4& v, const GradXform& X, float acc) {
+__device__ __forceinline__ double sq_acc4_f32(const float4& v, const GradXform& X, double acc) {
   const float a = X(v.x), b = X(v.y), d = X(v.z), e = X(v.w);
-  acc = fmaf(a, a, acc); acc = fmaf(b, b, acc); acc = fmaf(d, d, acc); acc = fmaf(e, e, acc);
+  acc = sqacc(a, acc); acc = sqacc(b, acc); acc = sqacc(d, acc); acc = sqacc(e, acc);
   return acc;
 }
 
 // kDiv: whether the grads are divided first; the division (a call on its slow path) is compiled only where used, so
 // the common path keeps all of its loads in registers.
 template <bool kDiv>
-__device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
+__device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, double* red) {
   const int total = A.chunk_start[A.n];
   const GradXform X{kDiv ? 1 : 0, A.div, 0, 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
@@ -118,7 +184,7 @@ __device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
-    float acc = 0.f;
+    double acc = 0.0;
     if (end - begin == kChunk && aligned16(S.g)) {
       if (S.dtype == kBF16) {   // 2048 16-byte vectors: 8 per thread
         const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(S.g) + begin);
@@ -144,23 +210,24 @@ __device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, float* red) {
         acc = sq_acc4_f32(load_g4(S.g, i, S.dtype), X, acc);
       for (int64_t i = vend + threadIdx.x; i < end; i += kMtThreads) {
         const float a = X(load_g1(S.g, i, S.dtype));
-        acc = fmaf(a, a, acc);
+        acc = sqacc(a, acc);
       }
     } else {
       for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) {
         const float a = X(load_g1(S.g, i, S.dtype));
-        acc = fmaf(a, a, acc);
+        acc = sqacc(a, acc);
       }
     }
-    const float tot = block_sum(acc, red);
+    const double tot = block_sum(acc, red);
     if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
   }
 }
 
-// One instantiation per divisor mode (each gets its own register allocation): 48 registers, five blocks per SM.
+// One instantiation per divisor mode (each gets its own register allocation): without the division 48 registers and
+// five blocks per SM; the dividing one (its slow path is a call) four blocks, so that nothing spills.
 template <bool kDiv>
-__global__ void __launch_bounds__(kMtThreads, 5) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
-  __shared__ float red[kMtThreads / 32];
+__global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) sumsq_kernel(const __grid_constant__ SumsqArgs A) {
+  __shared__ double red[kMtThreads / 32];
   sumsq_chunks<kDiv>(A, red);
 }
 
@@ -168,14 +235,14 @@ __global__ void __launch_bounds__(kMtThreads, 5) sumsq_kernel(const __grid_const
 // Sum of partials[begin, end) over a warp in fp64: lane l adds elements l, l+32, ... in that order, then a fixed xor
 // tree. Loads go out eight at a time before their adds (out-of-range ones read as 0, and s + 0 = s for the
 // non-negative sums here), so a tensor of a few hundred chunks costs one or two load round trips. Result in every lane.
-__device__ __forceinline__ double warp_sum_partials(const float* partials, int begin, int end, int lane) {
+__device__ __forceinline__ double warp_sum_partials(const double* partials, int begin, int end, int lane) {
   double s = 0.0;
   for (int base = begin + lane; base < end; base += 8 * 32) {
-    float v[8];
+    double v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = base + 32 * k < end ? partials[base + 32 * k] : 0.f;
+    for (int k = 0; k < 8; ++k) v[k] = base + 32 * k < end ? partials[base + 32 * k] : 0.0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) s += static_cast<double>(v[k]);
+    for (int k = 0; k < 8; ++k) s += v[k];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -192,13 +259,13 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
   // three tensors per warp at a time: the first eight partials per lane of all three are loaded before any is summed
   // (a tensor's sum is the same as warp_sum_partials': lane l adds elements l, l+32, ... in order)
   for (int t0 = warp; t0 < A.n_tensors; t0 += 3 * nwarps) {
-    float v[3][8];
+    double v[3][8];
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
       const int t = t0 + u * nwarps;
       const int b = t < A.n_tensors ? A.tensor_chunk_start[t] : 0, e = t < A.n_tensors ? A.tensor_chunk_start[t + 1] : 0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[u][k] = b + lane + 32 * k < e ? A.partials[b + lane + 32 * k] : 0.f;
+      for (int k = 0; k < 8; ++k) v[u][k] = b + lane + 32 * k < e ? A.partials[b + lane + 32 * k] : 0.0;
     }
 #pragma unroll
     for (int u = 0; u < 3; ++u) {
@@ -208,13 +275,13 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
       MO_CHECK(b <= e);
       double s = 0.0;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) s += static_cast<double>(v[u][k]);
+      for (int k = 0; k < 8; ++k) s += v[u][k];
       for (int base = b + lane + 8 * 32; base < e; base += 8 * 32) {   // tensors of more than 256 chunks
-        float w[8];
+        double w[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) w[k] = base + 32 * k < e ? A.partials[base + 32 * k] : 0.f;
+        for (int k = 0; k < 8; ++k) w[k] = base + 32 * k < e ? A.partials[base + 32 * k] : 0.0;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s += static_cast<double>(w[k]);
+        for (int k = 0; k < 8; ++k) s += w[k];
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
@@ -244,16 +311,16 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
 
 // ---------------------------------------------------------------------------------------------------------------
 // Sum of every chunk partial in fixed order, in fp64 (one rank's share of the global sum of squares).
-__global__ void __launch_bounds__(1024) partials_total_kernel(const float* partials, int n, double* out) {
+__global__ void __launch_bounds__(1024) partials_total_kernel(const double* partials, int n, double* out) {
   __shared__ double red[32];
   double acc = 0.0;
   const int stride = static_cast<int>(blockDim.x);
   for (int base = threadIdx.x; base < n; base += 8 * stride) {   // thread order c, c + stride, ...; loads batched by 8
-    float v[8];
+    double v[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) v[k] = base + stride * k < n ? partials[base + stride * k] : 0.f;
+    for (int k = 0; k < 8; ++k) v[k] = base + stride * k < n ? partials[base + stride * k] : 0.0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) acc += static_cast<double>(v[k]);
+    for (int k = 0; k < 8; ++k) acc += v[k];
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
@@ -438,7 +505,7 @@ __device__ __forceinline__ float mom_elem(float g, float& buf, float mom, int ne
 // per SM and runs at the copy bandwidth (c1: 165 -> 144 us); the dividing instantiation is compute-heavier (205 us).
 template <bool kDiv>
 __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
-  __shared__ float red[kMtThreads / 32];
+  __shared__ double red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
   const GradXform X{kDiv ? A.has_div : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
@@ -447,7 +514,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
-    float acc = 0.f;
+    double acc = 0.0;
     int64_t i0 = begin;
     if (aligned16(S.buf) && g_vec_ok(S.g, S.dtype)) {
       if (end - begin == kChunk) {   // 4096 float4 of buf: 16 per thread, four quarters of 4, software-pipelined:
@@ -479,7 +546,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel
             const float u2 = mom_elem(X(gg.z), bb.z, S.mom, S.nesterov);
             const float u3 = mom_elem(X(gg.w), bb.w, S.mom, S.nesterov);
             bp[threadIdx.x + (q * 4 + k) * kMtThreads] = bb;
-            acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+            acc = sqacc(u0, acc); acc = sqacc(u1, acc); acc = sqacc(u2, acc); acc = sqacc(u3, acc);
           }
         }
         i0 = end;
@@ -493,7 +560,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel
           const float u2 = mom_elem(X(g.z), b.z, S.mom, S.nesterov);
           const float u3 = mom_elem(X(g.w), b.w, S.mom, S.nesterov);
           *reinterpret_cast<float4*>(S.buf + i) = b;
-          acc = fmaf(u0, u0, acc); acc = fmaf(u1, u1, acc); acc = fmaf(u2, u2, acc); acc = fmaf(u3, u3, acc);
+          acc = sqacc(u0, acc); acc = sqacc(u1, acc); acc = sqacc(u2, acc); acc = sqacc(u3, acc);
         }
         i0 = vend;
       }
@@ -502,9 +569,9 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel
       float b = S.buf[i];
       const float u = mom_elem(X(load_g1(S.g, i, S.dtype)), b, S.mom, S.nesterov);
       S.buf[i] = b;
-      acc = fmaf(u, u, acc);
+      acc = sqacc(u, acc);
     }
-    const float tot = block_sum(acc, red);
+    const double tot = block_sum(acc, red);
     if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
   }
 }
@@ -575,12 +642,12 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) ns_normalize_flat_ke
 // The flat counterpart of ns_out_kernel: the Muon apply of muon.py:97-99 (p = p*(1-decay) if decay;
 // p += -lr*(O*scale)) into the fp32 parameter, or a copy of the bf16 iterate to the output.
 __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_constant__ FlatOutArgs A) {
-  __shared__ float red[kMtThreads / 32];
+  __shared__ double red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const FlatOutSeg& S = A.seg[s];
-    float sq = 0.f;   // sum of the updated param's squares (norm tracking), fixed per-thread order
+    double sq = 0.0;   // sum of the updated param's squares (norm tracking), fixed per-thread order
     const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
     const int64_t end = min(begin + kChunk, S.numel);
     MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel);
@@ -612,8 +679,8 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
               qe[e] = fmaf(K.neg_lr, __fmul_rn(o[e], S.scale), v);
             }
             *reinterpret_cast<float4*>(p + i) = q[k];
-            sq = fmaf(q[k].x, q[k].x, sq); sq = fmaf(q[k].y, q[k].y, sq);
-            sq = fmaf(q[k].z, q[k].z, sq); sq = fmaf(q[k].w, q[k].w, sq);
+            sq = sqacc(q[k].x, sq); sq = sqacc(q[k].y, sq);
+            sq = sqacc(q[k].z, sq); sq = sqacc(q[k].w, sq);
             if (S.ema != nullptr) {   // the EMA follows the updated param in the same pass
               float4 e = *reinterpret_cast<float4*>(S.ema + i);
               e.x = ema_lerp(e.x, q[k].x, A.ema); e.y = ema_lerp(e.y, q[k].y, A.ema);
@@ -629,11 +696,11 @@ __global__ void __launch_bounds__(kMtThreads) ns_out_flat_kernel(const __grid_co
         if (K.has_decay) v = __fmul_rn(v, K.decay_mul);
         v = fmaf(K.neg_lr, __fmul_rn(__bfloat162float(x[i]), S.scale), v);
         p[i] = v;
-        sq = fmaf(v, v, sq);
+        sq = sqacc(v, sq);
         if (S.ema != nullptr) S.ema[i] = ema_lerp(S.ema[i], v, A.ema);
       }
       if (S.partials != nullptr) {   // block-uniform: every thread of the block works on this chunk
-        const float tot = block_sum(sq, red);
+        const double tot = block_sum(sq, red);
         if (threadIdx.x == 0) S.partials[c - A.chunk_start[s]] = tot;
       }
     } else {
@@ -816,7 +883,7 @@ __global__ void __launch_bounds__(kMtThreads, kEma ? 1 : 5) ns_out_kernel(const 
 #pragma unroll
       for (int e = 0; e < 4; ++e) v[k][e] = tile[4 * tx + e][ty + kTileRowsPerPass * k];
   }
-  float sq = 0.f;   // apply mode: sum of the updated param's squares over this thread's elements
+  double sq = 0.0;   // apply mode: sum of the updated param's squares over this thread's elements
 #pragma unroll
   for (int k = 0; k < 4; ++k) {   // output rows r0 + ty + 16k, columns c0 + 4tx .. +3
     const int orow = r0 + ty + kTileRowsPerPass * k, ocol = c0 + 4 * tx;
@@ -834,7 +901,7 @@ __global__ void __launch_bounds__(kMtThreads, kEma ? 1 : 5) ns_out_kernel(const 
           pf[e] = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
         }
         *reinterpret_cast<float4*>(p + idx) = pv;
-        sq = fmaf(pv.x, pv.x, sq); sq = fmaf(pv.y, pv.y, sq); sq = fmaf(pv.z, pv.z, sq); sq = fmaf(pv.w, pv.w, sq);
+        sq = sqacc(pv.x, sq); sq = sqacc(pv.y, sq); sq = sqacc(pv.z, sq); sq = sqacc(pv.w, sq);
         if (ema != nullptr) {
           float4 ev = pre ? pe[k] : *reinterpret_cast<float4*>(ema + idx);
           ev.x = ema_lerp(ev.x, pv.x, A.ema); ev.y = ema_lerp(ev.y, pv.y, A.ema);
@@ -849,7 +916,7 @@ __global__ void __launch_bounds__(kMtThreads, kEma ? 1 : 5) ns_out_kernel(const 
             if (K.has_decay) q = __fmul_rn(q, K.decay_mul);
             q = fmaf(K.neg_lr, __fmul_rn(v[k][e], M.scale), q);
             p[idx + e] = q;
-            sq = fmaf(q, q, sq);
+            sq = sqacc(q, sq);
             if (ema != nullptr) ema[idx + e] = ema_lerp(ema[idx + e], q, A.ema);
           }
       }
@@ -861,8 +928,8 @@ __global__ void __launch_bounds__(kMtThreads, kEma ? 1 : 5) ns_out_kernel(const 
     }
   }
   if (A.apply && M.partials != nullptr) {   // block-uniform (one matrix per grid row)
-    __shared__ float red[kMtThreads / 32];
-    const float tot = block_sum(sq, red);
+    __shared__ double red[kMtThreads / 32];
+    const double tot = block_sum(sq, red);
     if (threadIdx.x == 0) M.partials[blockIdx.x] = tot;
   }
 }

@@ -42,7 +42,7 @@ struct SumsqArgs {
   int chunk_base;            // index of this launch's first chunk in the partials array
   int has_div;               // divide by `div` first (train.py:945, grads /= total_n)
   float div;
-  float* partials;           // one fp32 sum of squares per chunk
+  double* partials;          // one fp64 sum of squares per chunk
   int chunk_start[kMaxNormSeg + 1];
   SumsqSeg seg[kMaxNormSeg];
 };
@@ -52,7 +52,7 @@ struct FinalizeArgs {
   int n_tensors;
   int has_clip;
   float max_norm;
-  const float* partials;
+  const double* partials;
   float* out;                // out[0] = total norm, out[1] = clip coefficient (1 when no clip)
   int* status;
   int tensor_chunk_start[kMaxFinalTensors + 1];
@@ -130,7 +130,7 @@ struct MomArgs {
   int has_div;
   float div;
   const float* coef;
-  float* partials;           // per chunk: sum of u^2 (feeds the Newton-Schulz normalisation)
+  double* partials;          // per chunk: fp64 sum of u^2 (feeds the Newton-Schulz normalisation)
   int chunk_start[kMaxMomSeg + 1];
   MomSeg seg[kMaxMomSeg];
 };
@@ -191,7 +191,7 @@ struct DenomArgs {
   int n;
   int base;                  // den index of this launch's first matrix
   float eps;
-  const float* partials;
+  const double* partials;
   float* den;
   int chunk_start[kMaxDenom + 1];
 };
@@ -208,7 +208,7 @@ struct OutMat {
   float neg_lr, decay_mul, scale;
   int has_decay;
   float* ema;                // apply mode: EMA of the parameter ([R][C], fp32), or null
-  float* partials;           // apply mode: per tile, the sum of the updated param's squares, or null
+  double* partials;          // apply mode: per tile, the fp64 sum of the updated param's squares, or null
   const double* lr_dev;      // apply mode: this step's lr read on the device, or null (neg_lr / decay_mul above)
   double wd, lr_max;         // with lr_dev: decay = lr*wd, or (lr*lr/lr_max)*wd when lr_max > 0 (Muon-SW)
 };
@@ -227,7 +227,7 @@ struct FlatOutSeg {
   float neg_lr, decay_mul, scale;
   int has_decay;
   float* ema;                // apply mode: EMA of the parameter (same layout), or null
-  float* partials;           // apply mode: per chunk of the segment, the sum of the updated param's squares, or null
+  double* partials;          // apply mode: per chunk of the segment, the fp64 sum of the updated param's squares, or null
   const double* lr_dev;      // apply mode: this step's lr read on the device, or null (neg_lr / decay_mul above)
   double wd, lr_max;         // with lr_dev: decay = lr*wd, or (lr*lr/lr_max)*wd when lr_max > 0 (Muon-SW)
 };

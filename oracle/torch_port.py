@@ -29,10 +29,16 @@ from .moteopt_oracle import MAX_STACK_BYTES, NS_A, NS_B, NS_C
 
 
 @torch.no_grad()
-def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
-    """mote/train/muon.py:26-43 on a CPU tensor G [..., m, n]; returns bf16."""
+def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, exact_norm: bool = False) -> torch.Tensor:
+    """mote/train/muon.py:26-43 on a tensor G [..., m, n] (CPU or CUDA); returns bf16. `exact_norm` replaces torch's
+    fp32 reduction for ||G||_F by the correctly rounded norm (an fp64 sum of the exactly squared fp32 entries, its
+    square root rounded to fp32): the one place where two faithful runs of muon.py:33 can differ in the last bit."""
     g32 = G.to(torch.float32)
-    X = (g32 / (g32.norm(dim=(-2, -1), keepdim=True) + eps)).to(torch.bfloat16)
+    if exact_norm:
+        nrm = g32.double().square().sum(dim=(-2, -1), keepdim=True).sqrt().to(torch.float32)
+    else:
+        nrm = g32.norm(dim=(-2, -1), keepdim=True)
+    X = (g32 / (nrm + eps)).to(torch.bfloat16)
     wide_side = X.shape[-2] > X.shape[-1]
     if wide_side:
         X = X.transpose(-2, -1)
@@ -61,10 +67,10 @@ def stacks(shapes: Sequence[Tuple[int, ...]], elem_bytes: int = 4) -> List[Tuple
 @torch.no_grad()
 def muon_update(params: Sequence[torch.Tensor], bufs: List[Optional[torch.Tensor]], *, lr: float,
                 momentum: float = 0.95, nesterov: bool = True, weight_decay: float = 0.0, ns_steps: int = 5,
-                rms_scale: float = 0.2, sw_decay: bool = False, lr_max: float = 1.0) -> None:
+                rms_scale: float = 0.2, sw_decay: bool = False, lr_max: float = 1.0, exact_norm: bool = False) -> None:
     """mote/train/muon.py:52-99 for one param group without `param_lr`: `params` carry `.grad`; `bufs[i]` is the
     momentum buffer of params[i], created on first use (zeros like the grad). The decay is lr * wd, or
-    lr^2 / lr_max * wd under Muon-SW (muon.py:76-79)."""
+    lr^2 / lr_max * wd under Muon-SW (muon.py:76-79). `exact_norm` as for newton_schulz."""
     upd: Dict[int, torch.Tensor] = {}
     live = []
     for i, p in enumerate(params):
@@ -82,7 +88,7 @@ def muon_update(params: Sequence[torch.Tensor], bufs: List[Optional[torch.Tensor
     for (m, n), idx in stacks([tuple(params[i].shape) for i in live], elem):
         members = [live[j] for j in idx]
         batch = torch.cat([upd[i] for i in members], dim=0) if len(members) > 1 else upd[members[0]]
-        orth = newton_schulz(batch, steps=ns_steps)
+        orth = newton_schulz(batch, steps=ns_steps, exact_norm=exact_norm)
         scale = rms_scale * max(m, n) ** 0.5
         row = 0
         for i in members:

@@ -91,10 +91,10 @@ def test_workspace_sizes_follow_the_layout():
     per = 48 * 768 * 768 * 2
     assert n >= 4 * per and n < 4 * per + 64 * 1024
     # a transposed shape needs the same iteration buffers as its transpose; only the apply pass's norm partials
-    # differ (one per 16K-element chunk when iterated as stored, one per 64 x 64 tile when transposed)
+    # differ (one fp64 sum per 16K-element chunk when iterated as stored, one per 64 x 64 tile when transposed)
     a = lib.moteopt_newton_schulz_workspace_size(2, 3072, 768)
     b = lib.moteopt_newton_schulz_workspace_size(2, 768, 3072)
-    assert abs(a - b) <= 4 * 2 * (3072 // 64) * (768 // 64) + 1024
+    assert abs(a - b) <= 8 * 2 * (3072 // 64) * (768 // 64) + 1024
     # invalid shapes report 0
     assert lib.moteopt_newton_schulz_workspace_size(0, 8, 8) == 0
     assert lib.moteopt_newton_schulz_workspace_size(1, -1, 8) == 0
@@ -192,13 +192,13 @@ def _kernel_resources():
 def test_kernel_register_budgets():
     """Registers and spills of every kernel, against the budgets their launch shapes were tuned for: the
     Newton-Schulz kernel's 320 threads at one CTA per SM with its 96 registers; no spills anywhere except the
-    16-byte one of the division-free momentum pass, whose register cap (four blocks per SM) was measured to run at
-    the copy bandwidth with it."""
+    20-byte one of the division-free momentum pass (its fp64 sum of squares included), whose register cap (four
+    blocks per SM) was measured to run at the copy bandwidth with it."""
     res = _kernel_resources()
     assert len(res) >= 20, sorted(res)
     ns = [v for k, v in res.items() if "ns_gemm_kernel" in k]
     assert ns and ns[0][0] <= 96 and ns[0][1] == 0
     for k, (regs, spill) in res.items():
-        allowed = 16 if "muon_momentum_kernelILb0E" in k else 0
+        allowed = 20 if "muon_momentum_kernelILb0E" in k else 0
         assert spill <= allowed, (k, regs, spill)
         assert regs <= 255, k

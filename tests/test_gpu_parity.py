@@ -13,7 +13,7 @@ import pytest
 import torch
 
 from oracle import moteopt_oracle as O
-from tests.conftest import golden
+from tests.conftest import golden, record
 from tests.golden.cases import ADAM_SHAPES, ADAM_WDS, NS_CASES, ns_input
 from mote_b200 import configs
 
@@ -55,10 +55,15 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
     ref = golden("ns_reference")
     u = ns_input(shape, seed)
     exact = O.newton_schulz_f64(u, 5)
+    seen = {}
     for steps, tol in ((1, 1e-3), (2, 5e-3), (5, 4e-2)):
         g = _ns_gpu(u, steps, dev)
         o = O.newton_schulz(u, steps)
         r = O.bf16_from_bits(ref[f"{name}_s{steps}"]).reshape(shape)
+        seen.update({f"k_o_{steps}": O.rel_frob(g, o), f"k_ref_{steps}": O.rel_frob(g, r)})
+        if steps == 5:
+            seen.update(k_e=O.rel_frob(g, exact), o_e=O.rel_frob(o, exact), ref_e=O.rel_frob(r, exact))
+        record("ns_vs_oracle_and_fixture", name, seen)
         assert O.rel_frob(g, o) <= tol, (name, steps, O.rel_frob(g, o))
         assert O.rel_frob(g, r) <= tol, (name, steps, O.rel_frob(g, r))
         if steps == 5:
@@ -72,9 +77,12 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
                                    (2, 1024, 1024), (1, 1024, 4096), (1, 4096, 1024), (1, 768, 2048), (1, 2048, 768)])
 def test_newton_schulz_benchmark_shapes(dev, shape):
     u = ns_input(shape, 123)
+    seen = {}
     for steps, tol in ((1, 1e-3), (5, 4e-2)):
         g = _ns_gpu(u, steps, dev)
         o = O.newton_schulz(u, steps)
+        seen[f"k_o_{steps}"] = O.rel_frob(g, o)
+        record("ns_benchmark_shapes_vs_oracle", "x".join(map(str, shape)), seen)
         assert O.rel_frob(g, o) <= tol, (shape, steps, O.rel_frob(g, o))
     assert O.rel_frob(g, O.newton_schulz_f64(u, 5)) <= O.rel_frob(o, O.newton_schulz_f64(u, 5)) + 3e-3
     _status_ok(dev)
