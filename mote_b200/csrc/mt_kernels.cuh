@@ -298,8 +298,9 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
       const float total = static_cast<float>(sqrt(acc));
       float coef = 1.0f;
       if (A.has_clip) {
-        // clamp(max_norm / (total + 1e-6), max=1) in fp32; a NaN norm gives a NaN coefficient, as in torch
-        const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
+        // clamp(max_norm / (total + 1e-6), max=1) as torch evaluates it: a Python float over a tensor is
+        // Tensor.__rdiv__, reciprocal(total + 1e-6) * max_norm (two fp32 roundings); a NaN norm gives NaN, as in torch
+        const float c = __fmul_rn(__frcp_rn(__fadd_rn(total, 1e-6f)), A.max_norm);
         coef = (c > 1.0f) ? 1.0f : c;
       }
       A.out[0] = total;
@@ -341,7 +342,7 @@ __global__ void coef_from_sums_kernel(const __grid_constant__ CoefArgs A) {
   const float total = static_cast<float>(sqrt(s));
   float coef = 1.0f;
   if (A.has_clip) {
-    const float c = __fdiv_rn(A.max_norm, __fadd_rn(total, 1e-6f));
+    const float c = __fmul_rn(__frcp_rn(__fadd_rn(total, 1e-6f)), A.max_norm);   // as norm_finalize_kernel
     coef = (c > 1.0f) ? 1.0f : c;
   }
   A.out[0] = total;

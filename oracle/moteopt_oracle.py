@@ -333,8 +333,10 @@ def grad_total_norm(grads: Sequence[np.ndarray]) -> np.float32:
 
 
 def clip_coef(total_norm: np.float32, max_norm: float) -> np.float32:
-    """torch clip coefficient: clamp(max_norm / (total + 1e-6), max=1), in fp32 tensor arithmetic."""
-    c = np.float32(np.float32(max_norm) / np.float32(np.float32(total_norm) + np.float32(1e-6)))
+    """torch clip coefficient: clamp(max_norm / (total + 1e-6), max=1), in fp32 tensor arithmetic. torch evaluates
+    the Python-float-over-tensor quotient as Tensor.__rdiv__, reciprocal(total + 1e-6) * max_norm: two roundings."""
+    r = np.float32(np.float32(1.0) / np.float32(np.float32(total_norm) + np.float32(1e-6)))
+    c = np.float32(r * np.float32(max_norm))
     return np.float32(min(c, np.float32(1.0))) if not np.isnan(c) else c
 
 

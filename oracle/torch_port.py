@@ -102,14 +102,35 @@ def muon_update(params: Sequence[torch.Tensor], bufs: List[Optional[torch.Tensor
 
 
 @torch.no_grad()
+def clip_grad_norm_exact_(params: Sequence[torch.Tensor], max_norm: float) -> torch.Tensor:
+    """torch.nn.utils.clip_grad_norm_ (torch's get_total_norm + _clip_grads_with_norm_, line for line) with each
+    fp32 reduction replaced by the correctly rounded norm: per-tensor norms and the norm of those norms from fp64 sums
+    of exact squares, rounded to fp32. The coefficient is torch's own expression, max_norm / (total + 1e-6), which
+    Tensor.__rdiv__ evaluates as reciprocal(total + 1e-6) * max_norm, clamped to 1, then one _foreach_mul_."""
+    grads = [p.grad for p in params if p.grad is not None]
+    norms = [g.double().square().sum().sqrt().to(torch.float32) for g in grads]
+    total = torch.stack(norms).double().square().sum().sqrt().to(torch.float32)
+    clip_coef = max_norm / (total + 1e-6)
+    torch._foreach_mul_(grads, torch.clamp(clip_coef, max=1.0))
+    return total
+
+
+@torch.no_grad()
 def optimizer_step(adam: Optional[torch.optim.Optimizer], muon_params: Sequence[torch.Tensor],
                    muon_bufs: List[Optional[torch.Tensor]], all_params: Sequence[torch.Tensor], *, divisor,
-                   max_norm: Optional[float], muon_kw: dict) -> Optional[torch.Tensor]:
+                   max_norm: Optional[float], muon_kw: dict, exact_norm: bool = False) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947: grads /= divisor, clip_grad_norm_(all params), AdamW step, Muon step. Returns the
-    pre-clip total norm. A workload without AdamW params passes adam=None; max_norm=None skips the clip."""
+    pre-clip total norm. A workload without AdamW params passes adam=None; max_norm=None skips the clip. `exact_norm`
+    takes every norm of the step correctly rounded: the clip's (clip_grad_norm_exact_) and, through muon_kw, the
+    Newton-Schulz normalisation's."""
     grads = [p.grad for p in all_params if p.grad is not None]
     torch._foreach_div_(grads, divisor)
-    total = torch.nn.utils.clip_grad_norm_(all_params, max_norm) if max_norm is not None else None
+    if max_norm is None:
+        total = None
+    elif exact_norm:
+        total = clip_grad_norm_exact_(all_params, max_norm)
+    else:
+        total = torch.nn.utils.clip_grad_norm_(all_params, max_norm)
     if adam is not None:
         adam.step()
     muon_update(muon_params, muon_bufs, **muon_kw)

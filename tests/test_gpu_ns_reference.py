@@ -127,8 +127,8 @@ def test_newton_schulz_against_the_reference_on_the_b200(dev, name, shape, seed)
 def _reference_c0_on(dev, w, inp, steps, max_norm, exact_norm=False):
     """The reference's step (train.py:944-947) run by torch on `dev`: grads /= n, clip_grad_norm_ (skipped when
     max_norm is None), AdamW (torch's, fused on CUDA as train.py:98 builds it), then the reference's Muon operations
-    (oracle/torch_port.py; `exact_norm`: with the correctly rounded norm in the normalisation). Returns the params and
-    the optimizer state as numpy arrays."""
+    (oracle/torch_port.py; `exact_norm`: with correctly rounded norms in the clip and the normalisation). Returns the
+    params and the optimizer state as numpy arrays."""
     ap = [torch.nn.Parameter(torch.from_numpy(p.copy()).to(dev)) for p in inp.adam_params]
     mp = [torch.nn.Parameter(torch.from_numpy(p.copy()).to(dev)) for p in inp.muon_params]
     nd = len(w.adam_decay_shapes)
@@ -141,7 +141,7 @@ def _reference_c0_on(dev, w, inp, steps, max_norm, exact_norm=False):
             p.grad = torch.from_numpy(g.copy()).to(dev)
         TP.optimizer_step(adam, mp, bufs, ap + mp, divisor=torch.tensor(C0_DIVISOR, device=dev), max_norm=max_norm,
                           muon_kw=dict(lr=w.muon_lr, momentum=w.muon_momentum, nesterov=True, weight_decay=w.muon_wd,
-                                       ns_steps=w.ns_steps, exact_norm=exact_norm))
+                                       ns_steps=w.ns_steps, exact_norm=exact_norm), exact_norm=exact_norm)
     return {"ap": [_f(p.detach()) for p in ap], "mp": [_f(p.detach()) for p in mp], "mb": [_f(b) for b in bufs],
             "am": [_f(adam.state[p]["exp_avg"]) for p in ap], "av": [_f(adam.state[p]["exp_avg_sq"]) for p in ap]}
 
@@ -181,7 +181,7 @@ def test_c0_ten_steps_against_the_reference_on_the_b200(dev):
     """Ten whole steps of c0 through the library (bf16 grads, divisor 4, clip 1.0): Muon parameters and momentum
     buffers bit for bit those of the reference's step on the B200 with the correctly rounded norm; against the
     reference with torch's norm and against its stored CPU run, parameters within 1e-3 relative (north star) or the
-    reference's own B200-vs-CPU distance where that is larger, updates p10 - p0 within 1e-2 or that distance; AdamW
+    reference's own B200-vs-CPU distance (+10 %) where that is larger, updates p10 - p0 within 1e-2 or that; AdamW
     state and parameters 1e-6 relative per element against the B200 reference (torch's fused AdamW)."""
     w = configs.c0()
     inp = configs.make_params(w, seed=0)
@@ -210,18 +210,18 @@ def test_c0_ten_steps_against_the_reference_on_the_b200(dev):
     record("c0_ten_steps", "clip_1.0", d)
     for a, b in zip(k["mp"] + k["mb"], rgx["mp"] + rgx["mb"]):
         assert np.array_equal(a, b), d
-    assert d["p_k_rc"] <= max(P_BAR, d["p_rg_rc"]), d
-    assert d["p_k_rg"] <= max(P_BAR, d["p_rg_rc"]), d
-    assert d["dp_k_rc"] <= max(NS_BAR, d["dp_rg_rc"]), d
+    assert d["p_k_rc"] <= max(P_BAR, 1.1 * d["p_rg_rc"]), d
+    assert d["p_k_rg"] <= max(P_BAR, 1.1 * d["p_rg_rc"]), d
+    assert d["dp_k_rc"] <= max(NS_BAR, 1.1 * d["dp_rg_rc"]), d
     assert max(d["adam_p_max_rel_k_rg"], d["adam_m_max_rel_k_rg"], d["adam_v_max_rel_k_rg"]) <= 1e-6, d
 
 
 def test_c0_ten_steps_with_an_active_clip_against_the_reference_on_the_b200(dev):
     """The same ten c0 steps with max_norm 0.05, so that the clip scales every step's grads (at max_norm 1.0 the c0
-    norm stays below it). The clip coefficient is then a rounded function of the global norm: the library's and
-    torch's norms may differ in the last bit, and the bf16 iteration amplifies that. Held to the north star's 1e-3,
-    or to the reference's own sensitivity where that is larger: the distance between its B200 runs with torch's norm
-    and with the correctly rounded one."""
+    norm stays below it). Muon parameters and momentum buffers bit for bit those of the reference's step on the B200
+    with correctly rounded norms (clip and normalisation); against the reference with torch's own norms, whose clip
+    coefficient can differ in its last bit (amplified by the bf16 iteration), within the north star's 1e-3 or twice
+    the reference's own sensitivity to its norms' rounding (its torch-norm run against its exact-norm run)."""
     w = configs.c0()
     inp = configs.make_params(w, seed=0)
     k = _library_c0(dev, w, inp, 10, 0.05)
@@ -235,6 +235,7 @@ def test_c0_ten_steps_with_an_active_clip_against_the_reference_on_the_b200(dev)
          "adam_v_max_rel_k_rg": _max_rel(k["av"], rg["av"])}
     RECORD["c0"]["clip_0.05"] = d
     record("c0_ten_steps", "clip_0.05", d)
-    assert d["p_k_rgx"] <= max(P_BAR, d["p_rg_rgx"]), d
+    for a, b in zip(k["mp"] + k["mb"], rgx["mp"] + rgx["mb"]):
+        assert np.array_equal(a, b), d
     assert d["p_k_rg"] <= max(P_BAR, 2 * d["p_rg_rgx"]), d
     assert max(d["adam_p_max_rel_k_rg"], d["adam_m_max_rel_k_rg"], d["adam_v_max_rel_k_rg"]) <= 1e-6, d

@@ -203,3 +203,22 @@ def test_ema_lerp_matches_torch(weight):
     torch._foreach_lerp_([ref], [torch.from_numpy(p)], weight)
     O.ema_lerp(e, p, weight)
     assert np.array_equal(e.view(np.uint32), ref.numpy().view(np.uint32))
+
+
+def test_clip_coefficient_is_torchs_expression():
+    """torch's clip coefficient, max_norm / (total + 1e-6) with a Python float over a tensor (torch.nn.utils.clip_grad's
+    _clip_grads_with_norm_), is Tensor.__rdiv__: reciprocal(total + 1e-6) * max_norm, two fp32 roundings. The
+    oracle's clip_coef reproduces it bit for bit (the library's norm kernels do the same two operations); a single
+    correctly rounded division would differ for max_norm != 1."""
+    import torch
+    rng = np.random.default_rng(3)
+    totals = (10.0 ** rng.uniform(-4, 4, 20000)).astype(np.float32)
+    t = torch.from_numpy(totals)
+    differs = 0
+    for max_norm in (1.0, 0.05, 0.3, 2.5, 7.0):
+        ref = torch.clamp(max_norm / (t + 1e-6), max=1.0).numpy()
+        got = np.array([O.clip_coef(x, max_norm) for x in totals], dtype=np.float32)
+        assert np.array_equal(got, ref), max_norm
+        one_div = np.minimum(np.float32(max_norm) / (totals + np.float32(1e-6)), np.float32(1.0)).astype(np.float32)
+        differs += int((one_div != ref).sum())
+    assert differs > 0
