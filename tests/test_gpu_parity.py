@@ -1,11 +1,17 @@
 """GPU parity: the CUDA path (through the C ABI) against the CPU oracle and the reference's golden outputs.
 
-Tolerances (why each is what it is is in tests/test_oracle_golden.py's docstring):
-  * Newton-Schulz, 1 iteration: <= 1e-3 relative Frobenius (same rounding points; only fp32 summation order differs)
-  * Newton-Schulz, 2 iterations: <= 5e-3
-  * Newton-Schulz, 5 iterations: <= 4e-2, and no farther from the exact fp64 iteration than the oracle + 3e-3
+Tolerances: the measured distance on a B200 plus a margin (the oracle runs on the CPU, whose fp32 matmul sums in
+another order than the tensor cores; the library against the reference's own iteration on the B200 is bit for bit,
+tests/test_gpu_ns_reference.py):
+  * Newton-Schulz vs the oracle and the reference's CPU fixtures, golden shapes: 1 iteration <= 1e-4 (measured 0),
+    2 iterations <= 5e-4 (measured 5.0e-5), 5 iterations <= 2e-2 (measured <= 1.5e-2), and no farther from the
+    exact fp64 iteration than the oracle + 1e-3 (measured <= 4.2e-5 farther)
+  * the benchmark shapes of c1/c2/c3: 1 iteration <= 1e-4 (measured <= 2.8e-5), 5 iterations <= 2e-2 (measured
+    <= 1.3e-2). 5 iterations amplify the CPU's fp32 summation order 5-10x per iteration; north star's 1e-2 bar is
+    stated against the reference's bf16 iteration on the B200, where the distance is 0.
   * AdamW exp_avg / exp_avg_sq and Muon momentum: 1e-6 relative per element (RMS-floored)
-  * params after 10 steps: AdamW 1e-6 (RMS-floored, 1e-9 absolute); Muon 1e-2 relative Frobenius
+  * params after 10 steps: AdamW 1e-6 (RMS-floored, 1e-9 absolute); Muon 1e-2 relative Frobenius against the CPU
+    oracle (the 5-iteration summation-order distance carried through 10 steps)
 """
 
 import numpy as np
@@ -56,7 +62,7 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
     u = ns_input(shape, seed)
     exact = O.newton_schulz_f64(u, 5)
     seen = {}
-    for steps, tol in ((1, 1e-3), (2, 5e-3), (5, 4e-2)):
+    for steps, tol in ((1, 1e-4), (2, 5e-4), (5, 2e-2)):
         g = _ns_gpu(u, steps, dev)
         o = O.newton_schulz(u, steps)
         r = O.bf16_from_bits(ref[f"{name}_s{steps}"]).reshape(shape)
@@ -67,7 +73,7 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
         assert O.rel_frob(g, o) <= tol, (name, steps, O.rel_frob(g, o))
         assert O.rel_frob(g, r) <= tol, (name, steps, O.rel_frob(g, r))
         if steps == 5:
-            assert O.rel_frob(g, exact) <= O.rel_frob(o, exact) + 3e-3
+            assert O.rel_frob(g, exact) <= O.rel_frob(o, exact) + 1e-3
     _status_ok(dev)
 
 
@@ -78,7 +84,7 @@ def test_newton_schulz_matches_oracle_and_reference(dev, name, shape, seed):
 def test_newton_schulz_benchmark_shapes(dev, shape):
     u = ns_input(shape, 123)
     seen = {}
-    for steps, tol in ((1, 1e-3), (5, 4e-2)):
+    for steps, tol in ((1, 1e-4), (5, 2e-2)):
         g = _ns_gpu(u, steps, dev)
         o = O.newton_schulz(u, steps)
         seen[f"k_o_{steps}"] = O.rel_frob(g, o)
