@@ -90,6 +90,9 @@ typedef struct moteopt_grad_config {
   int clip;                     /* 1: clip_grad_norm_(all params, max_norm) before the updates */
   double max_norm;
   double grad_divisor;          /* train.py:945: grads /= total_n first; 0 or 1 = no division */
+  const float* grad_divisor_device; /* or, when non-NULL, total_n as a DEVICE fp32 scalar, read by the kernels (the
+                                   trainer's total_n is a GPU tensor: no host round trip, and a captured step reads
+                                   each replay's value); overrides grad_divisor */
 } moteopt_grad_config;
 
 /* Optional work fused into moteopt_optimizer_step_ex (no counterpart in the reference's step, which does this work

@@ -59,7 +59,8 @@ class AdamWHparams(C.Structure):
 
 
 class GradConfig(C.Structure):
-    _fields_ = [("clip", C.c_int), ("max_norm", C.c_double), ("grad_divisor", C.c_double)]
+    _fields_ = [("clip", C.c_int), ("max_norm", C.c_double), ("grad_divisor", C.c_double),
+                ("grad_divisor_device", C.c_void_p)]
 
 
 class StepExtras(C.Structure):

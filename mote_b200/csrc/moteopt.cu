@@ -348,12 +348,13 @@ struct GradSource {          // one tensor of the global grad norm
 };
 
 int launch_sumsq(const std::vector<GradSource>& src, const std::vector<int>& chunk_start, double* partials, bool has_div,
-                 float div, int sms, cudaStream_t st) {
+                 float div, int sms, cudaStream_t st, const float* div_dev = nullptr) {
   SumsqArgs A;
   std::memset(&A, 0, sizeof(A));
   A.partials = partials;
   A.has_div = has_div;
   A.div = div;
+  A.div_dev = div_dev;
   for (size_t s0 = 0; s0 < src.size(); s0 += kMaxNormSeg) {
     const size_t n = std::min(src.size() - s0, static_cast<size_t>(kMaxNormSeg));
     A.n = static_cast<int>(n);
@@ -421,12 +422,13 @@ EmaConsts ema_consts(double weight) {
 // ema: per AdamW tensor, an EMA buffer or null; lr_dev: device array, one lr per tensor, or null
 int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparams* hp, bool has_div, float div,
                  const float* coef, int sms, cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0,
-                 const double* lr_dev = nullptr) {
+                 const double* lr_dev = nullptr, const float* div_dev = nullptr) {
   static thread_local AdamArgs A;
   std::memset(&A, 0, sizeof(A));
   A.ema = ema_consts(ema_weight);
   A.has_div = has_div;
   A.div = div;
+  A.div_dev = div_dev;
   A.coef = coef;
   const double w = 1.0 - hp->beta1;
   A.lerp_w = static_cast<float>(w);
@@ -519,7 +521,7 @@ EmaConsts ema_consts(double weight);
 bool stored_as_iterated(const GroupPlan& g) { return !g.transposed && g.m == g.rows && g.n == g.cols; }
 
 int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float div, const float* coef,
-                     const float* den, int sms, cudaStream_t st) {
+                     const float* den, int sms, cudaStream_t st, const float* div_dev = nullptr) {
   static thread_local FlatNormArgs A;
   for (size_t s0 = 0; s0 < segs.size(); s0 += kMaxFlatSeg) {
     const int cnt = static_cast<int>(std::min(segs.size() - s0, static_cast<size_t>(kMaxFlatSeg)));
@@ -527,6 +529,7 @@ int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float di
     A.n = cnt;
     A.has_div = has_div;
     A.div = div;
+    A.div_dev = div_dev;
     A.coef = coef;
     A.den = den;
     for (int i = 0; i < cnt; ++i) {
@@ -567,7 +570,8 @@ int launch_flat_out(const std::vector<FlatOutSeg>& segs, int apply, int sms, cud
 
 // The first half of the Muon update of `n` params: momentum and the Newton-Schulz normalisation X0.
 int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg, const Layout& L, char* ws,
-             bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st) {
+             bool has_div, float div, const float* coef, int* status, int sms, cudaStream_t st,
+             const float* div_dev = nullptr) {
   if (n == 0) return MOTEOPT_OK;
   double* mom_partials = reinterpret_cast<double*>(ws + L.off_mom);
   // flatten the matrices in group-major order
@@ -595,6 +599,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
     std::memset(&A, 0, sizeof(A));
     A.has_div = has_div;
     A.div = div;
+    A.div_dev = div_dev;
     A.coef = coef;
     A.partials = mom_partials;
     for (int s0 = 0; s0 < nm; s0 += kMaxMomSeg) {
@@ -626,6 +631,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
     std::memset(&A, 0, sizeof(A));
     A.has_div = has_div;
     A.div = div;
+    A.div_dev = div_dev;
     A.coef = coef;
     A.den = den;
     std::vector<FlatNormSeg> flat;
@@ -649,7 +655,7 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
         tiled.push_back(i);
       }
     }
-    MO_TRY(launch_flat_norm(flat, has_div, div, coef, den, sms, st));
+    MO_TRY(launch_flat_norm(flat, has_div, div, coef, den, sms, st, div_dev));
     const int nt = static_cast<int>(tiled.size());
     for (int s0 = 0; s0 < nt; s0 += kMaxNormMat) {
       const int cnt = std::min(nt - s0, kMaxNormMat);
@@ -1004,8 +1010,10 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
   Header* hdr = reinterpret_cast<Header*>(ws);
   int* status = &hdr->status;
   MO_CUDA(cudaMemsetAsync(hdr, 0, sizeof(Header), st));
-  const bool has_div = gcfg != nullptr && gcfg->grad_divisor != 0.0 && gcfg->grad_divisor != 1.0;
-  const float div = has_div ? static_cast<float>(gcfg->grad_divisor) : 1.0f;
+  // the divisor of train.py:945: a device scalar (grad_divisor_device) or a host value (0 or 1: none)
+  const float* div_dev = gcfg != nullptr ? gcfg->grad_divisor_device : nullptr;
+  const bool has_div = div_dev != nullptr || (gcfg != nullptr && gcfg->grad_divisor != 0.0 && gcfg->grad_divisor != 1.0);
+  const float div = has_div && div_dev == nullptr ? static_cast<float>(gcfg->grad_divisor) : 1.0f;
   const float* coef = ext_scale;
   if (clip) {
     std::vector<GradSource> src;
@@ -1013,15 +1021,15 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     for (int i = 0; i < n_muon; ++i)
       src.push_back(GradSource{muon[i].grad, muon[i].batch * muon[i].rows * muon[i].cols, muon[i].grad_dtype});
     double* partials = reinterpret_cast<double*>(ws + L.off_norm);
-    MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, div, sms, st));
+    MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, div, sms, st, div_dev));
     MO_TRY(launch_finalize(L.norm_tensor_chunk_start, partials, true, gcfg->max_norm, &hdr->norm, status, st));
     coef = &hdr->coef;
     if (out_norm != nullptr) MO_CUDA(cudaMemcpyAsync(out_norm, &hdr->norm, sizeof(float), cudaMemcpyDeviceToDevice, st));
   }
   const double* lr_dev = ex != nullptr ? ex->lr : nullptr;
-  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w, lr_dev));
+  if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w, lr_dev, div_dev));
   if (n_muon > 0) {
-    MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st));
+    MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st, div_dev));
     int final_src = 0;
     if (mcfg->ns_steps > 0) {
       if (t_ns_ev[0] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[0], st));
@@ -1161,6 +1169,7 @@ int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon,
   gc.clip = 0;
   gc.max_norm = 0.0;
   gc.grad_divisor = grad_divisor;
+  gc.grad_divisor_device = nullptr;
   return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, &gc, grad_coef, nullptr, workspace,
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -1177,6 +1186,7 @@ int moteopt_optimizer_step_with_coef_out(const moteopt_muon_param* muon, int n_m
   gc.clip = 0;
   gc.max_norm = 0.0;
   gc.grad_divisor = grad_divisor;
+  gc.grad_divisor_device = nullptr;
   return run_step(muon, n_muon, muon_cfg, adamw, n_adamw, adamw_hp, &gc, grad_coef, nullptr, workspace,
                   workspace_bytes, reinterpret_cast<cudaStream_t>(stream), muon_updates);
 }
@@ -1498,6 +1508,7 @@ int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, co
   S.partials = partials;
   S.has_div = 0;
   S.div = 1.0f;
+  S.div_dev = nullptr;
   A.coef = &hdr->coef;
   for (int s0 = 0; s0 < n; s0 += kMaxNormSeg) {
     const int cnt = std::min(n - s0, kMaxNormSeg);

@@ -115,6 +115,13 @@ __device__ __forceinline__ SharedDivisor shared_divisor(float den) {
   return s;
 }
 
+// The divisor of train.py:945 (grads /= total_n): a launch argument, or a device scalar (the trainer's total_n
+// tensor, read without a host round trip). Read only by launches that divide.
+template <typename Args>
+__device__ __forceinline__ float grad_div(const Args& A, bool used) {
+  return (used && A.div_dev != nullptr) ? *A.div_dev : A.div;
+}
+
 // train.py:945-946: g / total_n (fp32 division), then * clip coefficient (fp32 multiply)
 struct GradXform {
   int has_div;
@@ -177,7 +184,7 @@ __device__ __forceinline__ double sq_acc4_f32(const float4& v, const GradXform& 
 template <bool kDiv>
 __device__ __forceinline__ void sumsq_chunks(const SumsqArgs& A, double* red) {
   const int total = A.chunk_start[A.n];
-  const GradXform X{kDiv ? 1 : 0, A.div, 0, 1.f};
+  const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), 0, 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const SumsqSeg& S = A.seg[s];
@@ -398,7 +405,7 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
 template <bool kSmall>
 __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant__ AdamArgs A) {
   const int total = A.chunk_start[A.n];
-  const GradXform X{A.has_div, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{A.has_div, grad_div(A, A.has_div != 0), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
   const double dstep = A.dstep != nullptr ? static_cast<double>(*A.dstep) : 0.0;
   int s_cur = -1;
@@ -508,7 +515,8 @@ template <bool kDiv>
 __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 4) muon_momentum_kernel(const __grid_constant__ MomArgs A) {
   __shared__ double red[kMtThreads / 32];
   const int total = A.chunk_start[A.n];
-  const GradXform X{kDiv ? A.has_div : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{kDiv ? A.has_div : 0, grad_div(A, kDiv && A.has_div), A.coef != nullptr,
+                    A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const MomSeg& S = A.seg[s];
@@ -601,7 +609,7 @@ __device__ __forceinline__ float flat_u(float g, float b, const FlatNormSeg& S, 
 template <bool kDiv>
 __global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
   const int total = A.chunk_start[A.n];
-  const GradXform X{kDiv ? 1 : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
     const int s = find_seg(A.chunk_start, A.n, c);
     const FlatNormSeg& S = A.seg[s];
@@ -741,7 +749,7 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 5) ns_normalize_kernel(
   const int i0 = ti * kNormTile, j0 = tj * kNormTile;   // destination tile origin (X rows i, cols j)
   MO_CHECK(i0 < M.m_pad && j0 < M.n_pad);
   const SharedDivisor den = shared_divisor(A.den[M.den_index]);
-  const GradXform X{kDiv ? 1 : 0, A.div, A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;   // 16 x 16 threads, 4 columns each
   const int mv = M.transposed ? M.cols : M.rows;
   const int nv = M.transposed ? M.rows : M.cols;

@@ -42,6 +42,7 @@ struct SumsqArgs {
   int chunk_base;            // index of this launch's first chunk in the partials array
   int has_div;               // divide by `div` first (train.py:945, grads /= total_n)
   float div;
+  const float* div_dev;      // or, when non-null, by this device scalar (read once per block)
   double* partials;          // one fp64 sum of squares per chunk
   int chunk_start[kMaxNormSeg + 1];
   SumsqSeg seg[kMaxNormSeg];
@@ -99,6 +100,7 @@ struct AdamArgs {
   int n;
   int has_div;
   float div;
+  const float* div_dev;
   const float* coef;         // device clip coefficient, or null
   float lerp_w;              // 1 - beta1 (lerp weight)
   int lerp_small;            // weight < 0.5: m + w*(g-m); else g - (g-m)*(1-w)
@@ -129,6 +131,7 @@ struct MomArgs {
   int chunk_base;
   int has_div;
   float div;
+  const float* div_dev;
   const float* coef;
   double* partials;          // per chunk: fp64 sum of u^2 (feeds the Newton-Schulz normalisation)
   int chunk_start[kMaxMomSeg + 1];
@@ -157,6 +160,7 @@ struct NormArgs {
   int n;
   int has_div;
   float div;
+  const float* div_dev;
   const float* coef;
   const float* den;          // per matrix: ||u||_F + eps (mat_denom_kernel)
   NormMat mat[kMaxNormMat];
@@ -179,6 +183,7 @@ struct FlatNormArgs {
   int n;
   int has_div;
   float div;
+  const float* div_dev;
   const float* coef;
   const float* den;
   int chunk_start[kMaxFlatSeg + 1];

@@ -97,6 +97,19 @@ def adamw_array(items: Sequence[AdamWItem]):
     return arr
 
 
+def _device_divisor(grad_divisor, dev: torch.device) -> Optional[torch.Tensor]:
+    """A tensor divisor (the trainer's total_n, train.py:945) as the fp32 device scalar the kernels read: the tensor
+    itself when it already is one (so a captured step reads its value at every replay), else an fp32 copy on the
+    device, made on the current stream (no host round trip). A number gives None (passed by value)."""
+    if not isinstance(grad_divisor, torch.Tensor):
+        return None
+    if grad_divisor.numel() != 1:
+        raise ValueError("grad_divisor must be a number or a one-element tensor")
+    if grad_divisor.device == dev and grad_divisor.dtype == torch.float32:
+        return grad_divisor
+    return grad_divisor.detach().to(device=dev, dtype=torch.float32)
+
+
 def _device(muon: Sequence[MuonItem], adamw: Sequence[AdamWItem]) -> torch.device:
     for it in list(muon) + list(adamw):
         return it.param.device
@@ -115,7 +128,9 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
     AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
     max_norm is given. With `device_step` (a 0-dim fp32 CUDA tensor) AdamW's step count is that counter, which the
-    call increments on the device (the AdamItems' `step` is then ignored).
+    call increments on the device (the AdamItems' `step` is then ignored). `grad_divisor` is a number or a
+    one-element tensor (the trainer's total_n): a tensor is read by the kernels on the device, with no host
+    synchronisation.
 
     Fused extras (the work train.py:950-953 and elr.py:85-87 do in separate passes after the step):
     `ema` - one fp32 buffer (or None) per AdamW item, then per Muon item, updated as
@@ -132,7 +147,10 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
     hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps),
                         device_step.data_ptr() if device_step is not None else None)
-    gc = L.GradConfig(int(max_norm is not None), float(max_norm or 0.0), float(grad_divisor or 0.0))
+    div_t = _device_divisor(grad_divisor, dev)
+    gc = L.GradConfig(int(max_norm is not None), float(max_norm or 0.0),
+                      0.0 if div_t is not None else float(grad_divisor or 0.0),
+                      div_t.data_ptr() if div_t is not None else None)
     if max_norm is not None and out_norm is None:
         out_norm = torch.empty((), dtype=torch.float32, device=dev)
     onorm = C.c_void_p(out_norm.data_ptr() if out_norm is not None else 0)
@@ -276,6 +294,9 @@ class CapturedStep:
                  dynamic_lr: bool = False, ema: Optional[Sequence[Optional[torch.Tensor]]] = None,
                  ema_weight: float = 0.0, muon_norms: Optional[torch.Tensor] = None, moe: Optional[Sequence] = None):
         self.dev = _device(muon, adamw)
+        if isinstance(grad_divisor, torch.Tensor) and _device_divisor(grad_divisor, self.dev) is not grad_divisor:
+            raise ValueError("CapturedStep: a tensor grad_divisor must be a one-element fp32 tensor on the step's "
+                             "device (the graph reads it in place at every replay)")
         self.kw = dict(ns_steps=ns_steps, rms_scale=rms_scale, ns_eps=ns_eps, betas=betas, eps=eps,
                        max_norm=max_norm, grad_divisor=grad_divisor, ema=ema, ema_weight=ema_weight,
                        muon_norms=muon_norms)

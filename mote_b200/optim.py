@@ -249,9 +249,9 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Op
     if len(muon_sets) > 1:
         raise NotImplementedError("fused_step: all Muon groups must share ns_steps and rms_scale")
     (ns, rms), muon_items = next(iter(muon_sets.items())) if muon_sets else ((5, 0.2), [])
-    div = None
+    div = None   # a tensor (the trainer's total_n) stays on the device: the kernels read it there, no host sync
     if grad_divisor is not None:
-        div = float(grad_divisor.item()) if isinstance(grad_divisor, torch.Tensor) else float(grad_divisor)
+        div = grad_divisor if isinstance(grad_divisor, torch.Tensor) else float(grad_divisor)
     bufs = None
     if ema is not None:
         bufs = [ema.get(it.param) for it in adam_items] + [ema.get(it.param) for it in muon_items]

@@ -263,3 +263,55 @@ def test_multiopt_step_is_one_library_call_with_the_separate_steps_bits(dev, mon
         for k in s1["state"]:
             for name, t in s1["state"][k].items():
                 assert torch.equal(t, s2["state"][k][name]), (k, name)
+
+
+def test_device_divisor_equals_the_host_divisor_and_never_syncs(dev, monkeypatch):
+    """train.py:945 divides by total_n, a GPU tensor: fused_step(grad_divisor=tensor) reads it on the device (no
+    .item(), no host synchronisation) and gives the same bits as the same divisor passed as a number; an int64
+    total_n is converted on the device. A CapturedStep reads an fp32 device divisor in place at every replay."""
+    from mote_b200 import build_optimizer, fused_step
+    from mote_b200.functional import AdamWItem, CapturedStep, MuonItem, optimizer_step
+    m1, m2 = _tiny_model(dev), _tiny_model(dev)
+    o1 = build_optimizer(m1, 1e-2, 0.1, [2.0, 1.0], optimizer="muon")
+    o2 = build_optimizer(m2, 1e-2, 0.1, [2.0, 1.0], optimizer="muon")
+
+    def no_item(self):
+        raise AssertionError("host synchronisation: Tensor.item() called")
+    for step in range(3):
+        _grads(m1, step)
+        _grads(m2, step)
+        total_n = torch.tensor(3 + step, device=dev)   # int64, as a token count
+        monkeypatch.setattr(torch.Tensor, "item", no_item)
+        n1 = fused_step(o1, max_norm=0.05, grad_divisor=total_n)
+        monkeypatch.undo()
+        n2 = fused_step(o2, max_norm=0.05, grad_divisor=float(3 + step))
+        assert torch.equal(n1, n2)
+    for p, q in zip(m1.parameters(), m2.parameters()):
+        assert torch.equal(p, q)
+    # captured: the divisor tensor is updated in place between replays
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(9)
+    ps = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in [(64, 96), (96, 64)]]
+    gs = [(torch.randn(p.shape, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for p in ps]
+    a = torch.randn(300, generator=gen, device=dev) * 0.02
+    ag = (torch.randn(300, generator=gen, device=dev) * 1e-3).to(torch.bfloat16)
+    sets = [([p.clone() for p in ps], [torch.zeros_like(p) for p in ps], a.clone(), torch.zeros_like(a),
+             torch.zeros_like(a)) for _ in range(2)]
+    divs = [2.0, 5.0, 7.0, 3.0]
+    mp, mb, ap, am, av = sets[0]
+    for k, d in enumerate(divs):
+        optimizer_step([MuonItem(p, g, b, 0.02, 0.002) for p, g, b in zip(mp, gs, mb)],
+                       [AdamWItem(ap, ag, am, av, 3e-4, 0.1, k + 1)], betas=(0.9, 0.95), max_norm=0.01,
+                       grad_divisor=d)
+    mp2, mb2, ap2, am2, av2 = sets[1]
+    div_t = torch.zeros((), device=dev)
+    cs = CapturedStep([MuonItem(p, g, b, 0.02, 0.002) for p, g, b in zip(mp2, gs, mb2)],
+                      [AdamWItem(ap2, ag, am2, av2, 3e-4, 0.1, 0)], betas=(0.9, 0.95), max_norm=0.01,
+                      grad_divisor=div_t)
+    for d in divs:
+        div_t.fill_(d)
+        cs()
+    torch.cuda.synchronize()
+    assert cs.graph is not None
+    for x, y in zip(mp + mb + [ap, am, av], mp2 + mb2 + [ap2, am2, av2]):
+        assert torch.equal(x, y)
