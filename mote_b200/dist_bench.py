@@ -10,6 +10,7 @@ ranks per phase) and a bitwise check that every rank ends the timed steps with t
 
 from __future__ import annotations
 
+import contextlib
 import datetime
 import json
 import statistics
@@ -58,10 +59,17 @@ def _sharded_setup(w, plan, rank, dev, grad_seed):
     return st
 
 
-def _phases(st, w, n: int, dev) -> dict:
-    """Mean ms of each phase of `n` eager steps on this rank (events recorded after each phase)."""
+def _phases(st, w, n: int, dev, gate_ms: float = 20.0) -> dict:
+    """Mean ms of each phase of `n` eager steps on this rank (events recorded after each phase). Each step is queued
+    behind a bounded GPU sleep (torch.cuda._sleep, a clock-counting kernel of about gate_ms) issued right after a
+    barrier on every rank, so the host has enqueued the whole step, collectives included, before the GPU starts it:
+    the phase times are GPU time, not the host's launch work."""
     acc = {p: [] for p in PHASES}
+    cycles = int(gate_ms * 2.0e6)   # SM cycles at up to 2 GHz: at least gate_ms
     for _ in range(n):
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda._sleep(cycles)
         marks = []
         st.step(max_norm=w.clip, marks=marks)
         torch.cuda.synchronize(dev)
@@ -176,7 +184,8 @@ def run(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         dist.barrier()
         l1 = L.lib.moteopt_launch_count()
-        with ClockSampler(gpu_id) as clk:
+        # clocks sampled by rank 0 alone (one nvidia-smi for the node; the line reports rank 0's GPU)
+        with ClockSampler(gpu_id) if rank == 0 else contextlib.nullcontext() as clk:
             e0.record(stream)
             for _ in range(args.steps):
                 run_step()
@@ -236,8 +245,8 @@ def run(args, rank: int, world: int, local_rank: int):
                        "IPC mappings, one-element all-reduce as the ordering barrier)" if not peer_error
                        else f"NCCL all-gather of bf16 O ({peer_error})")},
             "ranks_equal": ranks_equal,
-            "phases_ms": {"how": "eager steps, CUDA events after each phase on every rank; max and mean over ranks",
-                          **phases},
+            "phases_ms": {"how": "eager steps queued behind a GPU sleep (so host launch work is hidden), CUDA events "
+                                 "after each phase on every rank; max and mean over ranks", **phases},
             "roofline": {"bound": "tensor", "kernel": "ns_gemm_kernel", "achieved": round(achieved, 1),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
@@ -252,7 +261,7 @@ def run(args, rank: int, world: int, local_rank: int):
                            "stream while the previous step computes, then moved to the grad regions; norm read back. "
                            "Every rank uploads its own grads at once, so the aggregate host-to-device rate "
                            "(h2d_aggregate_gbs) bounds the loop as N grows"},
-            "clocks": clk.summary(),
+            "clocks": clk.summary() if rank == 0 else None,
             "gpu_launches": int(allv[:, 3].sum()),
             "zero1_adamw_sweep": zero1,
         }
