@@ -34,6 +34,8 @@ EXPORTS = (
     "moteopt_newton_schulz_workspace_size", "moteopt_newton_schulz",
     "moteopt_moe_update_bias",
     "moteopt_selftest_divide", "moteopt_selftest_wait_timeout",
+    "moteopt_optimizer_step_workspace_size_cfg", "moteopt_muon_step_workspace_size_cfg",
+    "moteopt_newton_schulz_workspace_size_variant", "moteopt_newton_schulz_variant",
 )
 
 
@@ -45,7 +47,7 @@ class MuonParam(C.Structure):
 
 
 class MuonConfig(C.Structure):
-    _fields_ = [("ns_steps", C.c_int), ("rms_scale", C.c_double), ("ns_eps", C.c_double)]
+    _fields_ = [("ns_steps", C.c_int), ("rms_scale", C.c_double), ("ns_eps", C.c_double), ("ns_variant", C.c_int)]
 
 
 class AdamWTensor(C.Structure):
@@ -124,6 +126,11 @@ def _load() -> C.CDLL:
         "moteopt_moe_update_bias": (i32, [C.POINTER(MoeBias), i32, vp]),
         "moteopt_selftest_divide": (i32, [vp, vp, vp, i64, vp]),
         "moteopt_selftest_wait_timeout": (i32, [i32, dbl, vp, vp, vp, vp]),
+        "moteopt_optimizer_step_workspace_size_cfg": (sz, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
+                                                           C.POINTER(AdamWTensor), i32]),
+        "moteopt_muon_step_workspace_size_cfg": (sz, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig)]),
+        "moteopt_newton_schulz_workspace_size_variant": (sz, [i64, i64, i64, i32]),
+        "moteopt_newton_schulz_variant": (i32, [vp, i32, vp, i64, i64, i64, i32, dbl, i32, vp, sz, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

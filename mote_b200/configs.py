@@ -53,6 +53,20 @@ class Workload:
             tot += batch * self.ns_steps * (4.0 * a * a * b + 2.0 * a ** 3)
         return tot
 
+    def ns_flops_gram(self) -> float:
+        """Algorithmic Newton-Schulz FLOPs per step with the opt-in Gram variant (moteopt_muon_config::ns_variant 1):
+        matrices whose long side is at least twice the short one take 4 s^2 l + (4 steps - 3) 2 s^3, the others the
+        reference iteration's steps (4 s^2 l + 2 s^3)."""
+        tot = 0.0
+        for s in self.muon_shapes:
+            batch = int(np.prod(s[:-2])) if len(s) > 2 else 1
+            a, b = min(s[-2], s[-1]), max(s[-2], s[-1])
+            if b >= 2 * a:
+                tot += batch * (4.0 * a * a * b + (4.0 * self.ns_steps - 3.0) * 2.0 * a ** 3)
+            else:
+                tot += batch * self.ns_steps * (4.0 * a * a * b + 2.0 * a ** 3)
+        return tot
+
     def ns_flops_issued(self, tile: int = 256) -> float:
         """Newton-Schulz FLOPs the tensor cores perform per step: the Gram (X X^T) and polynomial (A A) products are
         symmetric, so only their output blocks on and above the diagonal (tile x tile, clipped at the edge) are

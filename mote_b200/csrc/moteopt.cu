@@ -90,7 +90,8 @@ int device_setup(int* sms) {
     if (major != 10 || minor != 0)
       return fail(MOTEOPT_ERR_DEVICE, "libmoteopt is built for sm_100a (B200); device " + std::to_string(dev) +
                                           " is sm_" + std::to_string(major) + std::to_string(minor));
-    MO_CUDA(cudaFuncSetAttribute(ns::ns_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
+    MO_CUDA(cudaFuncSetAttribute(ns::ns_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
+    MO_CUDA(cudaFuncSetAttribute(ns::ns_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ns::kSmemBytes));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (count / 2), 1, 1);
     cfg.blockDim = dim3(ns::kThreads, 1, 1);
@@ -103,7 +104,10 @@ int device_setup(int* sms) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters, ns::ns_gemm_kernel, &cfg));
+    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters, ns::ns_gemm_kernel<false>, &cfg));
+    int clusters_gram = 0;
+    MO_CUDA(cudaOccupancyMaxActiveClusters(&clusters_gram, ns::ns_gemm_kernel<true>, &cfg));
+    clusters = std::min(clusters, clusters_gram);
     if (clusters < 1) return fail(MOTEOPT_ERR_DEVICE, "the 2-CTA Newton-Schulz kernel cannot be resident on this device");
     d.sms = count;
     d.pairs = clusters;
@@ -187,7 +191,14 @@ struct GroupPlan {
   int mv, nv, m, n;        // X dims: valid and padded to multiples of 8
   std::vector<MatRef> mats;
   size_t off_x0 = 0, off_x1 = 0, off_a = 0, off_b = 0;
+  // The opt-in Gram variant (moteopt_muon_config::ns_variant 1) on a matrix whose long side is at least twice its
+  // short one: X0 in, the result in X1; A holds R, B holds B, and the m x m buffers T, Q0, Q1 come in addition.
+  bool gram = false;
+  size_t off_t = 0, off_q0 = 0, off_q1 = 0;
 };
+
+// The X buffer (0: X0, 1: X1) that holds a group's final iterate after `steps` Newton-Schulz iterations.
+int out_buffer(const GroupPlan& g, int steps) { return steps == 0 ? 0 : (g.gram ? 1 : (steps & 1)); }
 
 struct Layout {
   std::vector<GroupPlan> groups;          // Newton-Schulz shape groups, in launch order
@@ -213,7 +224,8 @@ int64_t apply_partials_per_slice(int64_t r, int64_t c) {
 }
 
 int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shapes, const std::vector<int64_t>& norm_numels,
-                 int ns_steps, Layout* L) {
+                 int ns_steps, Layout* L, int ns_variant = 0) {
+  if (ns_variant != 0 && ns_variant != 1) return fail(MOTEOPT_ERR_INVALID, "ns_variant must be 0 or 1");
   L->groups.clear();
   std::map<ShapeKey, std::vector<MatRef>> by_shape;
   std::vector<ShapeKey> order;
@@ -237,6 +249,7 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
       g.nv = g.transposed ? g.rows : g.cols;
       g.m = static_cast<int>(align_up(g.mv, 8));
       g.n = static_cast<int>(align_up(g.nv, 8));
+      g.gram = ns_variant == 1 && ns_steps > 0 && g.nv >= 2 * g.mv;
       g.mats.assign(all.begin() + start, all.begin() + std::min(all.size(), start + kMaxMatsPerGroup));
       L->groups.push_back(std::move(g));
     }
@@ -284,6 +297,14 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
       off = align_up(off + ab, 1024);
       g.off_b = off;
       off = align_up(off + ab, 1024);
+      if (g.gram) {
+        g.off_t = off;
+        off = align_up(off + ab, 1024);
+        g.off_q0 = off;
+        off = align_up(off + ab, 1024);
+        g.off_q1 = off;
+        off = align_up(off + ab, 1024);
+      }
     }
   }
   L->bytes = off;
@@ -502,6 +523,8 @@ int check_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hparam
 int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cfg) {
   if (n < 0 || (n > 0 && (p == nullptr || cfg == nullptr))) return fail(MOTEOPT_ERR_INVALID, "bad Muon param list");
   if (cfg != nullptr && (cfg->ns_steps < 0 || cfg->ns_steps > 100)) return fail(MOTEOPT_ERR_INVALID, "ns_steps out of range");
+  if (cfg != nullptr && cfg->ns_variant != 0 && cfg->ns_variant != 1)
+    return fail(MOTEOPT_ERR_INVALID, "ns_variant must be 0 (the reference iteration) or 1 (Gram Newton-Schulz)");
   for (int i = 0; i < n; ++i) {
     const moteopt_muon_param& x = p[i];
     if (!x.param || !x.grad || !x.momentum_buffer)
@@ -690,35 +713,103 @@ int run_muon(const moteopt_muon_param* P, int n, const moteopt_muon_config* cfg,
   return MOTEOPT_OK;
 }
 
-// Newton-Schulz iterations over every group; `final_src` receives the X buffer holding the result.
-int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStream_t st, int* final_src) {
-  *final_src = 0;
-  if (steps == 0) return MOTEOPT_OK;
-  // launch sets: <= kMaxGroups groups and <= kMaxApply matrices each
-  std::vector<std::pair<size_t, size_t>> sets;   // [begin, end) group ranges
-  {
-    size_t b = 0, mats = 0;
-    for (size_t i = 0; i < L.groups.size(); ++i) {
-      const size_t c = L.groups[i].mats.size();
-      if (i > b && (i - b >= static_cast<size_t>(ns::kMaxGroups) || mats + c > static_cast<size_t>(ns::kMaxApply))) {
-        sets.emplace_back(b, i);
-        b = i;
-        mats = 0;
-      }
-      mats += c;
-    }
-    if (b < L.groups.size()) sets.emplace_back(b, L.groups.size());
+// A tensor map of one bf16 [depth][outer][inner] buffer, cached by its address, geometry and box (the Gram
+// variant's phases point the launch's operand roles at different buffers).
+struct OneMapKey {
+  uintptr_t base;
+  uint64_t inner, outer, depth;
+  uint32_t bi, bo;
+  int swz, dev;
+  bool operator<(const OneMapKey& o) const {
+    return std::tie(base, inner, outer, depth, bi, bo, swz, dev) <
+           std::tie(o.base, o.inner, o.outer, o.depth, o.bi, o.bo, o.swz, o.dev);
   }
+};
+std::map<OneMapKey, CUtensorMap> g_one_maps;
+
+int one_map(void* base, uint64_t inner, uint64_t outer, uint64_t depth, uint32_t bi, uint32_t bo,
+            CUtensorMapSwizzle swz, CUtensorMap* out) {
+  int dev = 0;
+  MO_CUDA(cudaGetDevice(&dev));
+  const OneMapKey key{reinterpret_cast<uintptr_t>(base), inner, outer, depth, bi, bo, static_cast<int>(swz), dev};
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  auto it = g_one_maps.find(key);
+  if (it != g_one_maps.end()) {
+    *out = it->second;
+    return MOTEOPT_OK;
+  }
+  CUtensorMap m;
+  MO_TRY(make_map(&m, base, inner, outer, depth, bi, bo, swz));
+  if (g_one_maps.size() > 16384) g_one_maps.clear();
+  g_one_maps[key] = m;
+  *out = m;
+  return MOTEOPT_OK;
+}
+
+// The three views the kernel uses of one buffer: K-major operand (box 64 x 128), MN-major operand (box 64 x 64),
+// epilogue (32 x 32, 64-byte swizzle).
+struct Views {
+  CUtensorMap k, mn, e;
+};
+int buffer_views(void* base, uint64_t inner, uint64_t outer, uint64_t depth, Views* v) {
+  MO_TRY(one_map(base, inner, outer, depth, ns::BK, ns::HM, CU_TENSOR_MAP_SWIZZLE_128B, &v->k));
+  MO_TRY(one_map(base, inner, outer, depth, 64, ns::BK, CU_TENSOR_MAP_SWIZZLE_128B, &v->mn));
+  MO_TRY(one_map(base, inner, outer, depth, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B, &v->e));
+  return MOTEOPT_OK;
+}
+
+// Launch sets: runs of at most kMaxGroups groups and kMaxApply matrices.
+std::vector<std::vector<const GroupPlan*>> launch_sets(const std::vector<const GroupPlan*>& groups) {
+  std::vector<std::vector<const GroupPlan*>> sets;
+  size_t mats = 0;
+  for (const GroupPlan* g : groups) {
+    if (sets.empty() || sets.back().size() >= static_cast<size_t>(ns::kMaxGroups) ||
+        mats + g->mats.size() > static_cast<size_t>(ns::kMaxApply)) {
+      sets.emplace_back();
+      mats = 0;
+    }
+    sets.back().push_back(g);
+    mats += g->mats.size();
+  }
+  return sets;
+}
+
+// The tile tables of a launch over Lh.g[0..n_groups): phase `only` alone (one launch per phase), or all three phases
+// of an iteration (only = -1).
+void tile_tables(ns::Launch& Lh, int only) {
+  Lh.per_iter = 0;
+  for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
+    Lh.tile_start[ph][0] = 0;
+    for (int gi = 0; gi < Lh.n_groups; ++gi) {
+      const ns::Group& G = Lh.g[gi];
+      const int T = static_cast<int>(cdiv(G.m, ns::TM));
+      Lh.tiles_m[gi] = T;
+      Lh.tiles_n[gi] = static_cast<int>(cdiv(G.n, ns::TN));
+      const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
+      Lh.tile_start[ph][gi + 1] = Lh.tile_start[ph][gi] + ((only < 0 || only == ph) ? G.count * per : 0);
+    }
+    Lh.phase_tiles[ph] = Lh.tile_start[ph][Lh.n_groups];
+    Lh.per_iter += Lh.phase_tiles[ph];
+  }
+}
+
+// The reference iteration (mote/train/muon.py:37-40) over `groups`: one persistent launch per set, or one launch per
+// phase and iteration (moteopt_ns_set_persistent).
+int run_ns_reference(const std::vector<const GroupPlan*>& groups, const Layout& L, char* ws, int steps, int* status,
+                     cudaStream_t st) {
   static thread_local ns::Launch Lh;   // ~20 KB: kept off the stack
   int* done = reinterpret_cast<int*>(ws + L.off_done);
-  for (const auto& set : sets) {
+  for (const auto& set : launch_sets(groups)) {
     std::memset(&Lh, 0, sizeof(Lh));
-    Lh.n_groups = static_cast<int>(set.second - set.first);
+    Lh.n_groups = static_cast<int>(set.size());
     Lh.status = status;
+    Lh.ca = ns::kNsA;
+    Lh.cb = ns::kNsB;
+    Lh.cc = ns::kNsC;
     int first = 0;
-    for (size_t gi = set.first; gi < set.second; ++gi) {
-      const GroupPlan& g = L.groups[gi];
-      ns::Group& G = Lh.g[gi - set.first];
+    for (size_t gi = 0; gi < set.size(); ++gi) {
+      const GroupPlan& g = *set[gi];
+      ns::Group& G = Lh.g[gi];
       MapSet ms;
       MO_TRY(group_maps(ws, g, &ms));
       G.xk[0] = ms.xk[0];
@@ -749,20 +840,7 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
     // the tile sequence [iteration][phase][group][matrix][tile]: 256 x 256 tiles, one per CTA pair; A and B are
     // symmetric, so their phases have the upper-triangle blocks only
     Lh.src0 = 0;
-    Lh.per_iter = 0;
-    for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
-      Lh.tile_start[ph][0] = 0;
-      for (int gi = 0; gi < Lh.n_groups; ++gi) {
-        const ns::Group& G = Lh.g[gi];
-        const int T = static_cast<int>(cdiv(G.m, ns::TM));
-        Lh.tiles_m[gi] = T;
-        Lh.tiles_n[gi] = static_cast<int>(cdiv(G.n, ns::TN));
-        const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
-        Lh.tile_start[ph][gi + 1] = Lh.tile_start[ph][gi] + G.count * per;
-      }
-      Lh.phase_tiles[ph] = Lh.tile_start[ph][Lh.n_groups];
-      Lh.per_iter += Lh.phase_tiles[ph];
-    }
+    tile_tables(Lh, -1);
     const int pairs = device_pairs();
     const int mode = g_ns_persistent.load(std::memory_order_relaxed);
     if (mode == 1 || (mode < 0 && Lh.per_iter <= kPersistentMaxWaves * pairs)) {
@@ -781,7 +859,7 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
       attr[0].val.cooperative = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      MO_CUDA(cudaLaunchKernelEx(&cfg, ns::ns_gemm_kernel, Lh));
+      MO_CUDA(cudaLaunchKernelEx(&cfg, ns::ns_gemm_kernel<false>, Lh));
       MO_LAUNCHED("ns_gemm_kernel (persistent)");
     } else {
       Lh.done = nullptr;
@@ -791,13 +869,161 @@ int run_ns(const Layout& L, char* ws, int steps, int* status, int sms, cudaStrea
           Lh.t_begin = t0;
           Lh.t_end = t0 + Lh.phase_tiles[ph];
           t0 = Lh.t_end;
-          ns::ns_gemm_kernel<<<2 * std::min(Lh.phase_tiles[ph], pairs), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
+          ns::ns_gemm_kernel<false><<<2 * std::min(Lh.phase_tiles[ph], pairs), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
           MO_LAUNCHED("ns_gemm_kernel");
         }
       }
     }
-    *final_src = steps & 1;
   }
+  return MOTEOPT_OK;
+}
+
+// The opt-in Gram Newton-Schulz variant (the reference's research notes, docs/research/efficiency-campaign-2026-08-23.md
+// :903-911; not the reference's iteration) on matrices whose long side is at least twice the short one, X (m x n,
+// m <= n) -> X1:
+//   R = X X^T; for k < steps: B = b R + c R R; Q = a I + B (k = 0) or a Q + B Q; if k < steps - 1: T = a R + B R,
+//   R = a T + B T. Finally X1 = Q X.
+// Every product is a phase of the tcgen05 kernel with the launch's operand roles pointed at the variant's buffers,
+// one launch per phase (the kernel boundary orders them), and rounds once with its a*Y / b*R term (round_once).
+// Storage, which oracle/moteopt_oracle.py::gram_newton_schulz_blocked follows: R and T are stored whole (the Gram
+// phase writes R's upper tiles, ns_mirror_kernel the rest), B's upper tiles only (the polynomial phase reads R's tiles
+// below the diagonal through their mirrors; the update phases read B's likewise), Q whole; the final product reads
+// Q through its upper tiles.
+int run_ns_gram(const std::vector<const GroupPlan*>& groups, char* ws, int steps, int* status, cudaStream_t st) {
+  static thread_local ns::Launch Lh;
+  const int pairs = device_pairs();
+  for (const auto& set : launch_sets(groups)) {
+    const int ng = static_cast<int>(set.size());
+    struct Bufs {
+      Views x0, x1, r, b, t, q[2];
+    };
+    std::vector<Bufs> vb(ng);
+    for (int gi = 0; gi < ng; ++gi) {
+      const GroupPlan& g = *set[gi];
+      const uint64_t c = g.mats.size();
+      MO_TRY(buffer_views(ws + g.off_x0, g.n, g.m, c, &vb[gi].x0));
+      MO_TRY(buffer_views(ws + g.off_x1, g.n, g.m, c, &vb[gi].x1));
+      MO_TRY(buffer_views(ws + g.off_a, g.m, g.m, c, &vb[gi].r));
+      MO_TRY(buffer_views(ws + g.off_b, g.m, g.m, c, &vb[gi].b));
+      MO_TRY(buffer_views(ws + g.off_t, g.m, g.m, c, &vb[gi].t));
+      MO_TRY(buffer_views(ws + g.off_q0, g.m, g.m, c, &vb[gi].q[0]));
+      MO_TRY(buffer_views(ws + g.off_q1, g.m, g.m, c, &vb[gi].q[1]));
+    }
+    // one phase over every group of the set; `roles` points group gi's operand maps at its buffers
+    auto phase = [&](int ph, bool wide, float ca, bool no_aux, auto&& roles) -> int {
+      std::memset(&Lh, 0, sizeof(Lh));
+      Lh.n_groups = ng;
+      Lh.status = status;
+      Lh.ca = ca;
+      Lh.cb = ns::kNsB;
+      Lh.cc = ns::kNsC;
+      Lh.round_once = 1;
+      Lh.no_aux = no_aux ? 1 : 0;
+      int first = 0;
+      for (int gi = 0; gi < ng; ++gi) {
+        const GroupPlan& g = *set[gi];
+        ns::Group& G = Lh.g[gi];
+        // every map slot holds a valid map (the kernel prefetches all of them); the phase's roles override
+        const CUtensorMap& any = vb[gi].r.e;
+        G.xk[0] = G.xk[1] = G.xmn[0] = G.xmn[1] = G.ak = G.bk = G.amn = G.bmn = G.xe[0] = G.xe[1] = G.ae = G.be = any;
+        roles(gi, G);
+        G.m = g.m;
+        G.n = wide ? g.n : g.m;   // m x n products (the Gram phase, the final Q X) or m x m ones
+        G.mv = g.mv;
+        G.nv = wide ? g.nv : g.mv;
+        G.count = static_cast<int>(g.mats.size());
+        G.first = first;
+        G.transposed = g.transposed;
+        first += G.count;
+      }
+      tile_tables(Lh, ph);
+      Lh.src0 = 0;
+      Lh.done = nullptr;
+      Lh.t_begin = 0;
+      Lh.t_end = Lh.per_iter;
+      ns::ns_gemm_kernel<true><<<2 * std::min(Lh.t_end, pairs), ns::kThreads, ns::kSmemBytes, st>>>(Lh);
+      MO_LAUNCHED("ns_gemm_kernel (Gram variant)");
+      return MOTEOPT_OK;
+    };
+    // ns_mirror_kernel (q1 false: src = dst = R) or ns_gram_q1_kernel (q1 true: B -> Q0) over every group of the set
+    auto elementwise = [&](bool q1) -> int {
+      for (int gi = 0; gi < ng; ++gi) {
+        const GroupPlan& g = *set[gi];
+        ns::SymArgs A;
+        A.src = reinterpret_cast<__nv_bfloat16*>(ws + (q1 ? g.off_b : g.off_a));
+        A.dst = reinterpret_cast<__nv_bfloat16*>(ws + (q1 ? g.off_q0 : g.off_a));
+        A.m = g.m;
+        A.mv = g.mv;
+        A.a = ns::kNsA;
+        const int tiles = static_cast<int>(cdiv(g.m, 32));
+        const dim3 grid(static_cast<unsigned>(tiles * tiles), static_cast<unsigned>(g.mats.size()));
+        if (q1) ns::ns_gram_q1_kernel<<<grid, 256, 0, st>>>(A);
+        else ns::ns_mirror_kernel<<<grid, 256, 0, st>>>(A);
+        MO_LAUNCHED(q1 ? "ns_gram_q1_kernel" : "ns_mirror_kernel");
+      }
+      return MOTEOPT_OK;
+    };
+    // R = X X^T (upper tiles), then whole
+    MO_TRY(phase(ns::kGram, true, 0.f, false, [&](int gi, ns::Group& G) {
+      G.xk[0] = vb[gi].x0.k;
+      G.ae = vb[gi].r.e;
+    }));
+    MO_TRY(elementwise(false));
+    int q = 0;   // the Q buffer holding the current Q
+    for (int k = 0; k < steps; ++k) {
+      MO_TRY(phase(ns::kPoly, false, 0.f, false, [&](int gi, ns::Group& G) {   // B = b R + c R R
+        G.ak = vb[gi].r.k;
+        G.amn = vb[gi].r.mn;
+        G.ae = vb[gi].r.e;
+        G.be = vb[gi].b.e;
+      }));
+      if (k == 0) {   // Q = a I + B
+        MO_TRY(elementwise(true));
+      } else {        // Q' = a Q + B Q
+        MO_TRY(phase(ns::kUpdate, false, ns::kNsA, false, [&](int gi, ns::Group& G) {
+          G.bk = vb[gi].b.k;
+          G.bmn = vb[gi].b.mn;
+          G.xmn[0] = vb[gi].q[q].mn;
+          G.xe[0] = vb[gi].q[q].e;
+          G.xe[1] = vb[gi].q[q ^ 1].e;
+        }));
+        q ^= 1;
+      }
+      if (k + 1 < steps) {
+        MO_TRY(phase(ns::kUpdate, false, ns::kNsA, false, [&](int gi, ns::Group& G) {   // T = a R + B R
+          G.bk = vb[gi].b.k;
+          G.bmn = vb[gi].b.mn;
+          G.xmn[0] = vb[gi].r.mn;
+          G.xe[0] = vb[gi].r.e;
+          G.xe[1] = vb[gi].t.e;
+        }));
+        MO_TRY(phase(ns::kUpdate, false, ns::kNsA, false, [&](int gi, ns::Group& G) {   // R = a T + B T
+          G.bk = vb[gi].b.k;
+          G.bmn = vb[gi].b.mn;
+          G.xmn[0] = vb[gi].t.mn;
+          G.xe[0] = vb[gi].t.e;
+          G.xe[1] = vb[gi].r.e;
+        }));
+      }
+    }
+    MO_TRY(phase(ns::kUpdate, true, 0.f, true, [&](int gi, ns::Group& G) {   // X1 = Q X (Q through its upper tiles)
+      G.bk = vb[gi].q[q].k;
+      G.bmn = vb[gi].q[q].mn;
+      G.xmn[0] = vb[gi].x0.mn;
+      G.xe[0] = vb[gi].x0.e;
+      G.xe[1] = vb[gi].x1.e;
+    }));
+  }
+  return MOTEOPT_OK;
+}
+
+// Newton-Schulz iterations over every group (the final iterate of group g is in X[out_buffer(g, steps)]).
+int run_ns(const Layout& L, char* ws, int steps, int* status, cudaStream_t st) {
+  if (steps == 0) return MOTEOPT_OK;
+  std::vector<const GroupPlan*> ref, gram;
+  for (const GroupPlan& g : L.groups) (g.gram ? gram : ref).push_back(&g);
+  if (!ref.empty()) MO_TRY(run_ns_reference(ref, L, ws, steps, status, st));
+  if (!gram.empty()) MO_TRY(run_ns_gram(gram, ws, steps, status, st));
   return MOTEOPT_OK;
 }
 
@@ -821,7 +1047,7 @@ std::vector<ns::MatApply> muon_apply_table(const moteopt_muon_param* P, const mo
 // ema: per Muon param, an EMA buffer or null (null array: none)
 // norms: n_muon outputs (||p_new||_F per Muon param), or null; lr_dev: device array of one lr per Muon param, with
 // the host arrays wd / lr_max (see moteopt_step_extras), or null
-int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int src,
+int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const Layout& L, char* ws, int steps,
               cudaStream_t st, float* const* ema = nullptr, double ema_weight = 0.0, float* norms = nullptr,
               const double* lr_dev = nullptr, const double* wd = nullptr, const double* lr_max = nullptr) {
   double* apply_partials = reinterpret_cast<double*>(ws + L.off_apply);
@@ -845,7 +1071,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       if (stored_as_iterated(g)) {
         FlatOutSeg S;
         std::memset(&S, 0, sizeof(S));
-        S.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+        S.x = ws + (out_buffer(g, steps) ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
         S.out = tab[k].p;
         S.numel = static_cast<int64_t>(g.rows) * g.cols;
         S.neg_lr = tab[k].neg_lr;
@@ -864,7 +1090,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       }
       OutMat M;
       std::memset(&M, 0, sizeof(M));
-      M.x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+      M.x = ws + (out_buffer(g, steps) ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
       M.out = tab[k].p;
       M.ema = e;
       M.partials = part;
@@ -920,7 +1146,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
 
 // The final iterate of every matrix copied out (bf16, the parameter's orientation) to out[param] at the matrix's
 // slice, instead of being applied: the sharded step's owners produce the updates that the ranks all-gather.
-int run_copy_out(const moteopt_muon_param* P, const Layout& L, char* ws, int src, void* const* out, int sms,
+int run_copy_out(const moteopt_muon_param* P, const Layout& L, char* ws, int steps, void* const* out, int sms,
                  cudaStream_t st) {
   static thread_local OutArgs A;
   std::memset(&A, 0, sizeof(A));
@@ -932,7 +1158,7 @@ int run_copy_out(const moteopt_muon_param* P, const Layout& L, char* ws, int src
       const MatRef& r = g.mats[pos];
       const moteopt_muon_param& p = P[r.src];
       void* dst = static_cast<char*>(out[r.src]) + static_cast<size_t>(r.slice) * p.rows * p.cols * 2;
-      const void* x = ws + (src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+      const void* x = ws + (out_buffer(g, steps) ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
       if (stored_as_iterated(g)) {
         FlatOutSeg S;
         std::memset(&S, 0, sizeof(S));
@@ -1004,7 +1230,8 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
     for (int i = 0; i < n_muon; ++i) norm_numels.push_back(muon[i].batch * muon[i].rows * muon[i].cols);
   }
   Layout L;
-  MO_TRY(build_layout(muon_shapes(muon, n_muon), norm_numels, n_muon > 0 ? mcfg->ns_steps : 0, &L));
+  MO_TRY(build_layout(muon_shapes(muon, n_muon), norm_numels, n_muon > 0 ? mcfg->ns_steps : 0, &L,
+                      n_muon > 0 ? mcfg->ns_variant : 0));
   MO_TRY(check_ws(workspace, ws_bytes, L.bytes));
   char* ws = static_cast<char*>(workspace);
   Header* hdr = reinterpret_cast<Header*>(ws);
@@ -1030,14 +1257,13 @@ int run_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_conf
   if (n_adam > 0) MO_TRY(launch_adamw(adam, n_adam, ahp, has_div, div, coef, sms, st, ema, ema_w, lr_dev, div_dev));
   if (n_muon > 0) {
     MO_TRY(run_muon(muon, n_muon, mcfg, L, ws, has_div, div, coef, status, sms, st, div_dev));
-    int final_src = 0;
     if (mcfg->ns_steps > 0) {
       if (t_ns_ev[0] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[0], st));
-      MO_TRY(run_ns(L, ws, mcfg->ns_steps, status, sms, st, &final_src));
+      MO_TRY(run_ns(L, ws, mcfg->ns_steps, status, st));
       if (t_ns_ev[1] != nullptr) MO_CUDA(cudaEventRecord(t_ns_ev[1], st));
     }
-    if (muon_out != nullptr) MO_TRY(run_copy_out(muon, L, ws, final_src, muon_out, sms, st));
-    else MO_TRY(run_apply(muon, mcfg, L, ws, final_src, st, ema != nullptr ? ema + n_adam : nullptr, ema_w,
+    if (muon_out != nullptr) MO_TRY(run_copy_out(muon, L, ws, mcfg->ns_steps, muon_out, sms, st));
+    else MO_TRY(run_apply(muon, mcfg, L, ws, mcfg->ns_steps, st, ema != nullptr ? ema + n_adam : nullptr, ema_w,
                           ex != nullptr ? ex->muon_norms : nullptr, lr_dev != nullptr ? lr_dev + n_adam : nullptr,
                           ex != nullptr ? ex->muon_wd : nullptr, ex != nullptr ? ex->muon_lr_max : nullptr));
   }
@@ -1131,15 +1357,26 @@ int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int 
   return MOTEOPT_OK;
 }
 
-size_t moteopt_optimizer_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps,
-                                             const moteopt_adamw_tensor* adamw, int n_adamw) {
-  if (n_muon < 0 || n_adamw < 0 || (n_muon > 0 && !muon) || (n_adamw > 0 && !adamw)) return 0;
+size_t moteopt_optimizer_step_workspace_size_cfg(const moteopt_muon_param* muon, int n_muon,
+                                                 const moteopt_muon_config* cfg, const moteopt_adamw_tensor* adamw,
+                                                 int n_adamw) {
+  if (n_muon < 0 || n_adamw < 0 || (n_muon > 0 && (!muon || !cfg)) || (n_adamw > 0 && !adamw)) return 0;
   std::vector<int64_t> numels;
   for (int i = 0; i < n_adamw; ++i) numels.push_back(adamw[i].numel);
   for (int i = 0; i < n_muon; ++i) numels.push_back(muon[i].batch * muon[i].rows * muon[i].cols);
   Layout L;
-  if (build_layout(muon_shapes(muon, n_muon), numels, ns_steps, &L) != MOTEOPT_OK) return 0;
+  if (build_layout(muon_shapes(muon, n_muon), numels, cfg ? cfg->ns_steps : 0, &L, cfg ? cfg->ns_variant : 0) !=
+      MOTEOPT_OK)
+    return 0;
   return L.bytes;
+}
+
+size_t moteopt_optimizer_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps,
+                                             const moteopt_adamw_tensor* adamw, int n_adamw) {
+  moteopt_muon_config c;
+  std::memset(&c, 0, sizeof(c));
+  c.ns_steps = ns_steps;
+  return moteopt_optimizer_step_workspace_size_cfg(muon, n_muon, &c, adamw, n_adamw);
 }
 
 int moteopt_optimizer_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* muon_cfg,
@@ -1330,11 +1567,19 @@ int moteopt_clip_coef_from_sums(const double* sums, int n, int clip, double max_
   return MOTEOPT_OK;
 }
 
-size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps) {
-  if (n_muon < 0 || (n_muon > 0 && !muon)) return 0;
+size_t moteopt_muon_step_workspace_size_cfg(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* cfg) {
+  if (n_muon < 0 || (n_muon > 0 && (!muon || !cfg))) return 0;
   Layout L;
-  if (build_layout(muon_shapes(muon, n_muon), {}, ns_steps, &L) != MOTEOPT_OK) return 0;
+  if (build_layout(muon_shapes(muon, n_muon), {}, cfg ? cfg->ns_steps : 0, &L, cfg ? cfg->ns_variant : 0) != MOTEOPT_OK)
+    return 0;
   return L.bytes;
+}
+
+size_t moteopt_muon_step_workspace_size(const moteopt_muon_param* muon, int n_muon, int ns_steps) {
+  moteopt_muon_config c;
+  std::memset(&c, 0, sizeof(c));
+  c.ns_steps = ns_steps;
+  return moteopt_muon_step_workspace_size_cfg(muon, n_muon, &c);
 }
 
 int moteopt_muon_step(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* cfg,
@@ -1542,14 +1787,25 @@ int moteopt_clip_grad_norm_noalloc(void* const* grads, const int64_t* numels, co
   return MOTEOPT_OK;
 }
 
-size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
+size_t moteopt_newton_schulz_workspace_size_variant(int64_t batch, int64_t rows, int64_t cols, int ns_variant) {
   Layout L;
-  if (build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L) != MOTEOPT_OK) return 0;
+  if (build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L, ns_variant) != MOTEOPT_OK) return 0;
   return L.bytes;
+}
+
+size_t moteopt_newton_schulz_workspace_size(int64_t batch, int64_t rows, int64_t cols) {
+  return moteopt_newton_schulz_workspace_size_variant(batch, rows, cols, 0);
 }
 
 int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, int64_t rows, int64_t cols, int steps,
                           double eps, void* workspace, size_t workspace_bytes, moteopt_stream_t stream) {
+  return moteopt_newton_schulz_variant(G, g_dtype, out, batch, rows, cols, steps, eps, 0, workspace, workspace_bytes,
+                                       stream);
+}
+
+int moteopt_newton_schulz_variant(const void* G, int g_dtype, void* out, int64_t batch, int64_t rows, int64_t cols,
+                                  int steps, double eps, int ns_variant, void* workspace, size_t workspace_bytes,
+                                  moteopt_stream_t stream) {
   if (!G || !out) return fail(MOTEOPT_ERR_INVALID, "null input or output");
   if (g_dtype != kF32 && g_dtype != kBF16) return fail(MOTEOPT_ERR_INVALID, "G must be fp32 or bf16");
   if (steps < 0 || steps > 100) return fail(MOTEOPT_ERR_INVALID, "steps out of range");
@@ -1557,7 +1813,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
   int r = device_setup(&sms);
   if (r != MOTEOPT_OK) return r;
   Layout L;
-  r = build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L);
+  r = build_layout({std::make_tuple(batch, rows, cols)}, {}, 1, &L, ns_variant);
   if (r != MOTEOPT_OK) return r;
   r = check_ws(workspace, workspace_bytes, L.bytes);
   if (r != MOTEOPT_OK) return r;
@@ -1612,8 +1868,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
     else ns_normalize_kernel<false><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("ns_normalize_kernel");
   }
-  int final_src = 0;
-  r = run_ns(L, ws, steps, &hdr->status, sms, st, &final_src);
+  r = run_ns(L, ws, steps, &hdr->status, st);
   if (r != MOTEOPT_OK) return r;
   // copy out (transpose back)
   OutArgs O;
@@ -1625,7 +1880,7 @@ int moteopt_newton_schulz(const void* G, int g_dtype, void* out, int64_t batch, 
     for (size_t pos = 0; pos < g.mats.size(); ++pos, ++k) {
       OutMat M;
       std::memset(&M, 0, sizeof(M));
-      M.x = ws + (final_src ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
+      M.x = ws + (out_buffer(g, steps) ? g.off_x1 : g.off_x0) + pos * g.m * g.n * 2;
       M.out = static_cast<char*>(out) + static_cast<size_t>(g.mats[pos].slice) * per * 2;
       M.rows = g.rows;
       M.cols = g.cols;

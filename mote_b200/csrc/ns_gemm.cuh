@@ -41,7 +41,7 @@
 namespace moteopt {
 namespace ns {
 
-constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;   // mote/train/muon.py:31
+constexpr float kNsA = 3.4445f, kNsB = -4.7750f, kNsC = 2.0315f;   // mote/train/muon.py:31 (passed in Launch::ca/cb/cc)
 
 // ---------------------------------------------------------------------------------------------------------------
 struct Tile {
@@ -250,6 +250,7 @@ __device__ __forceinline__ uint32_t sw64(int r, int c) {
 // store has read it, refills it with the operand of the chunk two ahead. The accumulator release goes to the leader
 // CTA; in persistent mode each warp then waits for its stores to complete and counts the tile done for its matrix and
 // phase.
+template <bool kRoundOnce>
 __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_t* tfull, uint64_t* tempty,
                                          uint8_t* ebuf, uint64_t* ebar, uint32_t tmem_base, const WaitCtx& ctx) {
   constexpr int kChunks = TN / EPI_TILE / 2;
@@ -266,7 +267,7 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
   for (int t = L.t_begin + pair; t < L.t_end && ok; t += npairs, ++local) {
     const Tile x = decode_tile(L, t);
     const Group& G = L.g[x.gi];
-    const bool has_aux = x.phase != kGram;
+    const bool has_aux = x.phase != kGram && !(x.phase == kUpdate && L.no_aux);
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
     const int out_cols = x.phase == kUpdate ? G.n : G.m;
@@ -312,7 +313,7 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
         __syncwarp();
       }
       uint32_t out[16];
-      if (x.phase == kGram) {
+      if (!has_aux) {   // kGram, or the Gram variant's plain product: bf16 of the accumulator
 #pragma unroll
         for (int k = 0; k < 16; ++k) out[k] = pack_bf16x2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
       } else {
@@ -322,14 +323,22 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
           const uint4 w = *reinterpret_cast<const uint4*>(row + sw64(lane, cc));
           in[4 * cc] = w.x; in[4 * cc + 1] = w.y; in[4 * cc + 2] = w.z; in[4 * cc + 3] = w.w;
         }
-        if (x.phase == kPoly) {
+        if (kRoundOnce) {   // the Gram variant: out = bf16(coef * aux + acc'), the fp32 terms as the oracle forms them
+          const float ka = x.phase == kPoly ? L.cb : L.ca;
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            float p0 = __uint_as_float(r[2 * k]), p1 = __uint_as_float(r[2 * k + 1]);
+            if (x.phase == kPoly) { p0 = __fmul_rn(L.cc, p0); p1 = __fmul_rn(L.cc, p1); }            // c * (R @ R)
+            out[k] = pack_bf16x2(__fadd_rn(__fmul_rn(ka, bf16_lo(in[k])), p0), __fadd_rn(__fmul_rn(ka, bf16_hi(in[k])), p1));
+          }
+        } else if (x.phase == kPoly) {
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
             float aa0 = __uint_as_float(r[2 * k]), aa1 = __uint_as_float(r[2 * k + 1]);
             round2(aa0, aa1);                                                                   // A @ A
-            float t10 = __fmul_rn(kNsB, bf16_lo(in[k])), t11 = __fmul_rn(kNsB, bf16_hi(in[k]));
+            float t10 = __fmul_rn(L.cb, bf16_lo(in[k])), t11 = __fmul_rn(L.cb, bf16_hi(in[k]));
             round2(t10, t11);                                                                   // b * A
-            float t20 = __fmul_rn(kNsC, aa0), t21 = __fmul_rn(kNsC, aa1);
+            float t20 = __fmul_rn(L.cc, aa0), t21 = __fmul_rn(L.cc, aa1);
             round2(t20, t21);                                                                   // c * (A @ A)
             out[k] = pack_bf16x2(__fadd_rn(t10, t20), __fadd_rn(t11, t21));
           }
@@ -338,7 +347,7 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
           for (int k = 0; k < 16; ++k) {
             float bx0 = __uint_as_float(r[2 * k]), bx1 = __uint_as_float(r[2 * k + 1]);
             round2(bx0, bx1);                                                                   // B @ X
-            float ax0 = __fmul_rn(kNsA, bf16_lo(in[k])), ax1 = __fmul_rn(kNsA, bf16_hi(in[k]));
+            float ax0 = __fmul_rn(L.ca, bf16_lo(in[k])), ax1 = __fmul_rn(L.ca, bf16_hi(in[k]));
             round2(ax0, ax1);                                                                   // a * X
             out[k] = pack_bf16x2(__fadd_rn(ax0, bx0), __fadd_rn(ax1, bx1));
           }
@@ -384,6 +393,8 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// kRoundOnce: the Gram variant's epilogue (Launch::round_once); the reference iteration's instantiation is false.
+template <bool kRoundOnce>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_gemm_kernel(const __grid_constant__ Launch L) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -441,7 +452,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_gemm
     if (lane_id() == 0 && rank == 0) mma(L, sa, sb, full, empty, tfull, tempty, drain, tmem_base, ctx);
     __syncwarp();
   } else {
-    epilogue(L, rank, tfull, tempty, ebuf, ebar, tmem_base, ctx);
+    epilogue<kRoundOnce>(L, rank, tfull, tempty, ebuf, ebar, tmem_base, ctx);
   }
   tc_fence_before();
   __syncthreads();
@@ -451,6 +462,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1) ns_gemm
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicOr(L.status, kStatusAborted);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Gram Newton-Schulz helpers (the opt-in variant of docs/research/efficiency-campaign-2026-08-23.md:903-911 in the
+// reference project; not the reference's iteration). Both work on bf16 [count][m][m] matrices (m padded to a multiple
+// of 8, `mv` valid rows/columns), in 32 x 32 tiles through shared memory, one tile per block: grid (tiles, count).
+struct SymArgs {
+  __nv_bfloat16* src;   // read (its tiles on and above the 256 x 256 block diagonal)
+  __nv_bfloat16* dst;   // written
+  int m, mv;
+  float a;              // ns_gram_q1_kernel: the coefficient a of a*I
+};
+
+// In place: every 32 x 32 tile inside a 256 x 256 block below the block diagonal gets the transpose of its mirror
+// tile (src == dst), so that a Gram matrix whose upper blocks the Gram phase wrote is stored whole.
+__global__ void __launch_bounds__(256) ns_mirror_kernel(const __grid_constant__ SymArgs A) {
+  __shared__ __nv_bfloat16 t[32][33];
+  const int tiles = (A.m + 31) / 32;
+  const int ti = blockIdx.x / tiles, tj = blockIdx.x % tiles;   // destination tile (rows ti, columns tj)
+  if ((ti * 32) / TM <= (tj * 32) / TN) return;                 // on or above the block diagonal: stored already
+  const size_t base = static_cast<size_t>(blockIdx.y) * A.m * A.m;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int k = ty; k < 32; k += 8) {   // source tile (rows tj, columns ti), row k
+    const int r = tj * 32 + k, c = ti * 32 + tx;
+    t[k][tx] = (r < A.m && c < A.m) ? A.src[base + static_cast<size_t>(r) * A.m + c] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int r = ti * 32 + k, c = tj * 32 + tx;
+    if (r < A.m && c < A.m) A.dst[base + static_cast<size_t>(r) * A.m + c] = t[tx][k];
+  }
+}
+
+// Q1 = bf16(a*I + B~) for the variant's first iteration (its Q0 = I, so a*Q0 + B Q0 needs no product): B~ is B read
+// through its upper blocks (a tile below the block diagonal is the transpose of its mirror); the identity covers the
+// valid rows only, so the zero padding stays zero.
+__global__ void __launch_bounds__(256) ns_gram_q1_kernel(const __grid_constant__ SymArgs A) {
+  __shared__ __nv_bfloat16 t[32][33];
+  const int tiles = (A.m + 31) / 32;
+  const int ti = blockIdx.x / tiles, tj = blockIdx.x % tiles;
+  const bool mirror = (ti * 32) / TM > (tj * 32) / TN;
+  const size_t base = static_cast<size_t>(blockIdx.y) * A.m * A.m;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int k = ty; k < 32; k += 8) {
+    const int r = (mirror ? tj : ti) * 32 + k, c = (mirror ? ti : tj) * 32 + tx;
+    t[k][tx] = (r < A.m && c < A.m) ? A.src[base + static_cast<size_t>(r) * A.m + c] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  for (int k = ty; k < 32; k += 8) {
+    const int r = ti * 32 + k, c = tj * 32 + tx;
+    if (r >= A.m || c >= A.m) continue;
+    const float b = __bfloat162float(mirror ? t[tx][k] : t[k][tx]);
+    const float d = (r == c && r < A.mv) ? A.a : 0.f;
+    A.dst[base + static_cast<size_t>(r) * A.m + c] = __float2bfloat16_rn(__fadd_rn(d, b));
+  }
 }
 
 }  // namespace ns

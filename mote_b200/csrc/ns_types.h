@@ -79,6 +79,11 @@ struct Launch {
   int tiles_n[kMaxGroups];               // column blocks of X
   int* done;                             // persistent mode: [matrix][phase] completion arrivals; null: one phase per launch
   int* status;
+  float ca, cb, cc;                      // the quintic's coefficients a, b, c (mote/train/muon.py:31); ca = 0 with
+                                         // no_aux for a plain product
+  int round_once;                        // 0: the reference's rounding of every elementwise op; 1: the product and its
+                                         // a*Y (b*A) term summed in fp32 and rounded once (the Gram variant)
+  int no_aux;                            // kUpdate without the a*Y term: out = bf16(B X) (the Gram variant's Q X0)
 };
 // passed by value as a __grid_constant__ kernel parameter: within the 32764-byte parameter limit of sm_70+ launches
 static_assert(sizeof(Launch) <= 32764, "Launch exceeds the kernel parameter space");

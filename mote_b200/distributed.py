@@ -403,9 +403,11 @@ def capture(step: ShardedStep, max_norm: Optional[float] = 1.0, grad_divisor: Op
     return g, norm
 
 
-def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_scale: float = 0.2) -> Compute:
+def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_scale: float = 0.2,
+                 ns_variant: int = 0) -> Compute:
     """The step's compute on the CUDA library (libmoteopt.so). AdamW's step count is a device counter (so that a
-    captured step stays correct when replayed)."""
+    captured step stays correct when replayed). ns_variant as moteopt_muon_config::ns_variant (0: the reference's
+    iteration)."""
     import ctypes as C
 
     from . import _lib as L
@@ -443,9 +445,9 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
         if dev not in counter:
             counter[dev] = torch.zeros((), dtype=torch.float32, device=dev)
         m_arr, a_arr = muon_array(muon), adamw_array(adam)
-        nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adam))
+        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7, int(ns_variant))
+        nbytes = L.lib.moteopt_optimizer_step_workspace_size_cfg(m_arr, len(muon), C.byref(cfg), a_arr, len(adam))
         ws = workspace(dev, nbytes)
-        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
         hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps), counter[dev].data_ptr())
         outs = L.array(C.c_void_p, [o.data_ptr() for o in muon_out])
         L.check(L.lib.moteopt_optimizer_step_with_coef_out(
@@ -466,7 +468,7 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
             e.param = p.data_ptr()
             e.batch, e.rows, e.cols = (p.shape[0] if p.ndim == 3 else 1), p.shape[-2], p.shape[-1]
             e.lr, e.decay, e.momentum = float(it.lr), float(it.decay), float(it.momentum)
-        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7)
+        cfg = L.MuonConfig(int(ns_steps), float(rms_scale), 1e-7, int(ns_variant))
         ptrs = L.array(C.c_void_p, [o if isinstance(o, int) else o.data_ptr() for o in updates])
         emas = L.array(C.c_void_p, [e.data_ptr() for e in ema]) if ema is not None else None
         if norms is not None and (norms.dtype != torch.float32 or norms.numel() < len(muon) or not norms.is_cuda):

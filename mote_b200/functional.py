@@ -124,7 +124,7 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
                    device_step: Optional[torch.Tensor] = None,
                    ema: Optional[Sequence[Optional[torch.Tensor]]] = None, ema_weight: float = 0.0,
                    muon_norms: Optional[torch.Tensor] = None,
-                   lr_device: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
+                   lr_device: Optional[torch.Tensor] = None, ns_variant: int = 0) -> Optional[torch.Tensor]:
     """mote/train/train.py:944-947 in one call: grads /= grad_divisor; clip_grad_norm_(every grad, max_norm);
     AdamW; Muon. The grads are read, never written. Returns the pre-clip total norm (0-dim device tensor) when
     max_norm is given. With `device_step` (a 0-dim fp32 CUDA tensor) AdamW's step count is that counter, which the
@@ -133,6 +133,9 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     synchronisation.
 
     Fused extras (the work train.py:950-953 and elr.py:85-87 do in separate passes after the step):
+    `ns_variant` 1 runs the opt-in Gram Newton-Schulz variant on the Muon matrices whose long side is at least twice
+    the short one (not the reference's iteration; include/moteopt.h, moteopt_muon_config::ns_variant).
+
     `ema` - one fp32 buffer (or None) per AdamW item, then per Muon item, updated as
     torch._foreach_lerp_(ema, params, ema_weight) in the pass that writes the params; `muon_norms` - an fp32 CUDA
     tensor of len(muon) that receives ||p||_F of every Muon param after the update; `lr_device` - an fp64 CUDA tensor
@@ -140,11 +143,11 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
     `lr` (a schedule under graph capture; see MuonItem for the decay rule)."""
     dev = _device(muon, adamw)
     m_arr, a_arr = muon_array(muon), adamw_array(adamw)
-    nbytes = L.lib.moteopt_optimizer_step_workspace_size(m_arr, len(muon), ns_steps, a_arr, len(adamw))
+    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps), int(ns_variant))
+    nbytes = L.lib.moteopt_optimizer_step_workspace_size_cfg(m_arr, len(muon), C.byref(cfg), a_arr, len(adamw))
     if nbytes == 0:
-        raise L.MoteoptError("optimizer_step: invalid shapes")
+        raise L.MoteoptError("optimizer_step: invalid shapes or ns_variant")
     ws = workspace(dev, nbytes)
-    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
     hp = L.AdamWHparams(float(betas[0]), float(betas[1]), float(eps),
                         device_step.data_ptr() if device_step is not None else None)
     div_t = _device_divisor(grad_divisor, dev)
@@ -192,17 +195,19 @@ def optimizer_step(muon: Sequence[MuonItem] = (), adamw: Sequence[AdamWItem] = (
 
 @torch.no_grad()
 def muon_step(muon: Sequence[MuonItem], *, ns_steps: int = 5, rms_scale: float = 0.2, ns_eps: float = 1e-7,
-              grad_scale: Optional[torch.Tensor] = None) -> None:
-    """mote/train/muon.py:52-100 for a list of parameters (any mix of groups and shapes)."""
+              grad_scale: Optional[torch.Tensor] = None, ns_variant: int = 0) -> None:
+    """mote/train/muon.py:52-100 for a list of parameters (any mix of groups and shapes). ns_variant 1 runs the
+    opt-in Gram Newton-Schulz variant on matrices whose long side is at least twice the short one (include/moteopt.h,
+    moteopt_muon_config::ns_variant); 0, the default, is the reference's iteration."""
     if not muon:
         return
     dev = _device(muon, ())
     arr = muon_array(muon)
-    nbytes = L.lib.moteopt_muon_step_workspace_size(arr, len(muon), ns_steps)
+    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps), int(ns_variant))
+    nbytes = L.lib.moteopt_muon_step_workspace_size_cfg(arr, len(muon), C.byref(cfg))
     if nbytes == 0:
-        raise L.MoteoptError("muon_step: invalid shapes")
+        raise L.MoteoptError("muon_step: invalid shapes or ns_variant")
     ws = workspace(dev, nbytes)
-    cfg = L.MuonConfig(int(ns_steps), float(rms_scale), float(ns_eps))
     L.check(L.lib.moteopt_muon_step(arr, len(muon), C.byref(cfg),
                                     C.c_void_p(grad_scale.data_ptr() if grad_scale is not None else 0),
                                     C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
@@ -292,14 +297,15 @@ class CapturedStep:
                  rms_scale: float = 0.2, ns_eps: float = 1e-7, betas=(0.9, 0.95), eps: float = 1e-8,
                  max_norm: Optional[float] = None, grad_divisor: Optional[float] = None, start_step: int = 0,
                  dynamic_lr: bool = False, ema: Optional[Sequence[Optional[torch.Tensor]]] = None,
-                 ema_weight: float = 0.0, muon_norms: Optional[torch.Tensor] = None, moe: Optional[Sequence] = None):
+                 ema_weight: float = 0.0, muon_norms: Optional[torch.Tensor] = None, moe: Optional[Sequence] = None,
+                 ns_variant: int = 0):
         self.dev = _device(muon, adamw)
         if isinstance(grad_divisor, torch.Tensor) and _device_divisor(grad_divisor, self.dev) is not grad_divisor:
             raise ValueError("CapturedStep: a tensor grad_divisor must be a one-element fp32 tensor on the step's "
                              "device (the graph reads it in place at every replay)")
         self.kw = dict(ns_steps=ns_steps, rms_scale=rms_scale, ns_eps=ns_eps, betas=betas, eps=eps,
                        max_norm=max_norm, grad_divisor=grad_divisor, ema=ema, ema_weight=ema_weight,
-                       muon_norms=muon_norms)
+                       muon_norms=muon_norms, ns_variant=ns_variant)
         self.moe = list(moe) if moe else []
         self.muon, self.adamw = list(muon), list(adamw)
         self.device_step = torch.full((), float(start_step), dtype=torch.float32, device=self.dev)

@@ -67,9 +67,10 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
 
 
 @torch.no_grad()
-def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
+def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, variant: int = 0) -> torch.Tensor:
     """mote/train/muon.py:26-43: the quintic Newton-Schulz orthogonal factor of every matrix of G ([..., m, n]),
-    computed on tcgen05 tensor cores; returns bf16 of G's shape."""
+    computed on tcgen05 tensor cores; returns bf16 of G's shape. variant 1: the opt-in Gram Newton-Schulz variant
+    (not the reference's iteration) when the long side is at least twice the short one."""
     _require_cuda(G, "G")
     if G.ndim < 2:
         raise ValueError("newton_schulz needs a matrix or a batch of matrices")
@@ -81,13 +82,14 @@ def newton_schulz(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.T
     out = torch.empty(G.shape, dtype=torch.bfloat16, device=G.device)
     if G.numel() == 0:
         return out
-    nbytes = L.lib.moteopt_newton_schulz_workspace_size(batch, m, n)
+    nbytes = L.lib.moteopt_newton_schulz_workspace_size_variant(batch, m, n, int(variant))
     if nbytes == 0:
-        raise L.MoteoptError(f"newton_schulz: unsupported shape {tuple(G.shape)}")
+        raise L.MoteoptError(f"newton_schulz: unsupported shape {tuple(G.shape)} or variant {variant}")
     ws = workspace(G.device, nbytes)
-    L.check(L.lib.moteopt_newton_schulz(C.c_void_p(G.data_ptr()), grad_dtype_code(G), C.c_void_p(out.data_ptr()),
-                                        batch, m, n, int(steps), float(eps), C.c_void_p(ws.data_ptr()), ws.numel(),
-                                        C.c_void_p(stream_handle(G.device))), "moteopt_newton_schulz")
+    L.check(L.lib.moteopt_newton_schulz_variant(C.c_void_p(G.data_ptr()), grad_dtype_code(G),
+                                                C.c_void_p(out.data_ptr()), batch, m, n, int(steps), float(eps),
+                                                int(variant), C.c_void_p(ws.data_ptr()), ws.numel(),
+                                                C.c_void_p(stream_handle(G.device))), "moteopt_newton_schulz_variant")
     return out
 
 

@@ -42,14 +42,20 @@ class Muon(_MuonBase):
     weight decay, with per-parameter `param_lr` overrides (mote/train/muon.py:46-100). Every matrix of every group
     is orthogonalised in one batched tcgen05 launch sequence; the decay and the scaled update are then applied in
     one memory-bound pass over every parameter (muon.py:93-99). State: `momentum_buffer` (fp32, the parameter's
-    shape) per parameter."""
+    shape) per parameter.
+
+    `gram_ns=True` (keyword only, not in the reference's signature and not a param-group key, so checkpoints keep
+    the reference's layout) opts into the Gram Newton-Schulz variant of the reference's research notes
+    (docs/research/efficiency-campaign-2026-08-23.md:903-911) on matrices whose long side is at least twice the
+    short one: fewer FLOPs, not the reference's iteration."""
 
     def __init__(self, params, lr: float = 1e-3, momentum: float = 0.95, nesterov: bool = True,
                  weight_decay: float = 0.0, ns_steps: int = 5, rms_scale: float = 0.2, sw_decay: bool = False,
-                 lr_max: float = 1.0):
+                 lr_max: float = 1.0, *, gram_ns: bool = False):
         defaults = dict(lr=lr, momentum=momentum, nesterov=nesterov, weight_decay=weight_decay, ns_steps=ns_steps,
                         rms_scale=rms_scale, sw_decay=sw_decay, lr_max=lr_max)
         torch.optim.Optimizer.__init__(self, params, defaults)
+        self.ns_variant = 1 if gram_ns else 0
 
     def _items(self) -> Dict[Tuple[int, float], List[MuonItem]]:
         """Per (ns_steps, rms_scale): the step's MuonItems (muon.py:55-79)."""
@@ -79,7 +85,7 @@ class Muon(_MuonBase):
     def step(self, closure=None):
         loss = closure() if closure is not None else None
         for (ns, rms), items in self._items().items():
-            F.muon_step(items, ns_steps=ns, rms_scale=rms)
+            F.muon_step(items, ns_steps=ns, rms_scale=rms, ns_variant=getattr(self, "ns_variant", 0))
         return loss
 
 
@@ -198,7 +204,8 @@ def _fusable(opts) -> bool:
     muon_keys, adam_keys = set(), set()
     for o in opts:
         if isinstance(o, Muon):
-            muon_keys.update((int(g["ns_steps"]), float(g["rms_scale"])) for g in o.param_groups)
+            muon_keys.update((int(g["ns_steps"]), float(g["rms_scale"]), getattr(o, "ns_variant", 0))
+                             for g in o.param_groups)
         elif isinstance(o, AdamW):
             adam_keys.update((tuple(float(b) for b in g["betas"]), float(g["eps"])) for g in o.param_groups)
         else:
@@ -232,6 +239,10 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Op
     `moe` (the trainer's MoE layers) runs their routers' bias step after the optimizer step, as train.py:948-949
     (`for m in self._moe: m.update_bias()`), in one launch (functional.moe_update_bias)."""
     opts = getattr(opt, "opts", [opt])
+    variants = {getattr(o, "ns_variant", 0) for o in opts if isinstance(o, Muon)}
+    if len(variants) > 1:
+        raise NotImplementedError("fused_step: every Muon optimizer must use the same Newton-Schulz variant")
+    ns_variant = variants.pop() if variants else 0
     muon_sets: Dict[Tuple[int, float], List[MuonItem]] = {}
     adam_items: List[AdamWItem] = []
     betas, eps = (0.9, 0.999), 1e-8
@@ -256,7 +267,8 @@ def fused_step(opt, max_norm: Optional[float] = None, grad_divisor=None, ema: Op
     if ema is not None:
         bufs = [ema.get(it.param) for it in adam_items] + [ema.get(it.param) for it in muon_items]
     norm = F.optimizer_step(muon_items, adam_items, ns_steps=ns, rms_scale=rms, betas=betas, eps=eps,
-                            max_norm=max_norm, grad_divisor=div, ema=bufs, ema_weight=1.0 - float(ema_decay))
+                            max_norm=max_norm, grad_divisor=div, ema=bufs, ema_weight=1.0 - float(ema_decay),
+                            ns_variant=ns_variant)
     for o, bumped in bumps:
         o._bump(bumped)
     if moe:

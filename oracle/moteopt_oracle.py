@@ -191,6 +191,47 @@ def gram_newton_schulz(G: np.ndarray, steps: int = 5, eps: float = 1e-7) -> np.n
     return X
 
 
+def block_symmetric(M: np.ndarray, block: int = 256) -> np.ndarray:
+    """The matrix a kernel sees when it stores only the block x block tiles on and above the diagonal of M (m x m)
+    and reads a tile below the diagonal as the transpose of its mirror tile: tiles (i, j) with i > j replaced by
+    (j, i)^T; diagonal tiles as stored."""
+    out = np.array(M, copy=True)
+    m = M.shape[-1]
+    for i0 in range(block, m, block):
+        for j0 in range(0, i0, block):
+            out[..., i0:i0 + block, j0:j0 + block] = np.swapaxes(M[..., j0:j0 + block, i0:i0 + block], -1, -2)
+    return out
+
+
+def gram_newton_schulz_blocked(G: np.ndarray, steps: int = 5, eps: float = 1e-7, block: int = 256) -> np.ndarray:
+    """gram_newton_schulz with the storage of the library's GPU kernel (per-phase tcgen05 launches, 256 x 256 output
+    tiles): R and T are stored whole; B is computed on its upper tiles only (the polynomial phase, which reads R's
+    tiles below the diagonal through their mirrors); Q updates read B likewise; the final Q X0 reads Q through its
+    upper tiles. Every product accumulates in fp32 and rounds once to bf16 with its a*Y / b*R term."""
+    if steps < 1:
+        raise ValueError("steps must be >= 1")
+    X = ns_normalize(G, eps)
+    transposed = X.shape[-2] > X.shape[-1]
+    if transposed:
+        X = np.ascontiguousarray(np.swapaxes(X, -1, -2))
+    a, b, c = f32(NS_A), f32(NS_B), f32(NS_C)
+    m = X.shape[-2]
+    eye = np.eye(m, dtype=np.float32)
+    R = _fused_round(np.matmul(X, np.swapaxes(X, -1, -2)))
+    Q = None
+    for k in range(steps):
+        Rs = block_symmetric(R, block)
+        B = block_symmetric(_fused_round(b * Rs + c * np.matmul(Rs, Rs)), block)
+        Q = _fused_round(a * eye + B) if Q is None else _fused_round(a * Q + np.matmul(B, Q))
+        if k < steps - 1:
+            T = _fused_round(a * R + np.matmul(B, R))
+            R = _fused_round(a * T + np.matmul(B, T))
+    X = _fused_round(np.matmul(block_symmetric(Q, block), X))
+    if transposed:
+        X = np.ascontiguousarray(np.swapaxes(X, -1, -2))
+    return X
+
+
 def gram_newton_schulz_f64(G: np.ndarray, steps: int = 5, eps: float = 1e-7) -> np.ndarray:
     """The same schedule in fp64 with no rounding; in exact arithmetic it equals newton_schulz_f64."""
     if steps < 1:

@@ -61,7 +61,8 @@ int main(void) {
   P(moteopt_moe_bias) O(moteopt_moe_bias, expert_bias) O(moteopt_moe_bias, n_experts) O(moteopt_moe_bias, gamma)
   O(moteopt_muon_param, lr) O(moteopt_muon_param, nesterov) O(moteopt_muon_param, grad_dtype)
   O(moteopt_adamw_tensor, numel) O(moteopt_adamw_tensor, step) O(moteopt_adamw_tensor, grad_dtype)
-  O(moteopt_muon_config, rms_scale) O(moteopt_grad_config, max_norm) O(moteopt_grad_config, grad_divisor_device)
+  O(moteopt_muon_config, rms_scale) O(moteopt_muon_config, ns_variant) O(moteopt_grad_config, max_norm)
+  O(moteopt_grad_config, grad_divisor_device)
   O(moteopt_adamw_hparams, device_step)
   return 0;
 }
@@ -138,7 +139,7 @@ int main(void) {
   a[0].numel = 271 * 768; a[0].grad_dtype = MOTEOPT_DTYPE_F32;
   size_t ws = moteopt_optimizer_step_workspace_size(m, 2, 5, a, 1);
   size_t ns = moteopt_newton_schulz_workspace_size(4, 768, 768);
-  moteopt_muon_config mc = {5, 0.2, 1e-7};
+  moteopt_muon_config mc = {5, 0.2, 1e-7, 0};
   moteopt_adamw_hparams hp = {0.9, 0.95, 1e-8, NULL};
   moteopt_grad_config gc = {1, 1.0, 0.0, NULL};
   int rc = moteopt_optimizer_step(m, 2, &mc, a, 1, &hp, &gc, NULL, NULL, 0, NULL);   /* null pointers: refused */

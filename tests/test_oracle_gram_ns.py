@@ -59,3 +59,25 @@ def test_flops_fall_on_every_eligible_shape():
     assert O.gram_ns_flops(768, 768) > O.ns_flops(768, 768)
     # 768 x 3072: 4 s^2 l + 34 s^3 = 50 s^3 against 5 (4 s^2 l + 2 s^3) = 90 s^3, a 1.8x cut
     assert O.ns_flops(768, 3072) / O.gram_ns_flops(768, 3072) == pytest.approx(90 / 50)
+
+
+@pytest.mark.parametrize("shape", [(256, 1024), (2, 512, 2048), (1024, 300), (600, 1800), (768, 3072)])
+def test_the_kernel_storage_meets_the_same_bar(shape):
+    """The GPU kernel's storage (gram_newton_schulz_blocked: R, T whole; B and the final Q read through their upper
+    256 x 256 tiles) is as accurate as the reference iteration, and stays near the specification."""
+    u = ns_input(shape, 11)
+    g = O.gram_newton_schulz_blocked(u, 5)
+    o = O.newton_schulz(u, 5)
+    exact = O.newton_schulz_f64(u, 5)
+    assert O.rel_frob(g, o) <= NS5_TOL
+    assert O.rel_frob(g, exact) <= O.rel_frob(o, exact) + EXACT_SLACK
+    assert O.rel_frob(g, O.gram_newton_schulz(u, 5)) <= 2e-2
+    assert np.array_equal(g, O.bf16_round(g))
+
+
+def test_block_symmetric_reads_lower_tiles_through_their_mirrors():
+    m = np.arange(600 * 600, dtype=np.float32).reshape(600, 600)
+    s = O.block_symmetric(m, 256)
+    assert np.array_equal(s[:256, :], m[:256, :]) and np.array_equal(s[256:512, 256:], m[256:512, 256:])
+    assert np.array_equal(s[256:512, :256], m[:256, 256:512].T) and np.array_equal(s[512:, 256:512], m[256:512, 512:].T)
+    assert np.array_equal(s[512:, 512:], m[512:, 512:])
