@@ -885,10 +885,10 @@ int run_ns_reference(const std::vector<const GroupPlan*>& groups, const Layout& 
 //   R = a T + B T. Finally X1 = Q X.
 // Every product is a phase of the tcgen05 kernel with the launch's operand roles pointed at the variant's buffers,
 // one launch per phase (the kernel boundary orders them), and rounds once with its a*Y / b*R term (round_once).
-// Storage, which oracle/moteopt_oracle.py::gram_newton_schulz_blocked follows: R and T are stored whole (the Gram
-// phase writes R's upper tiles, ns_mirror_kernel the rest), B's upper tiles only (the polynomial phase reads R's tiles
-// below the diagonal through their mirrors; the update phases read B's likewise), Q whole; the final product reads
-// Q through its upper tiles.
+// Storage, which oracle/moteopt_oracle.py::gram_newton_schulz_blocked follows: R is exactly symmetric (the Gram phase
+// writes its upper tiles and ns_symmetrize_kernel mirrors every element below the diagonal, again after each R
+// update), T and Q are stored whole, B on its upper tiles (the update phases read its tiles below the diagonal through
+// their mirrors; B from a symmetric R is symmetric), and the final product reads Q through its upper tiles.
 int run_ns_gram(const std::vector<const GroupPlan*>& groups, char* ws, int steps, int* status, cudaStream_t st) {
   static thread_local ns::Launch Lh;
   const int pairs = device_pairs();
@@ -945,7 +945,7 @@ int run_ns_gram(const std::vector<const GroupPlan*>& groups, char* ws, int steps
       MO_LAUNCHED("ns_gemm_kernel (Gram variant)");
       return MOTEOPT_OK;
     };
-    // ns_mirror_kernel (q1 false: src = dst = R) or ns_gram_q1_kernel (q1 true: B -> Q0) over every group of the set
+    // ns_symmetrize_kernel (q1 false: src = dst = R) or ns_gram_q1_kernel (q1 true: B -> Q0) over every group of the set
     auto elementwise = [&](bool q1) -> int {
       for (int gi = 0; gi < ng; ++gi) {
         const GroupPlan& g = *set[gi];
@@ -958,12 +958,12 @@ int run_ns_gram(const std::vector<const GroupPlan*>& groups, char* ws, int steps
         const int tiles = static_cast<int>(cdiv(g.m, 32));
         const dim3 grid(static_cast<unsigned>(tiles * tiles), static_cast<unsigned>(g.mats.size()));
         if (q1) ns::ns_gram_q1_kernel<<<grid, 256, 0, st>>>(A);
-        else ns::ns_mirror_kernel<<<grid, 256, 0, st>>>(A);
-        MO_LAUNCHED(q1 ? "ns_gram_q1_kernel" : "ns_mirror_kernel");
+        else ns::ns_symmetrize_kernel<<<grid, 256, 0, st>>>(A);
+        MO_LAUNCHED(q1 ? "ns_gram_q1_kernel" : "ns_symmetrize_kernel");
       }
       return MOTEOPT_OK;
     };
-    // R = X X^T (upper tiles), then whole
+    // R = X X^T (upper tiles), then whole and exactly symmetric
     MO_TRY(phase(ns::kGram, true, 0.f, false, [&](int gi, ns::Group& G) {
       G.xk[0] = vb[gi].x0.k;
       G.ae = vb[gi].r.e;
@@ -1004,6 +1004,7 @@ int run_ns_gram(const std::vector<const GroupPlan*>& groups, char* ws, int steps
           G.xe[0] = vb[gi].t.e;
           G.xe[1] = vb[gi].r.e;
         }));
+        MO_TRY(elementwise(false));   // R exactly symmetric again
       }
     }
     MO_TRY(phase(ns::kUpdate, true, 0.f, true, [&](int gi, ns::Group& G) {   // X1 = Q X (Q through its upper tiles)

@@ -475,13 +475,15 @@ struct SymArgs {
   float a;              // ns_gram_q1_kernel: the coefficient a of a*I
 };
 
-// In place: every 32 x 32 tile inside a 256 x 256 block below the block diagonal gets the transpose of its mirror
-// tile (src == dst), so that a Gram matrix whose upper blocks the Gram phase wrote is stored whole.
-__global__ void __launch_bounds__(256) ns_mirror_kernel(const __grid_constant__ SymArgs A) {
+// In place (src == dst): every element below the main diagonal gets its mirror above it, R[r][c] = R[c][r] for r > c,
+// so R is exactly symmetric. The polynomial phase reads R as its right operand row-wise (R R^T) and shares the
+// left operand on diagonal tiles, which is R R only for an exactly symmetric R; the Gram phase's R = X X^T is (its
+// upper blocks are written, the rest comes from here), an update's R = a T + B T is not until this runs.
+__global__ void __launch_bounds__(256) ns_symmetrize_kernel(const __grid_constant__ SymArgs A) {
   __shared__ __nv_bfloat16 t[32][33];
   const int tiles = (A.m + 31) / 32;
   const int ti = blockIdx.x / tiles, tj = blockIdx.x % tiles;   // destination tile (rows ti, columns tj)
-  if ((ti * 32) / TM <= (tj * 32) / TN) return;                 // on or above the block diagonal: stored already
+  if (ti < tj) return;                                          // above the diagonal: kept
   const size_t base = static_cast<size_t>(blockIdx.y) * A.m * A.m;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   for (int k = ty; k < 32; k += 8) {   // source tile (rows tj, columns ti), row k
@@ -491,7 +493,7 @@ __global__ void __launch_bounds__(256) ns_mirror_kernel(const __grid_constant__ 
   __syncthreads();
   for (int k = ty; k < 32; k += 8) {
     const int r = ti * 32 + k, c = tj * 32 + tx;
-    if (r < A.m && c < A.m) A.dst[base + static_cast<size_t>(r) * A.m + c] = t[tx][k];
+    if (r < A.m && c < A.m && r > c) A.dst[base + static_cast<size_t>(r) * A.m + c] = t[tx][k];
   }
 }
 

@@ -203,11 +203,17 @@ def block_symmetric(M: np.ndarray, block: int = 256) -> np.ndarray:
     return out
 
 
+def symmetric_upper(M: np.ndarray) -> np.ndarray:
+    """M with every element below the main diagonal replaced by its mirror above it (exactly symmetric)."""
+    return np.triu(M) + np.swapaxes(np.triu(M, 1), -1, -2)
+
+
 def gram_newton_schulz_blocked(G: np.ndarray, steps: int = 5, eps: float = 1e-7, block: int = 256) -> np.ndarray:
     """gram_newton_schulz with the storage of the library's GPU kernel (per-phase tcgen05 launches, 256 x 256 output
-    tiles): R and T are stored whole; B is computed on its upper tiles only (the polynomial phase, which reads R's
-    tiles below the diagonal through their mirrors); Q updates read B likewise; the final Q X0 reads Q through its
-    upper tiles. Every product accumulates in fp32 and rounds once to bf16 with its a*Y / b*R term."""
+    tiles): R is kept exactly symmetric (its upper triangle mirrored, after X X^T and after every R update), T and Q
+    are stored whole, B is computed on its upper tiles only and read through their mirrors below the diagonal, and
+    the final Q X0 reads Q through its upper tiles. Every product accumulates in fp32 and rounds once to bf16 with
+    its a*Y / b*R term."""
     if steps < 1:
         raise ValueError("steps must be >= 1")
     X = ns_normalize(G, eps)
@@ -217,15 +223,14 @@ def gram_newton_schulz_blocked(G: np.ndarray, steps: int = 5, eps: float = 1e-7,
     a, b, c = f32(NS_A), f32(NS_B), f32(NS_C)
     m = X.shape[-2]
     eye = np.eye(m, dtype=np.float32)
-    R = _fused_round(np.matmul(X, np.swapaxes(X, -1, -2)))
+    R = symmetric_upper(_fused_round(np.matmul(X, np.swapaxes(X, -1, -2))))
     Q = None
     for k in range(steps):
-        Rs = block_symmetric(R, block)
-        B = block_symmetric(_fused_round(b * Rs + c * np.matmul(Rs, Rs)), block)
+        B = block_symmetric(_fused_round(b * R + c * np.matmul(R, R)), block)
         Q = _fused_round(a * eye + B) if Q is None else _fused_round(a * Q + np.matmul(B, Q))
         if k < steps - 1:
             T = _fused_round(a * R + np.matmul(B, R))
-            R = _fused_round(a * T + np.matmul(B, T))
+            R = symmetric_upper(_fused_round(a * T + np.matmul(B, T)))
     X = _fused_round(np.matmul(block_symmetric(Q, block), X))
     if transposed:
         X = np.ascontiguousarray(np.swapaxes(X, -1, -2))

@@ -2,11 +2,13 @@
 notes, docs/research/efficiency-campaign-2026-08-23.md:903-911; not the reference's iteration).
 
 Against its specification with the kernel's storage (oracle.gram_newton_schulz_blocked): the same rounding points
-(every product rounded once with its a*Y / b*R term), so only the fp32 summation order inside a product differs
-(the CPU's against the tensor cores'). The measured distances are recorded with the session's parity record
+(every product rounded once with its a*Y / b*R term) and the same storage (R exactly symmetric, B and the final Q read
+through their upper 256 x 256 tiles), so only the fp32 summation order inside a product differs (the CPU's against
+the tensor cores'). Measured on a B200: at most 8e-5, 2.2e-4 and 3.4e-3 after 1, 2 and 5 iterations over the shapes
+below; the bars are those plus a margin. The measured distances are recorded with the session's parity record
 (tests/conftest.py). Its accuracy bar is the one the reference's own iteration is held to: no farther from the exact
-fp64 iteration than the library's reference iteration, plus 3e-3. Matrices the variant does not take (long side
-under twice the short one) keep the reference iteration bit for bit.
+fp64 iteration than the library's reference iteration (measured: about half as far, 1.2-1.5e-2 against 2.3-3.4e-2).
+Matrices the variant does not take (long side under twice the short one) keep the reference iteration bit for bit.
 """
 
 import numpy as np
@@ -18,7 +20,7 @@ from tests.conftest import record
 
 pytestmark = pytest.mark.gpu
 
-EXACT_SLACK = 3e-3
+EXACT_SLACK = 0.0
 
 # every Gram-eligible matrix shape of c1 (768x3072 both ways, 512x2048), c2 (1024x4096 both ways), c3 (768x2048 both
 # ways), and odd, padded and multi-block ones
@@ -51,7 +53,7 @@ def test_gram_variant_matches_its_specification(dev, shape):
     u = _input(shape, sum(shape))
     exact = O.newton_schulz_f64(u, 5)
     d = {}
-    for steps, tol in ((1, 1e-3), (2, 5e-3), (5, 2e-2)):
+    for steps, tol in ((1, 5e-4), (2, 1e-3), (5, 1e-2)):
         g = _ns(u, steps, dev, 1)
         o = O.gram_newton_schulz_blocked(u, steps)
         d[f"k_o_{steps}"] = O.rel_frob(g, o)

@@ -63,8 +63,9 @@ def test_flops_fall_on_every_eligible_shape():
 
 @pytest.mark.parametrize("shape", [(256, 1024), (2, 512, 2048), (1024, 300), (600, 1800), (768, 3072)])
 def test_the_kernel_storage_meets_the_same_bar(shape):
-    """The GPU kernel's storage (gram_newton_schulz_blocked: R, T whole; B and the final Q read through their upper
-    256 x 256 tiles) is as accurate as the reference iteration, and stays near the specification."""
+    """The GPU kernel's storage (gram_newton_schulz_blocked: R exactly symmetric, T whole; B and the final Q read
+    through their upper 256 x 256 tiles) is as accurate as the reference iteration, and stays near the
+    specification."""
     u = ns_input(shape, 11)
     g = O.gram_newton_schulz_blocked(u, 5)
     o = O.newton_schulz(u, 5)
@@ -81,3 +82,10 @@ def test_block_symmetric_reads_lower_tiles_through_their_mirrors():
     assert np.array_equal(s[:256, :], m[:256, :]) and np.array_equal(s[256:512, 256:], m[256:512, 256:])
     assert np.array_equal(s[256:512, :256], m[:256, 256:512].T) and np.array_equal(s[512:, 256:512], m[256:512, 512:].T)
     assert np.array_equal(s[512:, 512:], m[512:, 512:])
+
+
+def test_symmetric_upper_mirrors_every_element_below_the_diagonal():
+    m = np.arange(2 * 7 * 7, dtype=np.float32).reshape(2, 7, 7)
+    s = O.symmetric_upper(m)
+    assert np.array_equal(s, np.swapaxes(s, -1, -2))
+    assert np.array_equal(np.triu(s), np.triu(m))
