@@ -181,11 +181,15 @@ def run(args, rank: int, world: int, local_rank: int):
             run_step()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         gpu_id = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
-        torch.cuda.synchronize(dev)
-        dist.barrier()
-        l1 = L.lib.moteopt_launch_count()
-        # clocks sampled by rank 0 alone (one nvidia-smi for the node; the line reports rank 0's GPU)
+        # clocks sampled by rank 0 alone (one nvidia-smi for the node; the line reports rank 0's GPU). The sampler
+        # starts before the barrier: every rank enters the timed region together, so no rank's collectives wait
+        # for rank 0's sampler to come up inside another rank's timed region
         with ClockSampler(gpu_id) if rank == 0 else contextlib.nullcontext() as clk:
+            torch.cuda.synchronize(dev)
+            dist.barrier()
+            if clk is not None:
+                clk.restart()
+            l1 = L.lib.moteopt_launch_count()
             e0.record(stream)
             for _ in range(args.steps):
                 run_step()
@@ -225,6 +229,8 @@ def run(args, rank: int, world: int, local_rank: int):
         achieved = float(allv[slow, 4]) / (ns_ms * 1e-3) / 1e12 if ns_ms > 0 else 0.0
         phases = {p: {"max": round(float(allv[:, 5 + k].max()), 4), "mean": round(float(allv[:, 5 + k].mean()), 4)}
                   for k, p in enumerate(PHASES)}
+        phases["owned_update"]["per_rank"] = [round(float(x), 4) for x in allv[:, 5 + PHASES.index("owned_update")]]
+        phases["newton_schulz_per_rank"] = [round(float(x), 4) for x in allv[:, 2]]
         # per GPU: 1/N of the reference FLOPs and state bytes; received in the exchange: the other ranks' bf16 O
         o_bytes = 2.0 * w.numel()[0]
         roof = step_roofline(w.ns_flops() / world, w.state_bytes() / world, o_bytes * (world - 1) / world, peaks, ms)

@@ -127,6 +127,10 @@ class ClockSampler:
         self.t0 = time.monotonic()
         return self
 
+    def restart(self):
+        """Keep only the samples taken from now on (the timed region starts here)."""
+        self.t0 = time.monotonic()
+
     def __exit__(self, *exc):
         self.t1 = time.monotonic()
         if self.proc is not None:
