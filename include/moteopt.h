@@ -189,6 +189,39 @@ MOTEOPT_API int moteopt_grad_sumsq(const void* const* grads, const int64_t* nume
                                    moteopt_stream_t stream);
 MOTEOPT_API int moteopt_clip_coef_from_sums(const double* sums, int n, int clip, double max_norm, float* out_norm_coef,
                                             moteopt_stream_t stream);
+
+/*      The clip's norm as the single-GPU step forms it (the norm of the per-tensor norms, torch's get_total_norm), from
+ *      per-rank per-tensor sums: every grad tensor has an index t in [0, n_tensors) and a rank holds at most one
+ *      piece of it (a ZeRO-1 slice or the whole tensor).
+ *      moteopt_grad_sumsq_tensors: out_tensor_sums[tensors[i]] (device fp64, n_tensors) = sum over grad i of
+ *      (g / grad_divisor)^2, 0 for indices no grad names.
+ *      moteopt_peer_reduce_sumsq: the grad reduce-scatter over peer memory fused with the same sums. Piece p sums its
+ *      `world` sources (src[q]: the piece in rank q's grads, mapped into this process, e.g. through
+ *      moteopt_ipc_import; src[rank] local) element by element in fp32 in rank order, rounds once to `dtype` and
+ *      stores to dst; out_tensor_sums as above over the reduced values. Every source must be complete before the
+ *      call's kernels run and must not change until they end (the caller orders that, e.g. with a collective).
+ *      moteopt_clip_coef_from_tensor_sums: sums [world][n_tensors] (every rank's out_tensor_sums, e.g. all-gathered)
+ *      -> out_norm_coef (device, 2 floats) = [total norm, clip coefficient]: per tensor the ranks' sums added in rank
+ *      order, its fp32 norm, then the fp32 norm of those norms and min(1, max_norm / (norm + 1e-6)) (1 when
+ *      clip == 0), as moteopt_optimizer_step forms them. */
+#define MOTEOPT_MAX_PEERS 8
+typedef struct {
+  void* dst;                           /* this rank's reduced piece */
+  const void* src[MOTEOPT_MAX_PEERS];  /* the piece in rank q's grads, q < world */
+  int64_t numel;
+  int dtype;                           /* MOTEOPT_DTYPE_*: sources and destination */
+  int tensor;                          /* index of the grad tensor the piece belongs to */
+} moteopt_peer_piece;
+MOTEOPT_API int moteopt_grad_sumsq_tensors(const void* const* grads, const int64_t* numels, const int* dtypes,
+                                           const int* tensors, int n, int n_tensors, double grad_divisor,
+                                           double* out_tensor_sums, void* workspace, size_t workspace_bytes,
+                                           moteopt_stream_t stream);
+MOTEOPT_API size_t moteopt_peer_reduce_workspace_size(const moteopt_peer_piece* pieces, int n_pieces);
+MOTEOPT_API int moteopt_peer_reduce_sumsq(const moteopt_peer_piece* pieces, int n_pieces, int world, int n_tensors,
+                                          double grad_divisor, double* out_tensor_sums, void* workspace,
+                                          size_t workspace_bytes, moteopt_stream_t stream);
+MOTEOPT_API int moteopt_clip_coef_from_tensor_sums(const double* sums, int world, int n_tensors, int clip,
+                                                   double max_norm, float* out_norm_coef, moteopt_stream_t stream);
 MOTEOPT_API int moteopt_optimizer_step_with_coef(const moteopt_muon_param* muon, int n_muon,
                                                  const moteopt_muon_config* muon_cfg, const moteopt_adamw_tensor* adamw,
                                                  int n_adamw, const moteopt_adamw_hparams* adamw_hp,

@@ -36,7 +36,10 @@ EXPORTS = (
     "moteopt_selftest_divide", "moteopt_selftest_wait_timeout",
     "moteopt_optimizer_step_workspace_size_cfg", "moteopt_muon_step_workspace_size_cfg",
     "moteopt_newton_schulz_workspace_size_variant", "moteopt_newton_schulz_variant",
+    "moteopt_grad_sumsq_tensors", "moteopt_peer_reduce_workspace_size", "moteopt_peer_reduce_sumsq",
+    "moteopt_clip_coef_from_tensor_sums",
 )
+MAX_PEERS = 8
 
 
 class MuonParam(C.Structure):
@@ -72,6 +75,11 @@ class StepExtras(C.Structure):
 
 class MoeBias(C.Structure):
     _fields_ = [("load_acc", C.c_void_p), ("expert_bias", C.c_void_p), ("n_experts", C.c_int), ("gamma", C.c_float)]
+
+
+class PeerPiece(C.Structure):
+    _fields_ = [("dst", C.c_void_p), ("src", C.c_void_p * MAX_PEERS), ("numel", C.c_int64), ("dtype", C.c_int),
+                ("tensor", C.c_int)]
 
 
 class MoteoptError(RuntimeError):
@@ -131,6 +139,11 @@ def _load() -> C.CDLL:
         "moteopt_muon_step_workspace_size_cfg": (sz, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig)]),
         "moteopt_newton_schulz_workspace_size_variant": (sz, [i64, i64, i64, i32]),
         "moteopt_newton_schulz_variant": (i32, [vp, i32, vp, i64, i64, i64, i32, dbl, i32, vp, sz, vp]),
+        "moteopt_grad_sumsq_tensors": (i32, [C.POINTER(vp), C.POINTER(C.c_int64), C.POINTER(C.c_int),
+                                             C.POINTER(C.c_int), i32, i32, dbl, vp, vp, sz, vp]),
+        "moteopt_peer_reduce_workspace_size": (sz, [C.POINTER(PeerPiece), i32]),
+        "moteopt_peer_reduce_sumsq": (i32, [C.POINTER(PeerPiece), i32, i32, i32, dbl, vp, vp, sz, vp]),
+        "moteopt_clip_coef_from_tensor_sums": (i32, [vp, i32, i32, i32, dbl, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)

@@ -1568,6 +1568,156 @@ int moteopt_clip_coef_from_sums(const double* sums, int n, int clip, double max_
   return MOTEOPT_OK;
 }
 
+// piece_sums_kernel over pieces [0, n) whose chunk partials start at chunk_start[p] (a prefix array of n + 1)
+static int launch_piece_sums(const std::vector<int>& chunk_start, const int* tensors, int n, int n_tensors,
+                             const double* partials, double* out, cudaStream_t st) {
+  if (n > kMaxPieceSums) return fail(MOTEOPT_ERR_LIMIT, "more than 2048 grad pieces in one call");
+  static thread_local PieceSumArgs A;
+  std::memset(&A, 0, sizeof(A));
+  A.n_pieces = n;
+  A.n_tensors = n_tensors;
+  A.partials = partials;
+  A.out = out;
+  for (int p = 0; p <= n; ++p) A.chunk_start[p] = chunk_start[p];
+  for (int p = 0; p < n; ++p) A.tensor[p] = tensors[p];
+  piece_sums_kernel<<<1, 1024, 0, st>>>(A);
+  MO_LAUNCHED("piece_sums_kernel");
+  return MOTEOPT_OK;
+}
+
+static int check_tensor_ids(const int* tensors, int n, int n_tensors) {
+  if (n_tensors < 1 || n_tensors > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "n_tensors must be 1..4096");
+  std::vector<char> seen(static_cast<size_t>(n_tensors), 0);
+  for (int p = 0; p < n; ++p) {
+    if (tensors[p] < 0 || tensors[p] >= n_tensors) return fail(MOTEOPT_ERR_INVALID, "tensor index out of range");
+    if (seen[tensors[p]]) return fail(MOTEOPT_ERR_INVALID, "two pieces of one tensor in one call");
+    seen[tensors[p]] = 1;
+  }
+  return MOTEOPT_OK;
+}
+
+int moteopt_grad_sumsq_tensors(const void* const* grads, const int64_t* numels, const int* dtypes, const int* tensors,
+                               int n, int n_tensors, double grad_divisor, double* out_tensor_sums, void* workspace,
+                               size_t workspace_bytes, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!grads || !numels || !dtypes || !tensors)) || out_tensor_sums == nullptr)
+    return fail(MOTEOPT_ERR_INVALID, "bad grad list or null output");
+  for (int i = 0; i < n; ++i) {
+    if (dtypes[i] != kF32 && dtypes[i] != kBF16) return fail(MOTEOPT_ERR_INVALID, "grad dtype must be fp32 or bf16");
+    if (numels[i] < 0 || (numels[i] > 0 && grads[i] == nullptr)) return fail(MOTEOPT_ERR_INVALID, "bad grad tensor");
+  }
+  MO_TRY(check_tensor_ids(tensors, n, n_tensors));
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  Layout L;
+  MO_TRY(build_layout({}, std::vector<int64_t>(numels, numels + n), 0, &L));
+  MO_TRY(check_ws(workspace, workspace_bytes, L.bytes));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  std::vector<GradSource> src;
+  for (int i = 0; i < n; ++i) src.push_back(GradSource{grads[i], numels[i], dtypes[i]});
+  double* partials = reinterpret_cast<double*>(ws + L.off_norm);
+  const bool has_div = grad_divisor != 0.0 && grad_divisor != 1.0;
+  MO_TRY(launch_sumsq(src, L.norm_tensor_chunk_start, partials, has_div, has_div ? static_cast<float>(grad_divisor) : 1.f,
+                      sms, st));
+  return launch_piece_sums(L.norm_tensor_chunk_start, tensors, n, n_tensors, partials, out_tensor_sums, st);
+}
+
+size_t moteopt_peer_reduce_workspace_size(const moteopt_peer_piece* pieces, int n_pieces) {
+  if (n_pieces < 0 || (n_pieces > 0 && pieces == nullptr)) return 0;
+  std::vector<int64_t> numels;
+  for (int p = 0; p < n_pieces; ++p) numels.push_back(pieces[p].numel);
+  return moteopt_grad_sumsq_workspace_size(numels.data(), n_pieces);
+}
+
+int moteopt_peer_reduce_sumsq(const moteopt_peer_piece* pieces, int n_pieces, int world, int n_tensors,
+                              double grad_divisor, double* out_tensor_sums, void* workspace, size_t workspace_bytes,
+                              moteopt_stream_t stream) {
+  static_assert(MOTEOPT_MAX_PEERS == kMaxPeers, "peer count");
+  if (n_pieces < 0 || (n_pieces > 0 && pieces == nullptr) || out_tensor_sums == nullptr)
+    return fail(MOTEOPT_ERR_INVALID, "bad piece list or null output");
+  if (world < 1 || world > kMaxPeers) return fail(MOTEOPT_ERR_LIMIT, "world must be 1..8");
+  std::vector<int64_t> numels;
+  std::vector<int> tensors;
+  for (int p = 0; p < n_pieces; ++p) {
+    const moteopt_peer_piece& P = pieces[p];
+    if (P.dtype != kF32 && P.dtype != kBF16) return fail(MOTEOPT_ERR_INVALID, "grad dtype must be fp32 or bf16");
+    if (P.numel < 0) return fail(MOTEOPT_ERR_INVALID, "negative piece size");
+    if (P.numel > 0) {
+      if (P.dst == nullptr) return fail(MOTEOPT_ERR_INVALID, "null piece destination");
+      for (int q = 0; q < world; ++q)
+        if (P.src[q] == nullptr) return fail(MOTEOPT_ERR_INVALID, "null piece source");
+    }
+    numels.push_back(P.numel);
+    tensors.push_back(P.tensor);
+  }
+  MO_TRY(check_tensor_ids(tensors.data(), n_pieces, n_tensors));
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  Layout L;
+  MO_TRY(build_layout({}, numels, 0, &L));
+  MO_TRY(check_ws(workspace, workspace_bytes, L.bytes));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  double* partials = reinterpret_cast<double*>(static_cast<char*>(workspace) + L.off_norm);
+  const std::vector<int>& cs = L.norm_tensor_chunk_start;
+  static thread_local PeerReduceArgs A;
+  const bool has_div = grad_divisor != 0.0 && grad_divisor != 1.0;
+  for (int s0 = 0; s0 < n_pieces; s0 += kMaxPeerSegs) {
+    const int n = std::min(n_pieces - s0, kMaxPeerSegs);
+    std::memset(&A, 0, sizeof(A));
+    A.n = n;
+    A.world = world;
+    A.has_div = has_div;
+    A.div = has_div ? static_cast<float>(grad_divisor) : 1.f;
+    A.partials = partials;
+    A.chunk_base = cs[s0];
+    for (int i = 0; i < n; ++i) {
+      const moteopt_peer_piece& P = pieces[s0 + i];
+      A.seg[i].dst = P.dst;
+      for (int q = 0; q < world; ++q) A.seg[i].src[q] = P.src[q];
+      A.seg[i].numel = P.numel;
+      A.seg[i].dtype = P.dtype;
+      A.chunk_start[i] = cs[s0 + i] - A.chunk_base;
+    }
+    A.chunk_start[n] = cs[s0 + n] - A.chunk_base;
+    if (A.chunk_start[n] == 0) continue;
+    // two blocks of 256 threads per SM, each thread with 128 bytes of loads in flight
+    const int grid = std::max(1, std::min(A.chunk_start[n], sms * 2));
+    const int kw = world <= 1 ? 1 : world <= 2 ? 2 : world <= 4 ? 4 : 8;
+    auto go = [&](auto div_tag) {
+      constexpr bool kDiv = decltype(div_tag)::value;
+      switch (kw) {
+        case 1: peer_reduce_kernel<kDiv, 1><<<grid, kMtThreads, 0, st>>>(A); break;
+        case 2: peer_reduce_kernel<kDiv, 2><<<grid, kMtThreads, 0, st>>>(A); break;
+        case 4: peer_reduce_kernel<kDiv, 4><<<grid, kMtThreads, 0, st>>>(A); break;
+        default: peer_reduce_kernel<kDiv, 8><<<grid, kMtThreads, 0, st>>>(A); break;
+      }
+    };
+    if (has_div) go(std::true_type{});
+    else go(std::false_type{});
+    MO_LAUNCHED("peer_reduce_kernel");
+  }
+  return launch_piece_sums(cs, tensors.data(), n_pieces, n_tensors, partials, out_tensor_sums, st);
+}
+
+int moteopt_clip_coef_from_tensor_sums(const double* sums, int world, int n_tensors, int clip, double max_norm,
+                                       float* out_norm_coef, moteopt_stream_t stream) {
+  if (world < 1 || sums == nullptr || out_norm_coef == nullptr) return fail(MOTEOPT_ERR_INVALID, "bad sums");
+  if (n_tensors < 1 || n_tensors > kMaxFinalTensors) return fail(MOTEOPT_ERR_LIMIT, "n_tensors must be 1..4096");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  TensorCoefArgs A;
+  A.world = world;
+  A.n_tensors = n_tensors;
+  A.has_clip = clip != 0;
+  A.max_norm = static_cast<float>(max_norm);
+  A.sums = sums;
+  A.out = out_norm_coef;
+  A.status = nullptr;
+  tensor_coef_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(A);
+  MO_LAUNCHED("tensor_coef_kernel");
+  return MOTEOPT_OK;
+}
+
 size_t moteopt_muon_step_workspace_size_cfg(const moteopt_muon_param* muon, int n_muon, const moteopt_muon_config* cfg) {
   if (n_muon < 0 || (n_muon > 0 && (!muon || !cfg))) return 0;
   Layout L;

@@ -256,6 +256,29 @@ __device__ __forceinline__ double warp_sum_partials(const double* partials, int 
   return s;
 }
 
+// Warp 0's last stage of the global norm: total = fp32(sqrt(sum of the per-tensor norms' squares)), the squares summed
+// in fp64 (lane l takes tensors l, l+32, ... in order, then a fixed xor tree), and the clip coefficient.
+__device__ __forceinline__ void finish_total(const float* tnorm, int n_tensors, int has_clip, float max_norm, float* out,
+                                             int* status, int lane) {
+  double acc = 0.0;
+  for (int t = lane; t < n_tensors; t += 32) acc += static_cast<double>(tnorm[t]) * static_cast<double>(tnorm[t]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) {
+    const float total = static_cast<float>(sqrt(acc));
+    float coef = 1.0f;
+    if (has_clip) {
+      // clamp(max_norm / (total + 1e-6), max=1) as torch evaluates it: a Python float over a tensor is
+      // Tensor.__rdiv__, reciprocal(total + 1e-6) * max_norm (two fp32 roundings); a NaN norm gives NaN, as in torch
+      const float c = __fmul_rn(__frcp_rn(__fadd_rn(total, 1e-6f)), max_norm);
+      coef = (c > 1.0f) ? 1.0f : c;
+    }
+    out[0] = total;
+    out[1] = coef;
+    if (status != nullptr && !isfinite(total)) atomicOr(status, kStatusNonFinite);
+  }
+}
+
 // per-tensor norms -> total norm (the norm of the per-tensor norms, as torch's get_total_norm) -> clip coefficient.
 // One warp per tensor (lanes sum strided chunk partials in fp64, then a fixed xor tree), the per-tensor norms kept in
 // shared memory, then warp 0 sums their squares in the same fixed way: deterministic, and no serial chain of loads.
@@ -296,25 +319,7 @@ __global__ void __launch_bounds__(1024) norm_finalize_kernel(const __grid_consta
     }
   }
   __syncthreads();
-  if (warp == 0) {
-    double acc = 0.0;
-    for (int t = lane; t < A.n_tensors; t += 32) acc += static_cast<double>(tnorm[t]) * static_cast<double>(tnorm[t]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) {
-      const float total = static_cast<float>(sqrt(acc));
-      float coef = 1.0f;
-      if (A.has_clip) {
-        // clamp(max_norm / (total + 1e-6), max=1) as torch evaluates it: a Python float over a tensor is
-        // Tensor.__rdiv__, reciprocal(total + 1e-6) * max_norm (two fp32 roundings); a NaN norm gives NaN, as in torch
-        const float c = __fmul_rn(__frcp_rn(__fadd_rn(total, 1e-6f)), A.max_norm);
-        coef = (c > 1.0f) ? 1.0f : c;
-      }
-      A.out[0] = total;
-      A.out[1] = coef;
-      if (!isfinite(total)) atomicOr(A.status, kStatusNonFinite);
-    }
-  }
+  if (warp == 0) finish_total(tnorm, A.n_tensors, A.has_clip, A.max_norm, A.out, A.status, lane);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -355,6 +360,171 @@ __global__ void coef_from_sums_kernel(const __grid_constant__ CoefArgs A) {
   A.out[0] = total;
   A.out[1] = coef;
   if (A.status != nullptr && !isfinite(total)) atomicOr(A.status, kStatusNonFinite);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The sharded step's grad reduce-scatter, read from every rank's grad region over NVLink (peer mappings), fused with
+// the clip's sums of squares. Element k of a piece: the sum over ranks q = 0, 1, ... of src[q][k] in fp32, in that
+// order (the first value taken as it is), rounded once to the grads' type and stored to dst; then (dst[k] / div)^2
+// joins the chunk's fp64 partial. A chunk's elements reach a thread in sumsq_chunks' order (full aligned chunks: the
+// thread's 16-byte vectors t, t + 256, ...; ragged ones: 4-element vectors, then single elements), so the partials
+// of a piece equal sumsq_chunks' partials of the same reduced values.
+__device__ __forceinline__ void unpack8_bf16(const uint4& w, float* v) {
+  v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+  v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z); v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
+}
+__device__ __forceinline__ void add8_bf16(const uint4& w, float* v) {
+  v[0] = __fadd_rn(v[0], bf16_lo(w.x)); v[1] = __fadd_rn(v[1], bf16_hi(w.x));
+  v[2] = __fadd_rn(v[2], bf16_lo(w.y)); v[3] = __fadd_rn(v[3], bf16_hi(w.y));
+  v[4] = __fadd_rn(v[4], bf16_lo(w.z)); v[5] = __fadd_rn(v[5], bf16_hi(w.z));
+  v[6] = __fadd_rn(v[6], bf16_lo(w.w)); v[7] = __fadd_rn(v[7], bf16_hi(w.w));
+}
+__device__ __forceinline__ float4 add4(const float4& a, const float4& b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+// v rounded to the grads' type (as floats) and stored at g[i..i+3]
+__device__ __forceinline__ float4 store_g4(void* g, int64_t i, int dt, float4 v) {
+  if (dt == kBF16) {
+    const uint32_t lo = pack_bf16x2(v.x, v.y), hi = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(g) + i) = make_uint2(lo, hi);
+    return make_float4(bf16_lo(lo), bf16_hi(lo), bf16_lo(hi), bf16_hi(hi));
+  }
+  *reinterpret_cast<float4*>(reinterpret_cast<float*>(g) + i) = v;
+  return v;
+}
+__device__ __forceinline__ float store_g1(void* g, int64_t i, int dt, float v) {
+  if (dt == kBF16) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    reinterpret_cast<__nv_bfloat16*>(g)[i] = b;
+    return __bfloat162float(b);
+  }
+  reinterpret_cast<float*>(g)[i] = v;
+  return v;
+}
+
+// kW: the largest number of ranks the instantiation sums (1, 2, 4 or 8; world <= kW); each thread keeps 8 / kW of
+// its 16-byte vectors of every rank in flight at once (128 bytes), so the latency of peer loads is covered.
+template <bool kDiv, int kW>
+__device__ __forceinline__ void peer_reduce_chunks(const PeerReduceArgs& A, double* red) {
+  constexpr int U = 8 / kW;
+  const int total = A.chunk_start[A.n];
+  const GradXform X{kDiv ? 1 : 0, A.div, 0, 1.f};
+  const int world = A.world;
+  for (int c = blockIdx.x; c < total; c += gridDim.x) {
+    const int s = find_seg(A.chunk_start, A.n, c);
+    const PeerSeg& S = A.seg[s];
+    const int64_t begin = static_cast<int64_t>(c - A.chunk_start[s]) * kChunk;
+    const int64_t end = min(begin + kChunk, S.numel);
+    MO_CHECK(s >= 0 && s < A.n && begin >= 0 && begin < S.numel && world >= 1 && world <= kW);
+    bool a16 = aligned16(S.dst), vec = g_vec_ok(S.dst, S.dtype);
+    for (int q = 0; q < world; ++q) {
+      a16 = a16 && aligned16(S.src[q]);
+      vec = vec && g_vec_ok(S.src[q], S.dtype);
+    }
+    double acc = 0.0;
+    if (end - begin == kChunk && a16) {
+      if (S.dtype == kBF16) {   // 2048 16-byte vectors: thread t takes t + 256 k, k = 0..7
+        uint4* d = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(S.dst) + begin);
+        for (int k0 = 0; k0 < 8; k0 += U) {
+          uint4 w[kW][U];
+#pragma unroll
+          for (int q = 0; q < kW; ++q) {   // every rank's vectors in flight before the first add
+            if (q < world) {
+              const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(S.src[q]) + begin);
+#pragma unroll
+              for (int j = 0; j < U; ++j) w[q][j] = p[threadIdx.x + (k0 + j) * kMtThreads];
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < U; ++j) {
+            float v[8];
+            unpack8_bf16(w[0][j], v);
+#pragma unroll
+            for (int q = 1; q < kW; ++q)
+              if (q < world) add8_bf16(w[q][j], v);
+            const uint4 o = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                       pack_bf16x2(v[6], v[7]));
+            d[threadIdx.x + (k0 + j) * kMtThreads] = o;
+            acc = sq_acc8_bf16(o, X, acc);
+          }
+        }
+      } else {                  // 4096 16-byte vectors: thread t takes t + 256 k, k = 0..15
+        float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(S.dst) + begin);
+        for (int k0 = 0; k0 < 16; k0 += U) {
+          float4 w[kW][U];
+#pragma unroll
+          for (int q = 0; q < kW; ++q) {
+            if (q < world) {
+              const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(S.src[q]) + begin);
+#pragma unroll
+              for (int j = 0; j < U; ++j) w[q][j] = p[threadIdx.x + (k0 + j) * kMtThreads];
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < U; ++j) {
+            float4 v = w[0][j];
+#pragma unroll
+            for (int q = 1; q < kW; ++q)
+              if (q < world) v = add4(v, w[q][j]);
+            d[threadIdx.x + (k0 + j) * kMtThreads] = v;
+            acc = sq_acc4_f32(v, X, acc);
+          }
+        }
+      }
+    } else if (vec) {
+      const int64_t vend = begin + ((end - begin) & ~int64_t(3));
+      for (int64_t i = begin + 4 * threadIdx.x; i < vend; i += 4 * kMtThreads) {
+        float4 v = load_g4(S.src[0], i, S.dtype);
+        for (int q = 1; q < world; ++q) v = add4(v, load_g4(S.src[q], i, S.dtype));
+        acc = sq_acc4_f32(store_g4(S.dst, i, S.dtype, v), X, acc);
+      }
+      for (int64_t i = vend + threadIdx.x; i < end; i += kMtThreads) {
+        float v = load_g1(S.src[0], i, S.dtype);
+        for (int q = 1; q < world; ++q) v = __fadd_rn(v, load_g1(S.src[q], i, S.dtype));
+        acc = sqacc(X(store_g1(S.dst, i, S.dtype, v)), acc);
+      }
+    } else {
+      for (int64_t i = begin + threadIdx.x; i < end; i += kMtThreads) {
+        float v = load_g1(S.src[0], i, S.dtype);
+        for (int q = 1; q < world; ++q) v = __fadd_rn(v, load_g1(S.src[q], i, S.dtype));
+        acc = sqacc(X(store_g1(S.dst, i, S.dtype, v)), acc);
+      }
+    }
+    const double tot = block_sum(acc, red);
+    if (threadIdx.x == 0) A.partials[A.chunk_base + c] = tot;
+  }
+}
+
+template <bool kDiv, int kW>
+__global__ void __launch_bounds__(kMtThreads, 2) peer_reduce_kernel(const __grid_constant__ PeerReduceArgs A) {
+  __shared__ double red[kMtThreads / 32];
+  peer_reduce_chunks<kDiv, kW>(A, red);
+}
+
+// out[tensor[p]] = piece p's sum of squares (its partials summed as warp_sum_partials sums a tensor's), 0 elsewhere
+__global__ void __launch_bounds__(1024) piece_sums_kernel(const __grid_constant__ PieceSumArgs A) {
+  for (int t = static_cast<int>(threadIdx.x); t < A.n_tensors; t += static_cast<int>(blockDim.x)) A.out[t] = 0.0;
+  __syncthreads();
+  const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+  for (int p = warp; p < A.n_pieces; p += static_cast<int>(blockDim.x >> 5)) {
+    MO_CHECK(A.tensor[p] >= 0 && A.tensor[p] < A.n_tensors && A.chunk_start[p] <= A.chunk_start[p + 1]);
+    const double s = warp_sum_partials(A.partials, A.chunk_start[p], A.chunk_start[p + 1], lane);
+    if (lane == 0) A.out[A.tensor[p]] = s;
+  }
+}
+
+// The global norm from every rank's per-tensor sums: per tensor, the ranks' sums added in rank order (a tensor held
+// whole by one rank keeps its sum exactly), its norm rounded to fp32, then finish_total as norm_finalize_kernel.
+__global__ void __launch_bounds__(1024) tensor_coef_kernel(const __grid_constant__ TensorCoefArgs A) {
+  __shared__ float tnorm[kMaxFinalTensors];
+  for (int t = static_cast<int>(threadIdx.x); t < A.n_tensors; t += static_cast<int>(blockDim.x)) {
+    double s = 0.0;
+    for (int r = 0; r < A.world; ++r) s += A.sums[static_cast<size_t>(r) * A.n_tensors + t];
+    tnorm[t] = static_cast<float>(sqrt(s));
+  }
+  __syncthreads();
+  if ((threadIdx.x >> 5) == 0) finish_total(tnorm, A.n_tensors, A.has_clip, A.max_norm, A.out, A.status,
+                                            static_cast<int>(threadIdx.x & 31));
 }
 
 // ---------------------------------------------------------------------------------------------------------------

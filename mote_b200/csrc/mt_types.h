@@ -48,7 +48,53 @@ struct SumsqArgs {
   SumsqSeg seg[kMaxNormSeg];
 };
 
+// The sharded step's grad reduce-scatter over peer memory, fused with the clip's sums of squares: one piece is one
+// grad tensor's share of this rank's segment; src[q] is where that share starts in rank q's grad region (mapped into
+// this process; src[rank] is local); dst receives the sum over the ranks.
+constexpr int kMaxPeers = 8;
+constexpr int kMaxPeerSegs = 160;
+struct PeerSeg {
+  void* dst;
+  const void* src[kMaxPeers];
+  int64_t numel;
+  int dtype;
+  int pad_;
+};
+struct PeerReduceArgs {
+  int n;
+  int world;
+  int chunk_base;            // index of this launch's first chunk in the partials array
+  int has_div;
+  float div;
+  double* partials;          // one fp64 sum of squares per chunk of the reduced grads
+  int chunk_start[kMaxPeerSegs + 1];
+  PeerSeg seg[kMaxPeerSegs];
+};
+
+// Per-tensor sums of squares from chunk partials: out[tensor[p]] = sum of piece p's partials, 0 for tensors without a
+// piece here.
+constexpr int kMaxPieceSums = 2048;
+struct PieceSumArgs {
+  int n_pieces;
+  int n_tensors;
+  const double* partials;
+  double* out;
+  int chunk_start[kMaxPieceSums + 1];
+  int tensor[kMaxPieceSums];
+};
+
 constexpr int kMaxFinalTensors = 4096;
+
+// total norm and clip coefficient from every rank's per-tensor sums of squares ([world][n_tensors], fp64)
+struct TensorCoefArgs {
+  int world;
+  int n_tensors;
+  int has_clip;
+  float max_norm;
+  const double* sums;
+  float* out;                // out[0] = total norm, out[1] = clip coefficient (1 when no clip)
+  int* status;
+};
 struct FinalizeArgs {
   int n_tensors;
   int has_clip;

@@ -235,6 +235,7 @@ def run(args, rank: int, world: int, local_rank: int):
         o_bytes = 2.0 * w.numel()[0]
         roof = step_roofline(w.ns_flops() / world, w.state_bytes() / world, o_bytes * (world - 1) / world, peaks, ms)
         h2d = int((st.gm.numel() + st.ga.numel()) * 2)
+        peer_grads = st._peer_pieces is not None
         held["graph"] = None
         st.close()
         zero1 = None if args.no_other_configs else _zero1_sweep(world, rank, dev, peaks)
@@ -246,7 +247,10 @@ def run(args, rank: int, world: int, local_rank: int):
             "config": bench_config(w, world),
             "launch": {"timed": "CUDA graph of the whole sharded step" if captured
                        else f"eager (graph capture failed: {capture_error})", "collectives":
-                       "NCCL reduce-scatter (grads), all-gather (per-rank sums of squares), all-gather (AdamW fp32 "
+                       ("grads reduced by reading every rank's grads over NVLink (CUDA IPC mappings, one-element "
+                        "all-reduce as the ordering barrier; per-tensor sums of squares in the same pass)"
+                        if peer_grads else "NCCL reduce-scatter (grads)") +
+                       ", all-gather (per-rank per-tensor sums of squares), all-gather (AdamW fp32 "
                        "params); Muon updates: " + ("every rank's bf16 O read over NVLink by the apply kernel (CUDA "
                        "IPC mappings, one-element all-reduce as the ordering barrier)" if not peer_error
                        else f"NCCL all-gather of bf16 O ({peer_error})")},

@@ -10,8 +10,9 @@ Every parameter is a contiguous view of its region, so a model's parameters can 
 
 Step (grads: each rank's local, unreduced grads in the grad regions):
   1. reduce-scatter (sum) of both grad regions: rank r receives the reduced grads of its own segments;
-  2. rank r's sum of (g / divisor)^2 over what it owns, all-gathered and summed in rank order -> the global norm and
-     clip coefficient (bitwise identical on every rank);
+  2. rank r's sum of (g / divisor)^2 per grad tensor over what it owns, all-gathered; per tensor the ranks' sums
+     added in rank order -> the per-tensor norms -> their norm (torch's get_total_norm, as the single-GPU step forms
+     it) and the clip coefficient, bitwise identical on every rank;
   3. rank r runs AdamW on its slice and, for its matrices, Muon's momentum and Newton-Schulz, writing the
      orthogonalised updates O (bf16) into its segment of an update region laid out like the Muon param region;
   4. all-gather of the update region (bf16) and of the AdamW param region (fp32);
@@ -21,7 +22,11 @@ Step (grads: each rank's local, unreduced grads in the grad regions):
 With peer updates enabled (`enable_peer_updates`, NCCL only), steps 4-5 for the Muon region become one pass: every
 rank maps the other ranks' update regions (CUDA IPC, once), a one-element all-reduce orders the owners' writes
 before the reads, and the apply kernel reads each owner's O straight over NVLink while it updates the local params,
-so no gathered copy of O is ever written.
+so no gathered copy of O is ever written. The same mappings of the grad regions turn steps 1-2 into one pass: after a
+one-element all-reduce (every rank's grads complete), each rank reads its segments from every rank's grads over
+NVLink, sums them in rank order, stores the reduced grads and forms the per-tensor sums of squares in the same pass
+(moteopt_peer_reduce_sumsq); the later all-reduce before the O reads orders every rank's grad reads before any rank
+can overwrite its grads.
 Collectives go through torch.distributed (NCCL on GPUs; gloo works for the host-side tests). The compute steps are
 injected (`Compute`), so the same choreography runs with the CUDA library or with a CPU stand-in.
 """
@@ -125,19 +130,26 @@ def make_plan(muon_shapes, adam_shapes, world: int, ns_steps: int = 5) -> ShardP
 # -----------------------------------------------------------------------------------------------------------------
 @dataclass
 class Compute:
-    """The step's compute, injected: `sumsq(views, divisor) -> 0-dim fp64 tensor` (sum of (g/divisor)^2 over the
-    views), `coef(sums, max_norm) -> 2-element fp32 tensor [norm, coef]`, `update(muon_items, adam_items, coef,
+    """The step's compute, injected: `sumsq(views, tensors, n_tensors, divisor) -> fp64 tensor [n_tensors]` (per grad
+    tensor index, the sum of (g/divisor)^2 over the views that belong to it; 0 for the others), `coef(sums, n_tensors,
+    max_norm) -> 2-element fp32 tensor [norm, coef]` from every rank's sums ([world * n_tensors], rank-major: per
+    tensor the ranks' sums added in rank order, the fp32 norm of each tensor, then the norm of those norms),
+    `update(muon_items, adam_items, coef,
     divisor, muon_out)` with items as in mote_b200.functional (AdamW applied; Muon's update O written to the bf16
     tensors `muon_out`, one per Muon item), and `apply(muon_items, updates, ema=None, ema_weight=0.0, norms=None)`:
     p = p*(1-decay); p += -lr*(O*scale) for every item (grad and momentum buffer unused), then, when given,
     ema[k] = lerp(ema[k], p, ema_weight) and norms[k] = ||p||_F in the same pass. `ema(emas, params, weight)` lerps
-    tensors that no pass writes (the all-gathered AdamW region)."""
+    tensors that no pass writes (the all-gathered AdamW region). `peer_reduce(pieces, world, n_tensors, divisor) ->
+    fp64 [n_tensors]`, when given, reduces the grads straight from every rank's memory: each piece is (reduced view,
+    the piece's address in every rank's grad region, tensor index); it stores the reduced grads and returns `sumsq`'s
+    result for them."""
     sumsq: Callable
     coef: Callable
     update: Callable
     apply: Callable
     set_step: Optional[Callable] = None   # set_step(device, n): AdamW's step count, when the compute keeps one
     ema: Optional[Callable] = None
+    peer_reduce: Optional[Callable] = None
 
 
 def _reduce_scatter(out: torch.Tensor, flat: torch.Tensor, seg: int, rank: int, group=None) -> None:
@@ -186,6 +198,9 @@ class ShardedStep:
         self.peer_ptrs: Optional[List[int]] = None   # update region of every rank, mapped into this process
         self._peer_bases: List[int] = []
         self._flag = None
+        self._peer_pieces: Optional[list] = None     # the grad pieces this rank reduces from every rank's memory
+        self._gflag = None
+        self.n_tensors = len(plan.adam_shapes) + len(plan.muon_shapes)   # AdamW grads first, as the 1-GPU clip
         self.ema_decay: Optional[float] = None
         self.em: Optional[torch.Tensor] = None   # EMA of the Muon and AdamW param regions (every rank, replicated)
         self.ea: Optional[torch.Tensor] = None
@@ -204,28 +219,53 @@ class ShardedStep:
         self.em = torch.zeros_like(self.pm) if zero_init else self.pm.detach().clone()
         self.ea = torch.zeros_like(self.pa) if zero_init else self.pa.detach().clone()
 
-    def enable_peer_updates(self) -> None:
-        """Map every rank's update region into this process (CUDA IPC through libmoteopt); collective, eager, once."""
+    def enable_peer_updates(self, peer_grads: Optional[bool] = None) -> None:
+        """Map every rank's update region into this process (CUDA IPC through libmoteopt); collective, eager, once.
+        With `peer_grads` (and a Compute that has `peer_reduce`) the grad regions are mapped too, and the step reduces
+        the grads by reading them from every rank's memory instead of an NCCL reduce-scatter. By default it does so on
+        2 ranks only: on B200s with c1's 187 MB of bf16 grads the peer reduction (all-reduce barrier included) took
+        0.17 ms against NCCL's 0.25 ms at 2 ranks, tied at 4 (0.28 ms) and lost at 8 (0.36 against 0.29 ms, where
+        NCCL reduces inside the NVSwitch)."""
+        if peer_grads is None:
+            peer_grads = self.plan.world == 2
         import ctypes as C
 
         from . import _lib as L
-        handle = (C.c_ubyte * 64)()
-        off = C.c_uint64(0)
-        L.check(L.lib.moteopt_ipc_export(C.c_void_p(self.om.data_ptr()), handle, C.byref(off)), "moteopt_ipc_export")
-        mine = (bytes(handle), int(off.value))
-        allh: List[Tuple[bytes, int]] = [None] * self.plan.world   # type: ignore[list-item]
-        dist.all_gather_object(allh, mine, group=self.group)
-        ptrs = []
-        for r, (h, o) in enumerate(allh):
-            if r == self.rank:
-                ptrs.append(self.om.data_ptr())
-                continue
-            base = C.c_void_p(0)
-            L.check(L.lib.moteopt_ipc_import(bytes(h), C.byref(base)), "moteopt_ipc_import")
-            self._peer_bases.append(int(base.value))
-            ptrs.append(int(base.value) + o)
-        self.peer_ptrs = ptrs
+        opened = {}   # (rank, handle) -> base: tensors of one allocation share one mapping
+
+        def mapped(t: torch.Tensor) -> List[int]:
+            handle = (C.c_ubyte * 64)()
+            off = C.c_uint64(0)
+            L.check(L.lib.moteopt_ipc_export(C.c_void_p(t.data_ptr()), handle, C.byref(off)), "moteopt_ipc_export")
+            allh: List[Tuple[bytes, int]] = [None] * self.plan.world   # type: ignore[list-item]
+            dist.all_gather_object(allh, (bytes(handle), int(off.value)), group=self.group)
+            ptrs = []
+            for r, (h, o) in enumerate(allh):
+                if r == self.rank:
+                    ptrs.append(t.data_ptr())
+                    continue
+                if (r, h) not in opened:
+                    base = C.c_void_p(0)
+                    L.check(L.lib.moteopt_ipc_import(bytes(h), C.byref(base)), "moteopt_ipc_import")
+                    opened[(r, h)] = int(base.value)
+                    self._peer_bases.append(int(base.value))
+                ptrs.append(opened[(r, h)] + o)
+            return ptrs
+        self.peer_ptrs = mapped(self.om)
         self._flag = torch.zeros(1, dtype=torch.float32, device=self.om.device)
+        if peer_grads and self.compute.peer_reduce is not None:
+            gm = mapped(self.gm) if self.plan.muon_len else []
+            ga = mapped(self.ga) if self.plan.adam_len else []
+            pieces = []
+            na = len(self.plan.adam_shapes)
+            for i in self.mine:
+                nb = self.gm.element_size() * self.plan.muon_off[i]
+                pieces.append((self.reduced_muon_grad(i).reshape(-1), [b + nb for b in gm], na + i))
+            for i, start, n in self.pieces:
+                nb = self.ga.element_size() * (self.plan.adam_off[i] + start)
+                pieces.append((self.reduced_adam_grad(i, start, n), [b + nb for b in ga], i))
+            self._peer_pieces = pieces
+            self._gflag = torch.zeros(1, dtype=torch.float32, device=self.om.device)
         torch.cuda.synchronize(self.om.device)
         dist.barrier(group=self.group)
 
@@ -239,7 +279,7 @@ class ShardedStep:
         torch.cuda.synchronize(self.om.device)
         for b in self._peer_bases:
             L.check(L.lib.moteopt_ipc_close(C.c_void_p(b)), "moteopt_ipc_close")
-        self._peer_bases, self.peer_ptrs = [], None
+        self._peer_bases, self.peer_ptrs, self._peer_pieces = [], None, None
         dist.barrier(group=self.group)
 
     @torch.no_grad()
@@ -330,6 +370,11 @@ class ShardedStep:
         views += [self.reduced_adam_grad(i, start, n) for i, start, n in self.pieces]
         return views
 
+    def owned_tensor_ids(self) -> List[int]:
+        """The grad tensor index of each of owned_grad_views(): AdamW param i is i, Muon param i is n_adam + i."""
+        na = len(self.plan.adam_shapes)
+        return [na + i for i in self.mine] + [i for i, _, _ in self.pieces]
+
     @torch.no_grad()
     def step(self, max_norm: Optional[float] = 1.0, grad_divisor: Optional[float] = None,
              marks: Optional[list] = None, norms: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -346,13 +391,19 @@ class ShardedStep:
                 e.record()
                 marks.append((name, e))
         mark("start")
-        _reduce_scatter(self.gm_seg, self.gm, plan.m_seg, r, self.group)
-        _reduce_scatter(self.ga_seg, self.ga, plan.a_seg, r, self.group)
-        mark("reduce_scatter")
-        mine = self.compute.sumsq(self.owned_grad_views(), grad_divisor)
-        sums = torch.empty(plan.world, dtype=torch.float64, device=mine.device)
-        dist.all_gather_into_tensor(sums, mine.reshape(1), group=self.group)
-        norm_coef = self.compute.coef(sums, max_norm)
+        nt = self.n_tensors
+        if self._peer_pieces is not None:   # reduced from every rank's memory, the clip's sums in the same pass
+            dist.all_reduce(self._gflag, group=self.group)   # every rank's grads are complete before any is read
+            mine = self.compute.peer_reduce(self._peer_pieces, plan.world, nt, grad_divisor)
+            mark("reduce_scatter")
+        else:
+            _reduce_scatter(self.gm_seg, self.gm, plan.m_seg, r, self.group)
+            _reduce_scatter(self.ga_seg, self.ga, plan.a_seg, r, self.group)
+            mark("reduce_scatter")
+            mine = self.compute.sumsq(self.owned_grad_views(), self.owned_tensor_ids(), nt, grad_divisor)
+        sums = torch.empty(plan.world * nt, dtype=torch.float64, device=mine.device)
+        dist.all_gather_into_tensor(sums, mine.reshape(nt), group=self.group)
+        norm_coef = self.compute.coef(sums, nt, max_norm)
         mark("grad_norm")
         self.steps += 1
         muon = [MuonItem(self.muon_view(self.pm, i), self.reduced_muon_grad(i), self.bufs[i], self.muon_lr,
@@ -414,26 +465,52 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
     from .functional import adamw_array, muon_array
     from .ops import grad_dtype_code, stream_handle, workspace
 
-    def sumsq(views, divisor):
-        dev = views[0].device if views else torch.device("cuda", torch.cuda.current_device())
-        out = torch.zeros((), dtype=torch.float64, device=dev)
+    def sumsq(views, tensors, n_tensors, divisor):
         if not views:
-            return out
+            return torch.zeros(n_tensors, dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        dev = views[0].device
+        out = torch.empty(n_tensors, dtype=torch.float64, device=dev)   # every entry written by the library
         n = len(views)
         ptrs = L.array(C.c_void_p, [v.data_ptr() for v in views])
         numels = L.array(C.c_int64, [v.numel() for v in views])
         dts = L.array(C.c_int, [grad_dtype_code(v) for v in views])
+        ids = L.array(C.c_int, list(tensors))
         ws = workspace(dev, L.lib.moteopt_grad_sumsq_workspace_size(numels, n))
-        L.check(L.lib.moteopt_grad_sumsq(ptrs, numels, dts, n, float(divisor or 0.0), C.c_void_p(out.data_ptr()),
-                                         C.c_void_p(ws.data_ptr()), ws.numel(), C.c_void_p(stream_handle(dev))),
-                "moteopt_grad_sumsq")
+        L.check(L.lib.moteopt_grad_sumsq_tensors(ptrs, numels, dts, ids, n, n_tensors, float(divisor or 0.0),
+                                                 C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()), ws.numel(),
+                                                 C.c_void_p(stream_handle(dev))), "moteopt_grad_sumsq_tensors")
         return out
 
-    def coef(sums, max_norm):
+    def coef(sums, n_tensors, max_norm):
         out = torch.empty(2, dtype=torch.float32, device=sums.device)
-        L.check(L.lib.moteopt_clip_coef_from_sums(C.c_void_p(sums.data_ptr()), sums.numel(), int(max_norm is not None),
-                                                  float(max_norm or 0.0), C.c_void_p(out.data_ptr()),
-                                                  C.c_void_p(stream_handle(sums.device))), "moteopt_clip_coef_from_sums")
+        L.check(L.lib.moteopt_clip_coef_from_tensor_sums(
+            C.c_void_p(sums.data_ptr()), sums.numel() // n_tensors, n_tensors, int(max_norm is not None),
+            float(max_norm or 0.0), C.c_void_p(out.data_ptr()), C.c_void_p(stream_handle(sums.device))),
+            "moteopt_clip_coef_from_tensor_sums")
+        return out
+
+    packed = {}   # id of a piece list -> its ctypes array (built once per ShardedStep)
+
+    def peer_reduce(pieces, world, n_tensors, divisor):
+        if not pieces:
+            return torch.zeros(n_tensors, dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+        dev = pieces[0][0].device
+        out = torch.empty(n_tensors, dtype=torch.float64, device=dev)   # every entry written by the library
+        key = id(pieces)
+        if key not in packed:
+            arr = (L.PeerPiece * len(pieces))()
+            for k, (dst, srcs, t) in enumerate(pieces):
+                e = arr[k]
+                e.dst = dst.data_ptr()
+                for q, a in enumerate(srcs):
+                    e.src[q] = a
+                e.numel, e.dtype, e.tensor = dst.numel(), grad_dtype_code(dst), int(t)
+            packed[key] = (pieces, arr)   # the list is kept alive with its array, so its id stays unique
+        arr = packed[key][1]
+        ws = workspace(dev, L.lib.moteopt_peer_reduce_workspace_size(arr, len(pieces)))
+        L.check(L.lib.moteopt_peer_reduce_sumsq(arr, len(pieces), int(world), n_tensors, float(divisor or 0.0),
+                                                C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()), ws.numel(),
+                                                C.c_void_p(stream_handle(dev))), "moteopt_peer_reduce_sumsq")
         return out
 
     counter = {}
@@ -491,4 +568,4 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
             counter[dev] = torch.zeros((), dtype=torch.float32, device=dev)
         counter[dev].fill_(float(n))
 
-    return Compute(sumsq, coef, update, apply, set_step, ema)
+    return Compute(sumsq, coef, update, apply, set_step, ema, peer_reduce)

@@ -64,6 +64,8 @@ int main(void) {
   O(moteopt_muon_config, rms_scale) O(moteopt_muon_config, ns_variant) O(moteopt_grad_config, max_norm)
   O(moteopt_grad_config, grad_divisor_device)
   O(moteopt_adamw_hparams, device_step)
+  P(moteopt_peer_piece) O(moteopt_peer_piece, src) O(moteopt_peer_piece, numel) O(moteopt_peer_piece, dtype)
+  O(moteopt_peer_piece, tensor)
   return 0;
 }
 '''
@@ -76,7 +78,8 @@ int main(void) {
                                                                 check=True).stdout.splitlines())
     m = {"moteopt_muon_param": _lib.MuonParam, "moteopt_muon_config": _lib.MuonConfig,
          "moteopt_adamw_tensor": _lib.AdamWTensor, "moteopt_adamw_hparams": _lib.AdamWHparams,
-         "moteopt_grad_config": _lib.GradConfig, "moteopt_moe_bias": _lib.MoeBias}
+         "moteopt_grad_config": _lib.GradConfig, "moteopt_moe_bias": _lib.MoeBias,
+         "moteopt_peer_piece": _lib.PeerPiece}
     for k, v in got.items():
         if "." in k:
             t, f = k.split(".")
@@ -121,6 +124,24 @@ def test_entry_points_reject_bad_arguments_without_touching_a_device():
     assert lib.moteopt_ema_lerp(ptrs, ptrs, numel, 1, 0.1, None) == -1 and b"bad tensor" in lib.moteopt_last_error()
     assert lib.moteopt_muon_apply_ex(None, 1, None, None, None, 0.0, None, None, 0, None) == -1
     assert lib.moteopt_muon_apply_workspace_size(None, 3) == 0
+    # the sharded step's per-tensor sums and peer reduction check their pieces first
+    out = C.c_void_p(8)
+    piece = _lib.PeerPiece()
+    piece.dst, piece.numel, piece.dtype, piece.tensor = 8, 16, _lib.DTYPE_BF16, 0
+    one = (_lib.PeerPiece * 1)(piece)
+    assert lib.moteopt_peer_reduce_sumsq(one, 1, 9, 1, 0.0, out, None, 0, None) == -3   # more ranks than 8
+    assert lib.moteopt_peer_reduce_sumsq(one, 1, 2, 1, 0.0, out, None, 0, None) == -1   # null source
+    assert b"source" in lib.moteopt_last_error()
+    piece.src[0], piece.src[1], piece.tensor = 8, 8, 3
+    one = (_lib.PeerPiece * 1)(piece)
+    assert lib.moteopt_peer_reduce_sumsq(one, 1, 2, 2, 0.0, out, None, 0, None) == -1   # tensor index past n_tensors
+    assert b"tensor index" in lib.moteopt_last_error()
+    two = (_lib.PeerPiece * 2)(piece, piece)
+    assert lib.moteopt_peer_reduce_sumsq(two, 2, 2, 4, 0.0, out, None, 0, None) == -1   # one tensor twice
+    assert lib.moteopt_peer_reduce_workspace_size(None, 2) == 0
+    ids = (C.c_int * 1)(0)
+    assert lib.moteopt_grad_sumsq_tensors(ptrs, numel, ids, ids, 1, 1, 0.0, out, None, 0, None) == -1
+    assert lib.moteopt_clip_coef_from_tensor_sums(out, 2, 0, 1, 1.0, out, None) == -3
 
 
 C_HOST = r"""

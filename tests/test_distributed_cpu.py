@@ -29,8 +29,7 @@ def _free_port():
     return p
 
 
-def _coef(norm2: float, max_norm):
-    norm = np.float32(np.sqrt(norm2))
+def _coef(norm: np.float32, max_norm):
     if max_norm is None:
         return norm, np.float32(1.0)
     return norm, O.clip_coef(norm, max_norm)
@@ -38,17 +37,22 @@ def _coef(norm2: float, max_norm):
 
 def oracle_compute(w):
     """The step's compute as the oracle (numpy on CPU tensors' memory)."""
-    def sumsq(views, divisor):
-        s = 0.0
-        for v in views:
+    def sumsq(views, tensors, n_tensors, divisor):   # per grad tensor: its sum of squares over the views here
+        s = np.zeros(n_tensors, dtype=np.float64)
+        for v, t in zip(views, tensors):
             g = v.numpy().astype(np.float32)
             if divisor:
                 g = (g / np.float32(divisor)).astype(np.float32)
-            s += float((g.astype(np.float64) ** 2).sum())
-        return torch.tensor(s, dtype=torch.float64)
+            s[t] = float((g.astype(np.float64) ** 2).sum())
+        return torch.from_numpy(s)
 
-    def coef(sums, max_norm):
-        norm, c = _coef(float(sum(sums.tolist())), max_norm)
+    def coef(sums, n_tensors, max_norm):   # per tensor the ranks' sums in rank order, then the norm of the norms
+        per_rank = sums.numpy().reshape(-1, n_tensors)
+        tot = np.zeros(n_tensors, dtype=np.float64)
+        for row in per_rank:
+            tot = tot + row
+        norms = np.sqrt(tot).astype(np.float32)
+        norm, c = _coef(np.float32(np.sqrt(np.sum(np.square(norms.astype(np.float64))))), max_norm)
         return torch.tensor([norm, c], dtype=torch.float32)
 
     def update(muon, adam, coef_t, divisor, muon_out):
@@ -177,7 +181,7 @@ def _reference(world):
             tot_a = [(x + y).astype(np.float32) for x, y in zip(tot_a, ag)]
             tot_m = [(x + y).astype(np.float32) for x, y in zip(tot_m, mg)]
         allg = [(g / np.float32(DIV)).astype(np.float32) for g in tot_a + tot_m]
-        norm, c = _coef(float(sum((g.astype(np.float64) ** 2).sum() for g in allg)), CLIP)
+        norm, c = _coef(O.grad_total_norm(allg), CLIP)   # torch's get_total_norm, AdamW grads first
         norms.append(float(norm))
         allg = [(g * c).astype(np.float32) for g in allg]
         for i in range(len(inp.adam_params)):
