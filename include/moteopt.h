@@ -333,6 +333,8 @@ MOTEOPT_API int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, m
  *      moteopt_selftest_divide: out[i] = a[i] / d[i] (n fp32 device values) computed the way the Newton-Schulz
  *      normalisation divides by a shared norm (a correctly rounded reciprocal, one product, one Markstein
  *      correction), so a caller can hold it against IEEE division.
+ *      moteopt_selftest_grad_divide: out[i] = a[i] / d (one divisor for all n values) computed the way the passes
+ *      that read grads divide them by the trainer's total_n (train.py:945).
  *      moteopt_selftest_wait_timeout: runs the kernels' bounded waits on something that never completes and returns
  *      once they have given up: mode 0 waits on `counter` (a device int the caller keeps below 1: a persistent
  *      Newton-Schulz tile's input counter that nothing adds to), mode 1 on an mbarrier nothing arrives on (a pipeline
@@ -342,6 +344,7 @@ MOTEOPT_API int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, m
  *      MOTEOPT_STATUS_ABORTED; elapsed_ns (device, 2 values) receives how long each CTA waited. The GPU context stays
  *      usable afterwards. */
 MOTEOPT_API int moteopt_selftest_divide(const float* a, const float* d, float* out, int64_t n, moteopt_stream_t stream);
+MOTEOPT_API int moteopt_selftest_grad_divide(const float* a, float d, float* out, int64_t n, moteopt_stream_t stream);
 MOTEOPT_API int moteopt_selftest_wait_timeout(int mode, double limit_seconds, int* counter, int* status,
                                               unsigned long long* elapsed_ns, moteopt_stream_t stream);
 

@@ -37,7 +37,7 @@ EXPORTS = (
     "moteopt_optimizer_step_workspace_size_cfg", "moteopt_muon_step_workspace_size_cfg",
     "moteopt_newton_schulz_workspace_size_variant", "moteopt_newton_schulz_variant",
     "moteopt_grad_sumsq_tensors", "moteopt_peer_reduce_workspace_size", "moteopt_peer_reduce_sumsq",
-    "moteopt_clip_coef_from_tensor_sums",
+    "moteopt_clip_coef_from_tensor_sums", "moteopt_selftest_grad_divide",
 )
 MAX_PEERS = 8
 
@@ -134,6 +134,7 @@ def _load() -> C.CDLL:
         "moteopt_moe_update_bias": (i32, [C.POINTER(MoeBias), i32, vp]),
         "moteopt_selftest_divide": (i32, [vp, vp, vp, i64, vp]),
         "moteopt_selftest_wait_timeout": (i32, [i32, dbl, vp, vp, vp, vp]),
+        "moteopt_selftest_grad_divide": (i32, [vp, C.c_float, vp, i64, vp]),
         "moteopt_optimizer_step_workspace_size_cfg": (sz, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig),
                                                            C.POINTER(AdamWTensor), i32]),
         "moteopt_muon_step_workspace_size_cfg": (sz, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig)]),

@@ -497,8 +497,14 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, unit));
     }
     if (A.chunk_start[cnt] == 0) continue;
-    if (small) adamw_kernel<true><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
-    else adamw_kernel<false><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    const int grid = grid_for(A.chunk_start[cnt], sms);
+    if (small) {
+      if (A.has_div) adamw_kernel<true, true><<<grid, kMtThreads, 0, st>>>(A);
+      else adamw_kernel<true, false><<<grid, kMtThreads, 0, st>>>(A);
+    } else {
+      if (A.has_div) adamw_kernel<false, true><<<grid, kMtThreads, 0, st>>>(A);
+      else adamw_kernel<false, false><<<grid, kMtThreads, 0, st>>>(A);
+    }
     MO_LAUNCHED("adamw_kernel");
   }
   return MOTEOPT_OK;
@@ -2069,6 +2075,15 @@ __global__ void selftest_divide_kernel(const float* a, const float* d, float* ou
     out[i] = shared_divisor(d[i]).div(a[i]);
 }
 
+// out[i] = a[i] / d by GradDivisor (the grad division of train.py:945, one divisor for the whole pass)
+__global__ void selftest_grad_divide_kernel(const float* a, float d, float* out, int64_t n) {
+  GradDivisor g;
+  g.init(d);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = g.div(a[i]);
+}
+
 // Two CTAs, one waiting thread each, on something that never completes: mode 0 a completion counter nothing adds to
 // (wait_counter, as a persistent Newton-Schulz tile waits for its inputs), mode 1 an mbarrier nothing arrives on
 // (mbar_wait, as a pipeline stage waits for its loads). CTA 0 gives up after limit_ns and records the timeout; CTA 1
@@ -2106,6 +2121,17 @@ int moteopt_selftest_divide(const float* a, const float* d, float* out, int64_t 
   const int grid = static_cast<int>(std::min<int64_t>(cdiv(n, 256), 8 * sms));
   selftest_divide_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, d, out, n);
   MO_LAUNCHED("selftest_divide_kernel");
+  return MOTEOPT_OK;
+}
+
+int moteopt_selftest_grad_divide(const float* a, float d, float* out, int64_t n, moteopt_stream_t stream) {
+  if (n < 0 || (n > 0 && (!a || !out))) return fail(MOTEOPT_ERR_INVALID, "moteopt_selftest_grad_divide: bad arguments");
+  int sms = 0;
+  MO_TRY(device_setup(&sms));
+  if (n == 0) return MOTEOPT_OK;
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(n, 256), 8 * sms));
+  selftest_grad_divide_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, d, out, n);
+  MO_LAUNCHED("selftest_grad_divide_kernel");
   return MOTEOPT_OK;
 }
 

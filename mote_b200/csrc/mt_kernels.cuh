@@ -122,14 +122,49 @@ __device__ __forceinline__ float grad_div(const Args& A, bool used) {
   return (used && A.div_dev != nullptr) ? *A.div_dev : A.div;
 }
 
-// train.py:945-946: g / total_n (fp32 division), then * clip coefficient (fp32 multiply)
+// g / d for one divisor d shared by a whole pass (train.py:945, grads /= total_n), correctly rounded, without a
+// reciprocal per element: inside a window of |g| where q = RN(g r) (r = RN(1/d)) plus one Markstein correction is
+// the IEEE quotient (SharedDivisor's fast-path conditions with a factor-2 margin: |g| >= 2^-80 and
+// 2^-99 <= |g| / d <= 2^125, for 2^-100 <= d < 2^100) that quotient; zeros g r (+-0, IEEE's); everything else
+// __fdiv_rn. The window test is one unsigned compare on the bits of |g|.
+struct GradDivisor {
+  float d, r;
+  uint32_t lo, span;   // fast path when lo <= bits(|g|) <= lo + span
+  __device__ __forceinline__ void init(float den) {
+    d = den;
+    r = __frcp_rn(den);
+    if (den >= 0x1p-100f && den < 0x1p100f) {
+      lo = __float_as_uint(fmaxf(0x1p-80f, __fmul_rn(den, 0x1p-99f)));
+      span = __float_as_uint(fminf(0x1.fffffep127f, __fmul_rn(den, 0x1p125f))) - lo;
+    } else {   // empty window: bits(|g|) - lo wraps to at least 1
+      lo = 0xffffffffu;
+      span = 0u;
+    }
+  }
+  __device__ __forceinline__ float div(float g) const {
+    const uint32_t ab = __float_as_uint(g) & 0x7fffffffu;
+    if (ab - lo <= span) {
+      const float q = __fmul_rn(g, r);
+      return fmaf(fmaf(-q, d, g), r, q);
+    }
+    if (ab == 0u) return __fmul_rn(g, r);
+    return __fdiv_rn(g, d);
+  }
+};
+
+// train.py:945-946: g / total_n (fp32 division, correctly rounded: GradDivisor), then * clip coefficient (fp32
+// multiply)
 struct GradXform {
   int has_div;
-  float div;
   int has_coef;
   float coef;
+  GradDivisor gd;
+  __device__ __forceinline__ GradXform(int has_div_, float div, int has_coef_, float coef_)
+      : has_div(has_div_), has_coef(has_coef_), coef(coef_) {
+    if (has_div_) gd.init(div);   // read only when has_div
+  }
   __device__ __forceinline__ float operator()(float g) const {
-    if (has_div) g = __fdiv_rn(g, div);
+    if (has_div) g = gd.div(g);
     if (has_coef) g = __fmul_rn(g, coef);
     return g;
   }
@@ -571,11 +606,12 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
 
 // kSmall: kAdamChunk work units with both of a thread's vectors loaded up front (launches too small to fill the
 // GPU in kChunk units); else kChunk units walked one vector per thread at a time, which needs half the registers
-// and so runs twice the blocks per SM. A separate instantiation each, so each gets its own register allocation.
-template <bool kSmall>
+// and so runs twice the blocks per SM. kDiv: the grads are divided first (A.has_div). A separate instantiation each,
+// so each gets its own register allocation.
+template <bool kSmall, bool kDiv>
 __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant__ AdamArgs A) {
   const int total = A.chunk_start[A.n];
-  const GradXform X{A.has_div, grad_div(A, A.has_div != 0), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
   const double dstep = A.dstep != nullptr ? static_cast<double>(*A.dstep) : 0.0;
   int s_cur = -1;

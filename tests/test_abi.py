@@ -197,14 +197,18 @@ def _kernel_resources():
         pytest.skip("no ptxas report: rebuild with python -m mote_b200.build")
     if build.RESOURCES.stat().st_mtime < build.LIB.stat().st_mtime - 5:
         pytest.skip("the ptxas report is older than the library")
-    out, name = {}, None
+    out, name, props = {}, None, None
     for line in build.RESOURCES.read_text().splitlines():
         m = re.search(r"Compiling entry function '(\w+)'", line)
         if m:
             name = m.group(1)
             continue
+        m = re.search(r"Function properties for (\w+)", line)
+        if m:   # a kernel's own properties, or those of a device function it calls (not the kernel's)
+            props = m.group(1)
+            continue
         m = re.search(r"(\d+) bytes spill stores, (\d+) bytes spill loads", line)
-        if m and name:
+        if m and name and props == name:
             out.setdefault(name, [0, 0])[1] = max(int(m.group(1)), int(m.group(2)))
         m = re.search(r"Used (\d+) registers", line)
         if m and name:
@@ -216,12 +220,14 @@ def test_kernel_register_budgets():
     """Registers and spills of every kernel, against the budgets their launch shapes were tuned for: the
     Newton-Schulz kernel's 320 threads at one CTA per SM with its 96 registers; no spills anywhere except the
     20-byte one of the division-free momentum pass (its fp64 sum of squares included), whose register cap (four
-    blocks per SM) was measured to run at the copy bandwidth with it."""
+    blocks per SM) was measured to run at the copy bandwidth with it, and the 20 bytes the dividing AdamW pass in
+    16K-element units saves around the call of IEEE division's slow path (taken only for grads outside the grad
+    divisor's fast window)."""
     res = _kernel_resources()
     assert len(res) >= 20, sorted(res)
     ns = [v for k, v in res.items() if "ns_gemm_kernel" in k]
     assert ns and ns[0][0] <= 96 and ns[0][1] == 0
     for k, (regs, spill) in res.items():
-        allowed = 20 if "muon_momentum_kernelILb0E" in k else 0
+        allowed = 20 if ("muon_momentum_kernelILb0E" in k or "adamw_kernelILb0ELb1E" in k) else 0
         assert spill <= allowed, (k, regs, spill)
         assert regs <= 255, k

@@ -73,6 +73,41 @@ def test_shared_divisor_equals_ieee_division(dev, num, den):
                                  f"{got[i].item()!r} != {want[i].item()!r}")
 
 
+def _grad_divide(a: torch.Tensor, d: float) -> torch.Tensor:
+    from mote_b200 import _lib as L
+    out = torch.empty_like(a)
+    L.check(L.lib.moteopt_selftest_grad_divide(C.c_void_p(a.data_ptr()), C.c_float(d), C.c_void_p(out.data_ptr()),
+                                               a.numel(), C.c_void_p(torch.cuda.current_stream().cuda_stream)),
+            "selftest_grad_divide")
+    return out
+
+
+# token counts and other divisors: small integers, powers of two, significands just above 1 and just below 2, the
+# ends of the fast window's divisor range and beyond it
+GRAD_DIVISORS = [1.0, 2.0, 3.0, 7.0, 4096.0, 4097.0, 12345.0, 524287.0, 1e6, 3.3554431e7, 1.0000001, 1.9999999,
+                 0.1, 1e-7, 2.0 ** -100, 2.0 ** -101, 2.0 ** 99, 2.0 ** 100, 3e38]
+
+
+@pytest.mark.parametrize("d", GRAD_DIVISORS)
+def test_grad_divisor_equals_ieee_division(dev, d):
+    """The grads' division by total_n (train.py:945) in the passes that read grads: one divisor for a whole pass,
+    a fast path inside a window of |g| and IEEE division outside it; equal to torch's fp32 `/` bit for bit over
+    grads of 1e-45 .. 1e38 (both signs), zeros, infinities and NaN."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(int(d * 7) & 0xFFFF)
+    for lo, hi in ((1e-9, 10.0), (1e-45, 1e-30), (1e-30, 1e38)):
+        a = _loguniform(gen, 1 << 23, lo, hi, dev)
+        got, want = _grad_divide(a, d), a / torch.tensor(d, dtype=torch.float32, device=dev)
+        bad = ~((got == want) | (torch.isnan(got) & torch.isnan(want)))
+        assert int(bad.sum().item()) == 0, (d, lo, hi, int(bad.sum().item()))
+        assert torch.equal(torch.signbit(got), torch.signbit(want))
+    sp = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), float("nan"), 1.4e-45, -1.4e-45, 3.4028235e38],
+                      device=dev)
+    got, want = _grad_divide(sp, d), sp / torch.tensor(d, dtype=torch.float32, device=dev)
+    assert torch.equal(torch.signbit(got), torch.signbit(want))
+    assert bool(((got == want) | (torch.isnan(got) & torch.isnan(want))).all()), (got.tolist(), want.tolist())
+
+
 def test_shared_divisor_special_values(dev):
     nums = torch.tensor([0.0, -0.0, 1.0, -1.0, 3.0, 1e-7, 1e4, 1.17549435e-38, 1.4e-45, 3.4e38, float("inf"),
                          float("nan")], device=dev)
