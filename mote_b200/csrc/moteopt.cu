@@ -35,6 +35,10 @@ int fail(int code, const std::string& msg) {
   } while (0)
 
 std::atomic<unsigned long long> g_launches{0};
+// The persistent launch takes an iteration's matrices in two runs (each through all three phases) once an iteration
+// is at least kNsChunkWaves waves of tiles: c1 (32 waves) 1.44 -> 1.39 ms, the same bits; three runs gave 1.40 ms,
+// four 1.46 ms (the runs' phases get too short to keep every pair busy past their dependency waits).
+constexpr int kNsChunkWaves = 24;
 std::atomic<int> g_ns_persistent{-1};   // Newton-Schulz launch mode (moteopt_ns_set_persistent): 1, 0, or -1 = auto
 // Auto mode: one persistent launch while an iteration is at most this many waves of CTA-pair tiles; above it the
 // per-phase launches' ramps are amortised and their leaner tiles win (measured: c1 at 32 waves favours the
@@ -782,7 +786,11 @@ std::vector<std::vector<const GroupPlan*>> launch_sets(const std::vector<const G
 
 // The tile tables of a launch over Lh.g[0..n_groups): phase `only` alone (one launch per phase), or all three phases
 // of an iteration (only = -1).
-void tile_tables(ns::Launch& Lh, int only) {
+// The tile tables of a launch: `only` >= 0 keeps that phase alone; `chunks` > 1 (persistent mode only) splits every
+// group's matrices into that many runs, each run taken through its three phases before the next, so that the X, A
+// and B a run reads stay in L2 between its phases.
+void tile_tables(ns::Launch& Lh, int only, int chunks = 1) {
+  chunks = std::max(1, std::min(chunks, ns::kMaxChunks));
   Lh.per_iter = 0;
   for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
     Lh.tile_start[ph][0] = 0;
@@ -797,6 +805,25 @@ void tile_tables(ns::Launch& Lh, int only) {
     Lh.phase_tiles[ph] = Lh.tile_start[ph][Lh.n_groups];
     Lh.per_iter += Lh.phase_tiles[ph];
   }
+  Lh.n_chunks = chunks;
+  int acc = 0;
+  for (int c = 0; c <= chunks; ++c)
+    for (int gi = 0; gi < Lh.n_groups; ++gi) Lh.ck_b0[c][gi] = static_cast<int>(int64_t(Lh.g[gi].count) * c / chunks);
+  for (int c = 0; c < chunks; ++c) {
+    Lh.chunk_start[c] = acc;
+    for (int ph = ns::kGram; ph <= ns::kUpdate; ++ph) {
+      Lh.ck_tile_start[c][ph][0] = 0;
+      for (int gi = 0; gi < Lh.n_groups; ++gi) {
+        const int T = Lh.tiles_m[gi];
+        const int per = ph == ns::kUpdate ? T * Lh.tiles_n[gi] : T * (T + 1) / 2;
+        const int cnt = Lh.ck_b0[c + 1][gi] - Lh.ck_b0[c][gi];
+        Lh.ck_tile_start[c][ph][gi + 1] = Lh.ck_tile_start[c][ph][gi] + ((only < 0 || only == ph) ? cnt * per : 0);
+      }
+      Lh.ck_phase_tiles[c][ph] = Lh.ck_tile_start[c][ph][Lh.n_groups];
+      acc += Lh.ck_phase_tiles[c][ph];
+    }
+  }
+  Lh.chunk_start[chunks] = acc;   // == per_iter
 }
 
 // The reference iteration (mote/train/muon.py:37-40) over `groups`: one persistent launch per set, or one launch per
@@ -843,7 +870,7 @@ int run_ns_reference(const std::vector<const GroupPlan*>& groups, const Layout& 
       G.transposed = g.transposed;
       first += G.count;
     }
-    // the tile sequence [iteration][phase][group][matrix][tile]: 256 x 256 tiles, one per CTA pair; A and B are
+    // the tile sequence [iteration][chunk][phase][group][matrix][tile]: 256 x 256 tiles, one per CTA pair; A and B are
     // symmetric, so their phases have the upper-triangle blocks only
     Lh.src0 = 0;
     tile_tables(Lh, -1);
@@ -851,6 +878,7 @@ int run_ns_reference(const std::vector<const GroupPlan*>& groups, const Layout& 
     const int mode = g_ns_persistent.load(std::memory_order_relaxed);
     if (mode == 1 || (mode < 0 && Lh.per_iter <= kPersistentMaxWaves * pairs)) {
       // one cooperative launch for every iteration; the completion counters start at zero
+      tile_tables(Lh, -1, Lh.per_iter >= kNsChunkWaves * pairs ? 2 : 1);
       MO_CUDA(cudaMemsetAsync(done, 0, sizeof(int) * 3 * static_cast<size_t>(first), st));
       Lh.done = done;
       Lh.t_begin = 0;

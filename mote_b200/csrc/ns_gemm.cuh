@@ -8,7 +8,8 @@
 // are symmetric, so kGram and kPoly compute only the 256 x 256 blocks on and above the diagonal; a block below it is
 // read as the transpose of its mirror block (an MN-major operand).
 //
-// Work. A launch walks the tile sequence [iteration][phase][group][matrix][tile] over [t_begin, t_end); CTA pair p
+// Work. A launch walks the tile sequence [iteration][chunk][phase][group][matrix][tile] over [t_begin, t_end) (a
+// chunk is a run of every group's matrices; the persistent launch of a large problem has two); CTA pair p
 // takes tiles t_begin + p, t_begin + p + P, ... in order (P pairs). Two launch modes share the code:
 //   - one launch per phase (`done` null): the kernel boundary orders the phases;
 //   - one cooperative launch for all iterations (`done` non-null): before a tile reads a matrix's A, B or X, it waits
@@ -59,13 +60,16 @@ __device__ __forceinline__ Tile decode_tile(const Launch& L, int t) {
   Tile x;
   x.it = t / L.per_iter;
   int r = t - x.it * L.per_iter;
+  int c = 0;
+  while (c + 1 < L.n_chunks && r >= L.chunk_start[c + 1]) ++c;
+  r -= L.chunk_start[c];
   x.phase = 0;
-  while (x.phase < 2 && r >= L.phase_tiles[x.phase]) {
-    r -= L.phase_tiles[x.phase];
+  while (x.phase < 2 && r >= L.ck_phase_tiles[c][x.phase]) {
+    r -= L.ck_phase_tiles[c][x.phase];
     ++x.phase;
   }
   x.src = (L.src0 + x.it) & 1;
-  const int* ts = L.tile_start[x.phase];
+  const int* ts = L.ck_tile_start[c][x.phase];
   int gi = 0;
   while (gi + 1 < L.n_groups && r >= ts[gi + 1]) ++gi;
   r -= ts[gi];
@@ -88,6 +92,7 @@ __device__ __forceinline__ Tile decode_tile(const Launch& L, int t) {
     }
     tj = ti + r;
   }
+  x.b += L.ck_b0[c][gi];
   x.gi = gi;
   x.i0 = ti * TM;
   x.j0 = tj * TN;

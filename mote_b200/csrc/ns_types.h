@@ -25,6 +25,7 @@ constexpr uint32_t kTmemCols = 512;   // two 128 x 256 fp32 accumulators per CTA
 constexpr int kArrivalsPerTile = 2 * kEpiWarps;   // completion arrivals of one pair tile (every epilogue warp)
 
 constexpr int kMaxGroups = 8;     // shape groups per launch
+constexpr int kMaxChunks = 8;     // runs of matrices an iteration is split into (persistent mode)
 constexpr int kMaxApply = 512;    // matrices per shape group
 
 enum Phase : int {
@@ -66,7 +67,9 @@ struct MatApply {
   int has_decay;
 };
 
-// A launch walks the tile sequence [iteration][phase][group][matrix][tile] over [t_begin, t_end).
+// A launch walks the tile sequence [iteration][chunk][phase][group][matrix][tile] over [t_begin, t_end): chunk c of
+// an iteration holds, in every group, the matrices [ck_b0[c][g], ck_b0[c + 1][g]) (one chunk outside the persistent
+// mode, where the phases of an iteration must be contiguous).
 struct Launch {
   Group g[kMaxGroups];
   int n_groups;
@@ -75,6 +78,11 @@ struct Launch {
   int per_iter;                          // tiles of one iteration, all three phases
   int phase_tiles[3];                    // tiles of each phase in one iteration
   int tile_start[3][kMaxGroups + 1];     // per phase: prefix over the groups
+  int n_chunks;
+  int chunk_start[kMaxChunks + 1];       // per iteration: prefix of tiles over the chunks
+  int ck_phase_tiles[kMaxChunks][3];     // tiles of each phase within a chunk
+  int ck_tile_start[kMaxChunks][3][kMaxGroups + 1];   // per chunk and phase: prefix over the groups
+  int ck_b0[kMaxChunks + 1][kMaxGroups]; // first matrix of each group in each chunk
   int tiles_m[kMaxGroups];               // row blocks of X (= both block counts of A and B)
   int tiles_n[kMaxGroups];               // column blocks of X
   int* done;                             // persistent mode: [matrix][phase] completion arrivals; null: one phase per launch

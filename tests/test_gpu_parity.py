@@ -94,10 +94,11 @@ def test_newton_schulz_benchmark_shapes(dev, shape):
     _status_ok(dev)
 
 
-@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (1, 1100, 1300), (3, 130, 72)])
+@pytest.mark.parametrize("shape", [(4, 768, 768), (2, 768, 3072), (1, 1100, 1300), (3, 130, 72), (37, 768, 3072)])
 def test_newton_schulz_launch_modes_agree(dev, shape):
     """One persistent cooperative launch (completion counters between phases) and one launch per phase compute
-    the same bits, for 1 and 5 iterations."""
+    the same bits, for 1 and 5 iterations. 37 x 768 x 3072 is an iteration of 24 waves of tiles, where the
+    persistent launch takes the matrices in two runs (18 and 19)."""
     from mote_b200 import _lib as L
     from mote_b200 import ops
     u = torch.from_numpy(ns_input(shape, 77)).to(dev)
@@ -110,6 +111,34 @@ def test_newton_schulz_launch_modes_agree(dev, shape):
         L.lib.moteopt_ns_set_persistent(prev)
     for x, y in zip(a, b):
         assert torch.equal(x, y)
+    _status_ok(dev)
+
+
+def test_c1_muon_set_launch_modes_agree(dev):
+    """c1's 80 matrices (three shape groups, 32 waves of tiles per iteration: the persistent launch runs them in two
+    runs) step to the same bits in both launch modes."""
+    from mote_b200 import _lib as L
+    from mote_b200 import configs
+    from mote_b200.functional import MuonItem, muon_step
+    w = configs.CONFIGS["c1"]()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6)
+    base = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in w.muon_shapes]
+    grads = [(torch.randn(s, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for s in w.muon_shapes]
+    out = []
+    prev = L.lib.moteopt_ns_set_persistent(0)
+    try:
+        for mode in (0, 1):
+            L.lib.moteopt_ns_set_persistent(mode)
+            ps = [b.clone() for b in base]
+            items = [MuonItem(p, g, torch.zeros_like(p), 0.02, 0.002) for p, g in zip(ps, grads)]
+            muon_step(items, ns_steps=5)
+            torch.cuda.synchronize()
+            out.append(ps)
+    finally:
+        L.lib.moteopt_ns_set_persistent(prev)
+    for a, b in zip(*out):
+        assert torch.equal(a, b)
     _status_ok(dev)
 
 
