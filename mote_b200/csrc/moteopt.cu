@@ -2103,13 +2103,23 @@ __global__ void selftest_divide_kernel(const float* a, const float* d, float* ou
     out[i] = shared_divisor(d[i]).div(a[i]);
 }
 
-// out[i] = a[i] / d by GradDivisor (the grad division of train.py:945, one divisor for the whole pass)
+// out[i] = a[i] / d with one SharedDivisor for the whole pass (the grad division of train.py:945, and the
+// normalisation's four-at-a-time form): groups of four through div4, the tail through div
 __global__ void selftest_grad_divide_kernel(const float* a, float d, float* out, int64_t n) {
-  GradDivisor g;
-  g.init(d);
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    out[i] = g.div(a[i]);
+  const SharedDivisor g = shared_divisor(d);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; 4 * j < n; j += stride) {
+    const int64_t i = 4 * j;
+    if (i + 3 < n) {
+      const float4 q = g.div4(make_float4(a[i], a[i + 1], a[i + 2], a[i + 3]));
+      out[i] = q.x;
+      out[i + 1] = q.y;
+      out[i + 2] = q.z;
+      out[i + 3] = q.w;
+    } else {
+      for (int64_t k = i; k < n; ++k) out[k] = g.div(a[k]);
+    }
+  }
 }
 
 // Two CTAs, one waiting thread each, on something that never completes: mode 0 a completion counter nothing adds to
@@ -2157,7 +2167,7 @@ int moteopt_selftest_grad_divide(const float* a, float d, float* out, int64_t n,
   int sms = 0;
   MO_TRY(device_setup(&sms));
   if (n == 0) return MOTEOPT_OK;
-  const int grid = static_cast<int>(std::min<int64_t>(cdiv(n, 256), 8 * sms));
+  const int grid = static_cast<int>(std::min<int64_t>(cdiv(cdiv(n, 4), 256), 8 * sms));
   selftest_grad_divide_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a, d, out, n);
   MO_LAUNCHED("selftest_grad_divide_kernel");
   return MOTEOPT_OK;

@@ -38,18 +38,7 @@ __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_c
 __device__ __forceinline__ bool aligned8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 __device__ __forceinline__ bool g_vec_ok(const void* g, int dt) { return dt == kBF16 ? aligned8(g) : aligned16(g); }
 
-// a / d rounded to nearest (ties to even), for a divisor shared by many numerators. With r = RN(1/d), q = RN(a*r) and
-// the residual e = a - q*d (one fma), RN(q + e*r) is the correctly rounded quotient (Markstein's correction step,
-// "Computation of elementary functions on the IBM RISC System/6000 processor", 1990), provided the residual is exact
-// and nothing under- or overflows: |a| >= 2^-80, 2^-100 <= |q| < 2^126 and 2^-100 <= d < 2^100 (the common case:
-// the optimizer divides entries of 1e-9..10 by norms of 1e-7..1e4). Every other numerator is rare and takes an exact
-// inline path, no call: a = m 2^ea with |m| in [0.5, 1) and d = dm 2^ed with dm in [1, 2), so q' = RN(m / dm) by the
-// same correction lies in (0.25, 1); the quotient is q' 2^(ea-ed) scaled back with one rounding (overflow gives Inf,
-// underflow a subnormal or zero), and where that rounding falls exactly on a midpoint of the subnormal grid the
-// residual's sign picks the neighbour the exact quotient lies toward. Zeros, Inf and NaN numerators give a * r, which
-// is IEEE's a / d for them. Defined for every positive finite d; d = 0, Inf or NaN also give a * r (IEEE's result).
-// tests/test_gpu_selftest.py holds it against IEEE division bit for bit: the optimizer's ranges, their edges, tiny
-// and subnormal numerators, divisors across the whole exponent range, and special values.
+// Exact helpers of SharedDivisor's rare path (below).
 __device__ __forceinline__ float pow2f(int n) {   // 2^n for n in [-149, 127], exactly
   return n >= -126 ? __uint_as_float(static_cast<uint32_t>(n + 127) << 23) : __uint_as_float(1u << (n + 149));
 }
@@ -72,46 +61,98 @@ __device__ __forceinline__ float split_exp(float a, int bias, int* e) {
   *e = static_cast<int>((u >> 23) & 0xffu) - bias - shift;
   return __uint_as_float((u & 0x807fffffu) | (static_cast<uint32_t>(bias) << 23));
 }
+// a / d for one divisor d shared by many numerators (the normalisation's norm, the trainer's total_n), correctly
+// rounded, without a reciprocal per element: inside a window of |a| where q = RN(a r) (r = RN(1/d)) plus one
+// Markstein correction RN(q + (a - q d) r) is the IEEE quotient (Markstein, "Computation of elementary functions on
+// the IBM RISC System/6000 processor", 1990) (|a| >= 2^-80 and 2^-99 <= |a| / d <= 2^125, for 2^-100 <= d < 2^100: the
+// residual is exact and nothing under- or overflows; a factor-2 margin on each bound), that quotient, decided by one
+// unsigned compare on the bits of |a|. Zeros, infinities and NaN give a r (IEEE's result for them); every other
+// numerator takes div_rare, an exact inline path (no call): a = m 2^ea with |m| in [0.5, 1) and d = dm 2^ed with dm
+// in [1, 2), so q' = RN(m / dm) by the same correction lies in (0.25, 1); the quotient is q' 2^(ea-ed) scaled back
+// with one rounding (overflow gives Inf, underflow a subnormal or zero), and where that rounding falls exactly on a
+// midpoint of the subnormal grid the residual's sign picks the neighbour the exact quotient lies toward. A negative
+// divisor moves its sign onto the numerator (a / -d = -a / d exactly). tests/test_gpu_selftest.py holds it against
+// IEEE division bit for bit: the optimizer's ranges and their edges, tiny and subnormal numerators, divisors across
+// the whole exponent range, and special values.
 struct SharedDivisor {
-  float d, r;     // d and RN(1/d)
-  float dm, rm;   // d = dm 2^ed with dm in [1, 2), and RN(1/dm)
-  int ed;
-  bool fast_d;    // 2^-100 <= d < 2^100
-  bool finite;    // d is positive and finite
+  float d, r;          // |divisor| and RN(1 / |divisor|)
+  uint32_t lo, span;   // fast path when lo <= bits(|a|) <= lo + span
+  uint32_t sgn;        // the divisor's sign bit
   __device__ __forceinline__ float div_rare(float a) const {
-    int ea;
+    int ed, ea;
+    const float dm = split_exp(d, 127, &ed);
+    const float rm = __frcp_rn(dm);
     const float m = split_exp(a, 126, &ea);
     const float q1 = __fmul_rn(m, rm);
     const float qm = fmaf(fmaf(-q1, dm, m), rm, q1);   // RN(m / dm), in (0.25, 1)
     const float em = fmaf(-qm, dm, m);                  // exact: m / dm - qm has the sign of em
     const int n = ea - ed;
     float v = scale_once(qm, n);
-    if (fabsf(v) < 0x1p-126f && em != 0.f && n >= -152) {
+    // qm 2^n below 2^-126 (tested before the rounding, which can carry it up to 2^-126 itself): the second rounding is
+    // to the subnormal grid
+    if ((n <= -126 || (n == -125 && qm < 0.5f)) && em != 0.f && n >= -152) {
       const float w = __fmul_rn(qm, pow2f(n + 149));   // the quotient in units of 2^-149, exact
       if (fabsf(w - truncf(w)) == 0.5f) v = __fmul_rn(em > 0.f ? ceilf(w) : floorf(w), 0x1p-149f);
     }
     return v;
   }
   __device__ __forceinline__ float div(float a) const {
-    const float q = __fmul_rn(a, r);
-    if (fast_d && fabsf(a) >= 0x1p-80f && fabsf(q) >= 0x1p-100f && fabsf(q) < 0x1p126f) {
-      const float e = fmaf(-q, d, a);
-      return fmaf(e, r, q);
+    a = __uint_as_float(__float_as_uint(a) ^ sgn);
+    const uint32_t ab = __float_as_uint(a) & 0x7fffffffu;
+    if (ab - lo <= span) {
+      const float q = __fmul_rn(a, r);
+      return fmaf(fmaf(-q, d, a), r, q);
     }
-    if (a == 0.f || !finite || !(fabsf(a) <= 0x1.fffffep127f)) return q;
+    if (ab == 0u || ab >= 0x7f800000u || !(d > 0.f && d <= 0x1.fffffep127f)) return __fmul_rn(a, r);
     return div_rare(a);
+  }
+  // div4 for numerators known to satisfy |a| <= d with d > 0 (an entry over its matrix's norm plus eps: the norm is
+  // the correctly rounded root of the sum of the same entries' squares, so no entry exceeds it, and d finite means
+  // every entry is finite): only the window's lower bound can fail, tested on the smallest |a|
+  __device__ __forceinline__ float4 div4_bounded(float4 a) const {
+    const uint32_t m0 = __float_as_uint(a.x) & 0x7fffffffu, m1 = __float_as_uint(a.y) & 0x7fffffffu;
+    const uint32_t m2 = __float_as_uint(a.z) & 0x7fffffffu, m3 = __float_as_uint(a.w) & 0x7fffffffu;
+    if (min(min(m0, m1), min(m2, m3)) - lo <= span) {   // lo <= every |a| (and |a| <= d <= the upper bound)
+      const float q0 = __fmul_rn(a.x, r), q1 = __fmul_rn(a.y, r), q2 = __fmul_rn(a.z, r), q3 = __fmul_rn(a.w, r);
+      return make_float4(fmaf(fmaf(-q0, d, a.x), r, q0), fmaf(fmaf(-q1, d, a.y), r, q1),
+                         fmaf(fmaf(-q2, d, a.z), r, q2), fmaf(fmaf(-q3, d, a.w), r, q3));
+    }
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll 1
+    for (int e = 0; e < 4; ++e) v[e] = div(v[e]);   // one copy of the rare path
+    return make_float4(v[0], v[1], v[2], v[3]);
+  }
+  // four quotients: the fast path for all four, one window test on their smallest and largest |a|, and div() for
+  // the four when any of them lies outside the window (rare)
+  __device__ __forceinline__ float4 div4(float4 a) const {
+    const uint32_t b0 = __float_as_uint(a.x) ^ sgn, b1 = __float_as_uint(a.y) ^ sgn;
+    const uint32_t b2 = __float_as_uint(a.z) ^ sgn, b3 = __float_as_uint(a.w) ^ sgn;
+    const uint32_t m0 = b0 & 0x7fffffffu, m1 = b1 & 0x7fffffffu, m2 = b2 & 0x7fffffffu, m3 = b3 & 0x7fffffffu;
+    const uint32_t mn = min(min(m0, m1), min(m2, m3)), mx = max(max(m0, m1), max(m2, m3));
+    if (mn >= lo && mx - lo <= span) {
+      const float x0 = __uint_as_float(b0), x1 = __uint_as_float(b1), x2 = __uint_as_float(b2), x3 = __uint_as_float(b3);
+      const float q0 = __fmul_rn(x0, r), q1 = __fmul_rn(x1, r), q2 = __fmul_rn(x2, r), q3 = __fmul_rn(x3, r);
+      return make_float4(fmaf(fmaf(-q0, d, x0), r, q0), fmaf(fmaf(-q1, d, x1), r, q1),
+                         fmaf(fmaf(-q2, d, x2), r, q2), fmaf(fmaf(-q3, d, x3), r, q3));
+    }
+    float v[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll 1
+    for (int e = 0; e < 4; ++e) v[e] = div(v[e]);   // one copy of the rare path
+    return make_float4(v[0], v[1], v[2], v[3]);
   }
 };
 __device__ __forceinline__ SharedDivisor shared_divisor(float den) {
   SharedDivisor s;
-  s.d = den;
-  s.r = __frcp_rn(den);
-  s.finite = den > 0.f && den <= 0x1.fffffep127f;
-  s.fast_d = den >= 0x1p-100f && den < 0x1p100f;
-  s.ed = 0;
-  s.dm = 1.f;
-  if (s.finite) s.dm = split_exp(den, 127, &s.ed);
-  s.rm = __frcp_rn(s.dm);
+  s.sgn = __float_as_uint(den) & 0x80000000u;
+  s.d = fabsf(den);
+  s.r = __frcp_rn(s.d);
+  if (s.d >= 0x1p-100f && s.d < 0x1p100f) {
+    s.lo = __float_as_uint(fmaxf(0x1p-80f, __fmul_rn(s.d, 0x1p-99f)));
+    s.span = __float_as_uint(fminf(0x1.fffffep127f, __fmul_rn(s.d, 0x1p125f))) - s.lo;
+  } else {   // empty window: bits(|a|) - lo wraps to at least 1
+    s.lo = 0xffffffffu;
+    s.span = 0u;
+  }
   return s;
 }
 
@@ -122,46 +163,16 @@ __device__ __forceinline__ float grad_div(const Args& A, bool used) {
   return (used && A.div_dev != nullptr) ? *A.div_dev : A.div;
 }
 
-// g / d for one divisor d shared by a whole pass (train.py:945, grads /= total_n), correctly rounded, without a
-// reciprocal per element: inside a window of |g| where q = RN(g r) (r = RN(1/d)) plus one Markstein correction is
-// the IEEE quotient (SharedDivisor's fast-path conditions with a factor-2 margin: |g| >= 2^-80 and
-// 2^-99 <= |g| / d <= 2^125, for 2^-100 <= d < 2^100) that quotient; zeros g r (+-0, IEEE's); everything else
-// __fdiv_rn. The window test is one unsigned compare on the bits of |g|.
-struct GradDivisor {
-  float d, r;
-  uint32_t lo, span;   // fast path when lo <= bits(|g|) <= lo + span
-  __device__ __forceinline__ void init(float den) {
-    d = den;
-    r = __frcp_rn(den);
-    if (den >= 0x1p-100f && den < 0x1p100f) {
-      lo = __float_as_uint(fmaxf(0x1p-80f, __fmul_rn(den, 0x1p-99f)));
-      span = __float_as_uint(fminf(0x1.fffffep127f, __fmul_rn(den, 0x1p125f))) - lo;
-    } else {   // empty window: bits(|g|) - lo wraps to at least 1
-      lo = 0xffffffffu;
-      span = 0u;
-    }
-  }
-  __device__ __forceinline__ float div(float g) const {
-    const uint32_t ab = __float_as_uint(g) & 0x7fffffffu;
-    if (ab - lo <= span) {
-      const float q = __fmul_rn(g, r);
-      return fmaf(fmaf(-q, d, g), r, q);
-    }
-    if (ab == 0u) return __fmul_rn(g, r);
-    return __fdiv_rn(g, d);
-  }
-};
-
-// train.py:945-946: g / total_n (fp32 division, correctly rounded: GradDivisor), then * clip coefficient (fp32
+// train.py:945-946: g / total_n (fp32 division, correctly rounded: SharedDivisor), then * clip coefficient (fp32
 // multiply)
 struct GradXform {
   int has_div;
   int has_coef;
   float coef;
-  GradDivisor gd;
+  SharedDivisor gd;
   __device__ __forceinline__ GradXform(int has_div_, float div, int has_coef_, float coef_)
       : has_div(has_div_), has_coef(has_coef_), coef(coef_) {
-    if (has_div_) gd.init(div);   // read only when has_div
+    if (has_div_) gd = shared_divisor(div);   // read only when has_div
   }
   __device__ __forceinline__ float operator()(float g) const {
     if (has_div) g = gd.div(g);
@@ -811,9 +822,10 @@ __device__ __forceinline__ float flat_u(float g, float b, const FlatNormSeg& S, 
   return has_buf ? (S.nesterov ? fmaf(S.mom, b, g) : b) : g;
 }
 
-// kDiv as for the momentum kernel: four blocks per SM with the division, five without.
+// Four blocks per SM (64 registers) with or without the division: the exact quotient's window test needs the room
+// (five blocks spill; four measured 8 us faster at c1).
 template <bool kDiv>
-__global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
+__global__ void __launch_bounds__(kMtThreads, 4) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
   const int total = A.chunk_start[A.n];
   const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {
@@ -841,8 +853,8 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 4 : 5) ns_normalize_flat_ke
           const int64_t i = begin + 4 * static_cast<int64_t>(threadIdx.x + (h * 4 + k) * kMtThreads);
           const float u0 = flat_u(X(g[k].x), b[k].x, S, has_buf), u1 = flat_u(X(g[k].y), b[k].y, S, has_buf);
           const float u2 = flat_u(X(g[k].z), b[k].z, S, has_buf), u3 = flat_u(X(g[k].w), b[k].w, S, has_buf);
-          *reinterpret_cast<uint2*>(x + i) = make_uint2(pack_bf16x2(den.div(u0), den.div(u1)),
-                                                        pack_bf16x2(den.div(u2), den.div(u3)));
+          const float4 q = den.div4_bounded(make_float4(u0, u1, u2, u3));   // |u| <= ||u|| < den
+          *reinterpret_cast<uint2*>(x + i) = make_uint2(pack_bf16x2(q.x, q.y), pack_bf16x2(q.z, q.w));
         }
       }
       i0 = end;
@@ -978,12 +990,17 @@ __global__ void __launch_bounds__(kMtThreads, kDiv ? 1 : 5) ns_normalize_kernel(
     for (int k = 0; k < 4; ++k) {
       const float* gv = reinterpret_cast<const float*>(&g4[k]);
       const float* bv = reinterpret_cast<const float*>(&b4[k]);
+      float u[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float u = X(gv[e]);
-        if (M.buf != nullptr) u = M.nesterov ? fmaf(M.mom, bv[e], u) : bv[e];
-        v[k][e] = bf16_round_f(den.div(u));
+        u[e] = X(gv[e]);
+        if (M.buf != nullptr) u[e] = M.nesterov ? fmaf(M.mom, bv[e], u[e]) : bv[e];
       }
+      const float4 q = den.div4_bounded(make_float4(u[0], u[1], u[2], u[3]));   // |u| <= ||u|| < den
+      v[k][0] = bf16_round_f(q.x);
+      v[k][1] = bf16_round_f(q.y);
+      v[k][2] = bf16_round_f(q.z);
+      v[k][3] = bf16_round_f(q.w);
     }
   } else {
 #pragma unroll

@@ -90,9 +90,10 @@ GRAD_DIVISORS = [1.0, 2.0, 3.0, 7.0, 4096.0, 4097.0, 12345.0, 524287.0, 1e6, 3.3
 
 @pytest.mark.parametrize("d", GRAD_DIVISORS)
 def test_grad_divisor_equals_ieee_division(dev, d):
-    """The grads' division by total_n (train.py:945) in the passes that read grads: one divisor for a whole pass,
-    a fast path inside a window of |g| and IEEE division outside it; equal to torch's fp32 `/` bit for bit over
-    grads of 1e-45 .. 1e38 (both signs), zeros, infinities and NaN."""
+    """One divisor for a whole pass (the grads' division by total_n, train.py:945; the normalisation's four-at-a-time
+    form): a fast path inside a window of |a|, the exact rare path outside it; equal to torch's fp32 `/` bit for bit
+    over numerators of 1e-45 .. 1e38 (both signs, groups of four mixing in- and out-of-window values), quotients next
+    to the smallest normal and subnormal, zeros, infinities and NaN."""
     gen = torch.Generator(device=dev)
     gen.manual_seed(int(d * 7) & 0xFFFF)
     for lo, hi in ((1e-9, 10.0), (1e-45, 1e-30), (1e-30, 1e38)):
@@ -101,6 +102,14 @@ def test_grad_divisor_equals_ieee_division(dev, d):
         bad = ~((got == want) | (torch.isnan(got) & torch.isnan(want)))
         assert int(bad.sum().item()) == 0, (d, lo, hi, int(bad.sum().item()))
         assert torch.equal(torch.signbit(got), torch.signbit(want))
+    # quotients next to the smallest normal (2^-126), where rounding to 24 bits and then to the subnormal grid could
+    # round twice, and next to the smallest subnormal
+    x = torch.cat([2.0 ** -126 * (1 - torch.rand(1 << 20, generator=gen, device=dev, dtype=torch.float64) * 2 ** -18),
+                   2.0 ** -149 * (0.25 + 4 * torch.rand(1 << 20, generator=gen, device=dev, dtype=torch.float64))])
+    a = (x * d).to(torch.float32)
+    a = a[torch.isfinite(a)]
+    got, want = _grad_divide(a, d), a / torch.tensor(d, dtype=torch.float32, device=dev)
+    assert torch.equal(got, want), (d, int((got != want).sum().item()))
     sp = torch.tensor([0.0, -0.0, float("inf"), -float("inf"), float("nan"), 1.4e-45, -1.4e-45, 3.4028235e38],
                       device=dev)
     got, want = _grad_divide(sp, d), sp / torch.tensor(d, dtype=torch.float32, device=dev)
