@@ -333,9 +333,8 @@ MOTEOPT_API int moteopt_moe_update_bias(const moteopt_moe_bias* layers, int n, m
  *      moteopt_selftest_divide: out[i] = a[i] / d[i] (n fp32 device values) computed the way the Newton-Schulz
  *      normalisation divides by a shared norm (a correctly rounded reciprocal, one product, one Markstein
  *      correction), so a caller can hold it against IEEE division.
- *      moteopt_selftest_grad_divide: out[i] = a[i] / d (one divisor for all n values) computed the way the passes
- *      that read grads divide them by the trainer's total_n (train.py:945) and the normalisation divides four
- *      entries at a time (groups of four; the tail one by one).
+ *      moteopt_selftest_grad_divide: out[i] = a[i] / d (one divisor for all n values) computed the way the
+ *      normalisation divides a matrix by its norm, four entries at a time (groups of four; the tail one by one).
  *      moteopt_selftest_wait_timeout: runs the kernels' bounded waits on something that never completes and returns
  *      once they have given up: mode 0 waits on `counter` (a device int the caller keeps below 1: a persistent
  *      Newton-Schulz tile's input counter that nothing adds to), mode 1 on an mbarrier nothing arrives on (a pipeline

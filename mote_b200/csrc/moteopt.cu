@@ -501,14 +501,8 @@ int launch_adamw(const moteopt_adamw_tensor* t, int n, const moteopt_adamw_hpara
       A.chunk_start[i + 1] = A.chunk_start[i] + static_cast<int>(cdiv(x.numel, unit));
     }
     if (A.chunk_start[cnt] == 0) continue;
-    const int grid = grid_for(A.chunk_start[cnt], sms);
-    if (small) {
-      if (A.has_div) adamw_kernel<true, true><<<grid, kMtThreads, 0, st>>>(A);
-      else adamw_kernel<true, false><<<grid, kMtThreads, 0, st>>>(A);
-    } else {
-      if (A.has_div) adamw_kernel<false, true><<<grid, kMtThreads, 0, st>>>(A);
-      else adamw_kernel<false, false><<<grid, kMtThreads, 0, st>>>(A);
-    }
+    if (small) adamw_kernel<true><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
+    else adamw_kernel<false><<<grid_for(A.chunk_start[cnt], sms), kMtThreads, 0, st>>>(A);
     MO_LAUNCHED("adamw_kernel");
   }
   return MOTEOPT_OK;
@@ -2103,8 +2097,8 @@ __global__ void selftest_divide_kernel(const float* a, const float* d, float* ou
     out[i] = shared_divisor(d[i]).div(a[i]);
 }
 
-// out[i] = a[i] / d with one SharedDivisor for the whole pass (the grad division of train.py:945, and the
-// normalisation's four-at-a-time form): groups of four through div4, the tail through div
+// out[i] = a[i] / d with one SharedDivisor for the whole pass, as the normalisation divides a matrix by its norm:
+// groups of four through div4, the tail through div
 __global__ void selftest_grad_divide_kernel(const float* a, float d, float* out, int64_t n) {
   const SharedDivisor g = shared_divisor(d);
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;

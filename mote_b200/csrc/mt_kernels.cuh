@@ -163,19 +163,16 @@ __device__ __forceinline__ float grad_div(const Args& A, bool used) {
   return (used && A.div_dev != nullptr) ? *A.div_dev : A.div;
 }
 
-// train.py:945-946: g / total_n (fp32 division, correctly rounded: SharedDivisor), then * clip coefficient (fp32
-// multiply)
+// train.py:945-946: g / total_n (fp32 division, IEEE: __fdiv_rn), then * clip coefficient (fp32 multiply). The grads'
+// division stays the IEEE intrinsic: forms with one shared reciprocal (SharedDivisor) measured no faster on the
+// dividing passes, and every form that changed this struct slowed the non-dividing AdamW pass by 7 %.
 struct GradXform {
   int has_div;
+  float div;
   int has_coef;
   float coef;
-  SharedDivisor gd;
-  __device__ __forceinline__ GradXform(int has_div_, float div, int has_coef_, float coef_)
-      : has_div(has_div_), has_coef(has_coef_), coef(coef_) {
-    if (has_div_) gd = shared_divisor(div);   // read only when has_div
-  }
   __device__ __forceinline__ float operator()(float g) const {
-    if (has_div) g = gd.div(g);
+    if (has_div) g = __fdiv_rn(g, div);
     if (has_coef) g = __fmul_rn(g, coef);
     return g;
   }
@@ -617,12 +614,13 @@ __device__ __forceinline__ void adam_elem(float& p, float g, float& m, float& v,
 
 // kSmall: kAdamChunk work units with both of a thread's vectors loaded up front (launches too small to fill the
 // GPU in kChunk units); else kChunk units walked one vector per thread at a time, which needs half the registers
-// and so runs twice the blocks per SM. kDiv: the grads are divided first (A.has_div). A separate instantiation each,
-// so each gets its own register allocation.
-template <bool kSmall, bool kDiv>
+// and so runs twice the blocks per SM. A separate instantiation each, so each gets its own register allocation. The
+// division is a runtime flag here, not an instantiation: the division-free instantiation measured 7 % slower on 1e8
+// elements (0.466 against 0.436 ms) with the same registers.
+template <bool kSmall>
 __global__ void __launch_bounds__(kMtThreads) adamw_kernel(const __grid_constant__ AdamArgs A) {
   const int total = A.chunk_start[A.n];
-  const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
+  const GradXform X{A.has_div, grad_div(A, A.has_div != 0), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   const AdamConsts K{A.lerp_w, A.one_minus_w, A.beta2, A.one_minus_beta2, A.eps, A.lerp_small};
   const double dstep = A.dstep != nullptr ? static_cast<double>(*A.dstep) : 0.0;
   int s_cur = -1;
@@ -822,10 +820,10 @@ __device__ __forceinline__ float flat_u(float g, float b, const FlatNormSeg& S, 
   return has_buf ? (S.nesterov ? fmaf(S.mom, b, g) : b) : g;
 }
 
-// Four blocks per SM (64 registers) with or without the division: the exact quotient's window test needs the room
-// (five blocks spill; four measured 8 us faster at c1).
+// Four blocks per SM (64 registers) without the grads' division, three with it: the exact quotient's window test
+// needs the room (five blocks spill; four measured 8 us faster at c1 than five).
 template <bool kDiv>
-__global__ void __launch_bounds__(kMtThreads, 4) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
+__global__ void __launch_bounds__(kMtThreads, kDiv ? 3 : 4) ns_normalize_flat_kernel(const __grid_constant__ FlatNormArgs A) {
   const int total = A.chunk_start[A.n];
   const GradXform X{kDiv ? 1 : 0, grad_div(A, kDiv), A.coef != nullptr, A.coef != nullptr ? *A.coef : 1.f};
   for (int c = blockIdx.x; c < total; c += gridDim.x) {

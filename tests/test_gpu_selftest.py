@@ -90,8 +90,8 @@ GRAD_DIVISORS = [1.0, 2.0, 3.0, 7.0, 4096.0, 4097.0, 12345.0, 524287.0, 1e6, 3.3
 
 @pytest.mark.parametrize("d", GRAD_DIVISORS)
 def test_grad_divisor_equals_ieee_division(dev, d):
-    """One divisor for a whole pass (the grads' division by total_n, train.py:945; the normalisation's four-at-a-time
-    form): a fast path inside a window of |a|, the exact rare path outside it; equal to torch's fp32 `/` bit for bit
+    """One divisor for a whole pass (the normalisation's four-at-a-time form; also any shared divisor such as a token
+    count): a fast path inside a window of |a|, the exact rare path outside it; equal to torch's fp32 `/` bit for bit
     over numerators of 1e-45 .. 1e38 (both signs, groups of four mixing in- and out-of-window values), quotients next
     to the smallest normal and subnormal, zeros, infinities and NaN."""
     gen = torch.Generator(device=dev)
