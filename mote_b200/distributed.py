@@ -171,6 +171,12 @@ def _all_gather_inplace(flat: torch.Tensor, seg: int, rank: int, group=None) -> 
                                 else flat[rank * seg:(rank + 1) * seg], group=group)
 
 
+class PeerPieces(list):
+    """The grad pieces a rank reduces from every rank's memory: (reduced view, the piece's address in every rank's
+    grad region, grad tensor index); `packed` caches the compute's own encoding of the list."""
+    packed = None
+
+
 class ShardedStep:
     """Rank-local state and the step of the module docstring. `params_m`/`params_a` are the fp32 param regions,
     `grads_m`/`grads_a` the local grad regions (fp32 or bf16), of length plan.muon_len / plan.adam_len. The grad
@@ -264,7 +270,7 @@ class ShardedStep:
             for i, start, n in self.pieces:
                 nb = self.ga.element_size() * (self.plan.adam_off[i] + start)
                 pieces.append((self.reduced_adam_grad(i, start, n), [b + nb for b in ga], i))
-            self._peer_pieces = pieces
+            self._peer_pieces = PeerPieces(pieces)
             self._gflag = torch.zeros(1, dtype=torch.float32, device=self.om.device)
         torch.cuda.synchronize(self.om.device)
         dist.barrier(group=self.group)
@@ -489,15 +495,13 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
             "moteopt_clip_coef_from_tensor_sums")
         return out
 
-    packed = {}   # id of a piece list -> its ctypes array (built once per ShardedStep)
-
     def peer_reduce(pieces, world, n_tensors, divisor):
         if not pieces:
             return torch.zeros(n_tensors, dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
         dev = pieces[0][0].device
         out = torch.empty(n_tensors, dtype=torch.float64, device=dev)   # every entry written by the library
-        key = id(pieces)
-        if key not in packed:
+        arr = getattr(pieces, "packed", None)   # the ctypes array, built once and kept with its piece list
+        if arr is None:
             arr = (L.PeerPiece * len(pieces))()
             for k, (dst, srcs, t) in enumerate(pieces):
                 e = arr[k]
@@ -505,8 +509,8 @@ def cuda_compute(ns_steps: int = 5, betas=(0.9, 0.95), eps: float = 1e-8, rms_sc
                 for q, a in enumerate(srcs):
                     e.src[q] = a
                 e.numel, e.dtype, e.tensor = dst.numel(), grad_dtype_code(dst), int(t)
-            packed[key] = (pieces, arr)   # the list is kept alive with its array, so its id stays unique
-        arr = packed[key][1]
+            if isinstance(pieces, PeerPieces):
+                pieces.packed = arr
         ws = workspace(dev, L.lib.moteopt_peer_reduce_workspace_size(arr, len(pieces)))
         L.check(L.lib.moteopt_peer_reduce_sumsq(arr, len(pieces), int(world), n_tensors, float(divisor or 0.0),
                                                 C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()), ws.numel(),
