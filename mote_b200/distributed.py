@@ -22,7 +22,8 @@ Step (grads: each rank's local, unreduced grads in the grad regions):
 With peer updates enabled (`enable_peer_updates`, NCCL only), steps 4-5 for the Muon region become one pass: every
 rank maps the other ranks' update regions (CUDA IPC, once), a one-element all-reduce orders the owners' writes
 before the reads, and the apply kernel reads each owner's O straight over NVLink while it updates the local params,
-so no gathered copy of O is ever written. The same mappings of the grad regions turn steps 1-2 into one pass: after a
+so no gathered copy of O is ever written. Mappings of the grad regions (by default on 2 ranks, where this measured
+faster than NCCL's reduce-scatter) turn steps 1-2 into one pass: after a
 one-element all-reduce (every rank's grads complete), each rank reads its segments from every rank's grads over
 NVLink, sums them in rank order, stores the reduced grads and forms the per-tensor sums of squares in the same pass
 (moteopt_peer_reduce_sumsq); the later all-reduce before the O reads orders every rank's grad reads before any rank
