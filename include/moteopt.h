@@ -148,6 +148,11 @@ MOTEOPT_API long long moteopt_check_count(int clear);
  * default): the persistent launch for problems of up to 48 waves of tiles per iteration, per-phase launches above.
  * All compute the same bits. Process-wide; returns the previous mode. */
 MOTEOPT_API int moteopt_ns_set_persistent(int mode);
+/* Whether a matrix with more rows than columns (both multiples of 8) is iterated as stored (1, the default: A = X^T X,
+ * X' = a X + X B, the same products in the same order as the transposed iteration, and no transposing passes) or as
+ * its transpose (0). Returns the previous setting; it applies to calls made after it (no counterpart in the
+ * reference). */
+MOTEOPT_API int moteopt_ns_set_tall(int on);
 
 /* Read (and optionally clear) the workspace's status word and the last [total norm, clip coefficient].
  * Synchronises `stream`. Either output may be NULL. */

@@ -21,7 +21,7 @@ STATUS_NONFINITE = 4
 # every exported symbol of include/moteopt.h
 EXPORTS = (
     "moteopt_version", "moteopt_last_error", "moteopt_read_status", "moteopt_launch_count", "moteopt_check_count",
-    "moteopt_profile_ns_events", "moteopt_ns_set_persistent",
+    "moteopt_profile_ns_events", "moteopt_ns_set_persistent", "moteopt_ns_set_tall",
     "moteopt_optimizer_step_workspace_size", "moteopt_optimizer_step", "moteopt_optimizer_step_ex",
     "moteopt_optimizer_step_with_coef",
     "moteopt_optimizer_step_with_coef_out", "moteopt_muon_apply", "moteopt_muon_apply_workspace_size",
@@ -99,6 +99,7 @@ def _load() -> C.CDLL:
         "moteopt_check_count": (C.c_longlong, [i32]),
         "moteopt_profile_ns_events": (i32, [vp, vp]),
         "moteopt_ns_set_persistent": (i32, [i32]),
+        "moteopt_ns_set_tall": (i32, [i32]),
         "moteopt_read_status": (i32, [vp, C.POINTER(C.c_int), f32p, i32, vp]),
         "moteopt_optimizer_step_workspace_size": (sz, [C.POINTER(MuonParam), i32, i32, C.POINTER(AdamWTensor), i32]),
         "moteopt_optimizer_step": (i32, [C.POINTER(MuonParam), i32, C.POINTER(MuonConfig), C.POINTER(AdamWTensor), i32,

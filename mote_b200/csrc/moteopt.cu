@@ -39,7 +39,8 @@ std::atomic<unsigned long long> g_launches{0};
 // is at least kNsChunkWaves waves of tiles: c1 (32 waves) 1.44 -> 1.39 ms, the same bits; three runs gave 1.40 ms,
 // four 1.46 ms (the runs' phases get too short to keep every pair busy past their dependency waits).
 constexpr int kNsChunkWaves = 24;
-std::atomic<int> g_ns_persistent{-1};   // Newton-Schulz launch mode (moteopt_ns_set_persistent): 1, 0, or -1 = auto
+std::atomic<int> g_ns_persistent{-1};
+std::atomic<int> g_ns_tall{1};   // tall matrices iterated as stored (moteopt_ns_set_tall): 1, or 0 = transposed   // Newton-Schulz launch mode (moteopt_ns_set_persistent): 1, 0, or -1 = auto
 // Auto mode: one persistent launch while an iteration is at most this many waves of CTA-pair tiles; above it the
 // per-phase launches' ramps are amortised and their leaner tiles win (measured: c1 at 32 waves favours the
 // persistent launch, c2 at 197 waves the per-phase launches by ~10 %).
@@ -192,6 +193,7 @@ struct MatRef {
 struct GroupPlan {
   int rows, cols;          // source matrix dims (R x C)
   int transposed;          // R > C
+  int tall = 0;            // R > C iterated as stored: X is [count][R][C] (m = C, n = R), no transposing passes
   int mv, nv, m, n;        // X dims: valid and padded to multiples of 8
   std::vector<MatRef> mats;
   size_t off_x0 = 0, off_x1 = 0, off_a = 0, off_b = 0;
@@ -222,9 +224,15 @@ struct ShapeKey {
 // shapes: per source (batch, rows, cols); norm_numels: the tensors of the global grad norm (may be empty)
 // Partials one matrix's apply pass writes: one per 16K-element chunk when the matrix is iterated as stored (no
 // transpose, no padding: the flat kernel), else one per 64 x 64 tile (the tiled kernel).
-int64_t apply_partials_per_slice(int64_t r, int64_t c) {
-  const bool flat = r <= c && r % 8 == 0 && c % 8 == 0;
+int64_t apply_partials_per_slice(int64_t r, int64_t c, bool flat) {
   return flat ? cdiv(r * c, kChunk) : cdiv(c, kNormTile) * cdiv(r, kNormTile);
+}
+
+// A matrix is iterated as it is stored when it needs no padding and either has no more rows than columns or is
+// iterated tall (its X0 / final iterate then has the parameter's own layout and the normalise / apply are flat
+// passes).
+bool stored_as_iterated(const GroupPlan& g) {
+  return g.tall || (!g.transposed && g.m == g.rows && g.n == g.cols);
 }
 
 int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shapes, const std::vector<int64_t>& norm_numels,
@@ -254,6 +262,10 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
       g.m = static_cast<int>(align_up(g.mv, 8));
       g.n = static_cast<int>(align_up(g.nv, 8));
       g.gram = ns_variant == 1 && ns_steps > 0 && g.nv >= 2 * g.mv;
+      // a tall matrix without padding is iterated as stored (the same products in the same order as its transpose's
+      // iteration), except under the Gram variant, whose phases read X row-wise
+      g.tall = g.transposed && !g.gram && k.rows % 8 == 0 && k.cols % 8 == 0 &&
+               g_ns_tall.load(std::memory_order_relaxed) != 0;
       g.mats.assign(all.begin() + start, all.begin() + std::min(all.size(), start + kMaxMatsPerGroup));
       L->groups.push_back(std::move(g));
     }
@@ -282,10 +294,13 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
   off = align_up(off + 4 * (L->mat_chunk_start.size() - 1), 256);
   L->off_done = off;   // persistent Newton-Schulz: per matrix of a launch set and phase, completion arrivals
   off = align_up(off + 4 * 3 * static_cast<size_t>(ns::kMaxApply), 256);
+  std::map<ShapeKey, bool> flat_of;   // every group of a shape is iterated the same way
+  for (const GroupPlan& g : L->groups) flat_of[ShapeKey{g.rows, g.cols}] = stored_as_iterated(g);
   L->param_apply_start.assign(1, 0);   // the apply pass's sums of squares, contiguous per Muon param
   for (const auto& sh : shapes) {
     const int64_t b = std::get<0>(sh), r = std::get<1>(sh), c = std::get<2>(sh);
-    L->param_apply_start.push_back(L->param_apply_start.back() + static_cast<int>(b * apply_partials_per_slice(r, c)));
+    L->param_apply_start.push_back(L->param_apply_start.back() +
+                                   static_cast<int>(b * apply_partials_per_slice(r, c, flat_of[ShapeKey{r, c}])));
   }
   L->off_apply = off;
   off = align_up(off + sizeof(double) * static_cast<size_t>(L->param_apply_start.back()), 1024);
@@ -318,9 +333,10 @@ int build_layout(const std::vector<std::tuple<int64_t, int64_t, int64_t>>& shape
 // cache of encoded tensor maps, keyed by the group's buffers and geometry
 struct MapKey {
   uintptr_t x0, x1, a, b;
-  int m, n, count, dev;
+  int m, n, count, dev, tall;
   bool operator<(const MapKey& o) const {
-    return std::tie(x0, x1, a, b, m, n, count, dev) < std::tie(o.x0, o.x1, o.a, o.b, o.m, o.n, o.count, o.dev);
+    return std::tie(x0, x1, a, b, m, n, count, dev, tall) <
+           std::tie(o.x0, o.x1, o.a, o.b, o.m, o.n, o.count, o.dev, o.tall);
   }
 };
 struct MapSet {
@@ -334,7 +350,8 @@ int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
   MO_CUDA(cudaGetDevice(&dev));
   const int cnt = static_cast<int>(g.mats.size());
   MapKey key{reinterpret_cast<uintptr_t>(ws + g.off_x0), reinterpret_cast<uintptr_t>(ws + g.off_x1),
-             reinterpret_cast<uintptr_t>(ws + g.off_a), reinterpret_cast<uintptr_t>(ws + g.off_b), g.m, g.n, cnt, dev};
+             reinterpret_cast<uintptr_t>(ws + g.off_a), reinterpret_cast<uintptr_t>(ws + g.off_b), g.m, g.n, cnt, dev,
+             g.tall};
   std::lock_guard<std::mutex> lk(g_map_mu);
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
@@ -344,16 +361,17 @@ int group_maps(char* ws, const GroupPlan& g, MapSet* out) {
   MapSet s;
   std::memset(&s, 0, sizeof(s));
   void* x[2] = {ws + g.off_x0, ws + g.off_x1};
+  const int xin = g.tall ? g.m : g.n, xout = g.tall ? g.n : g.m;   // X is [count][xout][xin]
   for (int k = 0; k < 2; ++k) {
-    MO_TRY(make_map(&s.xk[k], x[k], g.n, g.m, cnt, ns::BK, ns::HM));
-    MO_TRY(make_map(&s.xmn[k], x[k], g.n, g.m, cnt, 64, ns::BK));
+    MO_TRY(make_map(&s.xk[k], x[k], xin, xout, cnt, ns::BK, ns::HM));
+    MO_TRY(make_map(&s.xmn[k], x[k], xin, xout, cnt, 64, ns::BK));
   }
   MO_TRY(make_map(&s.ak, ws + g.off_a, g.m, g.m, cnt, ns::BK, ns::HM));
   MO_TRY(make_map(&s.bk, ws + g.off_b, g.m, g.m, cnt, ns::BK, ns::HM));
   MO_TRY(make_map(&s.amn, ws + g.off_a, g.m, g.m, cnt, 64, ns::BK));
   MO_TRY(make_map(&s.bmn, ws + g.off_b, g.m, g.m, cnt, 64, ns::BK));
   for (int k = 0; k < 2; ++k)
-    MO_TRY(make_map(&s.xe[k], x[k], g.n, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
+    MO_TRY(make_map(&s.xe[k], x[k], xin, xout, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
   MO_TRY(make_map(&s.ae, ws + g.off_a, g.m, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
   MO_TRY(make_map(&s.be, ws + g.off_b, g.m, g.m, cnt, ns::EPI_TILE, ns::EPI_TILE, CU_TENSOR_MAP_SWIZZLE_64B));
   if (g_maps.size() > 4096) g_maps.clear();
@@ -543,9 +561,6 @@ int check_muon(const moteopt_muon_param* p, int n, const moteopt_muon_config* cf
 
 EmaConsts ema_consts(double weight);
 
-// A matrix is iterated as it is stored when it has no more rows than columns and needs no padding: its X0 / final
-// iterate then has the parameter's own layout and the normalise / apply are flat passes.
-bool stored_as_iterated(const GroupPlan& g) { return !g.transposed && g.m == g.rows && g.n == g.cols; }
 
 int launch_flat_norm(const std::vector<FlatNormSeg>& segs, int has_div, float div, const float* coef,
                      const float* den, int sms, cudaStream_t st, const float* div_dev = nullptr) {
@@ -862,6 +877,7 @@ int run_ns_reference(const std::vector<const GroupPlan*>& groups, const Layout& 
       G.count = static_cast<int>(g.mats.size());
       G.first = first;
       G.transposed = g.transposed;
+      G.tall = g.tall;
       first += G.count;
     }
     // the tile sequence [iteration][chunk][phase][group][matrix][tile]: 256 x 256 tiles, one per CTA pair; A and B are
@@ -1096,7 +1112,7 @@ int run_apply(const moteopt_muon_param* P, const moteopt_muon_config* cfg, const
       if (ema != nullptr && ema[ref.src] != nullptr) e = ema[ref.src] + static_cast<int64_t>(ref.slice) * pp.rows * pp.cols;
       double* part = norms == nullptr ? nullptr
                                      : apply_partials + L.param_apply_start[ref.src] +
-                                           static_cast<int64_t>(ref.slice) * apply_partials_per_slice(pp.rows, pp.cols);
+                                           static_cast<int64_t>(ref.slice) * apply_partials_per_slice(pp.rows, pp.cols, stored_as_iterated(g));
       if (stored_as_iterated(g)) {
         FlatOutSeg S;
         std::memset(&S, 0, sizeof(S));
@@ -1370,6 +1386,7 @@ int moteopt_ipc_close(void* base) {
 }
 
 int moteopt_ns_set_persistent(int mode) { return g_ns_persistent.exchange(mode < 0 ? -1 : (mode ? 1 : 0)); }
+int moteopt_ns_set_tall(int on) { return g_ns_tall.exchange(on ? 1 : 0); }
 
 int moteopt_read_status(void* workspace, int* status, float* norm_and_coef, int clear, moteopt_stream_t stream) {
   if (workspace == nullptr) return fail(MOTEOPT_ERR_INVALID, "workspace is null");
@@ -2034,13 +2051,13 @@ int moteopt_newton_schulz_variant(const void* G, int g_dtype, void* out, int64_t
       M.x = ws + g.off_x0 + static_cast<size_t>(posm[s0 + i]) * g.m * g.n * 2;
       M.rows = g.rows;
       M.cols = g.cols;
-      M.m_pad = g.m;
-      M.n_pad = g.n;
-      M.transposed = g.transposed;
+      M.m_pad = g.tall ? g.n : g.m;   // X's rows and columns (a tall X has the matrix's own layout)
+      M.n_pad = g.tall ? g.m : g.n;
+      M.transposed = g.tall ? 0 : g.transposed;
       M.dtype = g_dtype;
       M.den_index = s0 + i;
-      M.tiles_x = static_cast<int>(cdiv(g.n, kNormTile));
-      M.tiles = M.tiles_x * static_cast<int>(cdiv(g.m, kNormTile));
+      M.tiles_x = static_cast<int>(cdiv(M.n_pad, kNormTile));
+      M.tiles = M.tiles_x * static_cast<int>(cdiv(M.m_pad, kNormTile));
       max_tiles = std::max(max_tiles, M.tiles);
     }
     if (A.has_div) ns_normalize_kernel<true><<<dim3(max_tiles, cnt), kMtThreads, 0, st>>>(A);
@@ -2063,9 +2080,9 @@ int moteopt_newton_schulz_variant(const void* G, int g_dtype, void* out, int64_t
       M.out = static_cast<char*>(out) + static_cast<size_t>(g.mats[pos].slice) * per * 2;
       M.rows = g.rows;
       M.cols = g.cols;
-      M.m_pad = g.m;
-      M.n_pad = g.n;
-      M.transposed = g.transposed;
+      M.m_pad = g.tall ? g.n : g.m;
+      M.n_pad = g.tall ? g.m : g.n;
+      M.transposed = g.tall ? 0 : g.transposed;
       M.tiles_x = static_cast<int>(cdiv(g.cols, kNormTile));
       M.tiles = M.tiles_x * static_cast<int>(cdiv(g.rows, kNormTile));
       all.push_back(M);

@@ -79,8 +79,13 @@ __device__ __forceinline__ Tile decode_tile(const Launch& L, int t) {
     const int per = T * L.tiles_n[gi];
     x.b = r / per;
     r -= x.b * per;
-    ti = r / L.tiles_n[gi];
-    tj = r - ti * L.tiles_n[gi];
+    if (L.g[gi].tall) {   // n x m output: row blocks over the tall side
+      ti = r / T;
+      tj = r - ti * T;
+    } else {
+      ti = r / L.tiles_n[gi];
+      tj = r - ti * L.tiles_n[gi];
+    }
   } else {   // upper-triangle blocks, row-major
     const int per = T * (T + 1) / 2;
     x.b = r / per;
@@ -104,11 +109,25 @@ __device__ __forceinline__ int phase_k(int phase, const Group& G) { return phase
 // Whether k-block kb of tile x reads its A operand (rows i) and its B operand (rows j, or X for kUpdate) MN-major.
 // In kPoly (A A) and kUpdate (B X) the left factor is stored only at and above the diagonal: columns k in a block
 // left of row block i come from the mirror block (k, i) as a transposed box. kPoly's right factor is A again (rows
-// j); kUpdate's is X, always MN-major.
-__device__ __forceinline__ void operand_mn(const Tile& x, int kb, bool& a_mn, bool& b_mn) {
+// j); kUpdate's is X, always MN-major. A tall group (X stored n x m): the Gram phase X^T X reads columns i and j of
+// X, both MN-major; the update X B reads rows i of X K-major and B's rows j like kPoly's right factor.
+__device__ __forceinline__ void operand_mn(const Tile& x, int kb, bool tall, bool& a_mn, bool& b_mn) {
   const int kt = (kb * BK) / TM;
+  if (tall && x.phase != kPoly) {
+    a_mn = x.phase == kGram;
+    b_mn = x.phase == kGram || kt < x.j0 / TN;
+    return;
+  }
   a_mn = x.phase != kGram && kt < x.i0 / TM;
   b_mn = x.phase == kUpdate || (x.phase == kPoly && kt < x.j0 / TN);
+}
+
+// Rows and columns of tile x's output matrix (an n x m update of a tall group, else m x n or m x m).
+__device__ __forceinline__ int out_rows(const Tile& x, const Group& G) {
+  return (x.phase == kUpdate && G.tall) ? G.n : G.m;
+}
+__device__ __forceinline__ int out_cols(const Tile& x, const Group& G) {
+  return x.phase == kUpdate ? (G.tall ? G.m : G.n) : G.m;
 }
 
 // A diagonal block of the symmetric products (kGram X X^T, kPoly A A): its two operands are the same rows, read the
@@ -147,12 +166,13 @@ __device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t
       fence_proxy_async_global();   // the TMA loads below observe the data the counters released
     }
     const int nk = (phase_k(x.phase, G) + BK - 1) / BK;
-    MO_CHECK(x.gi >= 0 && x.gi < L.n_groups && x.b >= 0 && x.b < G.count && x.i0 < G.m &&
-             x.j0 < (x.phase == kUpdate ? G.n : G.m) && (x.phase == kUpdate || x.i0 <= x.j0) && nk > 0);
-    const CUtensorMap* amap = x.phase == kGram ? &G.xk[x.src] : (x.phase == kPoly ? &G.ak : &G.bk);
-    const CUtensorMap* amap_mn = x.phase == kPoly ? &G.amn : &G.bmn;
-    const CUtensorMap* bmap = x.phase == kGram ? &G.xk[x.src] : &G.ak;
-    const CUtensorMap* bmap_mn = x.phase == kPoly ? &G.amn : &G.xmn[x.src];
+    MO_CHECK(x.gi >= 0 && x.gi < L.n_groups && x.b >= 0 && x.b < G.count && x.i0 < out_rows(x, G) &&
+             x.j0 < out_cols(x, G) && (x.phase == kUpdate || x.i0 <= x.j0) && nk > 0);
+    const bool tall = G.tall != 0;
+    const CUtensorMap* amap = x.phase == kGram ? &G.xk[x.src] : (x.phase == kPoly ? &G.ak : (tall ? &G.xk[x.src] : &G.bk));
+    const CUtensorMap* amap_mn = x.phase == kPoly ? &G.amn : (x.phase == kGram ? &G.xmn[x.src] : &G.bmn);
+    const CUtensorMap* bmap = x.phase == kGram ? &G.xk[x.src] : (x.phase == kPoly ? &G.ak : &G.bk);
+    const CUtensorMap* bmap_mn = x.phase == kPoly ? &G.amn : (tall && x.phase == kUpdate ? &G.bmn : &G.xmn[x.src]);
     const int ia = x.i0 + HM * static_cast<int>(rank), jb = x.j0 + (TN / 2) * static_cast<int>(rank);
     const bool diag = on_diagonal(x);   // B = A: the stage holds one operand, which the MMA reads as both
     for (int kb = 0; kb < nk; ++kb) {
@@ -161,7 +181,7 @@ __device__ __forceinline__ void producer(const Launch& L, uint32_t rank, uint8_t
       if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (diag ? A_BYTES : STAGE_BYTES));
       const int k0 = kb * BK;
       bool a_mn, b_mn;
-      operand_mn(x, kb, a_mn, b_mn);
+      operand_mn(x, kb, tall, a_mn, b_mn);
       uint8_t* dsta = sa + stage * A_BYTES;
       if (a_mn) {   // rows ia..ia+127 of a block left of the diagonal = columns of the stored mirror block
         tma_load_3d_pair(dsta, amap_mn, bar, ia, k0, x.b);
@@ -217,7 +237,7 @@ __device__ __forceinline__ void mma(const Launch& L, uint8_t* sa, uint8_t* sb, u
       const uint32_t a0 = smem_u32(sa + stage * A_BYTES);
       const uint32_t b0 = on_diagonal(x) ? a0 : smem_u32(sb + stage * B_BYTES);
       bool a_mn, b_mn;
-      operand_mn(x, kb, a_mn, b_mn);
+      operand_mn(x, kb, G.tall != 0, a_mn, b_mn);
       const uint32_t idesc = idesc_bf16_f32(TM, TN, a_mn, b_mn);
 #pragma unroll
       for (int kk = 0; kk < BK / 16; ++kk) {
@@ -275,14 +295,14 @@ __device__ __forceinline__ void epilogue(const Launch& L, uint32_t rank, uint64_
     const bool has_aux = x.phase != kGram && !(x.phase == kUpdate && L.no_aux);
     const int acc = local & 1;
     const uint32_t use = static_cast<uint32_t>(local >> 1) & 1u;
-    const int out_cols = x.phase == kUpdate ? G.n : G.m;
+    const int ocols = out_cols(x, G);
     const int row0 = x.i0 + HM * static_cast<int>(rank) + q * 32;
-    const bool rows_ok = row0 < G.m;
+    const bool rows_ok = row0 < out_rows(x, G);
     const int jc0 = x.j0 + half * (kChunks * EPI_TILE);
     const CUtensorMap* omap = x.phase == kGram ? &G.ae : (x.phase == kPoly ? &G.be : &G.xe[x.src ^ 1]);
     const CUtensorMap* amap = x.phase == kPoly ? &G.ae : &G.xe[x.src];
     int nch = 0;
-    while (nch < kChunks && jc0 + nch * EPI_TILE < out_cols) ++nch;
+    while (nch < kChunks && jc0 + nch * EPI_TILE < ocols) ++nch;
     const bool work = rows_ok && nch > 0;
     int loaded = 1;
     if (lane == 0 && work) {

@@ -55,7 +55,8 @@ struct alignas(64) Group {
   int count;            // matrices in the group
   int first;            // index of the group's first matrix in the launch's matrix numbering
   int transposed;       // X = u^T (the parameter has more rows than columns)
-  int pad_;
+  int tall;             // X is a tall matrix as stored: [count][n][m] (n >= m rows); the Gram phase is X^T X with both
+                        // operands MN-major, the update X' = a X + X B runs over n x m tiles with B as the right factor
 };
 
 // The Muon apply of one matrix (mote/train/muon.py:93-99): p = p*(1-decay) (if decay), p += -lr*(O*scale).

@@ -114,6 +114,63 @@ def test_newton_schulz_launch_modes_agree(dev, shape):
     _status_ok(dev)
 
 
+@pytest.mark.parametrize("shape", [(2, 3072, 768), (1, 4096, 1024), (3, 2048, 768), (2, 520, 264), (4, 136, 72),
+                                   (3, 130, 72)])
+def test_tall_matrices_iterated_as_stored_equal_the_transposed_iteration(dev, shape):
+    """A matrix with more rows than columns iterated in its stored layout (A = X^T X, X' = a X + X B; the default)
+    gives the bits of its transpose's iteration, for 1 and 5 iterations and both launch modes; shapes not a multiple
+    of 8 (130 x 72) keep the transposed path either way."""
+    from mote_b200 import _lib as L
+    from mote_b200 import ops
+    u = torch.from_numpy(ns_input(shape, 91)).to(dev)
+    prev_tall = L.lib.moteopt_ns_set_tall(1)
+    prev_mode = L.lib.moteopt_ns_set_persistent(-1)
+    try:
+        out = {}
+        for tall in (1, 0):
+            L.lib.moteopt_ns_set_tall(tall)
+            for mode in (1, 0):
+                L.lib.moteopt_ns_set_persistent(mode)
+                out[(tall, mode)] = [ops.newton_schulz(u, s) for s in (1, 5)]
+    finally:
+        L.lib.moteopt_ns_set_tall(prev_tall)
+        L.lib.moteopt_ns_set_persistent(prev_mode)
+    for key, v in out.items():
+        for x, y in zip(v, out[(0, 1)]):
+            assert torch.equal(x, y), key
+    _status_ok(dev)
+
+
+def test_c1_muon_set_tall_and_transposed_agree(dev):
+    """c1's Muon step (12 of its 80 matrices are 3072 x 768) with tall matrices iterated as stored (flat normalise and
+    apply passes) equals the step with them transposed, bit for bit, params and momentum."""
+    from mote_b200 import _lib as L
+    from mote_b200 import configs
+    from mote_b200.functional import MuonItem, muon_step
+    w = configs.CONFIGS["c1"]()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(8)
+    base = [torch.randn(s, generator=gen, device=dev) * 0.02 for s in w.muon_shapes]
+    grads = [(torch.randn(s, generator=gen, device=dev) * 1e-3).to(torch.bfloat16) for s in w.muon_shapes]
+    out = []
+    prev = L.lib.moteopt_ns_set_tall(1)
+    try:
+        for tall in (1, 0):
+            L.lib.moteopt_ns_set_tall(tall)
+            ps = [b.clone() for b in base]
+            bufs = [torch.zeros_like(p) for p in ps]
+            items = [MuonItem(p, g, m, 0.02, 0.002) for p, g, m in zip(ps, grads, bufs)]
+            for _ in range(2):
+                muon_step(items, ns_steps=5)
+            torch.cuda.synchronize()
+            out.append((ps, bufs))
+    finally:
+        L.lib.moteopt_ns_set_tall(prev)
+    for a, b in zip(out[0][0] + out[0][1], out[1][0] + out[1][1]):
+        assert torch.equal(a, b)
+    _status_ok(dev)
+
+
 def test_c1_muon_set_launch_modes_agree(dev):
     """c1's 80 matrices (three shape groups, 32 waves of tiles per iteration: the persistent launch runs them in two
     runs) step to the same bits in both launch modes."""
