@@ -37,7 +37,8 @@ int fail(int code, const std::string& msg) {
 std::atomic<unsigned long long> g_launches{0};
 // The persistent launch takes an iteration's matrices in two runs (each through all three phases) once an iteration
 // is at least kNsChunkWaves waves of tiles: c1 (32 waves) 1.44 -> 1.39 ms, the same bits; three runs gave 1.40 ms,
-// four 1.46 ms (the runs' phases get too short to keep every pair busy past their dependency waits).
+// four 1.46 ms (the runs' phases get too short to keep every pair busy past their dependency waits), and two runs of
+// half of c1 (a 2-GPU rank's share, 16 waves) 0.76 against 0.71 ms for one.
 constexpr int kNsChunkWaves = 24;
 std::atomic<int> g_ns_persistent{-1};
 std::atomic<int> g_ns_tall{1};   // tall matrices iterated as stored (moteopt_ns_set_tall): 1, or 0 = transposed   // Newton-Schulz launch mode (moteopt_ns_set_persistent): 1, 0, or -1 = auto
